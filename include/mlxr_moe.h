@@ -1,0 +1,221 @@
+/*
+ * mlxr_moe.h — C ABI of the B200 (sm_100a) implementation of mlxr's MoE
+ * block and its quantised-matmul op family.
+ *
+ * The boundary follows the reference's FFI contract for these ops
+ * (crates/mlxr-sys -> mlx-c; wrapped by Guarded::try_from_op,
+ * crates/mlxr/src/utils/guard.rs:31-51): every entry point returns an int
+ * status, 0 on success; on failure a message is kept in a thread-local slot
+ * and read back with mlxr_cu_last_error() (the reference's C error callback
+ * into a thread-local, crates/mlxr/src/error.rs:229-290).
+ *
+ * Differences that follow from the device model:
+ *  - Arrays are caller-owned device pointers plus explicit sizes; nothing is
+ *    allocated on the compute path. Scratch comes from a caller-provided
+ *    workspace (mlxr_cu_moe_workspace_size).
+ *  - Work is queued asynchronously on the caller's stream (a cudaStream_t
+ *    passed as void*; NULL = the legacy default stream). Errors detected on
+ *    the device (a wait that timed out, an out-of-range expert index) land in
+ *    a status word read by mlxr_cu_moe_status().
+ *  - Only mode "affine" exists; bits in {2, 4, 8} for the op family, {4, 8}
+ *    for the MoE block; group sizes {32, 64, 128} (block: 64).
+ *
+ * Array layouts match MLX's packing as consumed by the reference:
+ *  packed weights uint32 [..., N, K*bits/32] with element j of a word at bits
+ *  [bits*j, bits*j+bits); scales/biases [..., N, K/group_size] in the
+ *  activation dtype (crates/mlxr/src/ops/quantization.rs:299-315 pins the
+ *  shapes).
+ */
+#ifndef MLXR_MOE_H
+#define MLXR_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MLXR_CU_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define MLXR_CU_API __attribute__((visibility("default")))
+#else
+#define MLXR_CU_API
+#endif
+
+typedef enum mlxr_cu_status {
+  MLXR_CU_OK = 0,
+  MLXR_CU_ERR_INVALID_ARGUMENT = 1, /* bad shape, null pointer, bad index */
+  MLXR_CU_ERR_UNSUPPORTED = 2,      /* bits / group size / mode not supported */
+  MLXR_CU_ERR_CUDA = 3,             /* a CUDA runtime or driver call failed */
+  MLXR_CU_ERR_WORKSPACE = 4,        /* workspace missing or too small */
+  MLXR_CU_ERR_TIMEOUT = 5,          /* a device-side bounded wait expired */
+  MLXR_CU_ERR_NCCL = 6,             /* a collective failed */
+  MLXR_CU_ERR_DEVICE_INDEX = 7      /* the device saw an out-of-range index */
+} mlxr_cu_status;
+
+typedef enum mlxr_cu_dtype {
+  MLXR_CU_BFLOAT16 = 0,
+  MLXR_CU_FLOAT16 = 1,
+  MLXR_CU_FLOAT32 = 2
+} mlxr_cu_dtype;
+
+/* ------------------------------------------------------------ errors -- */
+
+/* Last error message of the calling thread, or NULL. Replaces the
+ * thread-local LAST_MLX_ERROR slot (crates/mlxr/src/error.rs:239-290). */
+MLXR_CU_API const char* mlxr_cu_last_error(void);
+MLXR_CU_API void mlxr_cu_clear_error(void);
+MLXR_CU_API int mlxr_cu_abi_version(void);
+
+/* ---------------------------------------------------- the op family -- */
+
+/* quantize (crates/mlxr/src/ops/quantization.rs:47-70 -> mlx_quantize):
+ * w [rows, cols] in dtype -> wq uint32 [rows, cols*bits/32],
+ * scales/biases [rows, cols/group_size] in dtype. mode must be "affine" or
+ * NULL. group_size 0 / bits 0 select the reference defaults 64 / 4
+ * (quantization.rs:11-13). */
+MLXR_CU_API int mlxr_cu_quantize(const void* w, mlxr_cu_dtype dtype, int64_t rows, int64_t cols, int group_size, int bits,
+                     const char* mode, uint32_t* wq, void* scales, void* biases, void* stream);
+
+/* dequantize (quantization.rs:118-146 -> mlx_dequantize):
+ * out[r][k] = scale * q + bias (fp32 fma), written in out_dtype. */
+MLXR_CU_API int mlxr_cu_dequantize(const uint32_t* wq, const void* scales, const void* biases, mlxr_cu_dtype sb_dtype,
+                       int64_t rows, int64_t cols, int group_size, int bits, const char* mode, void* out,
+                       mlxr_cu_dtype out_dtype, void* stream);
+
+/* quantized_matmul (quantization.rs:81-112 -> mlx_quantized_matmul;
+ * QuantizedLinear::forward, crates/mlxr/src/layers/quantized.rs:356-371):
+ * x [M, K] (x_dtype; scales/biases share it) times the dequantised w:
+ *   transpose != 0: w packed [N, K*bits/32], out = x @ W^T
+ *   transpose == 0: w packed [K, N*bits/32], out = x @ W
+ * out [M, N] in x_dtype, fp32 accumulation. biases may not be NULL (affine). */
+MLXR_CU_API int mlxr_cu_quantized_matmul(const void* x, mlxr_cu_dtype x_dtype, int64_t M, int64_t K, const uint32_t* w,
+                             const void* scales, const void* biases, int64_t N, int transpose, int group_size,
+                             int bits, const char* mode, void* out, void* stream);
+
+/* gather_qmm (quantization.rs:171-221 -> mlx_gather_qmm):
+ * out[p] = x[lhs[p]] @ dequant(w[rhs[p]])^T for p in [0, num_indices),
+ * x [x_batch, M, K], w packed [w_batch, N, K*bits/32] (transpose) or
+ * [w_batch, K, N*bits/32]; out [num_indices, M, N] in x_dtype. lhs / rhs may
+ * be NULL, meaning the identity (MLX's broadcast of absent indices, flattened
+ * by the caller). sorted_indices is the reference's hint (rhs sorted
+ * ascending); results do not depend on it. */
+MLXR_CU_API int mlxr_cu_gather_qmm(const void* x, mlxr_cu_dtype x_dtype, int64_t x_batch, int64_t M, int64_t K,
+                       const uint32_t* w, const void* scales, const void* biases, int64_t w_batch, int64_t N,
+                       const uint32_t* lhs_indices, const uint32_t* rhs_indices, int64_t num_indices, int transpose,
+                       int group_size, int bits, const char* mode, int sorted_indices, void* out, void* stream);
+
+/* gather_mm (crates/mlxr/src/ops/arithmetic.rs:1577-1609 -> mlx_gather_mm):
+ * out[p] = a[lhs[p]] @ b[rhs[p]], a [a_batch, M, K], b [b_batch, K, N], all in
+ * dtype, fp32 accumulation. */
+MLXR_CU_API int mlxr_cu_gather_mm(const void* a, const void* b, mlxr_cu_dtype dtype, int64_t a_batch, int64_t M, int64_t K,
+                      int64_t b_batch, int64_t N, const uint32_t* lhs_indices, const uint32_t* rhs_indices,
+                      int64_t num_indices, int sorted_indices, void* out, void* stream);
+
+/* -------------------------------------------------------- MoE block -- */
+
+/* Block dimensions (Qwen 3.5/3.6 text config fields,
+ * crates/mlxr-lm/src/qwen3_5/text/config.rs:124-152). */
+typedef struct mlxr_cu_moe_config {
+  int32_t hidden_size;                     /* D */
+  int32_t num_experts;                     /* E */
+  int32_t num_experts_per_tok;             /* K */
+  int32_t moe_intermediate_size;           /* I */
+  int32_t shared_expert_intermediate_size; /* Is; 0 = no shared expert */
+  int32_t group_size;                      /* 64 */
+  int32_t bits;                            /* routed experts: 4 or 8 */
+  int32_t shared_bits;                     /* shared expert + its gate: 4 or 8 */
+  int32_t norm_topk_prob;                  /* 1 = renormalise top-k (moe.rs:136-138) */
+} mlxr_cu_moe_config;
+
+/* One quantised projection: packed weight, scales, biases (bf16). */
+typedef struct mlxr_cu_qlinear {
+  const uint32_t* weight;
+  const void* scales;
+  const void* biases;
+} mlxr_cu_qlinear;
+
+/* Parameters of Qwen35MoeBlock (crates/mlxr-lm/src/qwen3_5/text/moe.rs:52-78):
+ * router `gate` [E, D] bf16 (unquantised), `switch_mlp.{gate,up}_proj`
+ * [E, I, D*b/32] and `down_proj` [E, D, I*b/32] with scales/biases
+ * [E, N, Kin/64] bf16, and the optional shared expert
+ * (`shared_expert.{gate,up,down}_proj`, `shared_expert_gate` [1, D]). */
+typedef struct mlxr_cu_moe_weights {
+  const void* router_weight; /* [E, D] bf16 */
+  const float* router_bias;  /* [E] fp32 added to the logits, or NULL */
+  mlxr_cu_qlinear switch_gate;
+  mlxr_cu_qlinear switch_up;
+  mlxr_cu_qlinear switch_down;
+  mlxr_cu_qlinear shared_gate;
+  mlxr_cu_qlinear shared_up;
+  mlxr_cu_qlinear shared_down;
+  mlxr_cu_qlinear shared_expert_gate;
+} mlxr_cu_moe_weights;
+
+/* Optional routing outputs (any member may be NULL). indices/weights are the
+ * top-k in rank order (prob desc, expert asc); counts/offsets describe the
+ * stable expert-sorted order of the flat rows f = t*K + k (gather_sort,
+ * crates/mlxr-lm/src/nn/switch.rs:499-512); sorted_rows[pos] = f and
+ * inverse[f] = pos (scatter_unsort, switch.rs:514-517). */
+typedef struct mlxr_cu_moe_routing {
+  int32_t* indices;     /* [T, K] */
+  void* weights;        /* [T, K] bf16 */
+  int32_t* counts;      /* [E] */
+  int32_t* offsets;     /* [E + 1] */
+  int32_t* sorted_rows; /* [T*K] */
+  int32_t* inverse;     /* [T*K] */
+} mlxr_cu_moe_routing;
+
+/* Bytes of device workspace mlxr_cu_moe_block_forward needs for num_tokens. */
+MLXR_CU_API int mlxr_cu_moe_workspace_size(const mlxr_cu_moe_config* cfg, int64_t num_tokens, size_t* bytes);
+
+/* Qwen35MoeBlock::forward (moe.rs:116-146) for x [T, D] bf16 -> out [T, D]
+ * bf16: router -> permute -> grouped gate/up + SwiGLU -> grouped down ->
+ * weighted combine (+ sigmoid-gated shared expert). Replaces the chain of
+ * mlx_quantized_matmul / mlx_softmax_axis / mlx_argpartition_axis /
+ * mlx_take_along_axis / mlx_gather_qmm calls the block issues
+ * (SplitSwitchFfn::forward_with_combine, switch.rs:446-474). The workspace
+ * must be 256-byte aligned and at least mlxr_cu_moe_workspace_size bytes. */
+MLXR_CU_API int mlxr_cu_moe_block_forward(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights, const void* x,
+                              int64_t num_tokens, void* out, const mlxr_cu_moe_routing* routing, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
+/* Reads (synchronising on stream) the device status word of the last forward
+ * that used this workspace: MLXR_CU_OK, MLXR_CU_ERR_TIMEOUT or
+ * MLXR_CU_ERR_DEVICE_INDEX. */
+MLXR_CU_API int mlxr_cu_moe_status(const void* workspace, void* stream);
+
+/* Reads and clears (synchronising on stream) the device status word the op
+ * family (quantize ... gather_mm) shares on the current device:
+ * MLXR_CU_ERR_DEVICE_INDEX when an lhs/rhs index was outside its batch (the
+ * affected output blocks are left unwritten). */
+MLXR_CU_API int mlxr_cu_op_status(void* stream);
+
+/* Router alone (moe.rs:123-138): logits = x @ gate^T (+bias) rounded to
+ * bf16, softmax (fp32 inside, bf16 probabilities), top-k by (prob desc,
+ * expert asc), renormalised bf16 weights. logits / probs [T, E] bf16 may be
+ * NULL. Bit-exact with the routing contract the oracle states. */
+MLXR_CU_API int mlxr_cu_moe_router(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights, const void* x,
+                       int64_t num_tokens, int32_t* indices, void* topk_weights, void* logits, void* probs,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* Permute alone (gather_sort, switch.rs:499-512): stable sort of the flat
+ * rows by expert; x_sorted [T*K, D] bf16 receives x[sorted_rows[pos] / K]. */
+MLXR_CU_API int mlxr_cu_moe_permute(const mlxr_cu_moe_config* cfg, const int32_t* indices, int64_t num_tokens, const void* x,
+                        int32_t* counts, int32_t* offsets, int32_t* sorted_rows, int32_t* inverse, void* x_sorted,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------ synthetic inputs -- */
+
+/* Seeded N(0, stddev^2) samples rounded to bf16: Philox4x32-10 keyed by
+ * seed, counter (pair index, stream), Box-Muller in fp64 (the generator the
+ * benchmark configurations are defined with). */
+MLXR_CU_API int mlxr_cu_synth_normal_bf16(uint64_t seed, uint64_t stream_id, int64_t n, float stddev, void* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MLXR_MOE_H */

@@ -1,0 +1,74 @@
+"""Builds libmlxr_moe.so (the C-ABI library) in-tree for sm_100a.
+
+Each .cu is compiled to an object with nvcc (-gencode
+arch=compute_100a,code=sm_100a) and the objects are linked into one shared
+library next to this file. Rebuilds only what changed.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import subprocess
+import sys
+from concurrent.futures import ThreadPoolExecutor
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "csrc")
+BUILD = os.path.join(HERE, "_build")
+LIB = os.path.join(HERE, "libmlxr_moe.so")
+INCLUDE = os.path.join(os.path.dirname(HERE), "include")
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+
+SOURCES = ["quant_ops.cu", "grouped_gemm.cu", "moe_block.cu"]
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "-Xcompiler", "-fPIC,-fvisibility=hidden",
+    "--expt-relaxed-constexpr",
+    "-I" + INCLUDE,
+]
+
+
+def _deps_mtime() -> float:
+    m = os.path.getmtime(os.path.join(INCLUDE, "mlxr_moe.h"))
+    for f in os.listdir(CSRC):
+        if f.endswith((".cuh", ".h")):
+            m = max(m, os.path.getmtime(os.path.join(CSRC, f)))
+    return m
+
+
+def _compile(src: str, verbose_ptxas: bool) -> str:
+    obj = os.path.join(BUILD, src.replace(".cu", ".o"))
+    srcp = os.path.join(CSRC, src)
+    if os.path.exists(obj) and os.path.getmtime(obj) >= max(os.path.getmtime(srcp), _deps_mtime()) and not verbose_ptxas:
+        return obj
+    cmd = [NVCC, *NVCC_FLAGS, "-c", srcp, "-o", obj]
+    if verbose_ptxas:
+        cmd.insert(1, "-Xptxas=-v")
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        sys.stderr.write(r.stdout + r.stderr)
+        raise RuntimeError(f"nvcc failed for {src}")
+    if verbose_ptxas:
+        sys.stderr.write(r.stderr)
+    return obj
+
+
+def build(verbose_ptxas: bool = False) -> str:
+    os.makedirs(BUILD, exist_ok=True)
+    with ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
+        objs = list(ex.map(lambda s: _compile(s, verbose_ptxas), SOURCES))
+    if not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
+        cmd = [NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", LIB, *objs, "-cudart", "static"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            sys.stderr.write(r.stdout + r.stderr)
+            raise RuntimeError("link failed")
+    return LIB
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ptxas-v", action="store_true", help="print register / spill / smem usage")
+    a = ap.parse_args()
+    print(build(a.ptxas_v))

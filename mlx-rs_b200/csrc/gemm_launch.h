@@ -1,0 +1,35 @@
+// Launch interface of the grouped dequantising GEMM (grouped_gemm.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mlxr {
+
+struct GemmTile;
+
+struct GroupedGemmProblem {
+  int nmat;                   // 2 = gate/up pair with SwiGLU epilogue, 1 = plain
+  int bn;                     // token-tile width (16, 32, 64, 128, 256)
+  int bits;                   // 4 or 8
+  const uint32_t* w[2];       // packed weights, [w_rows, k_dim*bits/32]
+  const uint16_t* s[2];       // bf16 scales [w_rows, k_dim/64]
+  const uint16_t* b[2];       // bf16 biases
+  int64_t w_rows;             // num_experts * n_out
+  int n_out;                  // output features per expert (multiple of 128)
+  int k_dim;                  // reduction length (multiple of 64)
+  int num_experts;
+  const uint16_t* act;        // bf16 activations [act_rows, k_dim] (sorted rows)
+  int64_t act_rows;
+  const GemmTile* tiles;      // device tile list
+  const int32_t* num_tiles;   // device count
+  int max_tiles;
+  uint16_t* out;              // bf16 [rows, n_out]
+  int* status;
+  int grid;                   // 0 = one CTA per SM
+};
+
+int launch_grouped_gemm(const GroupedGemmProblem& p, cudaStream_t st);
+int num_sms_current();
+
+}  // namespace mlxr

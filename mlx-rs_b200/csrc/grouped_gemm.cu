@@ -1,0 +1,111 @@
+// Host side of the grouped dequantising GEMM: tensor-map encoding and the
+// dispatch over (matrices per item, token-tile width, bits).
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "gemm_launch.h"
+#include "grouped_gemm.cuh"
+
+namespace mlxr {
+
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D row-major tensor map: inner extent `inner` elements, `rows` rows.
+static int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                       uint64_t rows, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz) {
+  auto enc = get_encode_fn();
+  if (!enc) return set_error(MLXR_CU_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0)
+    return set_error(MLXR_CU_ERR_INVALID_ARGUMENT, "TMA operand %p is not 16-byte aligned", base);
+  if ((inner * elem_bytes) % 16 != 0)
+    return set_error(MLXR_CU_ERR_INVALID_ARGUMENT, "TMA row pitch %llu bytes is not a multiple of 16",
+                     (unsigned long long)(inner * elem_bytes));
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {inner * (uint64_t)elem_bytes};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(MLXR_CU_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) inner=%llu rows=%llu box=%u x %u", (int)r,
+                     (unsigned long long)inner, (unsigned long long)rows, box_inner, box_rows);
+  return MLXR_CU_OK;
+}
+
+int num_sms_current() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+template <int NMAT, int BN, int BITS>
+static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
+  using C = GG<NMAT, BN, BITS>;
+  CUtensorMap ta0, ta1, tb;
+  const uint64_t kw = (uint64_t)p.k_dim * BITS / 32;
+  if (int rc = make_map_2d(&ta0, p.w[0], CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, kw, (uint64_t)p.w_rows, C::KW, C::BM,
+                           CU_TENSOR_MAP_SWIZZLE_NONE))
+    return rc;
+  if (NMAT == 2) {
+    if (int rc = make_map_2d(&ta1, p.w[1], CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, kw, (uint64_t)p.w_rows, C::KW, C::BM,
+                             CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+  } else {
+    ta1 = ta0;
+  }
+  if (int rc = make_map_2d(&tb, p.act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)p.k_dim, (uint64_t)p.act_rows,
+                           C::BK, BN, CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  auto kern = grouped_dequant_gemm_kernel<NMAT, BN, BITS>;
+  static bool attr_set = false;  // per instantiation; idempotent if raced
+  if (!attr_set) {
+    MLXR_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    attr_set = true;
+  }
+  GemmArgs a;
+  a.scales[0] = p.s[0];
+  a.scales[1] = NMAT == 2 ? p.s[1] : p.s[0];
+  a.biases[0] = p.b[0];
+  a.biases[1] = NMAT == 2 ? p.b[1] : p.b[0];
+  a.tiles = p.tiles;
+  a.num_tiles = p.num_tiles;
+  a.out = p.out;
+  a.n_out = p.n_out;
+  a.k_dim = p.k_dim;
+  a.num_experts = p.num_experts;
+  a.max_tiles = p.max_tiles;
+  a.status = p.status;
+  const int grid = p.grid > 0 ? p.grid : num_sms_current();
+  kern<<<grid, C::NUM_THREADS, C::SMEM_BYTES, st>>>(ta0, ta1, tb, a);
+  MLXR_LAUNCH_CHECK("grouped_dequant_gemm_kernel");
+  return MLXR_CU_OK;
+}
+
+int launch_grouped_gemm(const GroupedGemmProblem& p, cudaStream_t st) {
+  if (p.n_out % 128 != 0 || p.k_dim % 64 != 0)
+    return set_error(MLXR_CU_ERR_INVALID_ARGUMENT, "grouped gemm: n_out=%d must be a multiple of 128 and K=%d of 64",
+                     p.n_out, p.k_dim);
+#define MLXR_GG_CASE(NM, BNV, BT) \
+  if (p.nmat == NM && p.bn == BNV && p.bits == BT) return launch_one<NM, BNV, BT>(p, st);
+  MLXR_GG_CASE(2, 16, 4) MLXR_GG_CASE(2, 32, 4) MLXR_GG_CASE(2, 64, 4) MLXR_GG_CASE(2, 128, 4)
+  MLXR_GG_CASE(1, 16, 4) MLXR_GG_CASE(1, 32, 4) MLXR_GG_CASE(1, 64, 4) MLXR_GG_CASE(1, 128, 4) MLXR_GG_CASE(1, 256, 4)
+  MLXR_GG_CASE(2, 16, 8) MLXR_GG_CASE(2, 32, 8) MLXR_GG_CASE(2, 64, 8) MLXR_GG_CASE(2, 128, 8)
+  MLXR_GG_CASE(1, 16, 8) MLXR_GG_CASE(1, 32, 8) MLXR_GG_CASE(1, 64, 8) MLXR_GG_CASE(1, 128, 8) MLXR_GG_CASE(1, 256, 8)
+#undef MLXR_GG_CASE
+  return set_error(MLXR_CU_ERR_UNSUPPORTED, "grouped gemm: no kernel for nmat=%d bn=%d bits=%d", p.nmat, p.bn, p.bits);
+}
+
+}  // namespace mlxr

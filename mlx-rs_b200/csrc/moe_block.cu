@@ -1,0 +1,427 @@
+// MoE block orchestration and its C ABI: Qwen35MoeBlock::forward
+// (crates/mlxr-lm/src/qwen3_5/text/moe.rs:116-146) on one device.
+//
+// Stream of work for x [T, D]:
+//   router_logits -> router_topk (+ shared-gate sigmoid)
+//   permute_count -> permute_scan (offsets, tile lists) -> permute_scatter
+//   grouped GEMM gate|up + SwiGLU  (x_sorted -> h_sorted)
+//   grouped GEMM down              (h_sorted -> y_sorted)
+//   [shared expert: dense GEMMs over x with the same kernels]
+//   combine (+ sigmoid-gated shared expert)
+// All scratch lives in the caller's workspace; nothing is allocated here.
+#include <cstring>
+
+#include "common.cuh"
+#include "gemm_launch.h"
+#include "routing.cuh"
+
+namespace mlxr {
+
+static __device__ int g_op_status;
+
+int* op_status_word() {
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_op_status);
+  if (e != cudaSuccess) {
+    check_cuda(e, "cudaGetSymbolAddress(op status)");
+    return nullptr;
+  }
+  return static_cast<int*>(p);
+}
+
+static inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+struct Layout {
+  int64_t T = 0, R = 0, rows_pad = 0, sh_rows_pad = 0;
+  int E = 0, K = 0, D = 0, I = 0, Is = 0, nblk = 0;
+  int bn1 = 0, bn2 = 0, bns = 0;
+  int max_t1 = 0, max_t2 = 0, max_tsh = 0;
+  size_t status = 0, logits = 0, idx = 0, w = 0, sig = 0, bcounts = 0, bbase = 0, counts = 0, offsets = 0,
+         sorted = 0, inv = 0, t1 = 0, n1 = 0, t2 = 0, n2 = 0, tsh = 0, nsh = 0, xs = 0, h = 0, y = 0, xpad = 0,
+         hsh = 0, ysh = 0, total = 0;
+};
+
+// Token-tile width from the mean number of rows per expert.
+static int pick_bn(double avg_rows, int max_bn) {
+  int bn;
+  if (avg_rows <= 12) bn = 16;
+  else if (avg_rows <= 24) bn = 32;
+  else if (avg_rows <= 48) bn = 64;
+  else if (avg_rows <= 160) bn = 128;
+  else bn = 256;
+  return bn < max_bn ? bn : max_bn;
+}
+
+static int validate(const mlxr_cu_moe_config* c, int64_t T) {
+  MLXR_CHECK_ARG(c != nullptr, "moe: null config");
+  MLXR_CHECK_ARG(T >= 0, "moe: negative token count");
+  MLXR_CHECK_ARG(c->hidden_size > 0 && c->hidden_size % 128 == 0, "moe: hidden_size=%d must be a positive multiple of 128",
+                 c->hidden_size);
+  MLXR_CHECK_ARG(c->num_experts >= 1 && c->num_experts <= PERM_MAX_E, "moe: num_experts=%d must be in [1, %d]",
+                 c->num_experts, PERM_MAX_E);
+  MLXR_CHECK_ARG(c->num_experts_per_tok >= 1 && c->num_experts_per_tok <= RT_MAXK &&
+                     c->num_experts_per_tok <= c->num_experts,
+                 "moe: num_experts_per_tok=%d must be in [1, min(32, num_experts)]", c->num_experts_per_tok);
+  MLXR_CHECK_ARG(c->moe_intermediate_size > 0 && c->moe_intermediate_size % 128 == 0,
+                 "moe: moe_intermediate_size=%d must be a positive multiple of 128", c->moe_intermediate_size);
+  MLXR_CHECK_ARG(c->shared_expert_intermediate_size >= 0 && c->shared_expert_intermediate_size % 128 == 0,
+                 "moe: shared_expert_intermediate_size=%d must be a multiple of 128", c->shared_expert_intermediate_size);
+  if (c->group_size != 64)
+    return set_error(MLXR_CU_ERR_UNSUPPORTED, "moe: group_size=%d is not supported (64)", c->group_size);
+  if (c->bits != 4 && c->bits != 8) return set_error(MLXR_CU_ERR_UNSUPPORTED, "moe: bits=%d is not supported (4, 8)", c->bits);
+  if (c->shared_expert_intermediate_size > 0 && c->shared_bits != 4 && c->shared_bits != 8)
+    return set_error(MLXR_CU_ERR_UNSUPPORTED, "moe: shared_bits=%d is not supported (4, 8)", c->shared_bits);
+  MLXR_CHECK_ARG(T * (int64_t)c->num_experts_per_tok < (int64_t)1 << 30, "moe: T*K=%lld too large",
+                 (long long)(T * c->num_experts_per_tok));
+  return MLXR_CU_OK;
+}
+
+static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T) {
+  Layout L;
+  L.T = T;
+  L.E = c->num_experts;
+  L.K = c->num_experts_per_tok;
+  L.D = c->hidden_size;
+  L.I = c->moe_intermediate_size;
+  L.Is = c->shared_expert_intermediate_size;
+  L.R = T * L.K;
+  L.rows_pad = L.R > 256 ? L.R : 256;
+  L.sh_rows_pad = T > 256 ? T : 256;
+  L.nblk = (int)((L.R + PERM_ROWS - 1) / PERM_ROWS);
+  if (L.nblk < 1) L.nblk = 1;
+  const double avg = L.E > 0 ? (double)L.R / L.E : 0.0;
+  L.bn1 = pick_bn(avg, 128);
+  L.bn2 = pick_bn(avg, 256);
+  L.bns = pick_bn((double)T, 128);
+  L.max_t1 = (int)(L.E + (L.R + L.bn1 - 1) / L.bn1 + 1);
+  L.max_t2 = (int)(L.E + (L.R + L.bn2 - 1) / L.bn2 + 1);
+  L.max_tsh = (int)((T + L.bns - 1) / L.bns + 1);
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o = align256(o + (bytes ? bytes : 1));
+    return at;
+  };
+  L.status = take(sizeof(int));
+  L.logits = take((size_t)T * L.E * 2);
+  L.idx = take((size_t)L.R * 4);
+  L.w = take((size_t)L.R * 2);
+  L.sig = take((size_t)T * 4);
+  L.bcounts = take((size_t)L.nblk * L.E * 4);
+  L.bbase = take((size_t)L.nblk * L.E * 4);
+  L.counts = take((size_t)L.E * 4);
+  L.offsets = take((size_t)(L.E + 1) * 4);
+  L.sorted = take((size_t)L.R * 4);
+  L.inv = take((size_t)L.R * 4);
+  L.t1 = take((size_t)L.max_t1 * sizeof(GemmTile));
+  L.n1 = take(4);
+  L.t2 = take((size_t)L.max_t2 * sizeof(GemmTile));
+  L.n2 = take(4);
+  L.tsh = take((size_t)L.max_tsh * sizeof(GemmTile));
+  L.nsh = take(4);
+  L.xs = take((size_t)L.rows_pad * L.D * 2);
+  L.h = take((size_t)L.rows_pad * L.I * 2);
+  L.y = take((size_t)L.R * L.D * 2);
+  if (L.Is > 0) {
+    L.xpad = take(T < 256 ? (size_t)256 * L.D * 2 : 0);
+    L.hsh = take((size_t)L.sh_rows_pad * L.Is * 2);
+    L.ysh = take((size_t)T * L.D * 2);
+  }
+  L.total = o;
+  return L;
+}
+
+template <typename P>
+static inline P* at(void* ws, size_t off) {
+  return reinterpret_cast<P*>(static_cast<uint8_t*>(ws) + off);
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+static int check_ws(const Layout& L, void* ws, size_t bytes) {
+  if (!ws) return set_error(MLXR_CU_ERR_WORKSPACE, "moe: workspace is NULL (need %zu bytes)", L.total);
+  if ((reinterpret_cast<uintptr_t>(ws) & 255) != 0)
+    return set_error(MLXR_CU_ERR_WORKSPACE, "moe: workspace %p is not 256-byte aligned", ws);
+  if (bytes < L.total) return set_error(MLXR_CU_ERR_WORKSPACE, "moe: workspace has %zu bytes, needs %zu", bytes, L.total);
+  return MLXR_CU_OK;
+}
+
+// ------------------------------------------------------------ stages ----
+static int run_router(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt, const Layout& L, const void* x,
+                      void* ws, uint16_t* logits, uint16_t* probs, cudaStream_t st) {
+  if (L.T == 0) return MLXR_CU_OK;
+  MLXR_CHECK_ARG(wt && wt->router_weight, "moe: router weight is NULL");
+  MLXR_CHECK_ARG(aligned16(x) && aligned16(wt->router_weight), "moe: x and the router weight must be 16-byte aligned");
+  dim3 g1((unsigned)((L.E + 63) / 64), (unsigned)((L.T + RT_TOK - 1) / RT_TOK));
+  MLXR_CHECK_ARG(g1.y <= 65535u, "moe: too many tokens for the router grid (%lld)", (long long)L.T);
+  router_logits_kernel<<<g1, 256, 0, st>>>(static_cast<const uint16_t*>(x), L.T, L.D,
+                                           static_cast<const uint16_t*>(wt->router_weight), L.E, wt->router_bias, logits);
+  MLXR_LAUNCH_CHECK("router_logits_kernel");
+  SharedGateArgs sg{nullptr, nullptr, nullptr, 8};
+  float* sig = nullptr;
+  if (L.Is > 0) {
+    MLXR_CHECK_ARG(wt->shared_expert_gate.weight && wt->shared_expert_gate.scales && wt->shared_expert_gate.biases,
+                   "moe: shared_expert_gate is NULL");
+    sg.w = wt->shared_expert_gate.weight;
+    sg.s = static_cast<const uint16_t*>(wt->shared_expert_gate.scales);
+    sg.b = static_cast<const uint16_t*>(wt->shared_expert_gate.biases);
+    sg.bits = c->shared_bits;
+    sig = at<float>(ws, L.sig);
+  }
+  router_topk_kernel<<<(unsigned)((L.T + 7) / 8), 256, 0, st>>>(
+      logits, L.T, L.E, L.K, c->norm_topk_prob, at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w), probs,
+      static_cast<const uint16_t*>(x), L.D, sg, sig);
+  MLXR_LAUNCH_CHECK("router_topk_kernel");
+  return MLXR_CU_OK;
+}
+
+static int run_permute(const Layout& L, const int32_t* idx, const void* x, void* ws, int32_t* counts, int32_t* offsets,
+                       int32_t* sorted, int32_t* inv, uint16_t* xs, cudaStream_t st) {
+  int* status = at<int>(ws, L.status);
+  if (L.R > 0) {
+    permute_count_kernel<<<L.nblk, 256, L.E * sizeof(int), st>>>(idx, L.R, L.E, at<int32_t>(ws, L.bcounts), status);
+    MLXR_LAUNCH_CHECK("permute_count_kernel");
+  } else {
+    MLXR_CUDA_TRY(cudaMemsetAsync(at<int32_t>(ws, L.bcounts), 0, (size_t)L.nblk * L.E * 4, st));
+  }
+  TileListOut l1{at<GemmTile>(ws, L.t1), at<int32_t>(ws, L.n1), L.bn1};
+  TileListOut l2{at<GemmTile>(ws, L.t2), at<int32_t>(ws, L.n2), L.bn2};
+  TileListOut lsh{L.Is > 0 ? at<GemmTile>(ws, L.tsh) : nullptr, at<int32_t>(ws, L.nsh), L.bns};
+  permute_scan_kernel<<<1, 1024, 0, st>>>(at<int32_t>(ws, L.bcounts), L.nblk, L.E, L.T, at<int32_t>(ws, L.bbase), counts,
+                                          offsets, l1, l2, lsh);
+  MLXR_LAUNCH_CHECK("permute_scan_kernel");
+  if (L.R > 0) {
+    permute_scatter_kernel<<<L.nblk, 256, 8 * L.E * sizeof(int), st>>>(idx, L.R, L.K, L.E, at<int32_t>(ws, L.bbase),
+                                                                       static_cast<const uint16_t*>(x), L.D, sorted,
+                                                                       inv, xs);
+    MLXR_LAUNCH_CHECK("permute_scatter_kernel");
+  }
+  return MLXR_CU_OK;
+}
+
+static int check_qlinear(const mlxr_cu_qlinear& q, const char* name) {
+  MLXR_CHECK_ARG(q.weight && q.scales && q.biases, "moe: %s weight/scales/biases must be non-NULL", name);
+  MLXR_CHECK_ARG(aligned16(q.weight), "moe: %s weight must be 16-byte aligned", name);
+  return MLXR_CU_OK;
+}
+
+static int run_experts(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt, const Layout& L, void* ws,
+                       cudaStream_t st) {
+  if (L.R == 0) return MLXR_CU_OK;
+  if (int rc = check_qlinear(wt->switch_gate, "switch_mlp.gate_proj")) return rc;
+  if (int rc = check_qlinear(wt->switch_up, "switch_mlp.up_proj")) return rc;
+  if (int rc = check_qlinear(wt->switch_down, "switch_mlp.down_proj")) return rc;
+  int* status = at<int>(ws, L.status);
+  GroupedGemmProblem p{};
+  p.nmat = 2;
+  p.bn = L.bn1;
+  p.bits = c->bits;
+  p.w[0] = wt->switch_gate.weight;
+  p.w[1] = wt->switch_up.weight;
+  p.s[0] = static_cast<const uint16_t*>(wt->switch_gate.scales);
+  p.s[1] = static_cast<const uint16_t*>(wt->switch_up.scales);
+  p.b[0] = static_cast<const uint16_t*>(wt->switch_gate.biases);
+  p.b[1] = static_cast<const uint16_t*>(wt->switch_up.biases);
+  p.w_rows = (int64_t)L.E * L.I;
+  p.n_out = L.I;
+  p.k_dim = L.D;
+  p.num_experts = L.E;
+  p.act = at<uint16_t>(ws, L.xs);
+  p.act_rows = L.rows_pad;
+  p.tiles = at<GemmTile>(ws, L.t1);
+  p.num_tiles = at<int32_t>(ws, L.n1);
+  p.max_tiles = L.max_t1;
+  p.out = at<uint16_t>(ws, L.h);
+  p.status = status;
+  if (int rc = launch_grouped_gemm(p, st)) return rc;
+
+  GroupedGemmProblem q{};
+  q.nmat = 1;
+  q.bn = L.bn2;
+  q.bits = c->bits;
+  q.w[0] = q.w[1] = wt->switch_down.weight;
+  q.s[0] = q.s[1] = static_cast<const uint16_t*>(wt->switch_down.scales);
+  q.b[0] = q.b[1] = static_cast<const uint16_t*>(wt->switch_down.biases);
+  q.w_rows = (int64_t)L.E * L.D;
+  q.n_out = L.D;
+  q.k_dim = L.I;
+  q.num_experts = L.E;
+  q.act = at<uint16_t>(ws, L.h);
+  q.act_rows = L.rows_pad;
+  q.tiles = at<GemmTile>(ws, L.t2);
+  q.num_tiles = at<int32_t>(ws, L.n2);
+  q.max_tiles = L.max_t2;
+  q.out = at<uint16_t>(ws, L.y);
+  q.status = status;
+  return launch_grouped_gemm(q, st);
+}
+
+static int run_shared(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt, const Layout& L, const void* x,
+                      void* ws, cudaStream_t st) {
+  if (L.Is == 0 || L.T == 0) return MLXR_CU_OK;
+  if (int rc = check_qlinear(wt->shared_gate, "shared_expert.gate_proj")) return rc;
+  if (int rc = check_qlinear(wt->shared_up, "shared_expert.up_proj")) return rc;
+  if (int rc = check_qlinear(wt->shared_down, "shared_expert.down_proj")) return rc;
+  int* status = at<int>(ws, L.status);
+  const uint16_t* act = static_cast<const uint16_t*>(x);
+  int64_t act_rows = L.T;
+  if (L.T < 256) {
+    MLXR_CUDA_TRY(cudaMemcpyAsync(at<uint16_t>(ws, L.xpad), x, (size_t)L.T * L.D * 2, cudaMemcpyDeviceToDevice, st));
+    act = at<uint16_t>(ws, L.xpad);
+    act_rows = 256;
+  }
+  GroupedGemmProblem p{};
+  p.nmat = 2;
+  p.bn = L.bns;
+  p.bits = c->shared_bits;
+  p.w[0] = wt->shared_gate.weight;
+  p.w[1] = wt->shared_up.weight;
+  p.s[0] = static_cast<const uint16_t*>(wt->shared_gate.scales);
+  p.s[1] = static_cast<const uint16_t*>(wt->shared_up.scales);
+  p.b[0] = static_cast<const uint16_t*>(wt->shared_gate.biases);
+  p.b[1] = static_cast<const uint16_t*>(wt->shared_up.biases);
+  p.w_rows = L.Is;
+  p.n_out = L.Is;
+  p.k_dim = L.D;
+  p.num_experts = 1;
+  p.act = act;
+  p.act_rows = act_rows;
+  p.tiles = at<GemmTile>(ws, L.tsh);
+  p.num_tiles = at<int32_t>(ws, L.nsh);
+  p.max_tiles = L.max_tsh;
+  p.out = at<uint16_t>(ws, L.hsh);
+  p.status = status;
+  if (int rc = launch_grouped_gemm(p, st)) return rc;
+  GroupedGemmProblem q{};
+  q.nmat = 1;
+  q.bn = L.bns;
+  q.bits = c->shared_bits;
+  q.w[0] = q.w[1] = wt->shared_down.weight;
+  q.s[0] = q.s[1] = static_cast<const uint16_t*>(wt->shared_down.scales);
+  q.b[0] = q.b[1] = static_cast<const uint16_t*>(wt->shared_down.biases);
+  q.w_rows = L.D;
+  q.n_out = L.D;
+  q.k_dim = L.Is;
+  q.num_experts = 1;
+  q.act = at<uint16_t>(ws, L.hsh);
+  q.act_rows = L.sh_rows_pad;
+  q.tiles = at<GemmTile>(ws, L.tsh);
+  q.num_tiles = at<int32_t>(ws, L.nsh);
+  q.max_tiles = L.max_tsh;
+  q.out = at<uint16_t>(ws, L.ysh);
+  q.status = status;
+  return launch_grouped_gemm(q, st);
+}
+
+}  // namespace mlxr
+
+using namespace mlxr;
+
+extern "C" {
+
+int mlxr_cu_moe_workspace_size(const mlxr_cu_moe_config* cfg, int64_t num_tokens, size_t* bytes) {
+  if (int rc = validate(cfg, num_tokens)) return rc;
+  MLXR_CHECK_ARG(bytes != nullptr, "moe_workspace_size: bytes is NULL");
+  *bytes = make_layout(cfg, num_tokens).total;
+  return MLXR_CU_OK;
+}
+
+int mlxr_cu_moe_block_forward(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights, const void* x,
+                              int64_t num_tokens, void* out, const mlxr_cu_moe_routing* routing, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  if (int rc = validate(cfg, num_tokens)) return rc;
+  MLXR_CHECK_ARG(weights != nullptr, "moe: weights is NULL");
+  const Layout L = make_layout(cfg, num_tokens);
+  if (int rc = check_ws(L, workspace, workspace_bytes)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  MLXR_CUDA_TRY(cudaMemsetAsync(at<int>(workspace, L.status), 0, sizeof(int), st));
+  if (num_tokens == 0) return MLXR_CU_OK;
+  MLXR_CHECK_ARG(x && out, "moe: x/out is NULL");
+  MLXR_CHECK_ARG(aligned16(x) && aligned16(out), "moe: x and out must be 16-byte aligned");
+  void* ws = workspace;
+  if (int rc = run_router(cfg, weights, L, x, ws, at<uint16_t>(ws, L.logits), nullptr, st)) return rc;
+  if (int rc = run_permute(L, at<int32_t>(ws, L.idx), x, ws, at<int32_t>(ws, L.counts), at<int32_t>(ws, L.offsets),
+                           at<int32_t>(ws, L.sorted), at<int32_t>(ws, L.inv), at<uint16_t>(ws, L.xs), st))
+    return rc;
+  if (int rc = run_experts(cfg, weights, L, ws, st)) return rc;
+  if (int rc = run_shared(cfg, weights, L, x, ws, st)) return rc;
+  combine_kernel<<<(unsigned)L.T, 128, 0, st>>>(at<uint16_t>(ws, L.y), at<int32_t>(ws, L.inv), at<uint16_t>(ws, L.w),
+                                                L.K, L.D, L.T, L.Is > 0 ? at<uint16_t>(ws, L.ysh) : nullptr,
+                                                at<float>(ws, L.sig), static_cast<uint16_t*>(out));
+  MLXR_LAUNCH_CHECK("combine_kernel");
+  if (routing) {
+    auto cp = [&](void* dst, size_t off, size_t bytes) -> int {
+      if (dst && bytes) MLXR_CUDA_TRY(cudaMemcpyAsync(dst, at<uint8_t>(ws, off), bytes, cudaMemcpyDeviceToDevice, st));
+      return MLXR_CU_OK;
+    };
+    if (int rc = cp(routing->indices, L.idx, (size_t)L.R * 4)) return rc;
+    if (int rc = cp(routing->weights, L.w, (size_t)L.R * 2)) return rc;
+    if (int rc = cp(routing->counts, L.counts, (size_t)L.E * 4)) return rc;
+    if (int rc = cp(routing->offsets, L.offsets, (size_t)(L.E + 1) * 4)) return rc;
+    if (int rc = cp(routing->sorted_rows, L.sorted, (size_t)L.R * 4)) return rc;
+    if (int rc = cp(routing->inverse, L.inv, (size_t)L.R * 4)) return rc;
+  }
+  return MLXR_CU_OK;
+}
+
+int mlxr_cu_moe_status(const void* workspace, void* stream) {
+  MLXR_CHECK_ARG(workspace != nullptr, "moe_status: workspace is NULL");
+  MLXR_CUDA_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  int v = 0;
+  MLXR_CUDA_TRY(cudaMemcpy(&v, workspace, sizeof(int), cudaMemcpyDeviceToHost));  // status is at offset 0
+  switch (v) {
+    case kDevOk: return MLXR_CU_OK;
+    case kDevTimeout: return set_error(MLXR_CU_ERR_TIMEOUT, "moe: a device-side wait timed out");
+    case kDevBadIndex: return set_error(MLXR_CU_ERR_DEVICE_INDEX, "moe: an expert index was outside [0, num_experts)");
+    default: return set_error(MLXR_CU_ERR_CUDA, "moe: device status %d", v);
+  }
+}
+
+int mlxr_cu_op_status(void* stream) {
+  int* p = op_status_word();
+  if (!p) return MLXR_CU_ERR_CUDA;
+  MLXR_CUDA_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  int v = 0;
+  MLXR_CUDA_TRY(cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost));
+  const int zero = 0;
+  MLXR_CUDA_TRY(cudaMemcpy(p, &zero, sizeof(int), cudaMemcpyHostToDevice));
+  if (v == kDevBadIndex) return set_error(MLXR_CU_ERR_DEVICE_INDEX, "an index was outside its batch");
+  if (v != 0) return set_error(MLXR_CU_ERR_CUDA, "device status %d", v);
+  return MLXR_CU_OK;
+}
+
+int mlxr_cu_moe_router(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights, const void* x,
+                       int64_t num_tokens, int32_t* indices, void* topk_weights, void* logits, void* probs,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = validate(cfg, num_tokens)) return rc;
+  const Layout L = make_layout(cfg, num_tokens);
+  if (int rc = check_ws(L, workspace, workspace_bytes)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  MLXR_CUDA_TRY(cudaMemsetAsync(at<int>(workspace, L.status), 0, sizeof(int), st));
+  if (num_tokens == 0) return MLXR_CU_OK;
+  MLXR_CHECK_ARG(x && indices && topk_weights, "moe_router: x/indices/weights is NULL");
+  uint16_t* lg = logits ? static_cast<uint16_t*>(logits) : at<uint16_t>(workspace, L.logits);
+  mlxr_cu_moe_config c2 = *cfg;
+  c2.shared_expert_intermediate_size = 0;  // the router alone does not evaluate the shared gate
+  Layout L2 = L;
+  L2.Is = 0;
+  if (int rc = run_router(&c2, weights, L2, x, workspace, lg, static_cast<uint16_t*>(probs), st)) return rc;
+  MLXR_CUDA_TRY(cudaMemcpyAsync(indices, at<int32_t>(workspace, L.idx), (size_t)L.R * 4, cudaMemcpyDeviceToDevice, st));
+  MLXR_CUDA_TRY(cudaMemcpyAsync(topk_weights, at<uint16_t>(workspace, L.w), (size_t)L.R * 2, cudaMemcpyDeviceToDevice, st));
+  return MLXR_CU_OK;
+}
+
+int mlxr_cu_moe_permute(const mlxr_cu_moe_config* cfg, const int32_t* indices, int64_t num_tokens, const void* x,
+                        int32_t* counts, int32_t* offsets, int32_t* sorted_rows, int32_t* inverse, void* x_sorted,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = validate(cfg, num_tokens)) return rc;
+  const Layout L = make_layout(cfg, num_tokens);
+  if (int rc = check_ws(L, workspace, workspace_bytes)) return rc;
+  MLXR_CHECK_ARG(indices && x && counts && offsets && sorted_rows && inverse && x_sorted, "moe_permute: NULL argument");
+  MLXR_CHECK_ARG(aligned16(x) && aligned16(x_sorted), "moe_permute: x and x_sorted must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  MLXR_CUDA_TRY(cudaMemsetAsync(at<int>(workspace, L.status), 0, sizeof(int), st));
+  return run_permute(L, indices, x, workspace, counts, offsets, sorted_rows, inverse, static_cast<uint16_t*>(x_sorted), st);
+}
+
+}  // extern "C"

@@ -1,0 +1,16 @@
+"""B200 (sm_100a) MoE block and quantised op family for mlxr, over a C ABI.
+
+Importing this package loads libmlxr_moe.so; it raises if the library is
+missing (there is no CPU fallback).
+"""
+from . import _lib, ops, synth
+from ._lib import MlxrError
+from .moe import (MoeConfig, QuantizedLinear, QuantizedSwitchLinear, Qwen35MoeBlock, Routing, SplitSwitchFfn,
+                  SwigluMlp)
+from .ops import dequantize, gather_mm, gather_qmm, quantize, quantized_matmul
+
+__all__ = [
+    "MlxrError", "MoeConfig", "QuantizedLinear", "QuantizedSwitchLinear", "Qwen35MoeBlock", "Routing",
+    "SplitSwitchFfn", "SwigluMlp", "dequantize", "gather_mm", "gather_qmm", "quantize", "quantized_matmul",
+    "ops", "synth", "_lib",
+]

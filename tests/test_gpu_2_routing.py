@@ -1,0 +1,100 @@
+"""GPU routing parity: the router (logits, probabilities, top-k indices and
+weights) and the permutation are bit-exact with the oracle's routing contract."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from conftest import bf16_np
+from mlxr_moe import synth
+from mlxr_moe.moe import MoeConfig
+
+pytestmark = pytest.mark.gpu
+
+
+def _router_block(D, E, K, zipf=False, seed=0):
+    """A block whose router is synthesised; experts are irrelevant here."""
+    from mlxr_moe import ops
+    from mlxr_moe.moe import Qwen35MoeBlock, QuantizedSwitchLinear, SplitSwitchFfn
+
+    cfg = MoeConfig(D, E, K, 128, bits=4)
+    router = ops.synth_normal_bf16(seed, synth.STREAM_ROUTER, (E, D), 0.02)
+    dummy = QuantizedSwitchLinear.from_switch_linear(ops.synth_normal_bf16(seed, 1, (1, 128, D), 0.02), 64, 4)
+    bias = synth.zipf_bias(E, seed) if zipf else None
+    return Qwen35MoeBlock(cfg, router, SplitSwitchFfn(dummy, dummy, dummy), router_bias=bias)
+
+
+@pytest.mark.parametrize(
+    "D,E,K,T,zipf",
+    [
+        (2048, 128, 8, 32, False),    # C1
+        (2048, 128, 8, 1, False),     # C2
+        (2048, 128, 8, 64, False),    # C2
+        (2048, 128, 8, 4096, True),   # C3 (Zipf-biased logits)
+        (2048, 512, 10, 2048, False), # C4 router (subset of the 16384 tokens)
+        (4096, 128, 8, 256, True),    # C5 decode batch
+    ],
+)
+def test_router_bitexact(D, E, K, T, zipf):
+    blk = _router_block(D, E, K, zipf)
+    x = synth.make_input(T, D)
+    idx, w, lg, pr = blk.router(x, want_logits=True)
+    torch.cuda.synchronize()
+    bias = None if blk.router_bias is None else blk.router_bias.cpu().numpy()
+    oi, ow, olg, opr = O.router(bf16_np(x), bf16_np(blk.gate), K, bias, True, want_logits=True)
+    np.testing.assert_array_equal(bf16_np(lg), olg)
+    np.testing.assert_array_equal(bf16_np(pr), opr)
+    np.testing.assert_array_equal(idx.cpu().numpy(), oi)
+    np.testing.assert_array_equal(bf16_np(w), ow)
+
+
+def test_router_ties_bitexact():
+    """Duplicated router rows give equal probabilities; ties go to the lower expert."""
+    blk = _router_block(2048, 128, 8)
+    g = blk.gate.clone()
+    g[5] = g[77]
+    g[6] = g[77]
+    g[100] = g[2]
+    blk.gate.copy_(g)
+    x = synth.make_input(512, 2048, stream_offset=3)
+    idx, w = blk.router(x)
+    oi, ow = O.router(bf16_np(x), bf16_np(blk.gate), 8)
+    np.testing.assert_array_equal(idx.cpu().numpy(), oi)
+    np.testing.assert_array_equal(bf16_np(w), ow)
+    rows = idx.cpu().numpy()
+    both = [(list(r).index(5), list(r).index(77)) for r in rows if 5 in r and 77 in r]
+    assert both and all(a < b for a, b in both)
+
+
+@pytest.mark.parametrize("T,K,E", [(1, 8, 128), (33, 8, 128), (4096, 8, 128), (16384, 10, 512)])
+def test_permute_bitexact(T, K, E):
+    D = 256
+    blk = _router_block(D, E, K)
+    x = synth.make_input(T, D, stream_offset=5)
+    g = torch.Generator(device="cpu").manual_seed(T)
+    # skewed indices: many rows on few experts, some experts empty
+    idx = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(T)]).to(torch.int32)
+    idx = torch.where(idx % 3 == 0, idx % 7, idx).to(torch.int32)
+    idx_d = idx.cuda()
+    counts, offsets, srt, inv, xs = blk.permute(idx_d, x)
+    torch.cuda.synchronize()
+    oc, oo, osrt, oinv = O.permute(idx.numpy(), E)
+    np.testing.assert_array_equal(counts.cpu().numpy(), oc)
+    np.testing.assert_array_equal(offsets.cpu().numpy(), oo)
+    np.testing.assert_array_equal(srt.cpu().numpy(), osrt)
+    np.testing.assert_array_equal(inv.cpu().numpy(), oinv)
+    ref = x[(srt.long() // K)]
+    assert torch.equal(xs, ref)
+
+
+def test_permute_bad_index_reports_status():
+    from mlxr_moe import MlxrError, _lib
+
+    blk = _router_block(256, 16, 2)
+    x = synth.make_input(8, 256)
+    idx = torch.zeros((8, 2), dtype=torch.int32, device="cuda")
+    idx[3, 1] = 9999
+    blk.permute(idx, x)
+    with pytest.raises(MlxrError) as ei:
+        blk.status()
+    assert ei.value.status == _lib.ERR_DEVICE_INDEX

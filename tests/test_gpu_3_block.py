@@ -1,0 +1,168 @@
+"""GPU parity of the whole MoE block (Qwen35MoeBlock.forward through
+mlxr_cu_moe_block_forward) against the oracle: routing bit-exact, outputs
+within max-abs 2e-2 / rtol 1e-2 of both oracle modes (bf16 out, fp32 accum)."""
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from conftest import ATOL, RTOL, assert_close_bf16, bf16_np, np_bf16_to_torch
+from gpu_helpers import block_to_oracle, run_gpu_block
+from mlxr_moe import synth
+from mlxr_moe.moe import MoeConfig
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "golden"))
+import make_golden as G  # noqa: E402
+
+FX = np.load(os.path.join(HERE, "golden", "moe_small.npz"))
+
+# Tighter bound against the fused oracle (same arithmetic contract: bf16
+# dequantised weights, fp32 accumulation, bf16 h and y).
+FUSED_ATOL, FUSED_RTOL = 4e-3, 1e-2
+
+_BLOCKS = {}
+
+
+def block_for(name):
+    if name not in _BLOCKS:
+        spec = synth.CONFIGS[name]
+        _BLOCKS[name] = (synth.make_block(spec["cfg"], 0, spec["zipf"]), None)
+    blk, ow = _BLOCKS[name]
+    if ow is None:
+        ow = block_to_oracle(blk)
+        _BLOCKS[name] = (blk, ow)
+    return blk, ow
+
+
+def check_block(blk, ow, x, staged=True):
+    cfg, W = ow
+    out, r = run_gpu_block(blk, x)
+    xo = bf16_np(x)
+    o_fu, idx, w = O.moe_block(cfg, W, xo, "fused")
+    np.testing.assert_array_equal(r.indices.cpu().numpy(), idx)
+    np.testing.assert_array_equal(bf16_np(r.weights), w)
+    _, _, srt, inv = O.permute(idx, cfg["num_experts"])
+    np.testing.assert_array_equal(r.sorted_rows.cpu().numpy(), srt)
+    np.testing.assert_array_equal(r.inverse.cpu().numpy(), inv)
+    got = bf16_np(out)
+    e_fu = assert_close_bf16(got, o_fu, FUSED_ATOL, FUSED_RTOL, "vs fused oracle")
+    e_st = None
+    if staged:
+        o_st, _, _ = O.moe_block(cfg, W, xo, "staged")
+        e_st = assert_close_bf16(got, o_st, ATOL, RTOL, "vs staged oracle")
+    return e_fu, e_st
+
+
+@pytest.mark.parametrize("name", list(G.BLOCKS))
+def test_golden_fixture_blocks(name):
+    """GPU on the committed fixtures (oracle outputs stored in tests/golden)."""
+    from mlxr_moe.moe import (MoeConfig, QuantizedLinear, QuantizedSwitchLinear, Qwen35MoeBlock, SplitSwitchFfn,
+                              SwigluMlp)
+
+    cfg, W, x = G.small_block(**G.BLOCKS[name])
+
+    def qs(t):
+        return QuantizedSwitchLinear(torch.from_numpy(t[0].view(np.int32)).cuda(), np_bf16_to_torch(t[1]),
+                                     np_bf16_to_torch(t[2]), 64, cfg["bits"])
+
+    def ql(t):
+        return QuantizedLinear(torch.from_numpy(t[0].view(np.int32)).cuda(), np_bf16_to_torch(t[1]),
+                               np_bf16_to_torch(t[2]), 64, cfg["bits"])
+
+    mc = MoeConfig(cfg["hidden"], cfg["num_experts"], cfg["top_k"], cfg["moe_intermediate"],
+                   cfg["shared_intermediate"], 64, cfg["bits"], cfg["shared_bits"])
+    sh = shg = None
+    if cfg["shared_intermediate"]:
+        sh = SwigluMlp(ql(W["sh_gate"]), ql(W["sh_up"]), ql(W["sh_down"]))
+        shg = ql(W["sh_expert_gate"])
+    bias = None if "router_bias" not in W else torch.from_numpy(W["router_bias"]).cuda()
+    blk = Qwen35MoeBlock(mc, np_bf16_to_torch(W["router"]), SplitSwitchFfn(qs(W["gate"]), qs(W["up"]), qs(W["down"])),
+                         sh, shg, bias)
+    out, r = run_gpu_block(blk, np_bf16_to_torch(x))
+    np.testing.assert_array_equal(r.indices.cpu().numpy(), FX[f"{name}/idx"])
+    np.testing.assert_array_equal(bf16_np(r.weights), FX[f"{name}/w"])
+    assert_close_bf16(bf16_np(out), FX[f"{name}/out_fused"], FUSED_ATOL, FUSED_RTOL, "vs fused fixture")
+    assert_close_bf16(bf16_np(out), FX[f"{name}/out_staged"], ATOL, RTOL, "vs staged fixture")
+
+
+def test_c1_reference_runnable_block():
+    blk, ow = block_for("c1")
+    check_block(blk, ow, synth.make_input(32, 2048))
+
+
+@pytest.mark.parametrize("T", [1, 8, 64])
+def test_c2_decode_sweep(T):
+    blk, ow = block_for("c2")
+    check_block(blk, ow, synth.make_input(T, 2048, stream_offset=T))
+
+
+def test_c3_prefill_zipf_full_size():
+    blk, ow = block_for("c3")
+    x = synth.make_input(4096, 2048)
+    check_block(blk, ow, x, staged=False)
+    # the Zipf bias concentrates load: the hottest expert takes far more than average
+    _, r = run_gpu_block(blk, x)
+    c = r.counts.cpu().numpy()
+    assert c.sum() == 4096 * 8 and c.max() > 4 * c.mean()
+
+
+def test_c4_wide_experts_with_shared_subset_and_full_properties():
+    blk, ow = block_for("c4")
+    x = synth.make_input(16384, 2048)
+    # parity on a 1024-token slice (the oracle finishes in seconds)
+    check_block(blk, ow, x[:1024].contiguous(), staged=True)
+    # full size: routing bit-exact, tokens independent of their batch
+    out_full, r = run_gpu_block(blk, x)
+    oi, ow_ = O.router(bf16_np(x), bf16_np(blk.gate), 10)
+    np.testing.assert_array_equal(r.indices.cpu().numpy(), oi)
+    out_part, _ = run_gpu_block(blk, x[:1024].contiguous())
+    assert_close_bf16(bf16_np(out_full[:1024]), bf16_np(out_part), 1e-2, 1e-2, "batch independence")
+    assert torch.isfinite(out_full.float()).all()
+
+
+def test_c5_large_block_decode_and_prefill_slice():
+    blk, ow = block_for("c5")
+    check_block(blk, ow, synth.make_input(256, 4096, stream_offset=1), staged=False)
+    x = synth.make_input(8192, 4096)
+    check_block(blk, ow, x[:512].contiguous(), staged=False)
+    out_full, r = run_gpu_block(blk, x)
+    bias = blk.router_bias.cpu().numpy()
+    oi, _ = O.router(bf16_np(x), bf16_np(blk.gate), 8, bias)
+    np.testing.assert_array_equal(r.indices.cpu().numpy(), oi)
+    out_part, _ = run_gpu_block(blk, x[:512].contiguous())
+    assert_close_bf16(bf16_np(out_full[:512]), bf16_np(out_part), 1e-2, 1e-2, "batch independence")
+
+
+def test_edge_cases_empty_ragged_and_hot_expert():
+    blk, ow = block_for("c2")
+    # T = 0: a no-op that succeeds
+    x0 = torch.empty((0, 2048), dtype=torch.bfloat16, device="cuda")
+    assert blk.forward(x0).shape == (0, 2048)
+    # ragged token count
+    check_block(blk, ow, synth.make_input(33, 2048, stream_offset=9), staged=False)
+    # every token routed to the same 8 experts: one expert gets many tiles
+    from mlxr_moe.moe import Qwen35MoeBlock
+
+    bias = torch.zeros(128, dtype=torch.float32, device="cuda")
+    bias[[3, 17, 40, 41, 42, 90, 126, 127]] = 1000.0
+    hot = Qwen35MoeBlock(blk.cfg, blk.gate, blk.switch_mlp, router_bias=bias)
+    cfg, W = ow
+    W = dict(W, router_bias=bias.cpu().numpy())
+    check_block(hot, (cfg, W), synth.make_input(700, 2048, stream_offset=11), staged=False)
+
+
+def test_determinism_and_op_level_chain():
+    blk, ow = block_for("c1")
+    x = synth.make_input(32, 2048, stream_offset=2)
+    a, _ = run_gpu_block(blk, x)
+    b, _ = run_gpu_block(blk, x)
+    assert torch.equal(a, b)
+    # the reference's op-by-op chain through the op family agrees with the fused block
+    c = blk.forward_ops(x)
+    assert_close_bf16(bf16_np(c), bf16_np(a), ATOL, RTOL, "op-level chain vs fused block")

@@ -1,0 +1,172 @@
+"""CPU tests of the oracle: the relations the reference's own tests assert,
+the routing contract, and the committed golden fixtures."""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "golden"))
+import make_golden as G  # noqa: E402
+
+FX = np.load(os.path.join(HERE, "golden", "moe_small.npz"))
+
+
+def rng_normal(seed, stream, shape, scale=1.0):
+    return O.bf16_to_f32(O.normal_bf16(seed, stream, shape, scale))
+
+
+# ------------------------------------------- reference test relations ------
+def test_quantize_dequantize_reference_bound():
+    """crates/mlxr/src/ops/quantization.rs:299-315: shapes and max error <= 127/2^bits."""
+    x = (np.ones((128, 1), np.float32) * np.arange(512, dtype=np.float32)[None, :]).astype(np.float32)
+    for bits in (2, 4, 8):
+        el_per_int = 32 // bits
+        q, s, b = O.quantize(x, 128, bits)
+        assert q.shape == (128, 512 // el_per_int)
+        assert s.shape == (128, 4) and b.shape == (128, 4)
+        xh = O.dequantize(q, s, b, 128, bits)
+        assert np.abs(x - xh).max() <= 127.0 / (1 << bits)
+
+
+def test_quantized_matmul_reference_relation():
+    """quantization.rs:318-341: qmm(x, w) == x @ dequant(w) within 1e-3 (transpose=false)."""
+    m, n, k = 32, 128, 128
+    x = rng_normal(0, 100, (m, k)) / np.sqrt(k)
+    w = rng_normal(0, 101, (k, n)) / np.sqrt(k)
+    wq, s, b = O.quantize(w.astype(np.float32), 64, 4)
+    wh = O.dequantize(wq, s, b, 64, 4)
+    yq = O.quantized_matmul(x.astype(np.float32), wq, s, b, transpose=False, group_size=64, bits=4)
+    yh = x.astype(np.float64) @ wh.astype(np.float64)
+    assert yq.shape == yh.shape
+    assert np.abs(yq - yh).max() < 1e-3
+
+
+def test_gather_qmm_reference_relation():
+    """quantization.rs:344-421: gather_qmm == gather_mm on dequantised transposed weights (1e-4)."""
+    m, n, k = 32, 64, 64
+    w = rng_normal(0, 102, (3, n, k)).astype(np.float32)
+    wq, s, b = O.quantize(w, 64, 4)
+    w_hat = np.swapaxes(O.dequantize(wq, s, b, 64, 4), -1, -2)
+    rhs = np.array([2, 1], np.int32)
+    for x_batch, lhs in ((1, np.array([0, 0], np.int32)), (5, np.array([0, 2], np.int32))):
+        x = rng_normal(0, 103 + x_batch, (x_batch, m, k)).astype(np.float32)
+        c1 = O.gather_mm(x, w_hat, lhs, rhs)
+        c2 = O.gather_qmm(x, wq, s, b, lhs, rhs, True, 64, 4)
+        np.testing.assert_allclose(c2, c1, rtol=1e-4, atol=1e-4)
+
+
+def test_gather_mm_reference_cases():
+    """arithmetic.rs:3099-3196: gather_mm == take + matmul, incl. the sorted-rhs case."""
+    a = rng_normal(0, 110, (1, 32, 32)).astype(np.float32)
+    b = rng_normal(0, 111, (3, 32, 32)).astype(np.float32)
+    rhs = np.array([2, 1], np.int32)
+    ref = np.stack([a[0] @ b[2], a[0] @ b[1]])
+    np.testing.assert_allclose(O.gather_mm(a, b, np.array([0, 0], np.int32), rhs), ref, rtol=1e-5, atol=1e-5)
+    a5 = rng_normal(0, 112, (5, 32, 32)).astype(np.float32)
+    ref = np.stack([a5[0] @ b[2], a5[2] @ b[1]])
+    np.testing.assert_allclose(O.gather_mm(a5, b, np.array([0, 2], np.int32), rhs), ref, rtol=1e-5, atol=1e-5)
+    a100 = rng_normal(0, 113, (100, 1, 100)).astype(np.float32)
+    b8 = rng_normal(0, 114, (8, 100, 100)).astype(np.float32)
+    r = np.sort(O.normal_bf16(0, 115, (100,), 1.0).view(np.int16).astype(np.int64) % 8).astype(np.int32)
+    ref = np.stack([a100[i] @ b8[r[i]] for i in range(100)])
+    np.testing.assert_allclose(O.gather_mm(a100, b8, np.arange(100, dtype=np.int32), r), ref, rtol=1e-4, atol=1e-4)
+
+
+def test_swiglu_matches_manual_silu_multiply():
+    """activations.rs:341-351 on the reference's own values."""
+    gate = np.array([1.0, -1.0, 0.5, 2.0], np.float32)
+    x = np.array([1.0, 2.0, 3.0, 4.0], np.float32)
+    fused = gate / (1 + np.exp(-gate)) * x
+    manual = gate * (1 / (1 + np.exp(-gate))) * x
+    assert np.abs(fused - manual).max() < 1e-5
+
+
+# --------------------------------------------------- routing contract ------
+def test_exp_route_accuracy_and_monotone():
+    t = np.linspace(-80.0, 0.0, 200001, dtype=np.float32)
+    e = O.exp_route(t).astype(np.float64)
+    ex = np.exp(t.astype(np.float64))
+    assert (np.abs(e - ex) / ex).max() < 2.5 * 2.0**-24
+    assert (np.diff(e) >= 0).all()
+    assert O.exp_route(np.array([0.0], np.float32))[0] == 1.0
+    assert O.exp_route(np.array([-200.0], np.float32))[0] == 0.0
+    # subnormal results are produced with a single rounding
+    sub = O.exp_route(np.array([-100.0], np.float32))[0]
+    assert 0.0 < sub < 1.2e-38
+
+
+def test_router_topk_order_and_ties():
+    D, E, K, T = 256, 32, 4, 64
+    x = O.normal_bf16(0, 120, (T, D), 1.0)
+    wg = O.normal_bf16(0, 121, (E, D), 0.02)
+    wg[7] = wg[3]  # duplicated rows -> identical logits -> tie broken by lower index
+    wg[20] = wg[3]
+    idx, w, lg, pr = O.router(x, wg, K, want_logits=True)
+    p = O.bf16_to_f32(pr)
+    for t in range(T):
+        key = sorted(range(E), key=lambda e: (-p[t, e], e))[:K]
+        assert list(idx[t]) == key
+        assert len(set(idx[t])) == K
+    sel = (idx == 3).any(1)
+    assert sel.any()
+    for t in np.nonzero(sel)[0]:
+        row = list(idx[t])
+        if 7 in row:
+            assert row.index(3) < row.index(7)
+    ws = O.bf16_to_f32(w).sum(1)
+    assert np.abs(ws - 1).max() < 0.02
+
+
+def test_permute_is_stable_counting_sort():
+    T, K, E = 300, 8, 64
+    idx = (O.normal_bf16(0, 130, (T, K), 1.0).view(np.int16).astype(np.int64) % E).astype(np.int32)
+    counts, offsets, srt, inv = O.permute(idx, E)
+    flat = idx.reshape(-1)
+    np.testing.assert_array_equal(srt, np.argsort(flat, kind="stable"))
+    np.testing.assert_array_equal(inv[srt], np.arange(T * K))
+    np.testing.assert_array_equal(counts, np.bincount(flat, minlength=E))
+    np.testing.assert_array_equal(offsets, np.concatenate([[0], np.cumsum(counts)]))
+
+
+# ------------------------------------------------------ golden fixtures ----
+@pytest.mark.parametrize("name", list(G.BLOCKS))
+def test_golden_block(name):
+    cfg, W, x = G.small_block(**G.BLOCKS[name])
+    for k, v in G.flat(f"{name}/", W).items():
+        assert G.digest(v) == str(FX[k + ".sha256"]), f"generator/quantiser drifted for {k}"
+    np.testing.assert_array_equal(x, FX[f"{name}/x"])
+    o_st, idx, w = O.moe_block(cfg, W, x, "staged")
+    o_fu, idx2, w2 = O.moe_block(cfg, W, x, "fused")
+    np.testing.assert_array_equal(idx, FX[f"{name}/idx"])
+    np.testing.assert_array_equal(idx2, FX[f"{name}/idx"])
+    np.testing.assert_array_equal(w, FX[f"{name}/w"])
+    np.testing.assert_array_equal(o_st, FX[f"{name}/out_staged"])
+    np.testing.assert_array_equal(o_fu, FX[f"{name}/out_fused"])
+    # staged vs fused stay within the block tolerance
+    d = np.abs(O.bf16_to_f32(o_st).astype(np.float64) - O.bf16_to_f32(o_fu))
+    assert (d <= 2e-2 + 1e-2 * np.abs(O.bf16_to_f32(o_st))).all()
+
+
+def test_golden_quantiser_and_generator():
+    x = (np.ones((128, 1), np.float32) * np.arange(512, dtype=np.float32)[None, :]).astype(np.float32)
+    for b in (2, 4, 8):
+        q, s, bb = O.quantize(x, 128, b)
+        np.testing.assert_array_equal(q, FX[f"quant_arange/b{b}.weight"])
+        np.testing.assert_array_equal(s, FX[f"quant_arange/b{b}.scales"])
+        np.testing.assert_array_equal(bb, FX[f"quant_arange/b{b}.biases"])
+    for st in (0, 1, 8):
+        np.testing.assert_array_equal(O.normal_bf16(0, st, (4096,), 1.0), FX[f"normal/seed0_stream{st}"])
+    z = O.bf16_to_f32(O.normal_bf16(0, 8, (1 << 16,), 1.0))
+    assert abs(z.mean()) < 0.02 and abs(z.std() - 1) < 0.02
+
+
+def test_block_empty_and_single_token():
+    cfg, W, x = G.small_block(seed=3, D=256, E=16, K=4, I=128, T=1, bits=4)
+    o, idx, w = O.moe_block(cfg, W, x, "fused")
+    assert o.shape == (1, 256) and idx.shape == (1, 4)
+    o0, idx0, _ = O.moe_block(cfg, W, x[:0], "fused")
+    assert o0.shape == (0, 256) and idx0.shape == (0, 4)
