@@ -1,0 +1,496 @@
+"""MoE-block benchmark (tokens/s and roofline fraction) on 1..8 B200s.
+
+`python bench.py --gpus N --steps K --warmup W` prints ONE JSON line.
+
+Workload (the decode sweep): the Qwen 3.5/3.6 MoE
+block with hidden 2048, 128 experts, top-8, expert intermediate 768, 4-bit
+affine gs64 experts, bf16 router; one step = one block forward at each token
+batch T in {1, 8, 64} on fresh inputs (73 tokens per step per GPU). Each
+forward is a captured CUDA graph of the library's block call. L2 is flushed
+(a 512 MiB write) before every forward; only the forwards are timed, with
+CUDA events on the launching stream. N > 1: one process per GPU, each serving
+its own batches with the experts replicated (no data-path collective),
+"scaling": "weak", value = all tokens / max-over-ranks time.
+
+`--impl reference` times the CPU restatement of the reference block (the
+reference's own MLX CPU path cannot be built here) on the host cores, on a
+bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "mlx-rs_b200"))
+
+WORKLOAD = "c2"
+BATCHES = [1, 8, 64]
+METRIC = "MoE-block tokens/s (decode sweep T=1,8,64; D=2048 E=128 K=8 I=768 q4 gs64)"
+UNIT = "tokens/s"
+L2_FLUSH_BYTES = 512 << 20
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def ncu_traffic(kernel_key: str):
+    """Per-launch DRAM bytes of a kernel from a committed ncu summary line:
+    `traffic_bytes_per_launch <key> <bytes>` in profiles/*.md."""
+    d = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(d):
+        return None
+    for fn in sorted(os.listdir(d)):
+        if not fn.endswith(".md"):
+            continue
+        with open(os.path.join(d, fn)) as f:
+            for line in f:
+                parts = line.strip().strip("`").split()
+                if len(parts) == 3 and parts[0] == "traffic_bytes_per_launch" and parts[1] == kernel_key:
+                    return int(float(parts[2]))
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def smi_id(torch, dev) -> str:
+    """nvidia-smi -i accepts the GPU UUID, which survives CUDA_VISIBLE_DEVICES remapping."""
+    try:
+        u = str(torch.cuda.get_device_properties(dev).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        return str(dev.index)
+
+
+def kernels_per_forward(cfg) -> int:
+    # router (logits, top-k) + permute (count, scan, scatter) + gate/up + down + combine
+    n = 2 + 3 + 2 + 1
+    if cfg.shared_expert_intermediate_size:
+        n += 2
+    return n
+
+
+def distinct_experts(routing) -> int:
+    return int((routing.counts > 0).sum().item())
+
+
+# ---------------------------------------------------------------- GPU arm ----
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+
+    from mlxr_moe import synth
+    from mlxr_moe.moe import Routing
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(dev)
+    peaks = measured_peaks()
+    spec = synth.CONFIGS[WORKLOAD]
+    cfg = spec["cfg"]
+    blk = synth.make_block(cfg, seed=0, zipf=spec["zipf"], device=dev)
+    D = cfg.hidden_size
+    st = torch.cuda.Stream(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    nsets = 4  # distinct input batches cycled through the steps
+
+    # Per batch size: static input/output/workspace buffers and one graph.
+    graphs = {}
+    with torch.cuda.stream(st):
+        for T in BATCHES:
+            xs = [synth.make_input(T, D, seed=0, stream_offset=1000 * rank + 10 * T + i, device=dev)
+                  for i in range(nsets)]
+            x_static = torch.empty_like(xs[0])
+            out = torch.empty_like(xs[0])
+            ws = torch.empty(blk.workspace_bytes(T), dtype=torch.uint8, device=dev)
+            x_static.copy_(xs[0])
+            for _ in range(2):  # warm: sets kernel attributes outside capture
+                blk.forward(x_static, out=out, workspace=ws)
+            torch.cuda.synchronize(dev)
+            blk.status(ws)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=st):
+                blk.forward(x_static, out=out, workspace=ws)
+            r = Routing(T, cfg.num_experts_per_tok, cfg.num_experts, dev)
+            blk.forward(xs[0], routing=r, workspace=ws)
+            torch.cuda.synchronize(dev)
+            graphs[T] = dict(x=xs, xs=x_static, out=out, ws=ws, g=g, U=distinct_experts(r))
+
+    # Stage events for the live per-kernel timing (dominant kernel: gate/up GEMM).
+    import ctypes as C
+
+    from mlxr_moe import _lib
+
+    def run_steps(nsteps, timed, stage_capture=False):
+        ev = []
+        with torch.cuda.stream(st):
+            for s in range(nsteps):
+                for T in BATCHES:
+                    G = graphs[T]
+                    G["xs"].copy_(G["x"][s % nsets])
+                    flush.fill_(s & 0xFF)
+                    if timed:
+                        a = torch.cuda.Event(enable_timing=True)
+                        b = torch.cuda.Event(enable_timing=True)
+                        a.record(st)
+                    G["g"].replay()
+                    if timed:
+                        b.record(st)
+                        ev.append((T, a, b))
+        return ev
+
+    run_steps(args.warmup, timed=False)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(smi_id(torch, dev))
+    clocks.start()
+    evs = run_steps(args.steps, timed=True)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    per_T = {T: [] for T in BATCHES}
+    for T, a, b in evs:
+        per_T[T].append(a.elapsed_time(b))
+    total_ms = sum(sum(v) for v in per_T.values())
+    if world > 1:
+        t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    tokens_per_step = sum(BATCHES)
+    value = world * tokens_per_step * args.steps / (total_ms / 1e3)
+
+    # Live stage timing: a second graph per batch size with the library's
+    # stage events recorded between its kernels (event-record nodes).
+    stage = {T: None for T in BATCHES}
+    for T in BATCHES:
+        G = graphs[T]
+        evs_s = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+        for e in evs_s:  # materialise the CUDA events before handing their handles over
+            e.record(st)
+        torch.cuda.synchronize(dev)
+        arr = (C.c_void_p * 7)(*[C.c_void_p(e.cuda_event) for e in evs_s])
+        gs = torch.cuda.CUDAGraph()
+        _lib.call("mlxr_cu_moe_set_stage_events", arr, 7)
+        try:
+            with torch.cuda.stream(st), torch.cuda.graph(gs, stream=st):
+                blk.forward(G["xs"], out=G["out"], workspace=G["ws"])
+        finally:
+            _lib.call("mlxr_cu_moe_set_stage_events", None, 0)
+        times = []
+        with torch.cuda.stream(st):
+            for s_ in range(max(5, args.steps)):
+                G["xs"].copy_(G["x"][s_ % nsets])
+                flush.fill_(s_ & 0xFF)
+                gs.replay()
+                torch.cuda.synchronize(dev)
+                times.append([evs_s[i].elapsed_time(evs_s[i + 1]) for i in range(6)])
+        med = [statistics.median(col) for col in zip(*times)]
+        stage[T] = dict(router_ms=med[0], permute_ms=med[1], gate_up_ms=med[2], down_ms=med[3], shared_ms=med[4],
+                        combine_ms=med[5])
+        del gs
+
+    # e2e: the same sweep through the public API with pinned host buffers.
+    e2e_ms = 0.0
+    h2d = d2h = 0
+    host_in = {T: [graphs[T]["x"][i].cpu().pin_memory() for i in range(nsets)] for T in BATCHES}
+    host_out = {T: torch.empty_like(graphs[T]["out"], device="cpu").pin_memory() for T in BATCHES}
+    e2e_evs = []
+    with torch.cuda.stream(st):
+        for s in range(args.warmup + args.steps):
+            for T in BATCHES:
+                G = graphs[T]
+                flush.fill_(s & 0xFF)
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record(st)
+                G["xs"].copy_(host_in[T][s % nsets], non_blocking=True)
+                G["g"].replay()
+                host_out[T].copy_(G["out"], non_blocking=True)
+                b.record(st)
+                if s >= args.warmup:
+                    e2e_evs.append((a, b))
+    torch.cuda.synchronize(dev)
+    e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_evs)
+    for T in BATCHES:
+        h2d += T * D * 2
+        d2h += T * D * 2
+    if world > 1:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * tokens_per_step * args.steps / (e2e_ms / 1e3)
+
+    # Roofline of the dominant kernel (gate/up GEMM) and of the whole block.
+    ge_bytes_unit = 2 * cfg.moe_intermediate_size * cfg.hidden_size * (cfg.bits / 8 + 4 / 64)
+    sweep = []
+    gu_bytes_total = gu_ms_total = 0.0
+    for T in BATCHES:
+        G = graphs[T]
+        ms = statistics.median(per_T[T])
+        U = G["U"]
+        blk_bytes = synth.algorithmic_bytes(cfg, T, U)
+        gu_bytes = U * ge_bytes_unit + T * cfg.num_experts_per_tok * (D + cfg.moe_intermediate_size) * 2
+        gu_bytes_total += gu_bytes
+        gu_ms_total += stage[T]["gate_up_ms"]
+        sweep.append(dict(tokens=T, distinct_experts=U, ms=ms, tokens_per_s=T / (ms / 1e3),
+                          block_gbs=blk_bytes / (ms / 1e3) / 1e9,
+                          block_hbm_frac=blk_bytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+                          stages_ms={k: round(v, 5) for k, v in stage[T].items()}))
+    achieved = gu_bytes_total / (gu_ms_total / 1e3) / 1e9
+    roofline = dict(bound="hbm", kernel="grouped_dequant_gemm (gate|up + SwiGLU)", achieved=achieved,
+                    peak=peaks["hbm_gbs"], unit="GB/s", frac=achieved / peaks["hbm_gbs"],
+                    peak_source=peaks["source"] + " hbm_gbs (burst copy)",
+                    traffic=ncu_traffic("gate_up_c2_T64"),
+                    algorithmic_bytes_per_launch={str(T): None for T in BATCHES})
+    for T in BATCHES:
+        U = graphs[T]["U"]
+        roofline["algorithmic_bytes_per_launch"][str(T)] = int(
+            U * ge_bytes_unit + T * cfg.num_experts_per_tok * (D + cfg.moe_intermediate_size) * 2)
+
+    extra = {}
+    if rank == 0 and not args.no_extra and world == 1:
+        extra = bench_extra(args, dev, st, flush, peaks)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(blk, graphs, args)
+
+    if world > 1:
+        dist.barrier()
+    del graphs
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (Philox seed 0): experts N(0,0.02) bf16 -> 4-bit affine gs64, router bf16, x N(0,1)",
+            "config": {"workload": "c2 decode sweep: one block forward at T=1, 8, 64 per step",
+                       "hidden": D, "experts": cfg.num_experts, "top_k": cfg.num_experts_per_tok,
+                       "moe_intermediate": cfg.moe_intermediate_size, "bits": cfg.bits, "group_size": cfg.group_size,
+                       "batches": BATCHES, "l2": "flushed before every forward (512 MiB write)",
+                       "graphs": "each forward replayed from a captured CUDA graph",
+                       "parallelism": "replicas" if world > 1 else "single GPU"},
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "note": "pinned host x -> device, graph replay, out -> pinned host, per forward"},
+            "gpu_launches": kernels_per_forward(cfg) * len(BATCHES) * args.steps,
+            "clocks": clk,
+            "sweep": sweep,
+            "extra": extra,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def bench_extra(args, dev, st, flush, peaks):
+    """The other BASELINE configurations on this GPU (informational lines)."""
+    import torch
+
+    from mlxr_moe import synth
+    from mlxr_moe.moe import Routing
+
+    res = {}
+    for name, T in (("c1", 32), ("c3", 4096), ("c5_decode", 256), ("c5_prefill", 8192), ("c4", 16384)):
+        key = name.split("_")[0]
+        spec = synth.CONFIGS[key]
+        cfg = spec["cfg"]
+        blk = synth.make_block(cfg, 0, spec["zipf"], dev)
+        x = synth.make_input(T, cfg.hidden_size, stream_offset=7, device=dev)
+        out = torch.empty_like(x)
+        ws = torch.empty(blk.workspace_bytes(T), dtype=torch.uint8, device=dev)
+        r = Routing(T, cfg.num_experts_per_tok, cfg.num_experts, dev)
+        with torch.cuda.stream(st):
+            blk.forward(x, routing=r, out=out, workspace=ws)
+            torch.cuda.synchronize(dev)
+            blk.status(ws)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=st):
+                blk.forward(x, out=out, workspace=ws)
+            times = []
+            for i in range(3 + max(5, args.steps // 2)):
+                flush.fill_(i & 0xFF)
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record(st)
+                g.replay()
+                b.record(st)
+                torch.cuda.synchronize(dev)
+                if i >= 3:
+                    times.append(a.elapsed_time(b))
+        ms = statistics.median(times)
+        U = distinct_experts(r)
+        fl = synth.algorithmic_flops(cfg, T)
+        by = synth.algorithmic_bytes(cfg, T, U)
+        tfl = fl / (ms / 1e3) / 1e12
+        gbs = by / (ms / 1e3) / 1e9
+        prefill = T >= 2048
+        res[name] = dict(tokens=T, ms=ms, tokens_per_s=T / (ms / 1e3), tflops=tfl, gbs=gbs,
+                         bound="tensor" if prefill else "hbm",
+                         frac=(tfl / peaks["bf16_tflops"]) if prefill else (gbs / peaks["hbm_gbs"]),
+                         distinct_experts=U, zipf=spec["zipf"])
+        del g, blk, ws, out, x
+        torch.cuda.empty_cache()
+    return res
+
+
+# ---------------------------------------------------------- CPU baseline ----
+def cpu_baseline(blk, graphs, args):
+    """The oracle (CPU restatement of the reference block, fused-fp32 mode,
+    OpenMP on every host core) on a bounded sample: the same sweep batches."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle as O
+    from gpu_helpers import block_to_oracle
+
+    from conftest import bf16_np
+
+    cfg, W = block_to_oracle(blk)
+    cores = O.max_threads()
+    times = []
+    reps = 3
+    for rep in range(reps):
+        t0 = time.perf_counter()
+        for T in BATCHES:
+            O.moe_block(cfg, W, bf16_np(graphs[T]["x"][rep % 4]), "fused")
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    return {"value": sum(BATCHES) / sec, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{reps} sweeps (T=1,8,64) of the block, median; oracle fused-fp32 mode, OpenMP {cores} threads"}
+
+
+def run_reference(args):
+    """--impl reference: the CPU port of the reference block (MLX's own CPU
+    path cannot be built here) timed on all host cores; rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    import numpy as np
+
+    import oracle as O
+
+    cfgd = dict(hidden=2048, num_experts=128, top_k=8, moe_intermediate=768, group_size=64, bits=4)
+    W = {"router": O.normal_bf16(0, 0, (128, 2048), 0.02)}
+    W["gate"] = O.quantize(O.normal_bf16(0, 1, (128, 768, 2048), 0.02), 64, 4)
+    W["up"] = O.quantize(O.normal_bf16(0, 2, (128, 768, 2048), 0.02), 64, 4)
+    W["down"] = O.quantize(O.normal_bf16(0, 3, (128, 2048, 768), 0.02), 64, 4)
+    xs = {T: O.normal_bf16(0, 8 + 10 * T, (T, 2048), 1.0) for T in BATCHES}
+    cores = O.max_threads()
+    for _ in range(args.warmup):
+        for T in BATCHES:
+            O.moe_block(cfgd, W, xs[T], "fused")
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for T in BATCHES:
+            O.moe_block(cfgd, W, xs[T], "fused")
+    sec = time.perf_counter() - t0
+    value = sum(BATCHES) * args.steps / sec
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 0, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * sec / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (Philox seed 0), same configuration as the GPU arm",
+        "config": {"workload": "c2 decode sweep: one block forward at T=1, 8, 64 per step", "batches": BATCHES},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} full sweeps on the oracle (CPU restatement; MLX unbuildable here)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+    _ = np
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-extra", action="store_true", help="skip the other BASELINE configurations")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -182,6 +182,14 @@ MLXR_CU_API int mlxr_cu_moe_block_forward(const mlxr_cu_moe_config* cfg, const m
                               int64_t num_tokens, void* out, const mlxr_cu_moe_routing* routing, void* workspace,
                               size_t workspace_bytes, void* stream);
 
+/* Profiling hook (no counterpart in the reference, which times with Apple's
+ * xctrace, justfile:96-142): with count = 7 events (cudaEvent_t as void*),
+ * later mlxr_cu_moe_block_forward calls on this thread record events[i] on
+ * their stream at stage boundaries: 0 start, 1 router done, 2 permute done,
+ * 3 gate/up GEMM done, 4 down GEMM done, 5 shared expert done, 6 combine
+ * done. count = 0 switches it off. */
+MLXR_CU_API int mlxr_cu_moe_set_stage_events(void* const* events, int count);
+
 /* Reads (synchronising on stream) the device status word of the last forward
  * that used this workspace: MLXR_CU_OK, MLXR_CU_ERR_TIMEOUT or
  * MLXR_CU_ERR_DEVICE_INDEX. */

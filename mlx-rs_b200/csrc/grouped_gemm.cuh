@@ -26,6 +26,10 @@
 
 #include "common.cuh"
 
+#ifndef MLXR_RAW_WAR_FENCE
+#define MLXR_RAW_WAR_FENCE 1
+#endif
+
 namespace mlxr {
 
 // One entry of the device-built tile list: expert, first sorted row, rows.
@@ -310,6 +314,11 @@ __global__ void __launch_bounds__(480, 1)
             wv[4 * i + 3] = v.w;
           }
         }
+#if MLXR_RAW_WAR_FENCE
+        // The slot is refilled by TMA (async proxy) once all warps release it:
+        // order this warp's generic-proxy reads before that write.
+        fence_proxy_async_smem();
+#endif
         __syncwarp();
         if (lane == 0) mbar_arrive(&raw_empty[rs]);
         const int os = oit % C::OS;
@@ -361,13 +370,12 @@ __global__ void __launch_bounds__(480, 1)
         uint32_t g[32];
         uint32_t u[32];
         if (CW == 32) {
-          tmem_ld_32x32b_x32(tbase + c * 32, g);
-          if (NMAT == 2) tmem_ld_32x32b_x32(tbase + BN + c * 32, u);
+          if (NMAT == 2) tmem_ld2_x32_wait(tbase + c * 32, tbase + BN + c * 32, g, u);
+          else tmem_ld_x32_wait(tbase + c * 32, g);
         } else {
-          tmem_ld_32x32b_x16(tbase, g);
-          if (NMAT == 2) tmem_ld_32x32b_x16(tbase + BN, u);
+          if (NMAT == 2) tmem_ld2_x16_wait(tbase, tbase + BN, g, u);
+          else tmem_ld_x16_wait(tbase, g);
         }
-        tmem_ld_wait();
         const int nvalid = rows - c * CW < CW ? rows - c * CW : CW;
 #pragma unroll
         for (int j = 0; j < CW; ++j) {

@@ -29,6 +29,15 @@ int* op_status_word() {
   return static_cast<int*>(p);
 }
 
+// Optional per-thread stage events (a profiling hook): when set, the block
+// forward records events[i] on its stream at each stage boundary.
+static thread_local cudaEvent_t t_stage_events[8];
+static thread_local int t_stage_count = 0;
+
+static inline void stage_mark(int i, cudaStream_t st) {
+  if (i < t_stage_count && t_stage_events[i]) cudaEventRecord(t_stage_events[i], st);
+}
+
 static inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 struct Layout {
@@ -206,7 +215,7 @@ static int check_qlinear(const mlxr_cu_qlinear& q, const char* name) {
 }
 
 static int run_experts(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt, const Layout& L, void* ws,
-                       cudaStream_t st) {
+                       cudaStream_t st, int mid_stage) {
   if (L.R == 0) return MLXR_CU_OK;
   if (int rc = check_qlinear(wt->switch_gate, "switch_mlp.gate_proj")) return rc;
   if (int rc = check_qlinear(wt->switch_up, "switch_mlp.up_proj")) return rc;
@@ -234,6 +243,7 @@ static int run_experts(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* w
   p.out = at<uint16_t>(ws, L.h);
   p.status = status;
   if (int rc = launch_grouped_gemm(p, st)) return rc;
+  stage_mark(mid_stage, st);
 
   GroupedGemmProblem q{};
   q.nmat = 1;
@@ -339,16 +349,22 @@ int mlxr_cu_moe_block_forward(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_w
   MLXR_CHECK_ARG(x && out, "moe: x/out is NULL");
   MLXR_CHECK_ARG(aligned16(x) && aligned16(out), "moe: x and out must be 16-byte aligned");
   void* ws = workspace;
+  stage_mark(0, st);
   if (int rc = run_router(cfg, weights, L, x, ws, at<uint16_t>(ws, L.logits), nullptr, st)) return rc;
+  stage_mark(1, st);
   if (int rc = run_permute(L, at<int32_t>(ws, L.idx), x, ws, at<int32_t>(ws, L.counts), at<int32_t>(ws, L.offsets),
                            at<int32_t>(ws, L.sorted), at<int32_t>(ws, L.inv), at<uint16_t>(ws, L.xs), st))
     return rc;
-  if (int rc = run_experts(cfg, weights, L, ws, st)) return rc;
+  stage_mark(2, st);
+  if (int rc = run_experts(cfg, weights, L, ws, st, 3)) return rc;
+  stage_mark(4, st);
   if (int rc = run_shared(cfg, weights, L, x, ws, st)) return rc;
+  stage_mark(5, st);
   combine_kernel<<<(unsigned)L.T, 128, 0, st>>>(at<uint16_t>(ws, L.y), at<int32_t>(ws, L.inv), at<uint16_t>(ws, L.w),
                                                 L.K, L.D, L.T, L.Is > 0 ? at<uint16_t>(ws, L.ysh) : nullptr,
                                                 at<float>(ws, L.sig), static_cast<uint16_t*>(out));
   MLXR_LAUNCH_CHECK("combine_kernel");
+  stage_mark(6, st);
   if (routing) {
     auto cp = [&](void* dst, size_t off, size_t bytes) -> int {
       if (dst && bytes) MLXR_CUDA_TRY(cudaMemcpyAsync(dst, at<uint8_t>(ws, off), bytes, cudaMemcpyDeviceToDevice, st));
@@ -361,6 +377,14 @@ int mlxr_cu_moe_block_forward(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_w
     if (int rc = cp(routing->sorted_rows, L.sorted, (size_t)L.R * 4)) return rc;
     if (int rc = cp(routing->inverse, L.inv, (size_t)L.R * 4)) return rc;
   }
+  return MLXR_CU_OK;
+}
+
+int mlxr_cu_moe_set_stage_events(void* const* events, int count) {
+  MLXR_CHECK_ARG(count >= 0 && count <= 8, "moe_set_stage_events: count=%d must be in [0, 8]", count);
+  MLXR_CHECK_ARG(count == 0 || events != nullptr, "moe_set_stage_events: events is NULL");
+  for (int i = 0; i < 8; ++i) t_stage_events[i] = i < count ? static_cast<cudaEvent_t>(events[i]) : nullptr;
+  t_stage_count = count;
   return MLXR_CU_OK;
 }
 
