@@ -158,10 +158,15 @@ def run_gpu(args):
     peaks = measured_peaks()
     spec = synth.CONFIGS[WORKLOAD]
     cfg = spec["cfg"]
+    # Everything (weight synthesis, inputs, workspaces, forwards) runs on one
+    # stream, so the caching allocator never hands a buffer that pending work
+    # on another stream still touches to the block.
+    st = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(st)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     blk = synth.make_block(cfg, seed=0, zipf=spec["zipf"], device=dev)
     D = cfg.hidden_size
-    st = torch.cuda.Stream(dev)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize(dev)
     nsets = 4  # distinct input batches cycled through the steps
 
     # Per batch size: static input/output/workspace buffers and one graph.
@@ -375,6 +380,7 @@ def bench_extra(args, dev, st, flush, peaks):
         out = torch.empty_like(x)
         ws = torch.empty(blk.workspace_bytes(T), dtype=torch.uint8, device=dev)
         r = Routing(T, cfg.num_experts_per_tok, cfg.num_experts, dev)
+        torch.cuda.synchronize(dev)
         with torch.cuda.stream(st):
             blk.forward(x, routing=r, out=out, workspace=ws)
             torch.cuda.synchronize(dev)

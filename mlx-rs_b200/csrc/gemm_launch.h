@@ -24,7 +24,8 @@ struct GroupedGemmProblem {
   const GemmTile* tiles;      // device tile list
   const int32_t* num_tiles;   // device count
   int max_tiles;
-  uint16_t* out;              // bf16 [rows, n_out]
+  uint16_t* out;              // bf16 [out_rows, n_out]
+  int64_t out_rows;
   int* status;
   int grid;                   // 0 = one CTA per SM
 };

@@ -87,6 +87,7 @@ static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
   a.k_dim = p.k_dim;
   a.num_experts = p.num_experts;
   a.max_tiles = p.max_tiles;
+  a.out_rows = p.out_rows;
   a.status = p.status;
   const int grid = p.grid > 0 ? p.grid : num_sms_current();
   kern<<<grid, C::NUM_THREADS, C::SMEM_BYTES, st>>>(ta0, ta1, tb, a);

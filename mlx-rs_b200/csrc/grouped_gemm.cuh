@@ -83,8 +83,17 @@ struct GemmArgs {
   int32_t k_dim;              // K (multiple of 64)
   int32_t num_experts;
   int32_t max_tiles;
+  int64_t out_rows;           // rows of `out` (and of the activation operand)
   int* status;
 };
+
+// A tile entry is used only if it names a valid expert and a row range inside
+// the output; every role evaluates the same predicate and skips bad entries,
+// so a corrupted tile list can never turn into a wild load or store.
+__device__ inline bool tile_ok(const GemmTile& t, const GemmArgs& a) {
+  return t.expert >= 0 && t.expert < a.num_experts && t.row_start >= 0 && t.row_count > 0 &&
+         (int64_t)t.row_start + t.row_count <= a.out_rows;
+}
 
 // 4-bit word (8 codes) -> 8 bf16 values s*q + b (one rounding, bf16 fma).
 __device__ inline uint4 dequant_word4(uint32_t w, __nv_bfloat162 s2, __nv_bfloat162 b2) {
@@ -209,6 +218,10 @@ __global__ void __launch_bounds__(480, 1)
       uint32_t it = 0;
       for (int item = blockIdx.x; item < num_items && !*abort_flag; item += gridDim.x) {
         const GemmTile t = args.tiles[item / mt_per_expert];
+        if (!tile_ok(t, args)) {
+          atomicCAS(args.status, 0, (int)kDevBadIndex);
+          continue;
+        }
         const int a_row = t.expert * n_out + (item % mt_per_expert) * C::BM;
         for (int ks = 0; ks < ksteps; ++ks, ++it) {
           const int s = it % C::RS;
@@ -226,6 +239,7 @@ __global__ void __launch_bounds__(480, 1)
       uint32_t it = 0;
       for (int item = blockIdx.x; item < num_items && !*abort_flag; item += gridDim.x) {
         const GemmTile t = args.tiles[item / mt_per_expert];
+        if (!tile_ok(t, args)) continue;
         for (int ks = 0; ks < ksteps; ++ks, ++it) {
           const int s = it % C::OS;
           if (!mbar_wait(&op_empty[s], ((it / C::OS) & 1) ^ 1, abort_flag, args.status)) break;
@@ -240,9 +254,12 @@ __global__ void __launch_bounds__(480, 1)
     if (lane == 0) {
       uint32_t it = 0, li = 0;
       bool ok = true;
-      for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x, ++li) {
+      for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
+        if (!tile_ok(args.tiles[item / mt_per_expert], args)) continue;
         const int ab = li % C::AB;
-        if (!mbar_wait(&acc_empty[ab], ((li / C::AB) & 1) ^ 1, abort_flag, args.status)) break;
+        const uint32_t acc_phase = (li / C::AB) & 1;
+        ++li;  // counts valid items only, exactly like the epilogue
+        if (!mbar_wait(&acc_empty[ab], acc_phase ^ 1, abort_flag, args.status)) break;
         tc_fence_after();
         const uint32_t d0 = tmem_base + (uint32_t)(ab * C::ACC_COLS);
         for (int ks = 0; ks < ksteps; ++ks, ++it) {
@@ -283,6 +300,7 @@ __global__ void __launch_bounds__(480, 1)
     bool ok = true;
     for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
       const GemmTile t = args.tiles[item / mt_per_expert];
+      if (!tile_ok(t, args)) continue;
       const int64_t srow = (int64_t)t.expert * n_out + (item % mt_per_expert) * C::BM + row;
       const uint16_t* sp = args.scales[mat] + srow * G;
       const uint16_t* bp = args.biases[mat] + srow * G;
@@ -354,11 +372,14 @@ __global__ void __launch_bounds__(480, 1)
     // ------------------------------------------------------- epilogue ----
     const int q = warp;  // TMEM lane quarter 0..3
     uint32_t li = 0;
-    for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++li) {
-      const int ab = li % C::AB;
-      if (!mbar_wait(&acc_full[ab], (li / C::AB) & 1, abort_flag, args.status)) break;
-      tc_fence_after();
+    for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
       const GemmTile t = args.tiles[item / mt_per_expert];
+      if (!tile_ok(t, args)) continue;
+      const int ab = li % C::AB;
+      const uint32_t acc_phase = (li / C::AB) & 1;
+      ++li;
+      if (!mbar_wait(&acc_full[ab], acc_phase, abort_flag, args.status)) break;
+      tc_fence_after();
       const int f = (item % mt_per_expert) * C::BM + q * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * C::ACC_COLS);
       uint16_t* outp = args.out + (int64_t)t.row_start * n_out + f;

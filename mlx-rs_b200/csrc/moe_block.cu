@@ -35,7 +35,8 @@ static thread_local cudaEvent_t t_stage_events[8];
 static thread_local int t_stage_count = 0;
 
 static inline void stage_mark(int i, cudaStream_t st) {
-  if (i < t_stage_count && t_stage_events[i]) cudaEventRecord(t_stage_events[i], st);
+  // External records become event nodes when the stream is being captured.
+  if (i < t_stage_count && t_stage_events[i]) cudaEventRecordWithFlags(t_stage_events[i], st, cudaEventRecordExternal);
 }
 
 static inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -241,6 +242,7 @@ static int run_experts(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* w
   p.num_tiles = at<int32_t>(ws, L.n1);
   p.max_tiles = L.max_t1;
   p.out = at<uint16_t>(ws, L.h);
+  p.out_rows = L.R;
   p.status = status;
   if (int rc = launch_grouped_gemm(p, st)) return rc;
   stage_mark(mid_stage, st);
@@ -262,6 +264,7 @@ static int run_experts(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* w
   q.num_tiles = at<int32_t>(ws, L.n2);
   q.max_tiles = L.max_t2;
   q.out = at<uint16_t>(ws, L.y);
+  q.out_rows = L.R;
   q.status = status;
   return launch_grouped_gemm(q, st);
 }
@@ -300,6 +303,7 @@ static int run_shared(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
   p.num_tiles = at<int32_t>(ws, L.nsh);
   p.max_tiles = L.max_tsh;
   p.out = at<uint16_t>(ws, L.hsh);
+  p.out_rows = L.T;
   p.status = status;
   if (int rc = launch_grouped_gemm(p, st)) return rc;
   GroupedGemmProblem q{};
@@ -319,6 +323,7 @@ static int run_shared(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
   q.num_tiles = at<int32_t>(ws, L.nsh);
   q.max_tiles = L.max_tsh;
   q.out = at<uint16_t>(ws, L.ysh);
+  q.out_rows = L.T;
   q.status = status;
   return launch_grouped_gemm(q, st);
 }
@@ -362,7 +367,8 @@ int mlxr_cu_moe_block_forward(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_w
   stage_mark(5, st);
   combine_kernel<<<(unsigned)L.T, 128, 0, st>>>(at<uint16_t>(ws, L.y), at<int32_t>(ws, L.inv), at<uint16_t>(ws, L.w),
                                                 L.K, L.D, L.T, L.Is > 0 ? at<uint16_t>(ws, L.ysh) : nullptr,
-                                                at<float>(ws, L.sig), static_cast<uint16_t*>(out));
+                                                at<float>(ws, L.sig), static_cast<uint16_t*>(out),
+                                                at<int>(ws, L.status));
   MLXR_LAUNCH_CHECK("combine_kernel");
   stage_mark(6, st);
   if (routing) {

@@ -370,6 +370,7 @@ __global__ void __launch_bounds__(256) permute_scatter_kernel(const int32_t* __r
     const uint32_t peers = __match_any_sync(0xffffffffu, e);
     int pos = -1;
     if (e >= 0) pos = wcnt[warp * E + e] + __popc(peers & lt_mask);
+    if (pos >= R) pos = -1;  // cannot happen for consistent counts; never write out of range
     __syncwarp();
     if (e >= 0 && lane == __ffs(peers) - 1) wcnt[warp * E + e] += __popc(peers);
     __syncwarp();
@@ -392,13 +393,21 @@ __global__ void __launch_bounds__(256) permute_scatter_kernel(const int32_t* __r
 __global__ void __launch_bounds__(128) combine_kernel(const uint16_t* __restrict__ y_sorted,
                                                      const int32_t* __restrict__ inv, const uint16_t* __restrict__ w,
                                                      int K, int D, int64_t T, const uint16_t* __restrict__ y_sh,
-                                                     const float* __restrict__ sig, uint16_t* __restrict__ out) {
+                                                     const float* __restrict__ sig, uint16_t* __restrict__ out,
+                                                     int* status) {
   __shared__ int rows[RT_MAXK];
   __shared__ float wk[RT_MAXK];
   const int64_t t = blockIdx.x;
   if (threadIdx.x < K) {
-    rows[threadIdx.x] = inv[t * K + threadIdx.x];
-    wk[threadIdx.x] = bf16_bits_to_f32(w[t * K + threadIdx.x]);
+    int r = inv[t * K + threadIdx.x];
+    float wv = bf16_bits_to_f32(w[t * K + threadIdx.x]);
+    if (r < 0 || (int64_t)r >= T * K) {  // never for a permutation built by permute_scatter_kernel
+      atomicCAS(status, 0, (int)kDevBadIndex);
+      r = 0;
+      wv = 0.0f;
+    }
+    rows[threadIdx.x] = r;
+    wk[threadIdx.x] = wv;
   }
   __syncthreads();
   const float sg = y_sh ? sig[t] : 0.0f;

@@ -49,6 +49,18 @@ def to_f32(a_u16):
     return (a_u16.astype(np.uint32) << 16).view(np.float32)
 
 
+def assert_mostly_tight(got_u16, want_u16, atol, rtol, max_frac, what="output"):
+    """At most max_frac of the elements may fall outside the tight bound
+    (bf16 outputs flip by an ulp or two when two fp32 accumulation orders
+    straddle a rounding boundary)."""
+    g = to_f32(got_u16).astype(np.float64)
+    w = to_f32(want_u16).astype(np.float64)
+    err = np.abs(g - w)
+    frac = float((err > atol + rtol * np.abs(w)).mean())
+    assert frac <= max_frac, f"{what}: {frac:.2e} of elements outside atol={atol} rtol={rtol} (allowed {max_frac})"
+    return frac
+
+
 def assert_close_bf16(got_u16, want_u16, atol=ATOL, rtol=RTOL, what="output"):
     g = to_f32(got_u16).astype(np.float64)
     w = to_f32(want_u16).astype(np.float64)
