@@ -182,6 +182,30 @@ MLXR_CU_API int mlxr_cu_moe_block_forward(const mlxr_cu_moe_config* cfg, const m
                               int64_t num_tokens, void* out, const mlxr_cu_moe_routing* routing, void* workspace,
                               size_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of mlxr_cu_moe_block_forward (no counterpart in
+ * the reference, whose ops always allocate their outputs through MLX). For
+ * callers that cannot allocate device memory at call time: a serving engine
+ * that reserves nearly all HBM up front and forbids later cudaMalloc (or
+ * cannot afford its implicit synchronisation), or a host runtime that binds
+ * this library over a plain C ABI without a device allocator to pass in.
+ * The caller passes inputs and outputs as for mlxr_cu_moe_block_forward; the
+ * scratch is a fixed 24 MiB array inside the library, held by every GPU that
+ * loads the library until the process exits. Requests needing more scratch
+ * (beyond 321 tokens for a hidden-2048 / 128-expert / top-8 / 768 block,
+ * 161 tokens for hidden 4096 / intermediate 1536)
+ * fail with MLXR_CU_ERR_WORKSPACE. The first call on each device looks the
+ * array's device address up (with that device current); make that first call
+ * before any stream capture. All calls share the one array, so calls that
+ * overlap on the GPU (different streams or threads) race: serialise them.
+ * device_status (device int, may be NULL) receives the device-side status
+ * word (0 ok, 1 wait timeout, 2 index out of range) when the forward ends.
+ * Nothing on this path calls cudaMalloc, cudaFree or an allocating routine. */
+MLXR_CU_API int mlxr_cu_moe_block_forward_noalloc(const mlxr_cu_moe_config* cfg,
+                                                  const mlxr_cu_moe_weights* weights, const void* x,
+                                                  int64_t num_tokens, void* out,
+                                                  const mlxr_cu_moe_routing* routing, int* device_status,
+                                                  void* stream);
+
 /* Profiling hook (no counterpart in the reference, which times with Apple's
  * xctrace, justfile:96-142): with count = 7 events (cudaEvent_t as void*),
  * later mlxr_cu_moe_block_forward calls on this thread record events[i] on

@@ -10,6 +10,7 @@
 //   combine (+ sigmoid-gated shared expert)
 // All scratch lives in the caller's workspace; nothing is allocated here.
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 #include "gemm_launch.h"
@@ -391,6 +392,73 @@ int mlxr_cu_moe_set_stage_events(void* const* events, int count) {
   MLXR_CHECK_ARG(count == 0 || events != nullptr, "moe_set_stage_events: events is NULL");
   for (int i = 0; i < 8; ++i) t_stage_events[i] = i < count ? static_cast<cudaEvent_t>(events[i]) : nullptr;
   t_stage_count = count;
+  return MLXR_CU_OK;
+}
+
+// ------------------------------------------------ allocation-free entry --
+// Some callers of this library cannot allocate device memory when they call
+// it: a serving engine that has reserved nearly all HBM for weights and KV
+// cache up front and treats any later cudaMalloc as an error (or cannot
+// afford its implicit device-wide synchronisation on a latency path), or a
+// host runtime that binds this library over a plain C ABI and has no device
+// allocator to hand it. For them mlxr_cu_moe_block_forward_noalloc runs the
+// block forward with its scratch in the fixed-size array below, which lives
+// in the library image: every GPU that loads the library holds
+// kNoAllocScratchBytes of it until the process exits, and nothing on this
+// path calls cudaMalloc, cudaFree or an allocating library routine.
+constexpr size_t kNoAllocScratchBytes = size_t(24) << 20;  // 24 MiB
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Host code cannot use g_noalloc_scratch as a device address (in host code it
+// names a host-side stand-in). The device address is looked up once per
+// device, with that device current, and cached.
+static void* noalloc_scratch(int* rc) {
+  static std::mutex mu;
+  static void* ptrs[128] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    *rc = check_cuda(e, "cudaGetDevice");
+    return nullptr;
+  }
+  if (dev < 0 || dev >= 128) {
+    *rc = set_error(MLXR_CU_ERR_CUDA, "moe_noalloc: device ordinal %d out of range", dev);
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      *rc = check_cuda(e != cudaSuccess ? e : cudaErrorInvalidSymbol, "cudaGetSymbolAddress(noalloc scratch)");
+      return nullptr;
+    }
+    ptrs[dev] = p;
+  }
+  *rc = MLXR_CU_OK;
+  return ptrs[dev];
+}
+
+int mlxr_cu_moe_block_forward_noalloc(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights,
+                                      const void* x, int64_t num_tokens, void* out,
+                                      const mlxr_cu_moe_routing* routing, int* device_status, void* stream) {
+  if (int rc = validate(cfg, num_tokens)) return rc;
+  const Layout L = make_layout(cfg, num_tokens);
+  if (L.total > kNoAllocScratchBytes)
+    return set_error(MLXR_CU_ERR_WORKSPACE,
+                     "moe_noalloc: %lld tokens need %zu bytes of scratch but the allocation-free entry point has %zu; "
+                     "split the batch or call mlxr_cu_moe_block_forward with a workspace",
+                     (long long)num_tokens, L.total, kNoAllocScratchBytes);
+  int rc = MLXR_CU_OK;
+  void* ws = noalloc_scratch(&rc);
+  if (!ws) return rc;
+  // The scratch keeps the previous call's contents; the forward clears its
+  // status word itself and rebuilds every other buffer before reading it.
+  if (int r2 = mlxr_cu_moe_block_forward(cfg, weights, x, num_tokens, out, routing, ws, kNoAllocScratchBytes, stream))
+    return r2;
+  if (device_status)
+    MLXR_CUDA_TRY(cudaMemcpyAsync(device_status, at<int>(ws, L.status), sizeof(int), cudaMemcpyDeviceToDevice,
+                                  static_cast<cudaStream_t>(stream)));
   return MLXR_CU_OK;
 }
 

@@ -38,6 +38,7 @@ EXPORTS = (
     "mlxr_cu_gather_mm",
     "mlxr_cu_moe_workspace_size",
     "mlxr_cu_moe_block_forward",
+    "mlxr_cu_moe_block_forward_noalloc",
     "mlxr_cu_moe_status",
     "mlxr_cu_moe_set_stage_events",
     "mlxr_cu_op_status",
@@ -126,6 +127,8 @@ def _load():
     lib.mlxr_cu_moe_workspace_size.argtypes = [C.POINTER(MoeConfig), I64, C.POINTER(C.c_size_t)]
     lib.mlxr_cu_moe_block_forward.argtypes = [C.POINTER(MoeConfig), C.POINTER(MoeWeights), P, I64, P,
                                               C.POINTER(MoeRouting), P, C.c_size_t, P]
+    lib.mlxr_cu_moe_block_forward_noalloc.argtypes = [C.POINTER(MoeConfig), C.POINTER(MoeWeights), P, I64, P,
+                                                      C.POINTER(MoeRouting), P, P]
     lib.mlxr_cu_moe_status.argtypes = [P, P]
     lib.mlxr_cu_moe_set_stage_events.argtypes = [C.POINTER(C.c_void_p), I32]
     lib.mlxr_cu_op_status.argtypes = [P]
