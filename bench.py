@@ -65,59 +65,70 @@ def ncu_traffic(kernel_key: str):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled through NVML every
+    5 ms while the timed region runs (the nvidia-smi clocks query reads the
+    same counters, but its 200 ms period is longer than a timed region).
+    Read-only: no clock or power setting is touched."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake_slowdown", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
+    def __init__(self, uuid: str):
+        self.uuid = uuid
+        self.samples = []
+        self.err = None
+        self._stop = threading.Event()
+        self.t = None
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except (FileNotFoundError, OSError):
-            self.proc = None
+            import pynvml as N
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            N.nvmlInit()
+            self.N = N
+            self.h = N.nvmlDeviceGetHandleByUUID(self.uuid)
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM)
+        except Exception as e:  # no NVML: report it instead of a clock
+            self.err = f"nvml unavailable: {e}"[:200]
+            return
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
+
+    def _run(self):
+        N = self.N
+        while not self._stop.is_set():
+            try:
+                mhz = N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM)
+                rs = N.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((mhz, rs))
+            except Exception as e:
+                self.err = str(e)[:200]
+                return
+            time.sleep(0.005)
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                smax.append(float(f[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        if self.t is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "error": self.err}
+        self._stop.set()
+        self.t.join(timeout=2)
+        sm = [m for m, _ in self.samples]
+        reasons = set()
+        for _, rs in self.samples:
+            for name, const in self.REASONS:
+                if rs & getattr(self.N, const, 0):
+                    reasons.add(name)
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+               "reasons": sorted(reasons), "samples": len(sm), "source": "nvml 5 ms"}
+        if not sm:
+            out["error"] = self.err or "no samples"
+        return out
 
 
 def smi_id(torch, dev) -> str:
-    """nvidia-smi -i accepts the GPU UUID, which survives CUDA_VISIBLE_DEVICES remapping."""
+    """The GPU's UUID (survives CUDA_VISIBLE_DEVICES remapping)."""
     try:
         u = str(torch.cuda.get_device_properties(dev).uuid)
         return u if u.startswith("GPU-") else "GPU-" + u
@@ -126,8 +137,8 @@ def smi_id(torch, dev) -> str:
 
 
 def kernels_per_forward(cfg) -> int:
-    # router (logits, top-k) + permute (count, scan, scatter) + gate/up + down + combine
-    n = 2 + 3 + 2 + 1
+    # router (logits, top-k) + permute (count, scan, scatter, gather) + gate/up + down + combine
+    n = 2 + 4 + 2 + 1
     if cfg.shared_expert_intermediate_size:
         n += 2
     return n
@@ -481,6 +492,23 @@ def run_reference(args):
     _ = np
 
 
+def run_case(args):
+    """Block forwards of one configuration, for ncu captures (not a bench number)."""
+    import torch
+
+    from mlxr_moe import synth
+
+    name, T = args.case.split(":")
+    spec = synth.CONFIGS[name]
+    blk = synth.make_block(spec["cfg"], 0, spec["zipf"])
+    x = synth.make_input(int(T), spec["cfg"].hidden_size)
+    for _ in range(args.iters):
+        blk.forward(x)
+    torch.cuda.synchronize()
+    blk.status()
+    print(f"case {args.case}: {args.iters} forwards ok")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -489,7 +517,13 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extra", action="store_true", help="skip the other BASELINE configurations")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--case", default=None,
+                    help="profiling driver: CONFIG:TOKENS (e.g. c2:64); runs only block forwards, prints nothing timed")
+    ap.add_argument("--iters", type=int, default=3, help="forwards for --case")
     args = ap.parse_args()
+    if args.case:
+        run_case(args)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

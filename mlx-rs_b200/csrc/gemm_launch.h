@@ -26,6 +26,8 @@ struct GroupedGemmProblem {
   int max_tiles;
   uint16_t* out;              // bf16 [out_rows, n_out]
   int64_t out_rows;
+  int perm_out;               // 1: write out's feature axis in the 4-bit chunk K order
+  int pair;                   // nmat 2 only: w[0] rows m and m+128 as the two matrices (plain store)
   int* status;
   int grid;                   // 0 = one CTA per SM
 };

@@ -88,6 +88,8 @@ static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
   a.num_experts = p.num_experts;
   a.max_tiles = p.max_tiles;
   a.out_rows = p.out_rows;
+  a.perm_out = p.perm_out;
+  a.pair = p.pair;
   a.status = p.status;
   const int grid = p.grid > 0 ? p.grid : num_sms_current();
   kern<<<grid, C::NUM_THREADS, C::SMEM_BYTES, st>>>(ta0, ta1, tb, a);
@@ -96,6 +98,8 @@ static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
 }
 
 int launch_grouped_gemm(const GroupedGemmProblem& p, cudaStream_t st) {
+  if (p.pair && (p.nmat != 2 || p.n_out % 256 != 0))
+    return set_error(MLXR_CU_ERR_INVALID_ARGUMENT, "grouped gemm: paired row blocks need nmat 2 and n_out %% 256 == 0");
   if (p.n_out % 128 != 0 || p.k_dim % 64 != 0)
     return set_error(MLXR_CU_ERR_INVALID_ARGUMENT, "grouped gemm: n_out=%d must be a multiple of 128 and K=%d of 64",
                      p.n_out, p.k_dim);

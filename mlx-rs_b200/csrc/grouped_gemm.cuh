@@ -8,27 +8,29 @@
 // the swiglu that follows (activations.rs:198-200).
 //
 // Orientation ("weights as M"): one work item is a 128-row slice of one
-// expert's weight matrix (the A operand, K-major, dequantised into shared
-// memory) times a tile of up to BN expert-sorted token rows (the B operand,
-// K-major, loaded by TMA with 128-byte swizzle). The accumulator D[128, BN]
-// lives in TMEM: lane = output feature, column = token. Decode batches use
-// small BN (16/32), prefill BN = 128 (gate/up) or 256 (down).
+// expert's weight matrix (the A operand) times a tile of up to BN
+// expert-sorted token rows (the B operand, K-major, loaded by TMA with
+// 128-byte swizzle). The dequantised A operand lives in tensor memory, not in
+// shared memory: the dequant thread that owns weight row r writes its bf16
+// values into TMEM lane r with tcgen05.st and tcgen05.mma reads A from TMEM
+// (the A-in-TMEM form). This keeps shared memory for the TMA streams only;
+// with A in shared memory, writing it and the tensor core re-reading it made
+// shared-memory bandwidth the limit of the decode path. The accumulator
+// D[128, BN] lives in TMEM too: lane = output feature, column = token.
+// Decode batches use small BN (16/32), prefill BN = 128 (gate/up) or 256 (down).
 //
 // Warp roles (480 threads):
 //   warps 0-3   epilogue: TMEM -> registers -> SwiGLU / plain -> bf16 global
-//   warps 4-11  dequant: packed uint32 tile (smem) -> bf16 swizzled A tile
+//   warps 4-11  dequant: packed uint32 tile (smem) -> bf16 A stage in TMEM
 //   warp 12     TMA producer for packed weight tiles (raw ring)
-//   warp 13     TMA producer for activation tiles (operand ring)
+//   warp 13     TMA producer for activation tiles (B ring)
 //   warp 14     TMEM allocator + single-thread tcgen05.mma issuer
-// Accumulators are double-buffered in TMEM when they fit (2*NMAT*BN <= 512),
-// so the epilogue of item i overlaps the main loop of item i+1.
+// TMEM columns: [0, AB*NMAT*BN) accumulators (double-buffered when they fit,
+// so the epilogue of item i overlaps the main loop of item i+1), then OS
+// stages of NMAT x 32 columns (128 rows x 64 bf16) of dequantised A.
 #pragma once
 
 #include "common.cuh"
-
-#ifndef MLXR_RAW_WAR_FENCE
-#define MLXR_RAW_WAR_FENCE 1
-#endif
 
 namespace mlxr {
 
@@ -48,28 +50,40 @@ struct GG {
   static constexpr int RAW_ROW = KW * 4;                  // bytes
   static constexpr int RAW_MAT = BM * RAW_ROW;
   static constexpr int RAW_STAGE = NMAT * RAW_MAT;
-  static constexpr int A_MAT = BM * BK * 2;               // 16 KB bf16
-  static constexpr int A_STAGE = NMAT * A_MAT;
   static constexpr int B_STAGE = BN * BK * 2;
-  static constexpr int RS = RAW_STAGE <= 8192 ? 8 : 4;    // raw ring depth
-  static constexpr int SMEM_BUDGET = 220 * 1024;
-  static constexpr int OS_FIT = (SMEM_BUDGET - RS * RAW_STAGE) / (A_STAGE + B_STAGE);
-  static constexpr int OS = OS_FIT > 4 ? 4 : OS_FIT;      // operand ring depth
-  static_assert(OS >= 2, "shared memory budget too small");
+  // Shared-memory rings: packed weights (raw) and activation tiles (B), each
+  // up to 96 KB deep so both streams are requested well ahead of use.
+  static constexpr int RS_WANT = (96 * 1024) / RAW_STAGE;
+  static constexpr int RS = RS_WANT > 16 ? 16 : RS_WANT;
+  static constexpr int BS_WANT = (96 * 1024) / B_STAGE;
+  static constexpr int BS = BS_WANT > 16 ? 16 : (BS_WANT < 3 ? 3 : BS_WANT);
+  // Tensor memory: accumulators, then the A stages.
   static constexpr int ACC_COLS = NMAT * BN;
-  static constexpr int AB = (2 * ACC_COLS <= 512) ? 2 : 1;
-  static constexpr int TMEM_NEED = AB * ACC_COLS;
+  static constexpr int A_COLS = NMAT * 32;                // one A stage: NMAT x (128 x 64 bf16)
+  static constexpr int AB = (2 * ACC_COLS + 2 * A_COLS <= 512) ? 2 : 1;
+  static constexpr int OS_FIT = (512 - AB * ACC_COLS) / A_COLS;
+  static constexpr int OS = OS_FIT > 4 ? 4 : OS_FIT;      // A-stage ring depth
+  static_assert(OS >= 2, "tensor memory too small for two A stages");
+  static constexpr int A_BASE = AB * ACC_COLS;
+  static constexpr int TMEM_NEED = A_BASE + OS * A_COLS;
   static constexpr int TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128
                                    : TMEM_NEED <= 256 ? 256 : 512;
-  static_assert(TMEM_NEED <= 512, "accumulators exceed tensor memory");
+  static_assert(TMEM_NEED <= 512, "tensor memory exceeded");
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128 must be a multiple of 16 in [16, 256]");
-  static constexpr int NUM_THREADS = 480;
-  static constexpr int OFF_A = 0;
-  static constexpr int OFF_B = OFF_A + OS * A_STAGE;
-  static constexpr int OFF_RAW = OFF_B + OS * B_STAGE;
+  // One MMA-issuing thread per matrix: issuing a tcgen05.mma costs the issuing
+  // thread tens of cycles whatever N is, so with narrow decode tiles a single
+  // issuer, not the tensor pipe, bounds the k-step rate.
+  static constexpr int ISSUERS = NMAT;
+  static constexpr int NUM_THREADS = 32 * (14 + ISSUERS);
+  static constexpr int OFF_B = 0;
+  static constexpr int OFF_RAW = OFF_B + BS * B_STAGE;
   static constexpr int OFF_BAR = OFF_RAW + RS * RAW_STAGE;
-  static constexpr int NUM_BARS = 2 * RS + 2 * OS + 2 * AB + 1;
-  static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 16 + 1024;  // + alignment slack
+  static constexpr int NUM_BARS = 2 * RS + 2 * OS + 2 * BS + 2 * AB + 1;
+  // At least 120 KB so that two CTAs never share an SM: each CTA holds its
+  // tensor memory for its whole (persistent) lifetime.
+  static constexpr int SMEM_USED = OFF_BAR + NUM_BARS * 8 + 16 + 1024;  // + alignment slack
+  static constexpr int SMEM_BYTES = SMEM_USED > 120 * 1024 ? SMEM_USED : 120 * 1024;
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory exceeded");
   static constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN);
 };
 
@@ -84,6 +98,9 @@ struct GemmArgs {
   int32_t num_experts;
   int32_t max_tiles;
   int64_t out_rows;           // rows of `out` (and of the activation operand)
+  int perm_out;               // store out's feature axis in the 4-bit chunk K order
+  int pair;                   // NMAT == 2 only: the two matrices are row blocks m and m+128
+                              // of one weight (plain epilogue) instead of gate and up (SwiGLU)
   int* status;
 };
 
@@ -95,15 +112,23 @@ __device__ inline bool tile_ok(const GemmTile& t, const GemmArgs& a) {
          (int64_t)t.row_start + t.row_count <= a.out_rows;
 }
 
-// 4-bit word (8 codes) -> 8 bf16 values s*q + b (one rounding, bf16 fma).
-__device__ inline uint4 dequant_word4(uint32_t w, __nv_bfloat162 s2, __nv_bfloat162 b2) {
+// K order inside every 8-element (16-byte) chunk of a 4-bit operand pair.
+// The 4-bit dequantiser emits codes (0,4), (1,5), (2,6), (3,7) as bf16 pairs
+// straight from the nibble masks, so A holds chunk elements in the order
+// {0,4,1,5,2,6,3,7}. The tensor core only needs A and B to agree on the K
+// order, so the activation operand is stored with the same order instead of
+// re-shuffling every weight: element e of a chunk sits at position kperm(e).
+__host__ __device__ inline int kperm_pos(int e) { return ((e & 3) << 1) | (e >> 2); }
+
+// 4-bit word (8 codes) -> 4 bf16 pairs s*q + b (one rounding, bf16 fma) in
+// the chunk order {0,4}, {1,5}, {2,6}, {3,7}.
+__device__ inline void dequant_word4(uint32_t w, __nv_bfloat162 s2, __nv_bfloat162 b2, uint32_t* d) {
   const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.0f, 128.0f);
   uint32_t t[4];
   t[0] = (w & 0x000F000Fu) | 0x43004300u;
   t[1] = ((w >> 4) & 0x000F000Fu) | 0x43004300u;
   t[2] = ((w >> 8) & 0x000F000Fu) | 0x43004300u;
   t[3] = ((w >> 12) & 0x000F000Fu) | 0x43004300u;
-  uint32_t d[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&t[i]);
@@ -111,13 +136,6 @@ __device__ inline uint4 dequant_word4(uint32_t w, __nv_bfloat162 s2, __nv_bfloat
     v = __hfma2(v, s2, b2);
     d[i] = *reinterpret_cast<uint32_t*>(&v);
   }
-  // d[i] holds codes (i, i+4); reorder to (0,1) (2,3) (4,5) (6,7).
-  uint4 o;
-  o.x = __byte_perm(d[0], d[1], 0x5410);
-  o.y = __byte_perm(d[2], d[3], 0x5410);
-  o.z = __byte_perm(d[0], d[1], 0x7632);
-  o.w = __byte_perm(d[2], d[3], 0x7632);
-  return o;
 }
 
 // Two 8-bit words (8 codes) -> 8 bf16 values: codes made exact in fp32 via
@@ -151,21 +169,22 @@ __device__ inline void drain_ring(uint64_t* full, uint32_t issued, volatile int*
 }
 
 template <int NMAT, int BN, int BITS>
-__global__ void __launch_bounds__(480, 1)
+__global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
     grouped_dequant_gemm_kernel(const __grid_constant__ CUtensorMap tm_a0, const __grid_constant__ CUtensorMap tm_a1,
                                 const __grid_constant__ CUtensorMap tm_b, const GemmArgs args) {
   using C = GG<NMAT, BN, BITS>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem + C::OFF_A;
   uint8_t* sB = smem + C::OFF_B;
   uint8_t* sRaw = smem + C::OFF_RAW;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* raw_full = bars;
   uint64_t* raw_empty = raw_full + C::RS;
-  uint64_t* op_full = raw_empty + C::RS;
-  uint64_t* op_empty = op_full + C::OS;
-  uint64_t* acc_full = op_empty + C::OS;
+  uint64_t* op_full = raw_empty + C::RS;   // dequantised A stage written to TMEM (8 dequant warps)
+  uint64_t* op_empty = op_full + C::OS;     // A stage consumed (MMA commit)
+  uint64_t* b_full = op_empty + C::OS;      // activation tile landed (TMA)
+  uint64_t* b_empty = b_full + C::BS;       // activation tile consumed (MMA commit)
+  uint64_t* acc_full = b_empty + C::BS;
   uint64_t* acc_empty = acc_full + C::AB;
   uint64_t* fin_bar = acc_empty + C::AB;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin_bar + 1);
@@ -180,14 +199,18 @@ __global__ void __launch_bounds__(480, 1)
       mbar_init(&raw_empty[i], 8);
     }
     for (int i = 0; i < C::OS; ++i) {
-      mbar_init(&op_full[i], 1 + 8);
-      mbar_init(&op_empty[i], 1);
+      mbar_init(&op_full[i], 8);
+      mbar_init(&op_empty[i], C::ISSUERS);
+    }
+    for (int i = 0; i < C::BS; ++i) {
+      mbar_init(&b_full[i], 1);
+      mbar_init(&b_empty[i], C::ISSUERS);
     }
     for (int i = 0; i < C::AB; ++i) {
-      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_full[i], C::ISSUERS);
       mbar_init(&acc_empty[i], 4);
     }
-    mbar_init(fin_bar, 1);
+    mbar_init(fin_bar, C::ISSUERS);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -206,7 +229,9 @@ __global__ void __launch_bounds__(480, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const int n_out = args.n_out;
-  const int mt_per_expert = n_out / C::BM;
+  const int pair = NMAT == 2 ? args.pair : 0;
+  const int mrows = pair ? 2 * C::BM : C::BM;  // output rows per work item
+  const int mt_per_expert = n_out / mrows;
   const int ksteps = args.k_dim / C::BK;
   int ntiles = *args.num_tiles;
   if (ntiles > args.max_tiles) ntiles = args.max_tiles;
@@ -222,13 +247,15 @@ __global__ void __launch_bounds__(480, 1)
           atomicCAS(args.status, 0, (int)kDevBadIndex);
           continue;
         }
-        const int a_row = t.expert * n_out + (item % mt_per_expert) * C::BM;
+        const int a_row = t.expert * n_out + (item % mt_per_expert) * mrows;
         for (int ks = 0; ks < ksteps; ++ks, ++it) {
           const int s = it % C::RS;
           if (!mbar_wait(&raw_empty[s], ((it / C::RS) & 1) ^ 1, abort_flag, args.status)) break;
           mbar_arrive_expect_tx(&raw_full[s], C::RAW_STAGE);
           tma_load_2d(sRaw + s * C::RAW_STAGE, &tm_a0, &raw_full[s], ks * C::KW, a_row);
-          if (NMAT == 2) tma_load_2d(sRaw + s * C::RAW_STAGE + C::RAW_MAT, &tm_a1, &raw_full[s], ks * C::KW, a_row);
+          if (NMAT == 2)
+            tma_load_2d(sRaw + s * C::RAW_STAGE + C::RAW_MAT, &tm_a1, &raw_full[s], ks * C::KW,
+                        a_row + (pair ? C::BM : 0));
         }
       }
       drain_ring<C::RS>(raw_full, it, abort_flag, args.status);
@@ -241,16 +268,20 @@ __global__ void __launch_bounds__(480, 1)
         const GemmTile t = args.tiles[item / mt_per_expert];
         if (!tile_ok(t, args)) continue;
         for (int ks = 0; ks < ksteps; ++ks, ++it) {
-          const int s = it % C::OS;
-          if (!mbar_wait(&op_empty[s], ((it / C::OS) & 1) ^ 1, abort_flag, args.status)) break;
-          mbar_arrive_expect_tx(&op_full[s], C::B_STAGE);
-          tma_load_2d(sB + s * C::B_STAGE, &tm_b, &op_full[s], ks * C::BK, t.row_start);
+          const int s = it % C::BS;
+          if (!mbar_wait(&b_empty[s], ((it / C::BS) & 1) ^ 1, abort_flag, args.status)) break;
+          mbar_arrive_expect_tx(&b_full[s], C::B_STAGE);
+          tma_load_2d(sB + s * C::B_STAGE, &tm_b, &b_full[s], ks * C::BK, t.row_start);
         }
       }
-      drain_ring<C::OS>(op_full, it, abort_flag, args.status);
+      drain_ring<C::BS>(b_full, it, abort_flag, args.status);
     }
-  } else if (warp == 14) {
-    // ----------------------------------------------------- MMA issuer ----
+  } else if (warp >= 14) {
+    // ---------------------------------------------------- MMA issuers ----
+    // Issuer mi issues the MMAs of matrix mi (gate / up) into its own
+    // accumulator; every stage and accumulator barrier expects one commit
+    // per issuer.
+    const int mi = warp - 14;
     if (lane == 0) {
       uint32_t it = 0, li = 0;
       bool ok = true;
@@ -264,23 +295,21 @@ __global__ void __launch_bounds__(480, 1)
         const uint32_t d0 = tmem_base + (uint32_t)(ab * C::ACC_COLS);
         for (int ks = 0; ks < ksteps; ++ks, ++it) {
           const int s = it % C::OS;
-          if (!mbar_wait(&op_full[s], (it / C::OS) & 1, abort_flag, args.status)) {
+          const int sb = it % C::BS;
+          if (!mbar_wait(&b_full[sb], (it / C::BS) & 1, abort_flag, args.status) ||
+              !mbar_wait(&op_full[s], (it / C::OS) & 1, abort_flag, args.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(sA + s * C::A_STAGE);
-          const uint32_t b_base = smem_u32(sB + s * C::B_STAGE);
+          const uint32_t a_tm = tmem_base + (uint32_t)(C::A_BASE + s * C::A_COLS);
+          const uint32_t b_base = smem_u32(sB + sb * C::B_STAGE);
 #pragma unroll
-          for (int kk = 0; kk < C::BK / 16; ++kk) {
-            const uint64_t bdesc = umma_desc_sw128(b_base + kk * 32);
-#pragma unroll
-            for (int m = 0; m < NMAT; ++m) {
-              const uint64_t adesc = umma_desc_sw128(a_base + m * C::A_MAT + kk * 32);
-              umma_bf16(d0 + (uint32_t)(m * BN), adesc, bdesc, C::IDESC, (ks | kk) != 0 ? 1u : 0u);
-            }
-          }
+          for (int kk = 0; kk < C::BK / 16; ++kk)
+            umma_bf16_ts(d0 + (uint32_t)(mi * BN), a_tm + (uint32_t)(mi * 32 + kk * 8), umma_desc_sw128(b_base + kk * 32),
+                         C::IDESC, (ks | kk) != 0 ? 1u : 0u);
           umma_commit(&op_empty[s]);
+          umma_commit(&b_empty[sb]);
         }
         if (ok) umma_commit(&acc_full[ab]);
       }
@@ -295,77 +324,106 @@ __global__ void __launch_bounds__(480, 1)
     const int row = dt & 127;
     const int c_lo = NMAT == 2 ? 0 : (dt >> 7) * 4;  // first 16 B chunk of this thread
     constexpr int NCH = NMAT == 2 ? 8 : 4;           // chunks per thread per k-step
-    const int G = args.k_dim / 64;
+    const int G = args.k_dim / 64;  // groups per row == k-steps; even (K is a multiple of 128)
+    const int G2 = G / 2;              // 32-bit words of bf16 scale pairs per row
     uint32_t rit = 0, oit = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
       const GemmTile t = args.tiles[item / mt_per_expert];
       if (!tile_ok(t, args)) continue;
-      const int64_t srow = (int64_t)t.expert * n_out + (item % mt_per_expert) * C::BM + row;
-      const uint16_t* sp = args.scales[mat] + srow * G;
-      const uint16_t* bp = args.biases[mat] + srow * G;
-      // Scale/bias prefetch ring (distance 2) held in registers.
-      uint16_t s0 = __ldg(sp), b0 = __ldg(bp);
-      uint16_t s1 = G > 1 ? __ldg(sp + 1) : 0, b1 = G > 1 ? __ldg(bp + 1) : 0;
-      for (int ks = 0; ks < ksteps; ++ks, ++rit, ++oit) {
-        uint16_t s2 = 0, b2v = 0;
-        if (ks + 2 < G) {
-          s2 = __ldg(sp + ks + 2);
-          b2v = __ldg(bp + ks + 2);
-        }
-        // Packed codes of this thread's slice.
-        const int rs = rit % C::RS;
-        if (!mbar_wait(&raw_full[rs], (rit / C::RS) & 1, abort_flag, args.status)) {
-          ok = false;
-          break;
-        }
-        uint32_t wv[NCH * BITS / 4];
-        {
-          const uint4* src = reinterpret_cast<const uint4*>(sRaw + rs * C::RAW_STAGE + mat * C::RAW_MAT +
-                                                            row * C::RAW_ROW + c_lo * BITS);
+      const int64_t srow = (int64_t)t.expert * n_out + (item % mt_per_expert) * mrows + (pair ? mat * C::BM : 0) + row;
+      // Scales and biases of this row, 8 groups (= 8 k-steps) per chunk,
+      // fetched with 4-byte loads two chunks ahead of their use.
+      const uint32_t* sp = reinterpret_cast<const uint32_t*>(args.scales[mat] + srow * G);
+      const uint32_t* bp = reinterpret_cast<const uint32_t*>(args.biases[mat] + srow * G);
+      uint32_t sc[4], bc[4], sn[4], bn[4];
 #pragma unroll
-          for (int i = 0; i < NCH * BITS / 16; ++i) {
-            const uint4 v = src[i];
-            wv[4 * i + 0] = v.x;
-            wv[4 * i + 1] = v.y;
-            wv[4 * i + 2] = v.z;
-            wv[4 * i + 3] = v.w;
-          }
-        }
-#if MLXR_RAW_WAR_FENCE
-        // The slot is refilled by TMA (async proxy) once all warps release it:
-        // order this warp's generic-proxy reads before that write.
-        fence_proxy_async_smem();
-#endif
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&raw_empty[rs]);
-        const int os = oit % C::OS;
-        if (!mbar_wait(&op_empty[os], ((oit / C::OS) & 1) ^ 1, abort_flag, args.status)) {
-          ok = false;
-          break;
-        }
-        uint8_t* dstA = sA + os * C::A_STAGE + mat * C::A_MAT;
-        if (BITS == 4) {
-          const __nv_bfloat162 s2v = __halves2bfloat162(__ushort_as_bfloat16(s0), __ushort_as_bfloat16(s0));
-          const __nv_bfloat162 b2 = __halves2bfloat162(__ushort_as_bfloat16(b0), __ushort_as_bfloat16(b0));
+      for (int w = 0; w < 4; ++w) {
+        sc[w] = w < G2 ? __ldg(sp + w) : 0u;
+        bc[w] = w < G2 ? __ldg(bp + w) : 0u;
+        sn[w] = 4 + w < G2 ? __ldg(sp + 4 + w) : 0u;
+        bn[w] = 4 + w < G2 ? __ldg(bp + 4 + w) : 0u;
+      }
+      for (int k8 = 0; k8 < ksteps && ok; k8 += 8) {
+        uint32_t sf[4], bf[4];
+        const int wf = (k8 >> 1) + 8;  // first word of the chunk after next
 #pragma unroll
-          for (int c = 0; c < NCH; ++c) {
-            const uint4 o = dequant_word4(wv[c], s2v, b2);
-            *reinterpret_cast<uint4*>(dstA + sw128_offset(row, c_lo + c)) = o;
-          }
-        } else {
-          const float sf = bf16_bits_to_f32(s0), bf = bf16_bits_to_f32(b0);
-#pragma unroll
-          for (int c = 0; c < NCH; ++c) {
-            const uint4 o = dequant_words8(wv[2 * c], wv[2 * c + 1], sf, bf);
-            *reinterpret_cast<uint4*>(dstA + sw128_offset(row, c_lo + c)) = o;
-          }
+        for (int w = 0; w < 4; ++w) {
+          sf[w] = wf + w < G2 ? __ldg(sp + wf + w) : 0u;
+          bf[w] = wf + w < G2 ? __ldg(bp + wf + w) : 0u;
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&op_full[os]);
-        s0 = s1; b0 = b1;
-        s1 = s2; b1 = b2v;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (k8 + j >= ksteps) break;
+          const uint16_t s16 = (j & 1) ? (uint16_t)(sc[j >> 1] >> 16) : (uint16_t)(sc[j >> 1] & 0xFFFFu);
+          const uint16_t b16 = (j & 1) ? (uint16_t)(bc[j >> 1] >> 16) : (uint16_t)(bc[j >> 1] & 0xFFFFu);
+          // Packed codes of this thread's slice.
+          const int rs = rit % C::RS;
+          if (!mbar_wait(&raw_full[rs], (rit / C::RS) & 1, abort_flag, args.status)) {
+            ok = false;
+            break;
+          }
+          uint32_t wv[NCH * BITS / 4];
+          {
+            const uint4* src = reinterpret_cast<const uint4*>(sRaw + rs * C::RAW_STAGE + mat * C::RAW_MAT +
+                                                              row * C::RAW_ROW + c_lo * BITS);
+#pragma unroll
+            for (int i = 0; i < NCH * BITS / 16; ++i) {
+              const uint4 v = src[i];
+              wv[4 * i + 0] = v.x;
+              wv[4 * i + 1] = v.y;
+              wv[4 * i + 2] = v.z;
+              wv[4 * i + 3] = v.w;
+            }
+          }
+          const int os = oit % C::OS;
+          if (!mbar_wait(&op_empty[os], ((oit / C::OS) & 1) ^ 1, abort_flag, args.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint32_t av[32];  // this thread's slice of the A row, bf16 pairs
+          if (BITS == 4) {
+            const __nv_bfloat162 s2v = __halves2bfloat162(__ushort_as_bfloat16(s16), __ushort_as_bfloat16(s16));
+            const __nv_bfloat162 b2 = __halves2bfloat162(__ushort_as_bfloat16(b16), __ushort_as_bfloat16(b16));
+#pragma unroll
+            for (int c = 0; c < NCH; ++c) dequant_word4(wv[c], s2v, b2, &av[4 * c]);
+          } else {
+            const float sfv = bf16_bits_to_f32(s16), bfv = bf16_bits_to_f32(b16);
+#pragma unroll
+            for (int c = 0; c < NCH; ++c) {
+              const uint4 o = dequant_words8(wv[2 * c], wv[2 * c + 1], sfv, bfv);
+              av[4 * c + 0] = o.x;
+              av[4 * c + 1] = o.y;
+              av[4 * c + 2] = o.z;
+              av[4 * c + 3] = o.w;
+            }
+          }
+          // TMEM lane = this thread's weight row; 4 columns per 16-byte chunk.
+          const uint32_t ta = tmem_base + ((uint32_t)((warp & 3) * 32) << 16) +
+                              (uint32_t)(C::A_BASE + os * C::A_COLS + mat * 32 + c_lo * 4);
+          if (NCH == 8) tmem_st_x32(ta, av);
+          else tmem_st_x16(ta, av);
+          tmem_st_wait();
+          // The raw slot is refilled by TMA (async proxy) once all warps
+          // release it: order this warp's generic reads of it before that.
+          fence_proxy_async_smem();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&raw_empty[rs]);
+            mbar_arrive(&op_full[os]);
+          }
+          ++rit;
+          ++oit;
+        }
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          sc[w] = sn[w];
+          bc[w] = bn[w];
+          sn[w] = sf[w];
+          bn[w] = bf[w];
+        }
       }
     }
   } else {
@@ -380,7 +438,9 @@ __global__ void __launch_bounds__(480, 1)
       ++li;
       if (!mbar_wait(&acc_full[ab], acc_phase, abort_flag, args.status)) break;
       tc_fence_after();
-      const int f = (item % mt_per_expert) * C::BM + q * 32 + lane;
+      const int fn = (item % mt_per_expert) * mrows + q * 32 + lane;
+      const int f = args.perm_out ? ((fn & ~7) | kperm_pos(fn & 7)) : fn;
+      uint16_t* outp2 = args.out + (int64_t)t.row_start * n_out + fn + C::BM;  // pair mode: second row block
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * C::ACC_COLS);
       uint16_t* outp = args.out + (int64_t)t.row_start * n_out + f;
       const int rows = t.row_count < BN ? t.row_count : BN;
@@ -398,12 +458,22 @@ __global__ void __launch_bounds__(480, 1)
           else tmem_ld_x16_wait(tbase, g);
         }
         const int nvalid = rows - c * CW < CW ? rows - c * CW : CW;
+        if (NMAT == 2 && pair) {
 #pragma unroll
-        for (int j = 0; j < CW; ++j) {
-          if (j < nvalid) {
-            float v = __uint_as_float(g[j]);
-            if (NMAT == 2) v = silu_f32(v) * __uint_as_float(u[j]);
-            outp[(int64_t)(c * CW + j) * n_out] = f32_to_bf16_bits(v);
+          for (int j = 0; j < CW; ++j) {
+            if (j < nvalid) {
+              outp[(int64_t)(c * CW + j) * n_out] = f32_to_bf16_bits(__uint_as_float(g[j]));
+              outp2[(int64_t)(c * CW + j) * n_out] = f32_to_bf16_bits(__uint_as_float(u[j]));
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < CW; ++j) {
+            if (j < nvalid) {
+              float v = __uint_as_float(g[j]);
+              if (NMAT == 2) v = silu_f32(v) * __uint_as_float(u[j]);
+              outp[(int64_t)(c * CW + j) * n_out] = f32_to_bf16_bits(v);
+            }
           }
         }
       }

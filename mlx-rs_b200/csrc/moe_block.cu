@@ -101,9 +101,9 @@ static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T) {
   L.nblk = (int)((L.R + PERM_ROWS - 1) / PERM_ROWS);
   if (L.nblk < 1) L.nblk = 1;
   const double avg = L.E > 0 ? (double)L.R / L.E : 0.0;
-  L.bn1 = pick_bn(avg, 128);
-  L.bn2 = pick_bn(avg, 256);
-  L.bns = pick_bn((double)T, 128);
+  L.bn1 = pick_bn(avg, 64);
+  L.bn2 = pick_bn(avg, (L.D % 256 == 0) ? 128 : 256);
+  L.bns = pick_bn((double)T, 64);
   L.max_t1 = (int)(L.E + (L.R + L.bn1 - 1) / L.bn1 + 1);
   L.max_t2 = (int)(L.E + (L.R + L.bn2 - 1) / L.bn2 + 1);
   L.max_tsh = (int)((T + L.bns - 1) / L.bns + 1);
@@ -134,7 +134,7 @@ static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T) {
   L.h = take((size_t)L.rows_pad * L.I * 2);
   L.y = take((size_t)L.R * L.D * 2);
   if (L.Is > 0) {
-    L.xpad = take(T < 256 ? (size_t)256 * L.D * 2 : 0);
+    L.xpad = take((T < 256 || c->shared_bits == 4) ? (size_t)L.sh_rows_pad * L.D * 2 : 0);
     L.hsh = take((size_t)L.sh_rows_pad * L.Is * 2);
     L.ysh = take((size_t)T * L.D * 2);
   }
@@ -187,7 +187,7 @@ static int run_router(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
 }
 
 static int run_permute(const Layout& L, const int32_t* idx, const void* x, void* ws, int32_t* counts, int32_t* offsets,
-                       int32_t* sorted, int32_t* inv, uint16_t* xs, cudaStream_t st) {
+                       int32_t* sorted, int32_t* inv, uint16_t* xs, int kperm, cudaStream_t st) {
   int* status = at<int>(ws, L.status);
   if (L.R > 0) {
     permute_count_kernel<<<L.nblk, 256, L.E * sizeof(int), st>>>(idx, L.R, L.E, at<int32_t>(ws, L.bcounts), status);
@@ -202,10 +202,14 @@ static int run_permute(const Layout& L, const int32_t* idx, const void* x, void*
                                           offsets, l1, l2, lsh);
   MLXR_LAUNCH_CHECK("permute_scan_kernel");
   if (L.R > 0) {
-    permute_scatter_kernel<<<L.nblk, 256, 8 * L.E * sizeof(int), st>>>(idx, L.R, L.K, L.E, at<int32_t>(ws, L.bbase),
-                                                                       static_cast<const uint16_t*>(x), L.D, sorted,
-                                                                       inv, xs);
+    permute_scatter_kernel<<<L.nblk, 256, 8 * L.E * sizeof(int), st>>>(idx, L.R, L.E, at<int32_t>(ws, L.bbase),
+                                                                       sorted, inv);
     MLXR_LAUNCH_CHECK("permute_scatter_kernel");
+    const int64_t gblocks = (L.R + 7) / 8;
+    const int gather_grid = (int)(gblocks < 4 * 148 ? gblocks : 4 * 148);
+    permute_gather_kernel<<<gather_grid, 256, 0, st>>>(sorted, L.R, L.K, static_cast<const uint16_t*>(x), L.D, kperm,
+                                                       xs);
+    MLXR_LAUNCH_CHECK("permute_gather_kernel");
   }
   return MLXR_CU_OK;
 }
@@ -213,6 +217,8 @@ static int run_permute(const Layout& L, const int32_t* idx, const void* x, void*
 static int check_qlinear(const mlxr_cu_qlinear& q, const char* name) {
   MLXR_CHECK_ARG(q.weight && q.scales && q.biases, "moe: %s weight/scales/biases must be non-NULL", name);
   MLXR_CHECK_ARG(aligned16(q.weight), "moe: %s weight must be 16-byte aligned", name);
+  MLXR_CHECK_ARG((reinterpret_cast<uintptr_t>(q.scales) & 3) == 0 && (reinterpret_cast<uintptr_t>(q.biases) & 3) == 0,
+                 "moe: %s scales/biases must be 4-byte aligned", name);
   return MLXR_CU_OK;
 }
 
@@ -244,13 +250,17 @@ static int run_experts(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* w
   p.max_tiles = L.max_t1;
   p.out = at<uint16_t>(ws, L.h);
   p.out_rows = L.R;
+  p.perm_out = c->bits == 4;  // h is the 4-bit down projection's activation operand
   p.status = status;
   if (int rc = launch_grouped_gemm(p, st)) return rc;
   stage_mark(mid_stage, st);
 
   GroupedGemmProblem q{};
-  q.nmat = 1;
-  q.bn = L.bn2;
+  // Two 128-row blocks of the down weight per work item (two accumulators,
+  // two MMA issuers) when D allows it.
+  q.pair = (L.D % 256 == 0) ? 1 : 0;
+  q.nmat = q.pair ? 2 : 1;
+  q.bn = q.pair ? (L.bn2 < 128 ? L.bn2 : 128) : L.bn2;
   q.bits = c->bits;
   q.w[0] = q.w[1] = wt->switch_down.weight;
   q.s[0] = q.s[1] = static_cast<const uint16_t*>(wt->switch_down.scales);
@@ -266,6 +276,7 @@ static int run_experts(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* w
   q.max_tiles = L.max_t2;
   q.out = at<uint16_t>(ws, L.y);
   q.out_rows = L.R;
+  q.perm_out = 0;
   q.status = status;
   return launch_grouped_gemm(q, st);
 }
@@ -279,10 +290,16 @@ static int run_shared(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
   int* status = at<int>(ws, L.status);
   const uint16_t* act = static_cast<const uint16_t*>(x);
   int64_t act_rows = L.T;
-  if (L.T < 256) {
-    MLXR_CUDA_TRY(cudaMemcpyAsync(at<uint16_t>(ws, L.xpad), x, (size_t)L.T * L.D * 2, cudaMemcpyDeviceToDevice, st));
+  const int kperm = c->shared_bits == 4;
+  if (L.T < 256 || kperm) {
+    // A padded (>= 256 rows) and, for 4-bit weights, K-order-permuted copy.
+    const int64_t gblocks = (L.T + 7) / 8;
+    const int grid = (int)(gblocks < 4 * 148 ? gblocks : 4 * 148);
+    permute_gather_kernel<<<grid, 256, 0, st>>>(nullptr, L.T, 1, static_cast<const uint16_t*>(x), L.D, kperm,
+                                                at<uint16_t>(ws, L.xpad));
+    MLXR_LAUNCH_CHECK("permute_gather_kernel(shared)");
     act = at<uint16_t>(ws, L.xpad);
-    act_rows = 256;
+    act_rows = L.sh_rows_pad;
   }
   GroupedGemmProblem p{};
   p.nmat = 2;
@@ -305,10 +322,12 @@ static int run_shared(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
   p.max_tiles = L.max_tsh;
   p.out = at<uint16_t>(ws, L.hsh);
   p.out_rows = L.T;
+  p.perm_out = c->shared_bits == 4;
   p.status = status;
   if (int rc = launch_grouped_gemm(p, st)) return rc;
   GroupedGemmProblem q{};
-  q.nmat = 1;
+  q.pair = (L.D % 256 == 0) ? 1 : 0;
+  q.nmat = q.pair ? 2 : 1;
   q.bn = L.bns;
   q.bits = c->shared_bits;
   q.w[0] = q.w[1] = wt->shared_down.weight;
@@ -325,6 +344,7 @@ static int run_shared(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
   q.max_tiles = L.max_tsh;
   q.out = at<uint16_t>(ws, L.ysh);
   q.out_rows = L.T;
+  q.perm_out = 0;
   q.status = status;
   return launch_grouped_gemm(q, st);
 }
@@ -359,7 +379,7 @@ int mlxr_cu_moe_block_forward(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_w
   if (int rc = run_router(cfg, weights, L, x, ws, at<uint16_t>(ws, L.logits), nullptr, st)) return rc;
   stage_mark(1, st);
   if (int rc = run_permute(L, at<int32_t>(ws, L.idx), x, ws, at<int32_t>(ws, L.counts), at<int32_t>(ws, L.offsets),
-                           at<int32_t>(ws, L.sorted), at<int32_t>(ws, L.inv), at<uint16_t>(ws, L.xs), st))
+                           at<int32_t>(ws, L.sorted), at<int32_t>(ws, L.inv), at<uint16_t>(ws, L.xs), cfg->bits == 4, st))
     return rc;
   stage_mark(2, st);
   if (int rc = run_experts(cfg, weights, L, ws, st, 3)) return rc;
@@ -519,7 +539,8 @@ int mlxr_cu_moe_permute(const mlxr_cu_moe_config* cfg, const int32_t* indices, i
   MLXR_CHECK_ARG(aligned16(x) && aligned16(x_sorted), "moe_permute: x and x_sorted must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   MLXR_CUDA_TRY(cudaMemsetAsync(at<int>(workspace, L.status), 0, sizeof(int), st));
-  return run_permute(L, indices, x, workspace, counts, offsets, sorted_rows, inverse, static_cast<uint16_t*>(x_sorted), st);
+  return run_permute(L, indices, x, workspace, counts, offsets, sorted_rows, inverse, static_cast<uint16_t*>(x_sorted),
+                     0, st);
 }
 
 }  // extern "C"

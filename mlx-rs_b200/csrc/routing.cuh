@@ -330,14 +330,12 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(const int32_t* __res
   }
 }
 
-// Stable in-block ranks and the row gather. 8 warps; warp w owns flat rows
+// Stable in-block ranks. 8 warps; warp w owns flat rows
 // [blk*2048 + w*256, +256).
-__global__ void __launch_bounds__(256) permute_scatter_kernel(const int32_t* __restrict__ idx, int64_t R, int K,
-                                                             int E, const int32_t* __restrict__ block_base,
-                                                             const uint16_t* __restrict__ x, int D,
+__global__ void __launch_bounds__(256) permute_scatter_kernel(const int32_t* __restrict__ idx, int64_t R, int E,
+                                                             const int32_t* __restrict__ block_base,
                                                              int32_t* __restrict__ sorted_rows,
-                                                             int32_t* __restrict__ inv,
-                                                             uint16_t* __restrict__ x_sorted) {
+                                                             int32_t* __restrict__ inv) {
   extern __shared__ int wcnt[];  // [8][E]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < 8 * E; i += blockDim.x) wcnt[i] = 0;
@@ -359,7 +357,6 @@ __global__ void __launch_bounds__(256) permute_scatter_kernel(const int32_t* __r
   }
   __syncthreads();
   const uint32_t lt_mask = (1u << lane) - 1u;
-  const int dvec = D / 8;
   for (int64_t c0 = wbeg; c0 < wend; c0 += 32) {
     const int64_t f = c0 + lane;
     int e = -1;
@@ -378,13 +375,38 @@ __global__ void __launch_bounds__(256) permute_scatter_kernel(const int32_t* __r
       sorted_rows[pos] = (int32_t)f;
       inv[f] = pos;
     }
-    for (int j = 0; j < 32; ++j) {
-      const int pj = __shfl_sync(0xffffffffu, pos, j);
-      const int64_t fj = __shfl_sync(0xffffffffu, f, j);
-      if (pj < 0) continue;
-      const uint4* src = reinterpret_cast<const uint4*>(x + (fj / K) * D);
-      uint4* dst = reinterpret_cast<uint4*>(x_sorted + (int64_t)pj * D);
-      for (int v = lane; v < dvec; v += 32) dst[v] = __ldg(src + v);
+  }
+}
+
+// x_sorted[pos] = x[sorted_rows[pos] / K] (sorted_rows NULL: the identity),
+// one warp per row, 16-byte loads and stores, the whole grid streaming. With
+// kperm the 8 elements of every 16-byte chunk are stored in the 4-bit
+// operand order {0,4,1,5,2,6,3,7} the grouped GEMM's dequantiser produces.
+__global__ void __launch_bounds__(256) permute_gather_kernel(const int32_t* __restrict__ sorted_rows, int64_t R, int K,
+                                                            const uint16_t* __restrict__ x, int D, int kperm,
+                                                            uint16_t* __restrict__ x_sorted) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int dvec = D / 8;
+  for (int64_t pos = (int64_t)blockIdx.x * 8 + warp; pos < R; pos += (int64_t)gridDim.x * 8) {
+    int64_t src_row = pos;
+    if (sorted_rows) {
+      const int32_t f = sorted_rows[pos];
+      if (f < 0 || (int64_t)f >= R) continue;
+      src_row = f / K;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(x + src_row * D);
+    uint4* dst = reinterpret_cast<uint4*>(x_sorted + pos * D);
+    for (int v = lane; v < dvec; v += 32) {
+      uint4 a = __ldg(src + v);
+      if (kperm) {
+        uint4 b;
+        b.x = __byte_perm(a.x, a.z, 0x5410);
+        b.y = __byte_perm(a.x, a.z, 0x7632);
+        b.z = __byte_perm(a.y, a.w, 0x5410);
+        b.w = __byte_perm(a.y, a.w, 0x7632);
+        a = b;
+      }
+      dst[v] = a;
     }
   }
 }
