@@ -138,7 +138,7 @@ def smi_id(torch, dev) -> str:
 
 def kernels_per_forward(cfg) -> int:
     # router (logits, top-k) + permute (count, scan, scatter, gather) + gate/up + down + combine
-    n = 2 + 4 + 2 + 1
+    n = 1 + 2 + 2 + 1  # router, permute (small path: ranks + gather), gate|up, down, combine
     if cfg.shared_expert_intermediate_size:
         n += 2
     return n

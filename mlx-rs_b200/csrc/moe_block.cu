@@ -101,7 +101,7 @@ static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T) {
   L.nblk = (int)((L.R + PERM_ROWS - 1) / PERM_ROWS);
   if (L.nblk < 1) L.nblk = 1;
   const double avg = L.E > 0 ? (double)L.R / L.E : 0.0;
-  L.bn1 = pick_bn(avg, 64);
+  L.bn1 = pick_bn(avg, 128);
   L.bn2 = pick_bn(avg, (L.D % 256 == 0) ? 128 : 256);
   L.bns = pick_bn((double)T, 64);
   L.max_t1 = (int)(L.E + (L.R + L.bn1 - 1) / L.bn1 + 1);
@@ -163,11 +163,6 @@ static int run_router(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
   if (L.T == 0) return MLXR_CU_OK;
   MLXR_CHECK_ARG(wt && wt->router_weight, "moe: router weight is NULL");
   MLXR_CHECK_ARG(aligned16(x) && aligned16(wt->router_weight), "moe: x and the router weight must be 16-byte aligned");
-  dim3 g1((unsigned)((L.E + 63) / 64), (unsigned)((L.T + RT_TOK - 1) / RT_TOK));
-  MLXR_CHECK_ARG(g1.y <= 65535u, "moe: too many tokens for the router grid (%lld)", (long long)L.T);
-  router_logits_kernel<<<g1, 256, 0, st>>>(static_cast<const uint16_t*>(x), L.T, L.D,
-                                           static_cast<const uint16_t*>(wt->router_weight), L.E, wt->router_bias, logits);
-  MLXR_LAUNCH_CHECK("router_logits_kernel");
   SharedGateArgs sg{nullptr, nullptr, nullptr, 8};
   float* sig = nullptr;
   if (L.Is > 0) {
@@ -179,32 +174,45 @@ static int run_router(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
     sg.bits = c->shared_bits;
     sig = at<float>(ws, L.sig);
   }
-  router_topk_kernel<<<(unsigned)((L.T + 7) / 8), 256, 0, st>>>(
-      logits, L.T, L.E, L.K, c->norm_topk_prob, at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w), probs,
-      static_cast<const uint16_t*>(x), L.D, sg, sig);
-  MLXR_LAUNCH_CHECK("router_topk_kernel");
+  const uint16_t* xp = static_cast<const uint16_t*>(x);
+  const uint16_t* wg = static_cast<const uint16_t*>(wt->router_weight);
+  // One token per CTA for small batches (latency), four for large ones
+  // (fewer re-reads of the router weight).
+  if (L.T <= 256) {
+    router_fused_kernel<1><<<(unsigned)L.T, RT_THREADS, L.E * sizeof(float), st>>>(
+        xp, L.T, L.D, wg, L.E, wt->router_bias, L.K, c->norm_topk_prob, at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w),
+        logits, probs, sg, sig);
+  } else {
+    router_fused_kernel<4><<<(unsigned)((L.T + 3) / 4), RT_THREADS, 4 * L.E * sizeof(float), st>>>(
+        xp, L.T, L.D, wg, L.E, wt->router_bias, L.K, c->norm_topk_prob, at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w),
+        logits, probs, sg, sig);
+  }
+  MLXR_LAUNCH_CHECK("router_fused_kernel");
   return MLXR_CU_OK;
 }
 
 static int run_permute(const Layout& L, const int32_t* idx, const void* x, void* ws, int32_t* counts, int32_t* offsets,
                        int32_t* sorted, int32_t* inv, uint16_t* xs, int kperm, cudaStream_t st) {
   int* status = at<int>(ws, L.status);
-  if (L.R > 0) {
-    permute_count_kernel<<<L.nblk, 256, L.E * sizeof(int), st>>>(idx, L.R, L.E, at<int32_t>(ws, L.bcounts), status);
-    MLXR_LAUNCH_CHECK("permute_count_kernel");
-  } else {
-    MLXR_CUDA_TRY(cudaMemsetAsync(at<int32_t>(ws, L.bcounts), 0, (size_t)L.nblk * L.E * 4, st));
-  }
   TileListOut l1{at<GemmTile>(ws, L.t1), at<int32_t>(ws, L.n1), L.bn1};
   TileListOut l2{at<GemmTile>(ws, L.t2), at<int32_t>(ws, L.n2), L.bn2};
   TileListOut lsh{L.Is > 0 ? at<GemmTile>(ws, L.tsh) : nullptr, at<int32_t>(ws, L.nsh), L.bns};
-  permute_scan_kernel<<<1, 1024, 0, st>>>(at<int32_t>(ws, L.bcounts), L.nblk, L.E, L.T, at<int32_t>(ws, L.bbase), counts,
-                                          offsets, l1, l2, lsh);
-  MLXR_LAUNCH_CHECK("permute_scan_kernel");
-  if (L.R > 0) {
+  if (L.nblk == 1) {
+    // Every flat row fits one block: count, scan, tile lists and ranks in one CTA.
+    permute_small_kernel<<<1, 1024, 9 * L.E * sizeof(int), st>>>(idx, L.R, L.E, L.T, counts, offsets, sorted, inv, l1,
+                                                                  l2, lsh, status);
+    MLXR_LAUNCH_CHECK("permute_small_kernel");
+  } else {
+    permute_count_kernel<<<L.nblk, 256, L.E * sizeof(int), st>>>(idx, L.R, L.E, at<int32_t>(ws, L.bcounts), status);
+    MLXR_LAUNCH_CHECK("permute_count_kernel");
+    permute_scan_kernel<<<1, 1024, 0, st>>>(at<int32_t>(ws, L.bcounts), L.nblk, L.E, L.T, at<int32_t>(ws, L.bbase),
+                                            counts, offsets, l1, l2, lsh);
+    MLXR_LAUNCH_CHECK("permute_scan_kernel");
     permute_scatter_kernel<<<L.nblk, 256, 8 * L.E * sizeof(int), st>>>(idx, L.R, L.E, at<int32_t>(ws, L.bbase),
                                                                        sorted, inv);
     MLXR_LAUNCH_CHECK("permute_scatter_kernel");
+  }
+  if (L.R > 0) {
     const int64_t gblocks = (L.R + 7) / 8;
     const int gather_grid = (int)(gblocks < 4 * 148 ? gblocks : 4 * 148);
     permute_gather_kernel<<<gather_grid, 256, 0, st>>>(sorted, L.R, L.K, static_cast<const uint16_t*>(x), L.D, kperm,
@@ -376,7 +384,7 @@ int mlxr_cu_moe_block_forward(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_w
   MLXR_CHECK_ARG(aligned16(x) && aligned16(out), "moe: x and out must be 16-byte aligned");
   void* ws = workspace;
   stage_mark(0, st);
-  if (int rc = run_router(cfg, weights, L, x, ws, at<uint16_t>(ws, L.logits), nullptr, st)) return rc;
+  if (int rc = run_router(cfg, weights, L, x, ws, nullptr, nullptr, st)) return rc;
   stage_mark(1, st);
   if (int rc = run_permute(L, at<int32_t>(ws, L.idx), x, ws, at<int32_t>(ws, L.counts), at<int32_t>(ws, L.offsets),
                            at<int32_t>(ws, L.sorted), at<int32_t>(ws, L.inv), at<uint16_t>(ws, L.xs), cfg->bits == 4, st))
@@ -386,7 +394,7 @@ int mlxr_cu_moe_block_forward(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_w
   stage_mark(4, st);
   if (int rc = run_shared(cfg, weights, L, x, ws, st)) return rc;
   stage_mark(5, st);
-  combine_kernel<<<(unsigned)L.T, 128, 0, st>>>(at<uint16_t>(ws, L.y), at<int32_t>(ws, L.inv), at<uint16_t>(ws, L.w),
+  combine_kernel<<<(unsigned)L.T, L.D >= 2048 ? 256 : 128, 0, st>>>(at<uint16_t>(ws, L.y), at<int32_t>(ws, L.inv), at<uint16_t>(ws, L.w),
                                                 L.K, L.D, L.T, L.Is > 0 ? at<uint16_t>(ws, L.ysh) : nullptr,
                                                 at<float>(ws, L.sig), static_cast<uint16_t*>(out),
                                                 at<int>(ws, L.status));

@@ -17,8 +17,8 @@
 // Permutation (gather_sort / scatter_unsort, crates/mlxr-lm/src/nn/switch.rs:
 // 499-517): the flat rows f = t*K + k are stably sorted by expert (a counting
 // sort: per-block histograms, one scan, stable in-block ranks by
-// __match_any_sync); the expert-sorted copy of x is gathered in the same pass
-// with 16-byte loads.
+// __match_any_sync; one CTA does all of it when the rows fit one block); a
+// wide gather then builds the expert-sorted copy of x with 16-byte loads.
 // Combine (combine_with_weights, switch.rs:223-234, plus the shared branch
 // and final add, moe.rs:118-120,145): out[t] = sum_k w[t,k] * y[inv[t*K+k]]
 // (+ sigmoid(x . g_s) * shared(x)), fp32 accumulation, one bf16 rounding.
@@ -56,76 +56,7 @@ __device__ inline float exp_route(float x) {
 __device__ inline float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ inline float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
-// --------------------------------------------------------- logits -------
-// A warp computes RT_TOK tokens x RT_EXP experts; a CTA of 8 warps covers
-// RT_TOK tokens x 64 experts.
-constexpr int RT_TOK = 4, RT_EXP = 8;
-
-__global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __restrict__ x, int64_t T, int D,
-                                                           const uint16_t* __restrict__ wg, int E,
-                                                           const float* __restrict__ bias,
-                                                           uint16_t* __restrict__ logits) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t t0 = (int64_t)blockIdx.y * RT_TOK;
-  const int e0 = (blockIdx.x * 8 + warp) * RT_EXP;
-  if (e0 >= E) return;
-  float acc[RT_TOK][RT_EXP];
-#pragma unroll
-  for (int i = 0; i < RT_TOK; ++i)
-#pragma unroll
-    for (int j = 0; j < RT_EXP; ++j) acc[i][j] = 0.0f;
-  const uint4* xr[RT_TOK];
-  const uint4* wr[RT_EXP];
-#pragma unroll
-  for (int i = 0; i < RT_TOK; ++i) xr[i] = reinterpret_cast<const uint4*>(x + (t0 + i < T ? t0 + i : T - 1) * D);
-#pragma unroll
-  for (int j = 0; j < RT_EXP; ++j) wr[j] = reinterpret_cast<const uint4*>(wg + (int64_t)(e0 + j < E ? e0 + j : E - 1) * D);
-  const int nchunks = D / 8;
-  for (int c = lane; c < nchunks; c += 32) {
-    uint4 xv[RT_TOK], wv[RT_EXP];
-#pragma unroll
-    for (int i = 0; i < RT_TOK; ++i) xv[i] = __ldg(xr[i] + c);
-#pragma unroll
-    for (int j = 0; j < RT_EXP; ++j) wv[j] = __ldg(wr[j] + c);
-#pragma unroll
-    for (int el = 0; el < 8; ++el) {
-      float xf[RT_TOK], wf[RT_EXP];
-#pragma unroll
-      for (int i = 0; i < RT_TOK; ++i) {
-        const uint32_t wd = el < 2 ? xv[i].x : el < 4 ? xv[i].y : el < 6 ? xv[i].z : xv[i].w;
-        xf[i] = (el & 1) ? bf_hi(wd) : bf_lo(wd);
-      }
-#pragma unroll
-      for (int j = 0; j < RT_EXP; ++j) {
-        const uint32_t wd = el < 2 ? wv[j].x : el < 4 ? wv[j].y : el < 6 ? wv[j].z : wv[j].w;
-        wf[j] = (el & 1) ? bf_hi(wd) : bf_lo(wd);
-      }
-#pragma unroll
-      for (int i = 0; i < RT_TOK; ++i)
-#pragma unroll
-        for (int j = 0; j < RT_EXP; ++j) acc[i][j] = __fmaf_rn(xf[i], wf[j], acc[i][j]);
-    }
-  }
-  float mine = 0.0f;
-#pragma unroll
-  for (int i = 0; i < RT_TOK; ++i)
-#pragma unroll
-    for (int j = 0; j < RT_EXP; ++j) {
-      float v = acc[i][j];
-#pragma unroll
-      for (int s = 16; s >= 1; s >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, s));
-      if (lane == i * RT_EXP + j) mine = v;
-    }
-  const int i = lane / RT_EXP, j = lane % RT_EXP;
-  const int64_t t = t0 + i;
-  const int e = e0 + j;
-  if (t < T && e < E) {
-    const float b = bias ? bias[e] : 0.0f;
-    logits[t * E + e] = f32_to_bf16_bits(__fadd_rn(mine, b));
-  }
-}
-
-// ------------------------------------------------ softmax + top-K -------
+// ------------------------------------------------------------ router ---
 constexpr int RT_MAXV = 32;  // E <= 1024
 constexpr int RT_MAXK = 32;
 
@@ -136,22 +67,17 @@ struct SharedGateArgs {
   int bits;
 };
 
-// One warp per token.
-__global__ void __launch_bounds__(256) router_topk_kernel(const uint16_t* __restrict__ logits, int64_t T, int E,
-                                                         int K, int renorm, int32_t* __restrict__ idx_out,
-                                                         uint16_t* __restrict__ w_out, uint16_t* __restrict__ probs_out,
-                                                         const uint16_t* __restrict__ x, int D, SharedGateArgs sg,
-                                                         float* __restrict__ sig_out) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t t = (int64_t)blockIdx.x * 8 + warp;
-  if (t >= T) return;
-  const uint16_t* lrow = logits + t * E;
+// Softmax + top-K + renormalisation of one token by one warp, from its bf16
+// logits held as floats in shared memory (lrow[0..E)).
+__device__ inline void route_token_warp(const float* lrow, int64_t t, int E, int K, int renorm, int lane,
+                                        int32_t* __restrict__ idx_out, uint16_t* __restrict__ w_out,
+                                        uint16_t* __restrict__ probs_out) {
   float lv[RT_MAXV];
   float mx = -INFINITY;
 #pragma unroll
   for (int m = 0; m < RT_MAXV; ++m) {
     const int e = lane + 32 * m;
-    lv[m] = e < E ? bf16_bits_to_f32(lrow[e]) : -INFINITY;
+    lv[m] = e < E ? lrow[e] : -INFINITY;
     mx = fmaxf(mx, lv[m]);
   }
 #pragma unroll
@@ -204,20 +130,106 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const uint16_t* __rest
     idx_out[t * K + lane] = my_e;
     w_out[t * K + lane] = renorm ? f32_to_bf16_bits(__fdiv_rn(my_p, dbf)) : f32_to_bf16_bits(my_p);
   }
-  if (sig_out) {
-    // sigmoid(x . dequant(g_s)) for the shared expert (moe.rs:119-120).
-    const int per = 32 / sg.bits;
-    const uint32_t mask = (1u << sg.bits) - 1u;
-    const uint16_t* xr = x + t * D;
-    float z = 0.0f;
-    for (int d = lane; d < D; d += 32) {
-      const uint32_t q = (__ldg(sg.w + d / per) >> ((d % per) * sg.bits)) & mask;
-      const float wv = __fmaf_rn(bf16_bits_to_f32(__ldg(sg.s + d / 64)), (float)q, bf16_bits_to_f32(__ldg(sg.b + d / 64)));
-      z = fmaf(bf16_bits_to_f32(__ldg(xr + d)), wv, z);
-    }
+}
+
+// sigmoid(x . dequant(g_s)) of one token by one warp (moe.rs:119-120).
+__device__ inline void shared_gate_warp(const uint16_t* __restrict__ xr, int D, const SharedGateArgs& sg, int lane,
+                                        float* out) {
+  const int per = 32 / sg.bits;
+  const uint32_t mask = (1u << sg.bits) - 1u;
+  float z = 0.0f;
+  for (int d = lane; d < D; d += 32) {
+    const uint32_t q = (__ldg(sg.w + d / per) >> ((d % per) * sg.bits)) & mask;
+    const float wv = __fmaf_rn(bf16_bits_to_f32(__ldg(sg.s + d / 64)), (float)q, bf16_bits_to_f32(__ldg(sg.b + d / 64)));
+    z = fmaf(bf16_bits_to_f32(__ldg(xr + d)), wv, z);
+  }
 #pragma unroll
-    for (int s = 16; s >= 1; s >>= 1) z += __shfl_xor_sync(0xffffffffu, z, s);
-    if (lane == 0) sig_out[t] = 1.0f / (1.0f + __expf(-z));
+  for (int s = 16; s >= 1; s >>= 1) z += __shfl_xor_sync(0xffffffffu, z, s);
+  if (lane == 0) *out = 1.0f / (1.0f + __expf(-z));
+}
+
+// The whole router for TPB tokens in one CTA of 16 warps. Warp w computes
+// the logits of expert groups w, w+16, ... (8 experts each) for the TPB
+// tokens into shared memory, in the contract's fixed FMA order: lane j folds
+// the 16-byte chunks j, j+32, ... of D (8 elements each, ascending), then an
+// xor butterfly; + bias; rounded to bf16. Warp t < TPB then routes token t.
+constexpr int RT_THREADS = 512;
+
+template <int TPB>
+__global__ void __launch_bounds__(RT_THREADS) router_fused_kernel(
+    const uint16_t* __restrict__ x, int64_t T, int D, const uint16_t* __restrict__ wg, int E,
+    const float* __restrict__ bias, int K, int renorm, int32_t* __restrict__ idx_out, uint16_t* __restrict__ w_out,
+    uint16_t* __restrict__ logits_out, uint16_t* __restrict__ probs_out, SharedGateArgs sg,
+    float* __restrict__ sig_out) {
+  extern __shared__ float s_lg[];  // [TPB][E]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t0 = (int64_t)blockIdx.x * TPB;
+  const uint4* xr[TPB];
+#pragma unroll
+  for (int i = 0; i < TPB; ++i) xr[i] = reinterpret_cast<const uint4*>(x + (t0 + i < T ? t0 + i : T - 1) * D);
+  const int nchunks = D / 8;
+  const int ngroups = (E + 7) / 8;
+  for (int g = warp; g < ngroups; g += RT_THREADS / 32) {
+    const int e0 = g * 8;
+    const uint4* wr[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) wr[j] = reinterpret_cast<const uint4*>(wg + (int64_t)(e0 + j < E ? e0 + j : E - 1) * D);
+    float acc[TPB][8];
+#pragma unroll
+    for (int i = 0; i < TPB; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+#pragma unroll 2
+    for (int c = lane; c < nchunks; c += 32) {
+      uint4 xv[TPB], wv[8];
+#pragma unroll
+      for (int i = 0; i < TPB; ++i) xv[i] = __ldg(xr[i] + c);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) wv[j] = __ldg(wr[j] + c);
+#pragma unroll
+      for (int el = 0; el < 8; ++el) {
+        float xf[TPB], wf[8];
+#pragma unroll
+        for (int i = 0; i < TPB; ++i) {
+          const uint32_t wd = el < 2 ? xv[i].x : el < 4 ? xv[i].y : el < 6 ? xv[i].z : xv[i].w;
+          xf[i] = (el & 1) ? bf_hi(wd) : bf_lo(wd);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t wd = el < 2 ? wv[j].x : el < 4 ? wv[j].y : el < 6 ? wv[j].z : wv[j].w;
+          wf[j] = (el & 1) ? bf_hi(wd) : bf_lo(wd);
+        }
+#pragma unroll
+        for (int i = 0; i < TPB; ++i)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(xf[i], wf[j], acc[i][j]);
+      }
+    }
+    float mine = 0.0f;
+#pragma unroll
+    for (int i = 0; i < TPB; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float v = acc[i][j];
+#pragma unroll
+        for (int s = 16; s >= 1; s >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, s));
+        if (lane == i * 8 + j) mine = v;
+      }
+    if (lane < TPB * 8) {
+      const int i = lane >> 3, e = e0 + (lane & 7);
+      if (e < E) {
+        const float b = bias ? bias[e] : 0.0f;
+        const uint16_t lb = f32_to_bf16_bits(__fadd_rn(mine, b));
+        s_lg[i * E + e] = bf16_bits_to_f32(lb);
+        if (logits_out && t0 + i < T) logits_out[(t0 + i) * E + e] = lb;
+      }
+    }
+  }
+  __syncthreads();
+  if (warp < TPB && t0 + warp < T) {
+    const int64_t t = t0 + warp;
+    route_token_warp(s_lg + warp * E, t, E, K, renorm, lane, idx_out, w_out, probs_out);
+    if (sig_out) shared_gate_warp(x + t * D, D, sg, lane, sig_out + t);
   }
 }
 
@@ -277,6 +289,40 @@ struct TileListOut {
   int bn;
 };
 
+// Tile lists for the grouped GEMMs (one per tile width) and the dense
+// shared-expert list, from each expert's total `tot` and offset `off`
+// (thread e of a 1024-thread block owns expert e).
+__device__ inline void build_tile_lists(int e, int E, int tot, int off, int64_t T, const TileListOut& l1,
+                                        const TileListOut& l2, const TileListOut& lsh, int* warp_sums, int* total) {
+  TileListOut lists[2] = {l1, l2};
+  for (int li = 0; li < 2; ++li) {
+    const TileListOut L = lists[li];
+    const int nt = e < E ? (tot + L.bn - 1) / L.bn : 0;
+    const int toff = block_exclusive_scan(nt, warp_sums, total);
+    for (int j = 0; j < nt; ++j) {
+      GemmTile g;
+      g.expert = e;
+      g.row_start = off + j * L.bn;
+      g.row_count = min(L.bn, tot - j * L.bn);
+      g.pad = 0;
+      L.tiles[toff + j] = g;
+    }
+    if (e == 0) *L.count = *total;
+  }
+  if (lsh.tiles) {
+    const int nt = (int)((T + lsh.bn - 1) / lsh.bn);
+    for (int j = e; j < nt; j += blockDim.x) {
+      GemmTile g;
+      g.expert = 0;
+      g.row_start = j * lsh.bn;
+      g.row_count = (int)min((int64_t)lsh.bn, T - (int64_t)j * lsh.bn);
+      g.pad = 0;
+      lsh.tiles[j] = g;
+    }
+    if (e == 0) *lsh.count = nt;
+  }
+}
+
 // Single CTA of 1024 threads: expert totals, offsets, per-block bases and
 // the GEMM tile lists (one per tile width) plus the dense shared-expert list.
 __global__ void __launch_bounds__(1024) permute_scan_kernel(const int32_t* __restrict__ block_counts, int nblk, int E,
@@ -301,32 +347,83 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(const int32_t* __res
     }
   }
   if (e == 0) offsets[E] = total;
-  TileListOut lists[2] = {l1, l2};
-  for (int li = 0; li < 2; ++li) {
-    const TileListOut L = lists[li];
-    const int nt = e < E ? (tot + L.bn - 1) / L.bn : 0;
-    const int toff = block_exclusive_scan(nt, warp_sums, &total);
-    for (int j = 0; j < nt; ++j) {
-      GemmTile g;
-      g.expert = e;
-      g.row_start = off + j * L.bn;
-      g.row_count = min(L.bn, tot - j * L.bn);
-      g.pad = 0;
-      L.tiles[toff + j] = g;
+  build_tile_lists(e, E, tot, off, T, l1, l2, lsh, warp_sums, &total);
+}
+
+// Stable ranks of a warp's contiguous row range [wbeg, wend): each row f
+// goes to position wbase[e] + (rows of the same expert before it), where
+// wbase[e] (shared memory) holds the warp's first position per expert.
+__device__ inline void rank_rows_warp(const int32_t* __restrict__ idx, int64_t wbeg, int64_t wend, int64_t R, int E,
+                                      int* wbase, int lane, int32_t* __restrict__ sorted_rows,
+                                      int32_t* __restrict__ inv) {
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  for (int64_t c0 = wbeg; c0 < wend; c0 += 32) {
+    const int64_t f = c0 + lane;
+    int e = -1;
+    if (f < wend) {
+      e = idx[f];
+      if (e < 0 || e >= E) e = -1;
     }
-    if (e == 0) *L.count = total;
+    const uint32_t peers = __match_any_sync(0xffffffffu, e);
+    int pos = -1;
+    if (e >= 0) pos = wbase[e] + __popc(peers & lt_mask);
+    if (pos >= R) pos = -1;  // cannot happen for consistent counts; never write out of range
+    __syncwarp();
+    if (e >= 0 && lane == __ffs(peers) - 1) wbase[e] += __popc(peers);
+    __syncwarp();
+    if (pos >= 0) {
+      sorted_rows[pos] = (int32_t)f;
+      inv[f] = pos;
+    }
   }
-  if (lsh.tiles) {
-    const int nt = (int)((T + lsh.bn - 1) / lsh.bn);
-    for (int j = e; j < nt; j += blockDim.x) {
-      GemmTile g;
-      g.expert = 0;
-      g.row_start = j * lsh.bn;
-      g.row_count = (int)min((int64_t)lsh.bn, T - (int64_t)j * lsh.bn);
-      g.pad = 0;
-      lsh.tiles[j] = g;
+}
+
+// The whole permutation when every flat row fits one 2048-row block: count,
+// scan, tile lists and the stable scatter in a single 1024-thread CTA.
+__global__ void __launch_bounds__(1024) permute_small_kernel(const int32_t* __restrict__ idx, int64_t R, int E,
+                                                            int64_t T, int32_t* __restrict__ counts,
+                                                            int32_t* __restrict__ offsets,
+                                                            int32_t* __restrict__ sorted_rows,
+                                                            int32_t* __restrict__ inv, TileListOut l1, TileListOut l2,
+                                                            TileListOut lsh, int* status) {
+  extern __shared__ int sm[];  // hist[E], then wcnt[8][E] (8 row ranges of 256)
+  __shared__ int warp_sums[32];
+  __shared__ int total;
+  int* hist = sm;
+  int* wcnt = sm + E;
+  for (int i = threadIdx.x; i < 9 * E; i += blockDim.x) sm[i] = 0;
+  __syncthreads();
+  for (int64_t f = threadIdx.x; f < R; f += blockDim.x) {
+    const int e = idx[f];
+    if (e < 0 || e >= E) {
+      atomicCAS(status, 0, (int)kDevBadIndex);
+    } else {
+      atomicAdd(&hist[e], 1);
+      atomicAdd(&wcnt[(int)(f / (PERM_ROWS / 8)) * E + e], 1);
     }
-    if (e == 0) *lsh.count = nt;
+  }
+  __syncthreads();
+  const int e = threadIdx.x;
+  const int tot = e < E ? hist[e] : 0;
+  const int off = block_exclusive_scan(tot, warp_sums, &total);
+  if (e < E) {
+    counts[e] = tot;
+    offsets[e] = off;
+    int run = off;
+    for (int w = 0; w < 8; ++w) {
+      const int c = wcnt[w * E + e];
+      wcnt[w * E + e] = run;
+      run += c;
+    }
+  }
+  if (e == 0) offsets[E] = total;
+  build_tile_lists(e, E, tot, off, T, l1, l2, lsh, warp_sums, &total);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp < 8) {
+    const int64_t wbeg = (int64_t)warp * (PERM_ROWS / 8);
+    const int64_t wend = min(wbeg + PERM_ROWS / 8, R);
+    rank_rows_warp(idx, wbeg, wend, R, E, wcnt + warp * E, lane, sorted_rows, inv);
   }
 }
 
@@ -356,26 +453,7 @@ __global__ void __launch_bounds__(256) permute_scatter_kernel(const int32_t* __r
     }
   }
   __syncthreads();
-  const uint32_t lt_mask = (1u << lane) - 1u;
-  for (int64_t c0 = wbeg; c0 < wend; c0 += 32) {
-    const int64_t f = c0 + lane;
-    int e = -1;
-    if (f < wend) {
-      e = idx[f];
-      if (e < 0 || e >= E) e = -1;
-    }
-    const uint32_t peers = __match_any_sync(0xffffffffu, e);
-    int pos = -1;
-    if (e >= 0) pos = wcnt[warp * E + e] + __popc(peers & lt_mask);
-    if (pos >= R) pos = -1;  // cannot happen for consistent counts; never write out of range
-    __syncwarp();
-    if (e >= 0 && lane == __ffs(peers) - 1) wcnt[warp * E + e] += __popc(peers);
-    __syncwarp();
-    if (e >= 0) {
-      sorted_rows[pos] = (int32_t)f;
-      inv[f] = pos;
-    }
-  }
+  rank_rows_warp(idx, wbeg, wend, R, E, wcnt + warp * E, lane, sorted_rows, inv);
 }
 
 // x_sorted[pos] = x[sorted_rows[pos] / K] (sorted_rows NULL: the identity),
@@ -412,7 +490,7 @@ __global__ void __launch_bounds__(256) permute_gather_kernel(const int32_t* __re
 }
 
 // ------------------------------------------------------------ combine ---
-__global__ void __launch_bounds__(128) combine_kernel(const uint16_t* __restrict__ y_sorted,
+__global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict__ y_sorted,
                                                      const int32_t* __restrict__ inv, const uint16_t* __restrict__ w,
                                                      int K, int D, int64_t T, const uint16_t* __restrict__ y_sh,
                                                      const float* __restrict__ sig, uint16_t* __restrict__ out,
@@ -438,13 +516,22 @@ __global__ void __launch_bounds__(128) combine_kernel(const uint16_t* __restrict
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-    for (int k = 0; k < K; ++k) {
-      const uint4 yv = __ldg(reinterpret_cast<const uint4*>(y_sorted + (int64_t)rows[k] * D) + v);
-      const uint32_t ww[4] = {yv.x, yv.y, yv.z, yv.w};
+    for (int k0 = 0; k0 < K; k0 += 8) {
+      uint4 yv[8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        acc[2 * i] = fmaf(wk[k], bf_lo(ww[i]), acc[2 * i]);
-        acc[2 * i + 1] = fmaf(wk[k], bf_hi(ww[i]), acc[2 * i + 1]);
+      for (int j = 0; j < 8; ++j)  // all loads of the group first
+        if (k0 + j < K) yv[j] = __ldg(reinterpret_cast<const uint4*>(y_sorted + (int64_t)rows[k0 + j] * D) + v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (k0 + j < K) {
+          const float wj = wk[k0 + j];
+          const uint32_t ww[4] = {yv[j].x, yv[j].y, yv[j].z, yv[j].w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            acc[2 * i] = fmaf(wj, bf_lo(ww[i]), acc[2 * i]);
+            acc[2 * i + 1] = fmaf(wj, bf_hi(ww[i]), acc[2 * i + 1]);
+          }
+        }
       }
     }
     if (y_sh) {
