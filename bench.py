@@ -9,8 +9,13 @@ batch T in {1, 8, 64} on fresh inputs (73 tokens per step per GPU). Each
 forward is a captured CUDA graph of the library's block call. L2 is flushed
 (a 512 MiB write) before every forward; only the forwards are timed, with
 CUDA events on the launching stream. N > 1: one process per GPU, each serving
-its own batches with the experts replicated (no data-path collective),
-"scaling": "weak", value = all tokens / max-over-ranks time.
+its own decode batches with the experts replicated (the decode sweep's units,
+token batches, are independent: no data-path collective), "scaling": "weak",
+value = all tokens / max-over-ranks time. At N > 1 the line also carries
+"expert_parallel": the largest configurations (C5 prefill 8192 tokens, C4
+16384 tokens, C5 decode 256) run expert-parallel over the N ranks with NCCL
+all-to-all dispatch and combine, strong scaling, beside the same batch on one
+GPU measured in the same run.
 
 `--impl reference` times the CPU restatement of the reference block (the
 reference's own MLX CPU path cannot be built here) on the host cores, on a
@@ -149,6 +154,37 @@ def distinct_experts(routing) -> int:
 
 
 # ---------------------------------------------------------------- GPU arm ----
+def stage_times(torch, C, _lib, blk, x_in, x_static, out, ws, st, flush, reps, dev):
+    """Median per-stage times (ms) of one block forward: a graph of the
+    forward captured with the library's stage events recorded between its
+    kernels (event-record nodes), replayed `reps` times with L2 flushed."""
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+    for e in evs:  # materialise the CUDA events before handing their handles over
+        e.record(st)
+    torch.cuda.synchronize(dev)
+    arr = (C.c_void_p * 7)(*[C.c_void_p(e.cuda_event) for e in evs])
+    gs = torch.cuda.CUDAGraph()
+    _lib.call("mlxr_cu_moe_set_stage_events", arr, 7)
+    try:
+        with torch.cuda.stream(st), torch.cuda.graph(gs, stream=st):
+            blk.forward(x_static, out=out, workspace=ws)
+    finally:
+        _lib.call("mlxr_cu_moe_set_stage_events", None, 0)
+    times = []
+    with torch.cuda.stream(st):
+        for i in range(reps):
+            if x_in[i % len(x_in)] is not x_static:
+                x_static.copy_(x_in[i % len(x_in)])
+            flush.fill_(i & 0xFF)
+            gs.replay()
+            torch.cuda.synchronize(dev)
+            times.append([evs[j].elapsed_time(evs[j + 1]) for j in range(6)])
+    del gs
+    med = [statistics.median(col) for col in zip(*times)]
+    return dict(router_ms=med[0], permute_ms=med[1], gate_up_ms=med[2], down_ms=med[3], shared_ms=med[4],
+                combine_ms=med[5])
+
+
 def run_gpu(args):
     import torch
     import torch.distributed as dist
@@ -251,33 +287,8 @@ def run_gpu(args):
 
     # Live stage timing: a second graph per batch size with the library's
     # stage events recorded between its kernels (event-record nodes).
-    stage = {T: None for T in BATCHES}
-    for T in BATCHES:
-        G = graphs[T]
-        evs_s = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
-        for e in evs_s:  # materialise the CUDA events before handing their handles over
-            e.record(st)
-        torch.cuda.synchronize(dev)
-        arr = (C.c_void_p * 7)(*[C.c_void_p(e.cuda_event) for e in evs_s])
-        gs = torch.cuda.CUDAGraph()
-        _lib.call("mlxr_cu_moe_set_stage_events", arr, 7)
-        try:
-            with torch.cuda.stream(st), torch.cuda.graph(gs, stream=st):
-                blk.forward(G["xs"], out=G["out"], workspace=G["ws"])
-        finally:
-            _lib.call("mlxr_cu_moe_set_stage_events", None, 0)
-        times = []
-        with torch.cuda.stream(st):
-            for s_ in range(max(5, args.steps)):
-                G["xs"].copy_(G["x"][s_ % nsets])
-                flush.fill_(s_ & 0xFF)
-                gs.replay()
-                torch.cuda.synchronize(dev)
-                times.append([evs_s[i].elapsed_time(evs_s[i + 1]) for i in range(6)])
-        med = [statistics.median(col) for col in zip(*times)]
-        stage[T] = dict(router_ms=med[0], permute_ms=med[1], gate_up_ms=med[2], down_ms=med[3], shared_ms=med[4],
-                        combine_ms=med[5])
-        del gs
+    stage = {T: stage_times(torch, C, _lib, blk, graphs[T]["x"], graphs[T]["xs"], graphs[T]["out"], graphs[T]["ws"],
+                            st, flush, max(5, args.steps), dev) for T in BATCHES}
 
     # e2e: the same sweep through the public API with pinned host buffers.
     e2e_ms = 0.0
@@ -340,6 +351,9 @@ def run_gpu(args):
     extra = {}
     if rank == 0 and not args.no_extra and world == 1:
         extra = bench_extra(args, dev, st, flush, peaks)
+    ep = None
+    if world > 1 and not args.no_extra:
+        ep = bench_ep(args, dev, st, world, rank)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -359,7 +373,8 @@ def run_gpu(args):
                        "moe_intermediate": cfg.moe_intermediate_size, "bits": cfg.bits, "group_size": cfg.group_size,
                        "batches": BATCHES, "l2": "flushed before every forward (512 MiB write)",
                        "graphs": "each forward replayed from a captured CUDA graph",
-                       "parallelism": "replicas" if world > 1 else "single GPU"},
+                       "parallelism": f"dp{world}: token batches per rank, experts replicated" if world > 1
+                       else "single GPU"},
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -368,6 +383,7 @@ def run_gpu(args):
             "clocks": clk,
             "sweep": sweep,
             "extra": extra,
+            "expert_parallel": ep,
         }
         print(json.dumps(line))
     if world > 1:
@@ -376,7 +392,11 @@ def run_gpu(args):
 
 def bench_extra(args, dev, st, flush, peaks):
     """The other BASELINE configurations on this GPU (informational lines)."""
+    import ctypes as C
+
     import torch
+
+    from mlxr_moe import _lib
 
     from mlxr_moe import synth
     from mlxr_moe.moe import Routing
@@ -411,6 +431,7 @@ def bench_extra(args, dev, st, flush, peaks):
                 if i >= 3:
                     times.append(a.elapsed_time(b))
         ms = statistics.median(times)
+        stg = stage_times(torch, C, _lib, blk, [x], x, out, ws, st, flush, 5, dev)
         U = distinct_experts(r)
         fl = synth.algorithmic_flops(cfg, T)
         by = synth.algorithmic_bytes(cfg, T, U)
@@ -420,8 +441,84 @@ def bench_extra(args, dev, st, flush, peaks):
         res[name] = dict(tokens=T, ms=ms, tokens_per_s=T / (ms / 1e3), tflops=tfl, gbs=gbs,
                          bound="tensor" if prefill else "hbm",
                          frac=(tfl / peaks["bf16_tflops"]) if prefill else (gbs / peaks["hbm_gbs"]),
-                         distinct_experts=U, zipf=spec["zipf"])
+                         distinct_experts=U, zipf=spec["zipf"],
+                         stages_ms={k: round(v, 5) for k, v in stg.items()})
         del g, blk, ws, out, x
+        torch.cuda.empty_cache()
+    return res
+
+
+def bench_ep(args, dev, st, world, rank):
+    """Expert parallelism across the `world` ranks (NCCL all-to-all of the
+    pairs and of the partial rows): the largest BASELINE configurations with
+    their token batch split evenly over the ranks (strong scaling: fixed total
+    tokens). Rank r holds experts e % world == r. Times are max over ranks;
+    the whole batch on rank 0 alone (full block, one GPU) gives the one-GPU
+    time in the same run."""
+    import torch
+    import torch.distributed as dist
+
+    from mlxr_moe import synth
+    from mlxr_moe.ep import ExpertParallelMoeBlock, TorchDistExchange
+
+    ex = TorchDistExchange()
+    res = {}
+    for name, T_total in (("c5_prefill", 8192), ("c4", 16384), ("c5_decode", 256)):
+        spec = synth.CONFIGS[name.split("_")[0]]
+        cfg = spec["cfg"]
+        D, K = cfg.hidden_size, cfg.num_experts_per_tok
+        T = T_total // world
+        full = synth.make_block(cfg, 0, spec["zipf"], dev)
+        blk = ExpertParallelMoeBlock.from_block(full, rank, world)
+        xs = [synth.make_input(T, D, stream_offset=500 + 16 * rank + i, device=dev) for i in range(2)]
+        bounds = dict(max_recv_pairs=world * T, max_recv_rows=world * T * K)
+        n_steps = max(5, args.steps // 2)
+        with torch.cuda.stream(st):
+            for i in range(3):
+                blk.forward(xs[i % 2], ex, **bounds)
+            torch.cuda.synchronize(dev)
+            blk.status()
+            dist.barrier()
+            times = []
+            for i in range(n_steps):
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record(st)
+                blk.forward(xs[i % 2], ex, **bounds)
+                b.record(st)
+                b.synchronize()
+                times.append(a.elapsed_time(b))
+        torch.cuda.synchronize(dev)
+        blk.status()
+        t = torch.tensor([statistics.median(times)], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        one = None
+        if rank == 0:  # the whole batch on this GPU alone, for the speed-up
+            x1 = synth.make_input(T_total, D, stream_offset=600, device=dev)
+            out1 = torch.empty_like(x1)
+            ws1 = torch.empty(full.workspace_bytes(T_total), dtype=torch.uint8, device=dev)
+            with torch.cuda.stream(st):
+                t1 = []
+                for i in range(3 + n_steps):
+                    a = torch.cuda.Event(enable_timing=True)
+                    b = torch.cuda.Event(enable_timing=True)
+                    a.record(st)
+                    full.forward(x1, out=out1, workspace=ws1)
+                    b.record(st)
+                    b.synchronize()
+                    if i >= 3:
+                        t1.append(a.elapsed_time(b))
+            one = statistics.median(t1)
+            del x1, out1, ws1
+        dist.barrier()
+        fl = synth.algorithmic_flops(cfg, T_total)
+        res[name] = dict(tokens=T_total, tokens_per_rank=T, ms=ms, tokens_per_s=T_total / (ms / 1e3),
+                         tflops_total=fl / (ms / 1e3) / 1e12, one_gpu_ms=one,
+                         speedup_vs_one_gpu=(one / ms) if one else None, zipf=spec["zipf"],
+                         placement="expert e on rank e % world",
+                         exchange="NCCL all_to_all_single: counts, pair rows, slot rows, partial rows")
+        del blk, full, xs
         torch.cuda.empty_cache()
     return res
 

@@ -239,6 +239,67 @@ MLXR_CU_API int mlxr_cu_moe_permute(const mlxr_cu_moe_config* cfg, const int32_t
                         int32_t* counts, int32_t* offsets, int32_t* sorted_rows, int32_t* inverse, void* x_sorted,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------- expert parallelism -- */
+/* No counterpart in the reference, which runs the whole block on one device
+ * (Qwen35MoeBlock::forward, crates/mlxr-lm/src/qwen3_5/text/moe.rs:116-146,
+ * has no collective). The block's experts are spread over `world` ranks, one
+ * process per GPU: expert e lives on rank e % world as local expert
+ * e / world; the router and the shared expert are replicated. A step on each
+ * rank, with the caller doing the two exchanges (e.g. NCCL all-to-all):
+ *   1. mlxr_cu_moe_ep_dispatch: route this rank's T tokens; list one pair per
+ *      (token, destination rank) holding one of the token's experts, sorted
+ *      by rank then token, with the token's x row and K slots of (local
+ *      expert << 16 | bf16 top-k weight) in k order (-1 = empty slot).
+ *   2. exchange: pairs for rank r (x_send rows and meta_send rows) go to r.
+ *   3. mlxr_cu_moe_ep_experts: the received pairs through this rank's
+ *      experts; each pair is reduced to one partial row (sum of w * expert
+ *      output over its slots).
+ *   4. exchange back: the partial rows return to their senders, in the order
+ *      they were sent.
+ *   5. mlxr_cu_moe_ep_combine: out[t] = sum of t's partial rows (in the order
+ *      of the k that first named each rank) + sigmoid gate * shared expert.
+ * Routing is bit-identical to the one-device block; outputs differ from it
+ * only by the bf16 rounding of each partial row. The three steps of a rank
+ * share one workspace: dispatch clears its status word, experts and combine
+ * add their device-side checks to it, and mlxr_cu_moe_status reads it after
+ * combine. */
+
+/* Workspace for all three steps of one rank: num_tokens of its own tokens,
+ * up to max_recv_pairs received pairs carrying up to max_recv_rows filled
+ * slots (bounds: world * num_tokens pairs; pairs * K rows). */
+MLXR_CU_API int mlxr_cu_moe_ep_workspace_size(const mlxr_cu_moe_config* cfg, int world, int64_t num_tokens,
+                                              int64_t max_recv_pairs, int64_t max_recv_rows, size_t* bytes);
+
+/* Step 1. send_counts [world][2] int32: pairs and filled slots for each
+ * destination rank. pair_pos [T*K] int32: send position of the pair of
+ * (t, k) when k is the first of t's experts on its rank, else -1. x_send
+ * [T * min(K, world), D] bf16 and meta_send [T * min(K, world), K] int32
+ * receive the pairs in send order (the first sum(pairs) rows are written).
+ * shared_gate [T] fp32 (sigmoid of the shared-expert gate; NULL without a
+ * shared expert) is kept for step 5. */
+MLXR_CU_API int mlxr_cu_moe_ep_dispatch(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights, int world,
+                                        const void* x, int64_t num_tokens, int32_t* send_counts, int32_t* pair_pos,
+                                        void* x_send, int32_t* meta_send, float* shared_gate, void* workspace,
+                                        size_t workspace_bytes, void* stream);
+
+/* Step 3. cfg is the full block's configuration; local_weights hold this
+ * rank's E / world experts in local order (switch_* members only). x_recv
+ * [num_pairs, D] bf16 and meta_recv [num_pairs, K] int32 as received;
+ * num_rows = the filled slots among them (the sum of the received
+ * send_counts[.][1]). partial [num_pairs, D] bf16 out. */
+MLXR_CU_API int mlxr_cu_moe_ep_experts(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* local_weights,
+                                       int world, const void* x_recv, const int32_t* meta_recv, int64_t num_pairs,
+                                       int64_t num_rows, void* partial, void* workspace, size_t workspace_bytes,
+                                       void* stream);
+
+/* Step 5. partial_back [num_pairs, D] bf16: the partial rows of this rank's
+ * pairs, in send order; pair_pos and shared_gate from step 1; weights for
+ * the shared expert (full block). out [T, D] bf16. */
+MLXR_CU_API int mlxr_cu_moe_ep_combine(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights,
+                                       const void* x, int64_t num_tokens, const void* partial_back, int64_t num_pairs,
+                                       const int32_t* pair_pos, const float* shared_gate, void* out,
+                                       void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------ synthetic inputs -- */
 
 /* Seeded N(0, stddev^2) samples rounded to bf16: Philox4x32-10 keyed by

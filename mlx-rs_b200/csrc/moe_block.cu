@@ -43,7 +43,9 @@ static inline void stage_mark(int i, cudaStream_t st) {
 static inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 struct Layout {
-  int64_t T = 0, R = 0, rows_pad = 0, sh_rows_pad = 0;
+  // R: flat (token, k) rows; rows: expert rows the buffers hold (R, or fewer
+  // when some flat rows are skipped, as on the receiving side of expert parallelism).
+  int64_t T = 0, R = 0, rows = 0, rows_pad = 0, sh_rows_pad = 0;
   int E = 0, K = 0, D = 0, I = 0, Is = 0, nblk = 0;
   int bn1 = 0, bn2 = 0, bns = 0;
   int max_t1 = 0, max_t2 = 0, max_tsh = 0;
@@ -87,7 +89,7 @@ static int validate(const mlxr_cu_moe_config* c, int64_t T) {
   return MLXR_CU_OK;
 }
 
-static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T) {
+static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T, int64_t rows_cap = -1) {
   Layout L;
   L.T = T;
   L.E = c->num_experts;
@@ -96,16 +98,17 @@ static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T) {
   L.I = c->moe_intermediate_size;
   L.Is = c->shared_expert_intermediate_size;
   L.R = T * L.K;
-  L.rows_pad = L.R > 256 ? L.R : 256;
+  L.rows = rows_cap >= 0 && rows_cap < L.R ? rows_cap : L.R;
+  L.rows_pad = L.rows > 256 ? L.rows : 256;
   L.sh_rows_pad = T > 256 ? T : 256;
   L.nblk = (int)((L.R + PERM_ROWS - 1) / PERM_ROWS);
   if (L.nblk < 1) L.nblk = 1;
-  const double avg = L.E > 0 ? (double)L.R / L.E : 0.0;
+  const double avg = L.E > 0 ? (double)L.rows / L.E : 0.0;
   L.bn1 = pick_bn(avg, 128);
   L.bn2 = pick_bn(avg, (L.D % 256 == 0) ? 128 : 256);
   L.bns = pick_bn((double)T, 64);
-  L.max_t1 = (int)(L.E + (L.R + L.bn1 - 1) / L.bn1 + 1);
-  L.max_t2 = (int)(L.E + (L.R + L.bn2 - 1) / L.bn2 + 1);
+  L.max_t1 = (int)(L.E + (L.rows + L.bn1 - 1) / L.bn1 + 1);
+  L.max_t2 = (int)(L.E + (L.rows + L.bn2 - 1) / L.bn2 + 1);
   L.max_tsh = (int)((T + L.bns - 1) / L.bns + 1);
   size_t o = 0;
   auto take = [&](size_t bytes) {
@@ -132,7 +135,7 @@ static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T) {
   L.nsh = take(4);
   L.xs = take((size_t)L.rows_pad * L.D * 2);
   L.h = take((size_t)L.rows_pad * L.I * 2);
-  L.y = take((size_t)L.R * L.D * 2);
+  L.y = take((size_t)L.rows * L.D * 2);
   if (L.Is > 0) {
     L.xpad = take((T < 256 || c->shared_bits == 4) ? (size_t)L.sh_rows_pad * L.D * 2 : 0);
     L.hsh = take((size_t)L.sh_rows_pad * L.Is * 2);
@@ -191,19 +194,21 @@ static int run_router(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
   return MLXR_CU_OK;
 }
 
+// skip != 0: rows with a negative index are left out (see permute_count_kernel).
 static int run_permute(const Layout& L, const int32_t* idx, const void* x, void* ws, int32_t* counts, int32_t* offsets,
-                       int32_t* sorted, int32_t* inv, uint16_t* xs, int kperm, cudaStream_t st) {
+                       int32_t* sorted, int32_t* inv, uint16_t* xs, int kperm, cudaStream_t st, int skip = 0) {
   int* status = at<int>(ws, L.status);
-  TileListOut l1{at<GemmTile>(ws, L.t1), at<int32_t>(ws, L.n1), L.bn1};
-  TileListOut l2{at<GemmTile>(ws, L.t2), at<int32_t>(ws, L.n2), L.bn2};
-  TileListOut lsh{L.Is > 0 ? at<GemmTile>(ws, L.tsh) : nullptr, at<int32_t>(ws, L.nsh), L.bns};
+  TileListOut l1{at<GemmTile>(ws, L.t1), at<int32_t>(ws, L.n1), L.bn1, L.max_t1};
+  TileListOut l2{at<GemmTile>(ws, L.t2), at<int32_t>(ws, L.n2), L.bn2, L.max_t2};
+  TileListOut lsh{L.Is > 0 ? at<GemmTile>(ws, L.tsh) : nullptr, at<int32_t>(ws, L.nsh), L.bns, L.max_tsh};
   if (L.nblk == 1) {
     // Every flat row fits one block: count, scan, tile lists and ranks in one CTA.
     permute_small_kernel<<<1, 1024, 9 * L.E * sizeof(int), st>>>(idx, L.R, L.E, L.T, counts, offsets, sorted, inv, l1,
-                                                                  l2, lsh, status);
+                                                                  l2, lsh, skip, status);
     MLXR_LAUNCH_CHECK("permute_small_kernel");
   } else {
-    permute_count_kernel<<<L.nblk, 256, L.E * sizeof(int), st>>>(idx, L.R, L.E, at<int32_t>(ws, L.bcounts), status);
+    permute_count_kernel<<<L.nblk, 256, L.E * sizeof(int), st>>>(idx, L.R, L.E, at<int32_t>(ws, L.bcounts), skip,
+                                                                 status);
     MLXR_LAUNCH_CHECK("permute_count_kernel");
     permute_scan_kernel<<<1, 1024, 0, st>>>(at<int32_t>(ws, L.bcounts), L.nblk, L.E, L.T, at<int32_t>(ws, L.bbase),
                                             counts, offsets, l1, l2, lsh);
@@ -212,11 +217,11 @@ static int run_permute(const Layout& L, const int32_t* idx, const void* x, void*
                                                                        sorted, inv);
     MLXR_LAUNCH_CHECK("permute_scatter_kernel");
   }
-  if (L.R > 0) {
-    const int64_t gblocks = (L.R + 7) / 8;
+  if (L.R > 0 && L.rows > 0) {
+    const int64_t gblocks = (L.rows + 7) / 8;
     const int gather_grid = (int)(gblocks < 4 * 148 ? gblocks : 4 * 148);
-    permute_gather_kernel<<<gather_grid, 256, 0, st>>>(sorted, L.R, L.K, static_cast<const uint16_t*>(x), L.D, kperm,
-                                                       xs);
+    permute_gather_kernel<<<gather_grid, 256, 0, st>>>(sorted, L.rows, L.R, L.K, static_cast<const uint16_t*>(x), L.D,
+                                                       kperm, xs, skip ? offsets + L.E : nullptr, status);
     MLXR_LAUNCH_CHECK("permute_gather_kernel");
   }
   return MLXR_CU_OK;
@@ -232,7 +237,7 @@ static int check_qlinear(const mlxr_cu_qlinear& q, const char* name) {
 
 static int run_experts(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt, const Layout& L, void* ws,
                        cudaStream_t st, int mid_stage) {
-  if (L.R == 0) return MLXR_CU_OK;
+  if (L.rows == 0) return MLXR_CU_OK;
   if (int rc = check_qlinear(wt->switch_gate, "switch_mlp.gate_proj")) return rc;
   if (int rc = check_qlinear(wt->switch_up, "switch_mlp.up_proj")) return rc;
   if (int rc = check_qlinear(wt->switch_down, "switch_mlp.down_proj")) return rc;
@@ -257,7 +262,7 @@ static int run_experts(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* w
   p.num_tiles = at<int32_t>(ws, L.n1);
   p.max_tiles = L.max_t1;
   p.out = at<uint16_t>(ws, L.h);
-  p.out_rows = L.R;
+  p.out_rows = L.rows;
   p.perm_out = c->bits == 4;  // h is the 4-bit down projection's activation operand
   p.status = status;
   if (int rc = launch_grouped_gemm(p, st)) return rc;
@@ -283,7 +288,7 @@ static int run_experts(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* w
   q.num_tiles = at<int32_t>(ws, L.n2);
   q.max_tiles = L.max_t2;
   q.out = at<uint16_t>(ws, L.y);
-  q.out_rows = L.R;
+  q.out_rows = L.rows;
   q.perm_out = 0;
   q.status = status;
   return launch_grouped_gemm(q, st);
@@ -303,8 +308,8 @@ static int run_shared(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
     // A padded (>= 256 rows) and, for 4-bit weights, K-order-permuted copy.
     const int64_t gblocks = (L.T + 7) / 8;
     const int grid = (int)(gblocks < 4 * 148 ? gblocks : 4 * 148);
-    permute_gather_kernel<<<grid, 256, 0, st>>>(nullptr, L.T, 1, static_cast<const uint16_t*>(x), L.D, kperm,
-                                                at<uint16_t>(ws, L.xpad));
+    permute_gather_kernel<<<grid, 256, 0, st>>>(nullptr, L.T, L.T, 1, static_cast<const uint16_t*>(x), L.D, kperm,
+                                                at<uint16_t>(ws, L.xpad), nullptr, status);
     MLXR_LAUNCH_CHECK("permute_gather_kernel(shared)");
     act = at<uint16_t>(ws, L.xpad);
     act_rows = L.sh_rows_pad;
@@ -355,6 +360,32 @@ static int run_shared(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
   q.perm_out = 0;
   q.status = status;
   return launch_grouped_gemm(q, st);
+}
+
+// Dispatch scratch: the block layout's router and permute buffers, then the
+// per-(token, k) destination ranks.
+static size_t ep_dispatch_bytes(const mlxr_cu_moe_config* c, int64_t T, size_t* dest_off) {
+  const Layout L = make_layout(c, T);
+  *dest_off = L.total;
+  return L.total + align256((size_t)(T * c->num_experts_per_tok) * 4 + 4);
+}
+
+static int ep_check_world(const mlxr_cu_moe_config* cfg, int world) {
+  MLXR_CHECK_ARG(world >= 1 && world <= 64 && cfg->num_experts % world == 0,
+                 "moe_ep: world=%d must be in [1, 64] and divide num_experts=%d", world, cfg->num_experts);
+  return MLXR_CU_OK;
+}
+
+static mlxr_cu_moe_config ep_local_config(const mlxr_cu_moe_config* cfg, int world) {
+  mlxr_cu_moe_config lc = *cfg;
+  lc.num_experts = cfg->num_experts / world;
+  lc.shared_expert_intermediate_size = 0;
+  return lc;  // num_experts_per_tok stays K: the number of slots per pair
+}
+
+// Receiving side: num_pairs pairs of K slots (flat rows), num_rows filled slots.
+static Layout ep_experts_layout(const mlxr_cu_moe_config* lc, int64_t num_pairs, int64_t num_rows) {
+  return make_layout(lc, num_pairs, num_rows);
 }
 
 }  // namespace mlxr
@@ -549,6 +580,154 @@ int mlxr_cu_moe_permute(const mlxr_cu_moe_config* cfg, const int32_t* indices, i
   MLXR_CUDA_TRY(cudaMemsetAsync(at<int>(workspace, L.status), 0, sizeof(int), st));
   return run_permute(L, indices, x, workspace, counts, offsets, sorted_rows, inverse, static_cast<uint16_t*>(x_sorted),
                      0, st);
+}
+
+// ------------------------------------------------ expert parallelism ---
+// One rank's share of the block when its experts are spread over `world`
+// ranks (expert e on rank e % world as local expert e / world). Per step:
+// mlxr_cu_moe_ep_dispatch routes this rank's tokens and lists one pair per
+// (token, destination rank) with its x row and its (local expert, weight)
+// slots; the caller exchanges the pairs (all-to-all); mlxr_cu_moe_ep_experts
+// runs the received pairs through this rank's experts and pre-reduces each
+// pair to one partial row; the caller returns the partial rows (the reverse
+// all-to-all); mlxr_cu_moe_ep_combine sums each token's partial rows and adds
+// the shared expert.
+
+int mlxr_cu_moe_ep_workspace_size(const mlxr_cu_moe_config* cfg, int world, int64_t num_tokens,
+                                  int64_t max_recv_pairs, int64_t max_recv_rows, size_t* bytes) {
+  if (int rc = validate(cfg, num_tokens)) return rc;
+  if (int rc = ep_check_world(cfg, world)) return rc;
+  MLXR_CHECK_ARG(bytes != nullptr, "moe_ep_workspace_size: bytes is NULL");
+  MLXR_CHECK_ARG(max_recv_pairs >= 0 && max_recv_rows >= 0, "moe_ep_workspace_size: negative receive bound");
+  if (int rc = validate(cfg, max_recv_pairs)) return rc;
+  const mlxr_cu_moe_config lc = ep_local_config(cfg, world);
+  size_t dest_off = 0;
+  size_t need = ep_dispatch_bytes(cfg, num_tokens, &dest_off);
+  const size_t e2 = ep_experts_layout(&lc, max_recv_pairs, max_recv_rows).total;
+  const size_t e3 = make_layout(cfg, num_tokens).total;
+  if (e2 > need) need = e2;
+  if (e3 > need) need = e3;
+  *bytes = need;
+  return MLXR_CU_OK;
+}
+
+int mlxr_cu_moe_ep_dispatch(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights, int world,
+                            const void* x, int64_t num_tokens, int32_t* send_counts, int32_t* pair_pos,
+                            void* x_send, int32_t* meta_send, float* shared_gate, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  if (int rc = validate(cfg, num_tokens)) return rc;
+  if (int rc = ep_check_world(cfg, world)) return rc;
+  MLXR_CHECK_ARG(weights != nullptr, "moe_ep_dispatch: weights is NULL");
+  size_t dest_off = 0;
+  const size_t need = ep_dispatch_bytes(cfg, num_tokens, &dest_off);
+  MLXR_CHECK_ARG(workspace && (reinterpret_cast<uintptr_t>(workspace) & 255) == 0 && workspace_bytes >= need,
+                 "moe_ep_dispatch: workspace NULL, not 256-byte aligned or smaller than %zu bytes", need);
+  MLXR_CHECK_ARG(send_counts != nullptr, "moe_ep_dispatch: send_counts is NULL");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* ws = workspace;
+  const Layout L = make_layout(cfg, num_tokens);
+  MLXR_CUDA_TRY(cudaMemsetAsync(at<int>(ws, L.status), 0, sizeof(int), st));
+  if (num_tokens == 0) {
+    MLXR_CUDA_TRY(cudaMemsetAsync(send_counts, 0, (size_t)world * 2 * 4, st));
+    return MLXR_CU_OK;
+  }
+  MLXR_CHECK_ARG(x && pair_pos && x_send && meta_send && aligned16(x) && aligned16(x_send),
+                 "moe_ep_dispatch: NULL or misaligned argument (x and x_send need 16-byte alignment)");
+  MLXR_CHECK_ARG(cfg->shared_expert_intermediate_size == 0 || shared_gate, "moe_ep_dispatch: shared_gate is NULL");
+  if (int rc = run_router(cfg, weights, L, x, ws, nullptr, nullptr, st)) return rc;
+  const int K = cfg->num_experts_per_tok;
+  const int64_t R = L.R;
+  int32_t* dest = at<int32_t>(ws, dest_off);
+  ep_pair_dest_kernel<<<(unsigned)((R + 255) / 256), 256, 0, st>>>(at<int32_t>(ws, L.idx), num_tokens, K, world, dest,
+                                                                    at<int>(ws, L.status));
+  MLXR_LAUNCH_CHECK("ep_pair_dest_kernel");
+  // Stable sort of the pairs by destination rank: the block permutation with
+  // `world` buckets, the non-first (token, k) rows skipped, x rows gathered
+  // unpermuted into x_send.
+  Layout P = L;
+  P.E = world;
+  P.Is = 0;
+  P.rows = num_tokens * (K < world ? K : world);
+  P.bn1 = P.bn2 = 1 << 30;  // tile lists are not used here
+  P.max_t1 = P.max_t2 = world + 1;
+  if (int rc = run_permute(P, dest, x, ws, at<int32_t>(ws, L.counts), at<int32_t>(ws, L.offsets),
+                           at<int32_t>(ws, L.sorted), pair_pos, static_cast<uint16_t*>(x_send), 0, st, 1))
+    return rc;
+  ep_counts_kernel<<<1, 1024, 0, st>>>(at<int32_t>(ws, L.idx), R, world, at<int32_t>(ws, L.counts), send_counts);
+  MLXR_LAUNCH_CHECK("ep_counts_kernel");
+  ep_pair_meta_kernel<<<(unsigned)((num_tokens + 127) / 128), 128, 0, st>>>(
+      at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w), pair_pos, num_tokens, K, world, P.rows, meta_send,
+      at<int>(ws, L.status));
+  MLXR_LAUNCH_CHECK("ep_pair_meta_kernel");
+  if (cfg->shared_expert_intermediate_size > 0)
+    MLXR_CUDA_TRY(cudaMemcpyAsync(shared_gate, at<float>(ws, L.sig), (size_t)num_tokens * 4, cudaMemcpyDeviceToDevice,
+                                  st));
+  return MLXR_CU_OK;
+}
+
+int mlxr_cu_moe_ep_experts(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* local_weights, int world,
+                           const void* x_recv, const int32_t* meta_recv, int64_t num_pairs, int64_t num_rows,
+                           void* partial, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = ep_check_world(cfg, world)) return rc;
+  if (int rc = validate(cfg, num_pairs)) return rc;
+  const mlxr_cu_moe_config lc = ep_local_config(cfg, world);
+  MLXR_CHECK_ARG(local_weights != nullptr, "moe_ep_experts: weights is NULL");
+  MLXR_CHECK_ARG(num_rows >= 0 && num_rows <= num_pairs * lc.num_experts_per_tok,
+                 "moe_ep_experts: num_rows=%lld must be in [0, num_pairs * K]", (long long)num_rows);
+  const Layout L = ep_experts_layout(&lc, num_pairs, num_rows);
+  if (int rc = check_ws(L, workspace, workspace_bytes)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* ws = workspace;  // the status word was cleared by this step's dispatch
+  if (num_pairs == 0) return MLXR_CU_OK;
+  MLXR_CHECK_ARG(x_recv && meta_recv && partial && aligned16(x_recv) && aligned16(partial),
+                 "moe_ep_experts: NULL or misaligned argument (x_recv and partial need 16-byte alignment)");
+  ep_slot_expert_kernel<<<(unsigned)((L.R + 255) / 256), 256, 0, st>>>(meta_recv, L.R, L.E, at<int32_t>(ws, L.idx),
+                                                                        at<int>(ws, L.status));
+  MLXR_LAUNCH_CHECK("ep_slot_expert_kernel");
+  if (int rc = run_permute(L, at<int32_t>(ws, L.idx), x_recv, ws, at<int32_t>(ws, L.counts), at<int32_t>(ws, L.offsets),
+                           at<int32_t>(ws, L.sorted), at<int32_t>(ws, L.inv), at<uint16_t>(ws, L.xs), lc.bits == 4, st, 1))
+    return rc;
+  if (int rc = run_experts(&lc, local_weights, L, ws, st, 7)) return rc;
+  if (L.rows == 0) {
+    MLXR_CUDA_TRY(cudaMemsetAsync(partial, 0, (size_t)num_pairs * L.D * 2, st));
+    return MLXR_CU_OK;
+  }
+  ep_reduce_kernel<<<(unsigned)num_pairs, L.D >= 2048 ? 256 : 128, 0, st>>>(
+      at<uint16_t>(ws, L.y), at<int32_t>(ws, L.inv), meta_recv, L.K, L.D, L.rows, static_cast<uint16_t*>(partial),
+      at<int>(ws, L.status));
+  MLXR_LAUNCH_CHECK("ep_reduce_kernel");
+  return MLXR_CU_OK;
+}
+
+int mlxr_cu_moe_ep_combine(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights, const void* x,
+                           int64_t num_tokens, const void* partial_back, int64_t num_pairs, const int32_t* pair_pos,
+                           const float* shared_gate, void* out, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  if (int rc = validate(cfg, num_tokens)) return rc;
+  const Layout L = make_layout(cfg, num_tokens);
+  if (int rc = check_ws(L, workspace, workspace_bytes)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* ws = workspace;  // the status word was cleared by this step's dispatch
+  if (num_tokens == 0) return MLXR_CU_OK;
+  MLXR_CHECK_ARG(x && pair_pos && out && aligned16(x) && aligned16(out) && (num_pairs == 0 || partial_back) &&
+                     aligned16(partial_back),
+                 "moe_ep_combine: NULL or misaligned argument");
+  const uint16_t* ysh = nullptr;
+  if (L.Is > 0) {
+    MLXR_CHECK_ARG(shared_gate != nullptr && weights != nullptr, "moe_ep_combine: shared_gate / weights is NULL");
+    // The block forward gets the shared tile list from its permute; here it is built alone.
+    shared_tiles_kernel<<<(unsigned)((L.max_tsh + 255) / 256), 256, 0, st>>>(at<GemmTile>(ws, L.tsh),
+                                                                             at<int32_t>(ws, L.nsh), L.T, L.bns,
+                                                                             L.max_tsh);
+    MLXR_LAUNCH_CHECK("shared_tiles_kernel");
+    if (int rc = run_shared(cfg, weights, L, x, ws, st)) return rc;
+    ysh = at<uint16_t>(ws, L.ysh);
+  }
+  ep_combine_kernel<<<(unsigned)L.T, L.D >= 2048 ? 256 : 128, 0, st>>>(
+      static_cast<const uint16_t*>(partial_back), pair_pos, L.K, L.D, num_pairs, ysh, shared_gate,
+      static_cast<uint16_t*>(out), at<int>(ws, L.status));
+  MLXR_LAUNCH_CHECK("ep_combine_kernel");
+  return MLXR_CU_OK;
 }
 
 }  // extern "C"

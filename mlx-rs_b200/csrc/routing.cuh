@@ -237,8 +237,10 @@ __global__ void __launch_bounds__(RT_THREADS) router_fused_kernel(
 constexpr int PERM_ROWS = 2048;  // flat rows per permute block (8 warps x 256)
 constexpr int PERM_MAX_E = 1024;
 
+// skip != 0: rows whose index is negative are left out of the permutation
+// (their inv entry becomes -1); otherwise a negative index is an error.
 __global__ void __launch_bounds__(256) permute_count_kernel(const int32_t* __restrict__ idx, int64_t R, int E,
-                                                           int32_t* __restrict__ block_counts, int* status) {
+                                                           int32_t* __restrict__ block_counts, int skip, int* status) {
   extern __shared__ int hist[];
   for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
   __syncthreads();
@@ -247,6 +249,7 @@ __global__ void __launch_bounds__(256) permute_count_kernel(const int32_t* __res
     const int64_t f = base + i;
     if (f < R) {
       const int e = idx[f];
+      if (e < 0 && skip) continue;
       if (e < 0 || e >= E) atomicCAS(status, 0, (int)kDevBadIndex);
       else atomicAdd(&hist[e], 1);
     }
@@ -287,6 +290,7 @@ struct TileListOut {
   GemmTile* tiles;
   int32_t* count;
   int bn;
+  int cap;  // entries the list holds; tiles beyond it are dropped (the gather flags the excess rows)
 };
 
 // Tile lists for the grouped GEMMs (one per tile width) and the dense
@@ -305,13 +309,13 @@ __device__ inline void build_tile_lists(int e, int E, int tot, int off, int64_t 
       g.row_start = off + j * L.bn;
       g.row_count = min(L.bn, tot - j * L.bn);
       g.pad = 0;
-      L.tiles[toff + j] = g;
+      if (toff + j < L.cap) L.tiles[toff + j] = g;
     }
-    if (e == 0) *L.count = *total;
+    if (e == 0) *L.count = min(*total, L.cap);
   }
   if (lsh.tiles) {
     const int nt = (int)((T + lsh.bn - 1) / lsh.bn);
-    for (int j = e; j < nt; j += blockDim.x) {
+    for (int j = e; j < nt && j < lsh.cap; j += blockDim.x) {
       GemmTile g;
       g.expert = 0;
       g.row_start = j * lsh.bn;
@@ -319,7 +323,7 @@ __device__ inline void build_tile_lists(int e, int E, int tot, int off, int64_t 
       g.pad = 0;
       lsh.tiles[j] = g;
     }
-    if (e == 0) *lsh.count = nt;
+    if (e == 0) *lsh.count = min(nt, lsh.cap);
   }
 }
 
@@ -374,6 +378,8 @@ __device__ inline void rank_rows_warp(const int32_t* __restrict__ idx, int64_t w
     if (pos >= 0) {
       sorted_rows[pos] = (int32_t)f;
       inv[f] = pos;
+    } else if (f < wend) {
+      inv[f] = -1;  // a skipped (or invalid, already flagged) row
     }
   }
 }
@@ -385,7 +391,7 @@ __global__ void __launch_bounds__(1024) permute_small_kernel(const int32_t* __re
                                                             int32_t* __restrict__ offsets,
                                                             int32_t* __restrict__ sorted_rows,
                                                             int32_t* __restrict__ inv, TileListOut l1, TileListOut l2,
-                                                            TileListOut lsh, int* status) {
+                                                            TileListOut lsh, int skip, int* status) {
   extern __shared__ int sm[];  // hist[E], then wcnt[8][E] (8 row ranges of 256)
   __shared__ int warp_sums[32];
   __shared__ int total;
@@ -395,6 +401,7 @@ __global__ void __launch_bounds__(1024) permute_small_kernel(const int32_t* __re
   __syncthreads();
   for (int64_t f = threadIdx.x; f < R; f += blockDim.x) {
     const int e = idx[f];
+    if (e < 0 && skip) continue;
     if (e < 0 || e >= E) {
       atomicCAS(status, 0, (int)kDevBadIndex);
     } else {
@@ -456,20 +463,30 @@ __global__ void __launch_bounds__(256) permute_scatter_kernel(const int32_t* __r
   rank_rows_warp(idx, wbeg, wend, R, E, wcnt + warp * E, lane, sorted_rows, inv);
 }
 
-// x_sorted[pos] = x[sorted_rows[pos] / K] (sorted_rows NULL: the identity),
-// one warp per row, 16-byte loads and stores, the whole grid streaming. With
+// x_sorted[pos] = x[sorted_rows[pos] / K] (sorted_rows NULL: the identity)
+// for pos < n_rows, one warp per row, 16-byte loads and stores, the whole
+// grid streaming. sorted_rows entries must lie in [0, n_flat). With count
+// (a permutation with skipped rows) only pos < *count is copied, and a count
+// above n_rows (more rows than the destination holds) is an error. With
 // kperm the 8 elements of every 16-byte chunk are stored in the 4-bit
 // operand order {0,4,1,5,2,6,3,7} the grouped GEMM's dequantiser produces.
-__global__ void __launch_bounds__(256) permute_gather_kernel(const int32_t* __restrict__ sorted_rows, int64_t R, int K,
-                                                            const uint16_t* __restrict__ x, int D, int kperm,
-                                                            uint16_t* __restrict__ x_sorted) {
+__global__ void __launch_bounds__(256) permute_gather_kernel(const int32_t* __restrict__ sorted_rows, int64_t n_rows,
+                                                            int64_t n_flat, int K, const uint16_t* __restrict__ x,
+                                                            int D, int kperm, uint16_t* __restrict__ x_sorted,
+                                                            const int32_t* __restrict__ count, int* status) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int dvec = D / 8;
-  for (int64_t pos = (int64_t)blockIdx.x * 8 + warp; pos < R; pos += (int64_t)gridDim.x * 8) {
+  int64_t n = n_rows;
+  if (count) {
+    const int64_t c = *count;
+    if (c > n_rows && blockIdx.x == 0 && threadIdx.x == 0) atomicCAS(status, 0, (int)kDevBadIndex);
+    n = min(n_rows, c);
+  }
+  for (int64_t pos = (int64_t)blockIdx.x * 8 + warp; pos < n; pos += (int64_t)gridDim.x * 8) {
     int64_t src_row = pos;
     if (sorted_rows) {
       const int32_t f = sorted_rows[pos];
-      if (f < 0 || (int64_t)f >= R) continue;
+      if (f < 0 || (int64_t)f >= n_flat) continue;
       src_row = f / K;
     }
     const uint4* src = reinterpret_cast<const uint4*>(x + src_row * D);
@@ -550,6 +567,236 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict
     o.w = pack_bf16x2(acc[6], acc[7]);
     reinterpret_cast<uint4*>(out + t * D)[v] = o;
   }
+}
+
+// ------------------------------------------------- expert parallelism ---
+// Expert e lives on rank e % world as that rank's local expert e / world.
+// Every token is sent once to each rank that owns at least one of its top-k
+// experts (one "pair" per (token, rank)); the pair carries up to K slots of
+// (local expert, top-k weight), and the receiving rank returns one partial
+// row per pair: the weighted sum of its experts' outputs for that token.
+
+// dest[t*K + k] = rank of expert idx[t*K + k] when k is the first of token t
+// that goes to that rank, -1 otherwise (so a stable sort of the non-negative
+// entries lists the pairs by rank, then token).
+__global__ void ep_pair_dest_kernel(const int32_t* __restrict__ idx, int64_t T, int K, int world,
+                                    int32_t* __restrict__ dest, int* status) {
+  const int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (f >= T * K) return;
+  const int64_t t = f / K;
+  const int k = (int)(f - t * K);
+  const int e = idx[f];
+  if (e < 0) {
+    atomicCAS(status, 0, (int)kDevBadIndex);
+    dest[f] = -1;
+    return;
+  }
+  const int r = e % world;
+  bool first = true;
+  for (int j = 0; j < k; ++j) {
+    const int ej = idx[t * K + j];
+    if (ej >= 0 && ej % world == r) {
+      first = false;
+      break;
+    }
+  }
+  dest[f] = first ? r : -1;
+}
+
+// send_counts[2r] = pairs sent to rank r (from the pair permutation),
+// send_counts[2r + 1] = (token, k) rows those pairs carry. One CTA.
+__global__ void __launch_bounds__(1024) ep_counts_kernel(const int32_t* __restrict__ idx, int64_t R, int world,
+                                                        const int32_t* __restrict__ pair_counts,
+                                                        int32_t* __restrict__ send_counts) {
+  __shared__ int hist[64];
+  if (threadIdx.x < 64) hist[threadIdx.x] = 0;
+  __syncthreads();
+  for (int64_t f = threadIdx.x; f < R; f += blockDim.x) {
+    const int e = idx[f];
+    if (e >= 0) atomicAdd(&hist[e % world], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x < world) {
+    send_counts[2 * threadIdx.x] = pair_counts[threadIdx.x];
+    send_counts[2 * threadIdx.x + 1] = hist[threadIdx.x];
+  }
+}
+
+__device__ __forceinline__ int32_t ep_slot(int local_expert, uint16_t weight_bits) {
+  return (int32_t)(((uint32_t)local_expert << 16) | weight_bits);
+}
+
+// One thread per token: for each pair of the token (send position pos =
+// pair_pos[t*K + k] of its first k), meta[pos*K + j] = the j-th of the
+// token's experts on that rank in k order, packed as (local expert << 16) |
+// bf16 weight bits; -1 fills the unused slots.
+__global__ void ep_pair_meta_kernel(const int32_t* __restrict__ idx, const uint16_t* __restrict__ w,
+                                    const int32_t* __restrict__ pair_pos, int64_t T, int K, int world,
+                                    int64_t max_pairs, int32_t* __restrict__ meta, int* status) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  const int32_t* ti = idx + t * K;
+  for (int k = 0; k < K; ++k) {
+    const int64_t pos = pair_pos[t * K + k];
+    if (pos < 0) continue;  // not the first k of its rank
+    if (pos >= max_pairs || ti[k] < 0) {
+      atomicCAS(status, 0, (int)kDevBadIndex);
+      continue;
+    }
+    const int r = ti[k] % world;
+    int j = 0;
+    for (int k2 = k; k2 < K; ++k2) {
+      const int e = ti[k2];
+      if (e >= 0 && e % world == r) meta[pos * K + j++] = ep_slot(e / world, w[t * K + k2]);
+    }
+    for (; j < K; ++j) meta[pos * K + j] = -1;
+  }
+}
+
+// Receiving side: idx_local[i] = local expert of slot i, -1 for an empty slot.
+__global__ void ep_slot_expert_kernel(const int32_t* __restrict__ meta, int64_t n, int E_local,
+                                      int32_t* __restrict__ idx_local, int* status) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int32_t m = meta[i];
+  int le = -1;
+  if (m >= 0) {
+    le = m >> 16;
+    if (le >= E_local) {
+      atomicCAS(status, 0, (int)kDevBadIndex);
+      le = -1;
+    }
+  }
+  idx_local[i] = le;
+}
+
+// acc[0..7] += sum_j wk[j] * rows_base[rows[j]][8v .. 8v+7] (fp32 fmaf, j
+// ascending), with the loads of each group of 8 rows issued first.
+__device__ __forceinline__ void weighted_rows_acc(const uint16_t* __restrict__ base, const int* rows,
+                                                  const float* wk, int n, int D, int v, float acc[8]) {
+  for (int k0 = 0; k0 < n; k0 += 8) {
+    uint4 yv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (k0 + j < n) yv[j] = __ldg(reinterpret_cast<const uint4*>(base + (int64_t)rows[k0 + j] * D) + v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (k0 + j < n) {
+        const float wj = wk[k0 + j];
+        const uint32_t ww[4] = {yv[j].x, yv[j].y, yv[j].z, yv[j].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          acc[2 * i] = fmaf(wj, bf_lo(ww[i]), acc[2 * i]);
+          acc[2 * i + 1] = fmaf(wj, bf_hi(ww[i]), acc[2 * i + 1]);
+        }
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void store_bf16x8(uint16_t* dst, const float acc[8]) {
+  uint4 o;
+  o.x = pack_bf16x2(acc[0], acc[1]);
+  o.y = pack_bf16x2(acc[2], acc[3]);
+  o.z = pack_bf16x2(acc[4], acc[5]);
+  o.w = pack_bf16x2(acc[6], acc[7]);
+  *reinterpret_cast<uint4*>(dst) = o;
+}
+
+// Receiving side, one CTA per received pair p: partial[p] = bf16(sum over
+// the pair's filled slots j, in slot order, of w_j * y_sorted[inv[p*K + j]]).
+__global__ void __launch_bounds__(256) ep_reduce_kernel(const uint16_t* __restrict__ y_sorted,
+                                                       const int32_t* __restrict__ inv,
+                                                       const int32_t* __restrict__ meta, int K, int D, int64_t rows,
+                                                       uint16_t* __restrict__ partial, int* status) {
+  __shared__ int rws[RT_MAXK];
+  __shared__ float wk[RT_MAXK];
+  __shared__ int nk;
+  const int64_t p = blockIdx.x;
+  if (threadIdx.x == 0) {
+    int n = 0;
+    for (int j = 0; j < K; ++j) {
+      const int32_t m = meta[p * K + j];
+      if (m < 0) continue;
+      const int r = inv[p * K + j];
+      if (r < 0 || (int64_t)r >= rows) {
+        atomicCAS(status, 0, (int)kDevBadIndex);
+        continue;
+      }
+      rws[n] = r;
+      wk[n] = bf16_bits_to_f32((uint16_t)(m & 0xFFFF));
+      ++n;
+    }
+    nk = n;
+  }
+  __syncthreads();
+  const int n = nk;
+  for (int v = threadIdx.x; v < D / 8; v += blockDim.x) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    weighted_rows_acc(y_sorted, rws, wk, n, D, v, acc);
+    store_bf16x8(partial + p * D + 8 * v, acc);
+  }
+}
+
+// Owning side, one CTA per token: out[t] = bf16(sum of the token's returned
+// partial rows, in the order of their first k, + sig[t] * y_sh[t]).
+__global__ void __launch_bounds__(256) ep_combine_kernel(const uint16_t* __restrict__ partial,
+                                                        const int32_t* __restrict__ pair_pos, int K, int D,
+                                                        int64_t num_pairs, const uint16_t* __restrict__ y_sh,
+                                                        const float* __restrict__ sig, uint16_t* __restrict__ out,
+                                                        int* status) {
+  __shared__ int rws[RT_MAXK + 1];
+  __shared__ float wk[RT_MAXK + 1];
+  __shared__ int nk;
+  const int64_t t = blockIdx.x;
+  if (threadIdx.x == 0) {
+    int n = 0;
+    for (int k = 0; k < K; ++k) {
+      const int32_t pos = pair_pos[t * K + k];
+      if (pos < 0) continue;
+      if ((int64_t)pos >= num_pairs) {
+        atomicCAS(status, 0, (int)kDevBadIndex);
+        continue;
+      }
+      rws[n] = pos;
+      wk[n] = 1.0f;
+      ++n;
+    }
+    nk = n;
+  }
+  __syncthreads();
+  const int n = nk;
+  const float sg = y_sh ? sig[t] : 0.0f;
+  for (int v = threadIdx.x; v < D / 8; v += blockDim.x) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    weighted_rows_acc(partial, rws, wk, n, D, v, acc);
+    if (y_sh) {
+      const uint4 yv = __ldg(reinterpret_cast<const uint4*>(y_sh + t * D) + v);
+      const uint32_t ww[4] = {yv.x, yv.y, yv.z, yv.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc[2 * i] = fmaf(sg, bf_lo(ww[i]), acc[2 * i]);
+        acc[2 * i + 1] = fmaf(sg, bf_hi(ww[i]), acc[2 * i + 1]);
+      }
+    }
+    store_bf16x8(out + t * D + 8 * v, acc);
+  }
+}
+
+// The dense shared-expert tile list alone (row tiles of width bn over T
+// tokens), for callers that run the shared expert without a permute.
+__global__ void shared_tiles_kernel(GemmTile* __restrict__ tiles, int32_t* __restrict__ count, int64_t T, int bn,
+                                    int cap) {
+  const int nt = (int)((T + bn - 1) / bn);
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < nt && j < cap; j += gridDim.x * blockDim.x) {
+    GemmTile g;
+    g.expert = 0;
+    g.row_start = j * bn;
+    g.row_count = (int)min((int64_t)bn, T - (int64_t)j * bn);
+    g.pad = 0;
+    tiles[j] = g;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) *count = min(nt, cap);
 }
 
 }  // namespace mlxr

@@ -1,0 +1,176 @@
+"""Expert parallelism on the GPU: the pair plan of the dispatch step is
+checked element by element against the one-device routing, and `world`
+ranks' worth of expert shards (run as virtual ranks on one GPU, or as two
+NCCL ranks on two GPUs) must reproduce the one-device block and the oracle."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from conftest import ATOL, RTOL, assert_close_bf16, assert_mostly_tight, bf16_np
+from gpu_helpers import block_to_oracle
+from mlxr_moe import synth
+from mlxr_moe.ep import ExpertParallelMoeBlock, loopback_forward
+from mlxr_moe.moe import Routing
+
+pytestmark = pytest.mark.gpu
+
+# EP against the one-device block: every element within the north-star bound,
+# all but 1e-4 of them within a tighter one (each partial row is rounded to
+# bf16 once before the owner adds it up).
+TIGHT_ATOL, TIGHT_RTOL, TIGHT_FRAC = 5e-3, 1e-2, 1e-4
+
+_BLOCKS = {}
+
+
+def block_for(name):
+    if name not in _BLOCKS:
+        spec = synth.CONFIGS[name]
+        _BLOCKS[name] = synth.make_block(spec["cfg"], 0, spec["zipf"])
+    return _BLOCKS[name]
+
+
+def expected_plan(idx, w_u16, world):
+    """Host restatement of the dispatch step from one-device routing."""
+    T, K = idx.shape
+    pairs = {r: [] for r in range(world)}  # r -> [(t, [(local expert, weight bits), ...])]
+    first_k = {}
+    for t in range(T):
+        seen = {}
+        for k in range(K):
+            e = int(idx[t, k])
+            r = e % world
+            if r not in seen:
+                seen[r] = []
+                first_k[(t, r)] = k
+                pairs[r].append((t, seen[r]))
+            seen[r].append((e // world, int(w_u16[t, k])))
+    counts = np.array([[len(pairs[r]), sum(len(s) for _, s in pairs[r])] for r in range(world)], np.int32)
+    pair_pos = np.full(T * K, -1, np.int32)
+    meta = []
+    tok = []
+    pos = 0
+    for r in range(world):
+        for t, slots in pairs[r]:
+            pair_pos[t * K + first_k[(t, r)]] = pos
+            m = [(le << 16) | wb for le, wb in slots] + [-1] * (K - len(slots))
+            meta.append(m)
+            tok.append(t)
+            pos += 1
+    return counts, pair_pos, np.array(meta, np.int64).astype(np.uint32).view(np.int32), np.array(tok)
+
+
+@pytest.mark.parametrize("name,T,world", [("c1", 32, 8), ("c4", 40, 4), ("c3", 300, 2)])
+def test_ep_dispatch_plan_is_exact(name, T, world):
+    full = block_for(name)
+    cfg = full.cfg
+    x = synth.make_input(T, cfg.hidden_size, stream_offset=31)
+    r = Routing(T, cfg.num_experts_per_tok, cfg.num_experts, x.device)
+    full.forward(x, routing=r)
+    blk = ExpertParallelMoeBlock.from_block(full, 0, world)
+    ws = blk.workspace(T, 0, 0, x.device)
+    plan = blk.dispatch(x, ws)
+    torch.cuda.synchronize()
+    blk.status()
+    idx = r.indices.cpu().numpy().reshape(T, -1)
+    wb = bf16_np(r.weights).reshape(T, -1)
+    counts, pair_pos, meta, tok = expected_plan(idx, wb, world)
+    np.testing.assert_array_equal(plan.send_counts.cpu().numpy(), counts)
+    np.testing.assert_array_equal(plan.pair_pos.cpu().numpy()[: T * cfg.num_experts_per_tok], pair_pos)
+    P = int(counts[:, 0].sum())
+    np.testing.assert_array_equal(plan.meta_send[:P].cpu().numpy(), meta)
+    np.testing.assert_array_equal(bf16_np(plan.x_send[:P]), bf16_np(x)[tok])
+
+
+@pytest.mark.parametrize("name,T,world", [("c1", 32, 2), ("c1", 32, 8), ("c4", 64, 4), ("c3", 512, 2),
+                                          ("c5", 96, 8)])
+def test_ep_loopback_matches_single_device(name, T, world):
+    full = block_for(name)
+    blocks = [ExpertParallelMoeBlock.from_block(full, r, world) for r in range(world)]
+    xs = [synth.make_input(T, full.cfg.hidden_size, stream_offset=40 + r) for r in range(world)]
+    outs = loopback_forward(blocks, xs)
+    torch.cuda.synchronize()
+    for b in blocks:
+        b.status()
+    for r in range(world):
+        want = full.forward(xs[r])
+        torch.cuda.synchronize()
+        assert_close_bf16(bf16_np(outs[r]), bf16_np(want), ATOL, RTOL, f"rank {r}")
+        assert_mostly_tight(bf16_np(outs[r]), bf16_np(want), TIGHT_ATOL, TIGHT_RTOL, TIGHT_FRAC, f"rank {r} tight")
+
+
+def test_ep_loopback_matches_oracle():
+    full = block_for("c1")
+    world, T = 4, 32
+    blocks = [ExpertParallelMoeBlock.from_block(full, r, world) for r in range(world)]
+    xs = [synth.make_input(T, 2048, stream_offset=70 + r) for r in range(world)]
+    outs = loopback_forward(blocks, xs)
+    torch.cuda.synchronize()
+    ocfg, ow = block_to_oracle(full)
+    for r in range(world):
+        want, _, _ = O.moe_block(ocfg, ow, bf16_np(xs[r]), "fused")
+        assert_close_bf16(bf16_np(outs[r]), want, ATOL, RTOL, f"rank {r} vs oracle")
+        want_st, _, _ = O.moe_block(ocfg, ow, bf16_np(xs[r]), "staged")
+        assert_close_bf16(bf16_np(outs[r]), want_st, ATOL, RTOL, f"rank {r} vs oracle (staged)")
+
+
+def test_ep_loopback_idle_rank():
+    """A rank with no tokens of its own still serves its experts."""
+    full = block_for("c4")
+    world = 2
+    blocks = [ExpertParallelMoeBlock.from_block(full, r, world) for r in range(world)]
+    xs = [synth.make_input(48, 2048, stream_offset=80),
+          torch.empty((0, 2048), dtype=torch.bfloat16, device="cuda")]
+    outs = loopback_forward(blocks, xs)
+    torch.cuda.synchronize()
+    for b in blocks:
+        b.status()
+    want = full.forward(xs[0])
+    assert outs[1].shape == (0, 2048)
+    assert_close_bf16(bf16_np(outs[0]), bf16_np(want), ATOL, RTOL, "rank 0")
+
+
+def _nccl_worker(rank, world, port, result_path):
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    from mlxr_moe.ep import TorchDistExchange
+
+    spec = synth.CONFIGS["c4"]
+    full = synth.make_block(spec["cfg"], 0, False, device="cuda")
+    blk = ExpertParallelMoeBlock.from_block(full, rank, world)
+    ex = TorchDistExchange()
+    worst = 0.0
+    ok = 1
+    for step in range(2):
+        x = synth.make_input(48 + 16 * rank, 2048, stream_offset=60 + 4 * rank + step, device="cuda")
+        out = blk.forward(x, ex)
+        want = full.forward(x)
+        torch.cuda.synchronize()
+        blk.status()
+        err = (out.float() - want.float()).abs()
+        worst = max(worst, err.max().item())
+        ok &= int(bool((err <= ATOL + RTOL * want.float().abs()).all()))
+    t = torch.tensor([ok], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    if rank == 0:
+        with open(result_path, "w") as f:
+            f.write(f"{int(t.item())} {worst}\n")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_nccl_two_gpus(tmp_path):
+    import torch.multiprocessing as mp
+
+    res = tmp_path / "ep.txt"
+    mp.spawn(_nccl_worker, args=(2, 29517, str(res)), nprocs=2, join=True)
+    ok, err = res.read_text().split()
+    assert ok == "1", f"max abs err {err}"
