@@ -70,11 +70,8 @@ static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
                            C::BK, BN, CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
   auto kern = grouped_dequant_gemm_kernel<NMAT, BN, BITS>;
-  static bool attr_set = false;  // per instantiation; idempotent if raced
-  if (!attr_set) {
-    MLXR_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> attr_done{0};  // per instantiation and device
+  if (int rc = ensure_smem_attr(kern, C::SMEM_BYTES, attr_done)) return rc;
   GemmArgs a;
   a.scales[0] = p.s[0];
   a.scales[1] = NMAT == 2 ? p.s[1] : p.s[0];

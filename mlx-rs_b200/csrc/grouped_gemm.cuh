@@ -19,12 +19,17 @@
 // D[128, BN] lives in TMEM too: lane = output feature, column = token.
 // Decode batches use small BN (16/32), prefill BN = 128 (gate/up) or 256 (down).
 //
-// Warp roles (480 threads):
+// Warp roles (736 threads, 768 with two weight matrices):
 //   warps 0-3   epilogue: TMEM -> registers -> SwiGLU / plain -> bf16 global
-//   warps 4-11  dequant: packed uint32 tile (smem) -> bf16 A stage in TMEM
-//   warp 12     TMA producer for packed weight tiles (raw ring)
-//   warp 13     TMA producer for activation tiles (B ring)
-//   warp 14     TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 4-19  dequant: packed uint32 tile (smem) -> bf16 A stage in TMEM;
+//               NGRP = 2 (two matrices) or 4 (one) groups of warps take
+//               turns by k-step, each thread a whole weight row of its
+//               k-steps, so the groups run a stage apart and hide each
+//               other's barrier, fence and TMEM-store latencies
+//   warp 20     TMA producer for packed weight tiles (raw ring)
+//   warp 21     TMA producer for activation tiles (B ring)
+//   warps 22-   one single-thread tcgen05.mma issuer per weight matrix
+//               (warp 22 also allocates TMEM)
 // TMEM columns: [0, AB*NMAT*BN) accumulators (double-buffered when they fit,
 // so the epilogue of item i overlaps the main loop of item i+1), then OS
 // stages of NMAT x 32 columns (128 rows x 64 bf16) of dequantised A.
@@ -51,18 +56,25 @@ struct GG {
   static constexpr int RAW_MAT = BM * RAW_ROW;
   static constexpr int RAW_STAGE = NMAT * RAW_MAT;
   static constexpr int B_STAGE = BN * BK * 2;
-  // Shared-memory rings: packed weights (raw) and activation tiles (B), each
-  // up to 96 KB deep so both streams are requested well ahead of use.
-  static constexpr int RS_WANT = (96 * 1024) / RAW_STAGE;
-  static constexpr int RS = RS_WANT > 16 ? 16 : RS_WANT;
-  static constexpr int BS_WANT = (96 * 1024) / B_STAGE;
-  static constexpr int BS = BS_WANT > 16 ? 16 : (BS_WANT < 3 ? 3 : BS_WANT);
   // Tensor memory: accumulators, then the A stages.
   static constexpr int ACC_COLS = NMAT * BN;
   static constexpr int A_COLS = NMAT * 32;                // one A stage: NMAT x (128 x 64 bf16)
   static constexpr int AB = (2 * ACC_COLS + 2 * A_COLS <= 512) ? 2 : 1;
   static constexpr int OS_FIT = (512 - AB * ACC_COLS) / A_COLS;
-  static constexpr int OS = OS_FIT > 4 ? 4 : OS_FIT;      // A-stage ring depth
+  // Stage ring depth. A stage is one k-step: a dequantised A tile in TMEM
+  // and the activation tile in shared memory, released together by one
+  // MMA commit per issuer. Bounded by tensor memory and by shared memory
+  // (keeping room for at least four raw stages).
+  static constexpr int SMEM_RINGS = 200 * 1024;
+  static constexpr int OS_SMEM = (SMEM_RINGS - 4 * RAW_STAGE) / B_STAGE;
+  static constexpr int OS_T = OS_FIT > 6 ? 6 : OS_FIT;
+  static constexpr int OS = OS_T < OS_SMEM ? OS_T : OS_SMEM;
+  // Packed-weight ring: up to 96 KB (16 stages) in what shared memory leaves.
+  static constexpr int RS_ROOM = (SMEM_RINGS - OS * B_STAGE) / RAW_STAGE;
+  static constexpr int RS_WANT = (96 * 1024) / RAW_STAGE;
+  static constexpr int RS_A = RS_WANT > 16 ? 16 : RS_WANT;
+  static constexpr int RS = RS_A < RS_ROOM ? RS_A : RS_ROOM;
+  static_assert(RS >= 4, "shared memory too small for the packed-weight ring");
   static_assert(OS >= 2, "tensor memory too small for two A stages");
   static constexpr int A_BASE = AB * ACC_COLS;
   static constexpr int TMEM_NEED = A_BASE + OS * A_COLS;
@@ -74,11 +86,20 @@ struct GG {
   // thread tens of cycles whatever N is, so with narrow decode tiles a single
   // issuer, not the tensor pipe, bounds the k-step rate.
   static constexpr int ISSUERS = NMAT;
-  static constexpr int NUM_THREADS = 32 * (14 + ISSUERS);
+  static constexpr int DQ_WARPS = 16;
+  static constexpr int W_RAW = 4 + DQ_WARPS;  // raw weight producer warp
+  static constexpr int W_B = W_RAW + 1;       // activation producer warp
+  static constexpr int W_MMA = W_B + 1;       // first MMA issuer warp (allocates TMEM)
+  static constexpr int NUM_THREADS = 32 * (W_MMA + ISSUERS);
+  // Dequant groups: group g takes the k-steps it with it % NGRP == g.
+  static constexpr int NGRP = (DQ_WARPS * 32) / (NMAT * BM);
+  static constexpr int GRP_WARPS = DQ_WARPS / NGRP;  // arrivals per stage
+  static constexpr int NCH = 8;                      // 8-weight chunks per row per k-step
+  static constexpr int WBYTES = NCH * BITS;          // packed bytes per thread per k-step
   static constexpr int OFF_B = 0;
-  static constexpr int OFF_RAW = OFF_B + BS * B_STAGE;
+  static constexpr int OFF_RAW = OFF_B + OS * B_STAGE;
   static constexpr int OFF_BAR = OFF_RAW + RS * RAW_STAGE;
-  static constexpr int NUM_BARS = 2 * RS + 2 * OS + 2 * BS + 2 * AB + 1;
+  static constexpr int NUM_BARS = 2 * RS + 3 * OS + 2 * AB + 1;
   // At least 120 KB so that two CTAs never share an SM: each CTA holds its
   // tensor memory for its whole (persistent) lifetime.
   static constexpr int SMEM_USED = OFF_BAR + NUM_BARS * 8 + 16 + 1024;  // + alignment slack
@@ -180,11 +201,10 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* raw_full = bars;
   uint64_t* raw_empty = raw_full + C::RS;
-  uint64_t* op_full = raw_empty + C::RS;   // dequantised A stage written to TMEM (8 dequant warps)
-  uint64_t* op_empty = op_full + C::OS;     // A stage consumed (MMA commit)
+  uint64_t* op_full = raw_empty + C::RS;   // dequantised A stage written to TMEM (dequant warps)
+  uint64_t* op_empty = op_full + C::OS;     // stage (A and activation tile) consumed (MMA commit)
   uint64_t* b_full = op_empty + C::OS;      // activation tile landed (TMA)
-  uint64_t* b_empty = b_full + C::BS;       // activation tile consumed (MMA commit)
-  uint64_t* acc_full = b_empty + C::BS;
+  uint64_t* acc_full = b_full + C::OS;
   uint64_t* acc_empty = acc_full + C::AB;
   uint64_t* fin_bar = acc_empty + C::AB;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin_bar + 1);
@@ -196,16 +216,13 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::RS; ++i) {
       mbar_init(&raw_full[i], 1);
-      mbar_init(&raw_empty[i], 8);
+      mbar_init(&raw_empty[i], C::GRP_WARPS);
     }
     for (int i = 0; i < C::OS; ++i) {
-      mbar_init(&op_full[i], 8);
+      mbar_init(&op_full[i], C::GRP_WARPS);
       mbar_init(&op_empty[i], C::ISSUERS);
     }
-    for (int i = 0; i < C::BS; ++i) {
-      mbar_init(&b_full[i], 1);
-      mbar_init(&b_empty[i], C::ISSUERS);
-    }
+    for (int i = 0; i < C::OS; ++i) mbar_init(&b_full[i], 1);
     for (int i = 0; i < C::AB; ++i) {
       mbar_init(&acc_full[i], C::ISSUERS);
       mbar_init(&acc_empty[i], 4);
@@ -214,11 +231,11 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 14) {
+  if (warp == C::W_MMA) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
-  if (warp == 12 && lane == 0) {
+  if (warp == C::W_RAW && lane == 0) {
     prefetch_tmap(&tm_a0);
     if (NMAT == 2) prefetch_tmap(&tm_a1);
     prefetch_tmap(&tm_b);
@@ -237,7 +254,7 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
   if (ntiles > args.max_tiles) ntiles = args.max_tiles;
   const int num_items = ntiles * mt_per_expert;
 
-  if (warp == 12) {
+  if (warp == C::W_RAW) {
     // ---------------------------------------------- raw weight producer --
     if (lane == 0) {
       uint32_t it = 0;
@@ -260,30 +277,39 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       }
       drain_ring<C::RS>(raw_full, it, abort_flag, args.status);
     }
-  } else if (warp == 13) {
+  } else if (warp == C::W_B) {
     // ------------------------------------------- activation producer ----
     if (lane == 0) {
       uint32_t it = 0;
+      int s = 0;
+      uint32_t ph = 0;
       for (int item = blockIdx.x; item < num_items && !*abort_flag; item += gridDim.x) {
         const GemmTile t = args.tiles[item / mt_per_expert];
         if (!tile_ok(t, args)) continue;
         for (int ks = 0; ks < ksteps; ++ks, ++it) {
-          const int s = it % C::BS;
-          if (!mbar_wait(&b_empty[s], ((it / C::BS) & 1) ^ 1, abort_flag, args.status)) break;
+          if (!mbar_wait(&op_empty[s], ph ^ 1, abort_flag, args.status)) break;
           mbar_arrive_expect_tx(&b_full[s], C::B_STAGE);
           tma_load_2d(sB + s * C::B_STAGE, &tm_b, &b_full[s], ks * C::BK, t.row_start);
+          if (++s == C::OS) {
+            s = 0;
+            ph ^= 1;
+          }
         }
       }
-      drain_ring<C::BS>(b_full, it, abort_flag, args.status);
+      drain_ring<C::OS>(b_full, it, abort_flag, args.status);
     }
-  } else if (warp >= 14) {
+  } else if (warp >= C::W_MMA) {
     // ---------------------------------------------------- MMA issuers ----
     // Issuer mi issues the MMAs of matrix mi (gate / up) into its own
     // accumulator; every stage and accumulator barrier expects one commit
     // per issuer.
-    const int mi = warp - 14;
+    const int mi = warp - C::W_MMA;
     if (lane == 0) {
-      uint32_t it = 0, li = 0;
+      const uint64_t bdesc0 = umma_desc_sw128(smem_u32(sB));
+      const uint32_t a0 = tmem_base + (uint32_t)(C::A_BASE + mi * 32);
+      uint32_t li = 0;
+      int s = 0;
+      uint32_t ph = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
         if (!tile_ok(args.tiles[item / mt_per_expert], args)) continue;
@@ -292,24 +318,21 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
         ++li;  // counts valid items only, exactly like the epilogue
         if (!mbar_wait(&acc_empty[ab], acc_phase ^ 1, abort_flag, args.status)) break;
         tc_fence_after();
-        const uint32_t d0 = tmem_base + (uint32_t)(ab * C::ACC_COLS);
-        for (int ks = 0; ks < ksteps; ++ks, ++it) {
-          const int s = it % C::OS;
-          const int sb = it % C::BS;
-          if (!mbar_wait(&b_full[sb], (it / C::BS) & 1, abort_flag, args.status) ||
-              !mbar_wait(&op_full[s], (it / C::OS) & 1, abort_flag, args.status)) {
+        const uint32_t d = tmem_base + (uint32_t)(ab * C::ACC_COLS + mi * BN);
+        for (int ks = 0; ks < ksteps; ++ks) {
+          if (!mbar_wait(&b_full[s], ph, abort_flag, args.status) ||
+              !mbar_wait(&op_full[s], ph, abort_flag, args.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_tm = tmem_base + (uint32_t)(C::A_BASE + s * C::A_COLS);
-          const uint32_t b_base = smem_u32(sB + sb * C::B_STAGE);
-#pragma unroll
-          for (int kk = 0; kk < C::BK / 16; ++kk)
-            umma_bf16_ts(d0 + (uint32_t)(mi * BN), a_tm + (uint32_t)(mi * 32 + kk * 8), umma_desc_sw128(b_base + kk * 32),
-                         C::IDESC, (ks | kk) != 0 ? 1u : 0u);
+          umma_bf16_ts_k64(d, a0 + (uint32_t)(s * C::A_COLS), bdesc0 + (uint64_t)(s * (C::B_STAGE >> 4)), C::IDESC,
+                           ks != 0 ? 1u : 0u);
           umma_commit(&op_empty[s]);
-          umma_commit(&b_empty[sb]);
+          if (++s == C::OS) {
+            s = 0;
+            ph ^= 1;
+          }
         }
         if (ok) umma_commit(&acc_full[ab]);
       }
@@ -319,111 +342,107 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
     }
   } else if (warp >= 4) {
     // -------------------------------------------------------- dequant ----
-    const int dt = threadIdx.x - 128;          // 0..255
-    const int mat = NMAT == 2 ? dt >> 7 : 0;   // gate / up
+    // Thread dt owns weight row dt % 128 (TMEM lane = row, so warp % 4 is
+    // the lane quarter) of matrix `mat`, and the k-steps of its group.
+    const int dt = threadIdx.x - 128;  // 0..511
     const int row = dt & 127;
-    const int c_lo = NMAT == 2 ? 0 : (dt >> 7) * 4;  // first 16 B chunk of this thread
-    constexpr int NCH = NMAT == 2 ? 8 : 4;           // chunks per thread per k-step
-    const int G = args.k_dim / 64;  // groups per row == k-steps; even (K is a multiple of 128)
-    const int G2 = G / 2;              // 32-bit words of bf16 scale pairs per row
-    uint32_t rit = 0, oit = 0;
+    const int sub = dt >> 7;           // 0..3
+    const int mat = NMAT == 2 ? (sub & 1) : 0;
+    const int grp = NMAT == 2 ? (sub >> 1) : sub;
+    constexpr int NGRP = C::NGRP;
+    const uint8_t* raw_mine = sRaw + mat * C::RAW_MAT + row * C::RAW_ROW;
+    const uint32_t ta_mine = tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(C::A_BASE + mat * 32);
+    int rs = 0, os = 0;          // ring slots of global k-step `it`, advanced incrementally
+    uint32_t rph = 0, oph = 0;   // their phases
+    uint32_t it = 0;
     bool ok = true;
+    auto advance = [&](int n) {
+      rs += n;
+      if (rs >= C::RS) {
+        rs -= C::RS;
+        rph ^= 1;
+      }
+      os += n;
+      if (os >= C::OS) {
+        os -= C::OS;
+        oph ^= 1;
+      }
+      it += n;
+    };
     for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
       const GemmTile t = args.tiles[item / mt_per_expert];
       if (!tile_ok(t, args)) continue;
       const int64_t srow = (int64_t)t.expert * n_out + (item % mt_per_expert) * mrows + (pair ? mat * C::BM : 0) + row;
-      // Scales and biases of this row, 8 groups (= 8 k-steps) per chunk,
-      // fetched with 4-byte loads two chunks ahead of their use.
-      const uint32_t* sp = reinterpret_cast<const uint32_t*>(args.scales[mat] + srow * G);
-      const uint32_t* bp = reinterpret_cast<const uint32_t*>(args.biases[mat] + srow * G);
-      uint32_t sc[4], bc[4], sn[4], bn[4];
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        sc[w] = w < G2 ? __ldg(sp + w) : 0u;
-        bc[w] = w < G2 ? __ldg(bp + w) : 0u;
-        sn[w] = 4 + w < G2 ? __ldg(sp + 4 + w) : 0u;
-        bn[w] = 4 + w < G2 ? __ldg(bp + 4 + w) : 0u;
-      }
-      for (int k8 = 0; k8 < ksteps && ok; k8 += 8) {
-        uint32_t sf[4], bf[4];
-        const int wf = (k8 >> 1) + 8;  // first word of the chunk after next
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          sf[w] = wf + w < G2 ? __ldg(sp + wf + w) : 0u;
-          bf[w] = wf + w < G2 ? __ldg(bp + wf + w) : 0u;
+      // (select, not index: a runtime index into the kernel parameters would
+      // copy them to local memory)
+      const uint16_t* sbase = mat ? args.scales[1] : args.scales[0];
+      const uint16_t* bbase = mat ? args.biases[1] : args.biases[0];
+      const uint16_t* sp = sbase + srow * ksteps;
+      const uint16_t* bp = bbase + srow * ksteps;
+      // First k-step of this item that belongs to the group.
+      int ks = (int)((grp - (int)(it % NGRP) + NGRP) % NGRP);
+      advance(ks < ksteps ? ks : ksteps);
+      if (ks >= ksteps) continue;
+      uint32_t s_nx = __ldg(sp + ks), b_nx = __ldg(bp + ks);  // one k-step ahead
+      for (; ks < ksteps; ks += NGRP) {
+        const uint32_t s16 = s_nx, b16 = b_nx;
+        if (ks + NGRP < ksteps) {
+          s_nx = __ldg(sp + ks + NGRP);
+          b_nx = __ldg(bp + ks + NGRP);
         }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (k8 + j >= ksteps) break;
-          const uint16_t s16 = (j & 1) ? (uint16_t)(sc[j >> 1] >> 16) : (uint16_t)(sc[j >> 1] & 0xFFFFu);
-          const uint16_t b16 = (j & 1) ? (uint16_t)(bc[j >> 1] >> 16) : (uint16_t)(bc[j >> 1] & 0xFFFFu);
-          // Packed codes of this thread's slice.
-          const int rs = rit % C::RS;
-          if (!mbar_wait(&raw_full[rs], (rit / C::RS) & 1, abort_flag, args.status)) {
-            ok = false;
-            break;
-          }
-          uint32_t wv[NCH * BITS / 4];
-          {
-            const uint4* src = reinterpret_cast<const uint4*>(sRaw + rs * C::RAW_STAGE + mat * C::RAW_MAT +
-                                                              row * C::RAW_ROW + c_lo * BITS);
-#pragma unroll
-            for (int i = 0; i < NCH * BITS / 16; ++i) {
-              const uint4 v = src[i];
-              wv[4 * i + 0] = v.x;
-              wv[4 * i + 1] = v.y;
-              wv[4 * i + 2] = v.z;
-              wv[4 * i + 3] = v.w;
-            }
-          }
-          const int os = oit % C::OS;
-          if (!mbar_wait(&op_empty[os], ((oit / C::OS) & 1) ^ 1, abort_flag, args.status)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          uint32_t av[32];  // this thread's slice of the A row, bf16 pairs
-          if (BITS == 4) {
-            const __nv_bfloat162 s2v = __halves2bfloat162(__ushort_as_bfloat16(s16), __ushort_as_bfloat16(s16));
-            const __nv_bfloat162 b2 = __halves2bfloat162(__ushort_as_bfloat16(b16), __ushort_as_bfloat16(b16));
-#pragma unroll
-            for (int c = 0; c < NCH; ++c) dequant_word4(wv[c], s2v, b2, &av[4 * c]);
-          } else {
-            const float sfv = bf16_bits_to_f32(s16), bfv = bf16_bits_to_f32(b16);
-#pragma unroll
-            for (int c = 0; c < NCH; ++c) {
-              const uint4 o = dequant_words8(wv[2 * c], wv[2 * c + 1], sfv, bfv);
-              av[4 * c + 0] = o.x;
-              av[4 * c + 1] = o.y;
-              av[4 * c + 2] = o.z;
-              av[4 * c + 3] = o.w;
-            }
-          }
-          // TMEM lane = this thread's weight row; 4 columns per 16-byte chunk.
-          const uint32_t ta = tmem_base + ((uint32_t)((warp & 3) * 32) << 16) +
-                              (uint32_t)(C::A_BASE + os * C::A_COLS + mat * 32 + c_lo * 4);
-          if (NCH == 8) tmem_st_x32(ta, av);
-          else tmem_st_x16(ta, av);
-          tmem_st_wait();
-          // The raw slot is refilled by TMA (async proxy) once all warps
-          // release it: order this warp's generic reads of it before that.
-          fence_proxy_async_smem();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(&raw_empty[rs]);
-            mbar_arrive(&op_full[os]);
-          }
-          ++rit;
-          ++oit;
+        if (!mbar_wait(&raw_full[rs], rph, abort_flag, args.status)) {
+          ok = false;
+          break;
         }
+        uint32_t wv[C::WBYTES / 4];
+        {
+          const uint4* src = reinterpret_cast<const uint4*>(raw_mine + rs * C::RAW_STAGE);
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          sc[w] = sn[w];
-          bc[w] = bn[w];
-          sn[w] = sf[w];
-          bn[w] = bf[w];
+          for (int i = 0; i < C::WBYTES / 16; ++i) {
+            const uint4 v = src[i];
+            wv[4 * i + 0] = v.x;
+            wv[4 * i + 1] = v.y;
+            wv[4 * i + 2] = v.z;
+            wv[4 * i + 3] = v.w;
+          }
         }
+        uint32_t av[32];  // this thread's A row for the k-step, bf16 pairs
+        if (BITS == 4) {
+          const uint32_t s2w = s16 | (s16 << 16), b2w = b16 | (b16 << 16);
+          const __nv_bfloat162 s2v = *reinterpret_cast<const __nv_bfloat162*>(&s2w);
+          const __nv_bfloat162 b2v = *reinterpret_cast<const __nv_bfloat162*>(&b2w);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) dequant_word4(wv[c], s2v, b2v, &av[4 * c]);
+        } else {
+          const float sfv = bf16_bits_to_f32((uint16_t)s16), bfv = bf16_bits_to_f32((uint16_t)b16);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const uint4 o = dequant_words8(wv[2 * c], wv[2 * c + 1], sfv, bfv);
+            av[4 * c + 0] = o.x;
+            av[4 * c + 1] = o.y;
+            av[4 * c + 2] = o.z;
+            av[4 * c + 3] = o.w;
+          }
+        }
+        // The codes are in registers: release the raw slot (TMA refills it
+        // through the async proxy, so order this warp's generic reads first).
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[rs]);
+        // Only the TMEM store needs the stage: wait for its release here, after
+        // the arithmetic, so the dequantisation overlaps the MMA round trip.
+        if (!mbar_wait(&op_empty[os], oph ^ 1, abort_flag, args.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        tmem_st_x32(ta_mine + (uint32_t)(os * C::A_COLS), av);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&op_full[os]);
+        const int step = ks + NGRP < ksteps ? NGRP : ksteps - ks;
+        advance(step);
       }
     }
   } else {
@@ -444,19 +463,14 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * C::ACC_COLS);
       uint16_t* outp = args.out + (int64_t)t.row_start * n_out + f;
       const int rows = t.row_count < BN ? t.row_count : BN;
-      constexpr int CW = BN >= 32 ? 32 : 16;  // TMEM columns per load
+      constexpr int CW = 16;  // TMEM columns per load (keeps the epilogue's registers small)
 #pragma unroll 1
       for (int c = 0; c < BN / CW; ++c) {
         if (c * CW >= rows) break;
         uint32_t g[32];
         uint32_t u[32];
-        if (CW == 32) {
-          if (NMAT == 2) tmem_ld2_x32_wait(tbase + c * 32, tbase + BN + c * 32, g, u);
-          else tmem_ld_x32_wait(tbase + c * 32, g);
-        } else {
-          if (NMAT == 2) tmem_ld2_x16_wait(tbase, tbase + BN, g, u);
-          else tmem_ld_x16_wait(tbase, g);
-        }
+        if (NMAT == 2) tmem_ld2_x16_wait(tbase + c * CW, tbase + BN + c * CW, g, u);
+        else tmem_ld_x16_wait(tbase + c * CW, g);
         const int nvalid = rows - c * CW < CW ? rows - c * CW : CW;
         if (NMAT == 2 && pair) {
 #pragma unroll
@@ -485,7 +499,7 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 14) {
+  if (warp == C::W_MMA) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }

@@ -42,6 +42,12 @@ static inline void stage_mark(int i, cudaStream_t st) {
 
 static inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
+// The first 256 bytes of every workspace: the device status word, then the
+// split router's per-token-block counters (both cleared by each call).
+constexpr size_t kStatusSlotBytes = 256;
+constexpr int kSplitRouterMaxT = 64;   // batches up to this size use router_split_kernel
+constexpr int kTileRouterMinT = 256;   // batches above this size use router_logits_tile_kernel
+
 struct Layout {
   // R: flat (token, k) rows; rows: expert rows the buffers hold (R, or fewer
   // when some flat rows are skipped, as on the receiving side of expert parallelism).
@@ -116,7 +122,7 @@ static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T, int64_t rows_c
     o = align256(o + (bytes ? bytes : 1));
     return at;
   };
-  L.status = take(sizeof(int));
+  L.status = take(kStatusSlotBytes);  // status word, then the split router's block counters
   L.logits = take((size_t)T * L.E * 2);
   L.idx = take((size_t)L.R * 4);
   L.w = take((size_t)L.R * 2);
@@ -179,9 +185,44 @@ static int run_router(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
   }
   const uint16_t* xp = static_cast<const uint16_t*>(x);
   const uint16_t* wg = static_cast<const uint16_t*>(wt->router_weight);
-  // One token per CTA for small batches (latency), four for large ones
-  // (fewer re-reads of the router weight).
-  if (L.T <= 256) {
+  // Small batches: logits spread over many CTAs, the last CTA of each token
+  // block routes it. Up to 256 tokens: one token per CTA (latency); beyond,
+  // four per CTA (fewer re-reads of the router weight).
+  if (L.T <= kSplitRouterMaxT) {
+    const int tpb = L.T <= 4 ? 1 : L.T <= 16 ? 2 : 4;
+    const int ngroups = (L.E + 7) / 8;
+    const dim3 grid((unsigned)((ngroups + RS_WARPS - 1) / RS_WARPS), (unsigned)((L.T + tpb - 1) / tpb));
+    uint16_t* lg = logits ? logits : at<uint16_t>(ws, L.logits);
+    int* counter = at<int>(ws, L.status) + 1;
+    const size_t smem = (size_t)tpb * L.E * sizeof(float);
+    const float* rb = wt->router_bias;
+    int32_t* io = at<int32_t>(ws, L.idx);
+    uint16_t* wo = at<uint16_t>(ws, L.w);
+    if (tpb == 1)
+      router_split_kernel<1><<<grid, RS_WARPS * 32, smem, st>>>(xp, L.T, L.D, wg, L.E, rb, L.K, c->norm_topk_prob, io, wo,
+                                                                lg, probs, sg, sig, counter);
+    else if (tpb == 2)
+      router_split_kernel<2><<<grid, RS_WARPS * 32, smem, st>>>(xp, L.T, L.D, wg, L.E, rb, L.K, c->norm_topk_prob, io, wo,
+                                                                lg, probs, sg, sig, counter);
+    else
+      router_split_kernel<4><<<grid, RS_WARPS * 32, smem, st>>>(xp, L.T, L.D, wg, L.E, rb, L.K, c->norm_topk_prob, io, wo,
+                                                                lg, probs, sg, sig, counter);
+    MLXR_LAUNCH_CHECK("router_split_kernel");
+    return MLXR_CU_OK;
+  } else if (L.T > kTileRouterMinT) {
+    uint16_t* lg = logits ? logits : at<uint16_t>(ws, L.logits);
+    static std::atomic<uint64_t> attr_done{0};  // 48 KB of dynamic shared memory
+    if (int rc = ensure_smem_attr(router_logits_tile_kernel, 2 * RT_STAGE, attr_done)) return rc;
+    const dim3 grid((unsigned)((L.E + RT_TE - 1) / RT_TE), (unsigned)((L.T + RT_TT - 1) / RT_TT));
+    router_logits_tile_kernel<<<grid, RT_TILE_THREADS, 2 * RT_STAGE, st>>>(xp, L.T, L.D, wg, L.E, wt->router_bias, lg);
+    MLXR_LAUNCH_CHECK("router_logits_tile_kernel");
+    route_rows_kernel<<<(unsigned)((L.T + RT_ROUTE_WARPS - 1) / RT_ROUTE_WARPS), RT_ROUTE_WARPS * 32,
+                        RT_ROUTE_WARPS * L.E * sizeof(float), st>>>(lg, xp, L.T, L.D, L.E, L.K, c->norm_topk_prob,
+                                                                    at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w),
+                                                                    probs, sg, sig);
+    MLXR_LAUNCH_CHECK("route_rows_kernel");
+    return MLXR_CU_OK;
+  } else if (L.T <= 256) {
     router_fused_kernel<1><<<(unsigned)L.T, RT_THREADS, L.E * sizeof(float), st>>>(
         xp, L.T, L.D, wg, L.E, wt->router_bias, L.K, c->norm_topk_prob, at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w),
         logits, probs, sg, sig);
@@ -409,7 +450,7 @@ int mlxr_cu_moe_block_forward(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_w
   const Layout L = make_layout(cfg, num_tokens);
   if (int rc = check_ws(L, workspace, workspace_bytes)) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  MLXR_CUDA_TRY(cudaMemsetAsync(at<int>(workspace, L.status), 0, sizeof(int), st));
+  MLXR_CUDA_TRY(cudaMemsetAsync(at<int>(workspace, L.status), 0, kStatusSlotBytes, st));
   if (num_tokens == 0) return MLXR_CU_OK;
   MLXR_CHECK_ARG(x && out, "moe: x/out is NULL");
   MLXR_CHECK_ARG(aligned16(x) && aligned16(out), "moe: x and out must be 16-byte aligned");
@@ -554,7 +595,7 @@ int mlxr_cu_moe_router(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights*
   const Layout L = make_layout(cfg, num_tokens);
   if (int rc = check_ws(L, workspace, workspace_bytes)) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  MLXR_CUDA_TRY(cudaMemsetAsync(at<int>(workspace, L.status), 0, sizeof(int), st));
+  MLXR_CUDA_TRY(cudaMemsetAsync(at<int>(workspace, L.status), 0, kStatusSlotBytes, st));
   if (num_tokens == 0) return MLXR_CU_OK;
   MLXR_CHECK_ARG(x && indices && topk_weights, "moe_router: x/indices/weights is NULL");
   uint16_t* lg = logits ? static_cast<uint16_t*>(logits) : at<uint16_t>(workspace, L.logits);
@@ -577,7 +618,7 @@ int mlxr_cu_moe_permute(const mlxr_cu_moe_config* cfg, const int32_t* indices, i
   MLXR_CHECK_ARG(indices && x && counts && offsets && sorted_rows && inverse && x_sorted, "moe_permute: NULL argument");
   MLXR_CHECK_ARG(aligned16(x) && aligned16(x_sorted), "moe_permute: x and x_sorted must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  MLXR_CUDA_TRY(cudaMemsetAsync(at<int>(workspace, L.status), 0, sizeof(int), st));
+  MLXR_CUDA_TRY(cudaMemsetAsync(at<int>(workspace, L.status), 0, kStatusSlotBytes, st));
   return run_permute(L, indices, x, workspace, counts, offsets, sorted_rows, inverse, static_cast<uint16_t*>(x_sorted),
                      0, st);
 }
@@ -626,7 +667,7 @@ int mlxr_cu_moe_ep_dispatch(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_wei
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   void* ws = workspace;
   const Layout L = make_layout(cfg, num_tokens);
-  MLXR_CUDA_TRY(cudaMemsetAsync(at<int>(ws, L.status), 0, sizeof(int), st));
+  MLXR_CUDA_TRY(cudaMemsetAsync(at<int>(ws, L.status), 0, kStatusSlotBytes, st));
   if (num_tokens == 0) {
     MLXR_CUDA_TRY(cudaMemsetAsync(send_counts, 0, (size_t)world * 2 * 4, st));
     return MLXR_CU_OK;

@@ -233,6 +233,237 @@ __global__ void __launch_bounds__(RT_THREADS) router_fused_kernel(
   }
 }
 
+// Small batches: the logits of TPB tokens are spread over many CTAs (warp w
+// of CTA (gx, gy) computes expert group 4*gx + w for tokens gy*TPB ...), in
+// the same per-logit FMA order as router_fused_kernel, into the bf16 logits
+// buffer lg [T, E]. The CTA that finishes the last expert group of a token
+// block (counter[gy], zero on entry) routes that block's tokens. This keeps
+// every SM streaming a slice of the router weight instead of one CTA per
+// token streaming all of it.
+constexpr int RS_WARPS = 4;
+
+template <int TPB>
+__global__ void __launch_bounds__(RS_WARPS * 32) router_split_kernel(
+    const uint16_t* __restrict__ x, int64_t T, int D, const uint16_t* __restrict__ wg, int E,
+    const float* __restrict__ bias, int K, int renorm, int32_t* __restrict__ idx_out, uint16_t* __restrict__ w_out,
+    uint16_t* __restrict__ lg, uint16_t* __restrict__ probs_out, SharedGateArgs sg, float* __restrict__ sig_out,
+    int* __restrict__ counter) {
+  extern __shared__ float s_lg[];  // [TPB][E] (last CTA of a token block only)
+  __shared__ int s_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t0 = (int64_t)blockIdx.y * TPB;
+  const int nchunks = D / 8;
+  const int ngroups = (E + 7) / 8;
+  const int g = blockIdx.x * RS_WARPS + warp;
+  if (g < ngroups) {
+    const uint4* xr[TPB];
+#pragma unroll
+    for (int i = 0; i < TPB; ++i) xr[i] = reinterpret_cast<const uint4*>(x + (t0 + i < T ? t0 + i : T - 1) * D);
+    const int e0 = g * 8;
+    const uint4* wr[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) wr[j] = reinterpret_cast<const uint4*>(wg + (int64_t)(e0 + j < E ? e0 + j : E - 1) * D);
+    float acc[TPB][8];
+#pragma unroll
+    for (int i = 0; i < TPB; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+#pragma unroll 2
+    for (int c = lane; c < nchunks; c += 32) {
+      uint4 xv[TPB], wv[8];
+#pragma unroll
+      for (int i = 0; i < TPB; ++i) xv[i] = __ldg(xr[i] + c);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) wv[j] = __ldg(wr[j] + c);
+#pragma unroll
+      for (int el = 0; el < 8; ++el) {
+        float xf[TPB], wf[8];
+#pragma unroll
+        for (int i = 0; i < TPB; ++i) {
+          const uint32_t wd = el < 2 ? xv[i].x : el < 4 ? xv[i].y : el < 6 ? xv[i].z : xv[i].w;
+          xf[i] = (el & 1) ? bf_hi(wd) : bf_lo(wd);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t wd = el < 2 ? wv[j].x : el < 4 ? wv[j].y : el < 6 ? wv[j].z : wv[j].w;
+          wf[j] = (el & 1) ? bf_hi(wd) : bf_lo(wd);
+        }
+#pragma unroll
+        for (int i = 0; i < TPB; ++i)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(xf[i], wf[j], acc[i][j]);
+      }
+    }
+    float mine = 0.0f;
+#pragma unroll
+    for (int i = 0; i < TPB; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float v = acc[i][j];
+#pragma unroll
+        for (int s = 16; s >= 1; s >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, s));
+        if (lane == i * 8 + j) mine = v;
+      }
+    if (lane < TPB * 8) {
+      const int i = lane >> 3, e = e0 + (lane & 7);
+      if (e < E && t0 + i < T) {
+        const float b = bias ? bias[e] : 0.0f;
+        lg[(t0 + i) * E + e] = f32_to_bf16_bits(__fadd_rn(mine, b));
+      }
+    }
+  }
+  // Publish this CTA's logits; the last CTA of the token block routes it.
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = (atomicAdd(&counter[blockIdx.y], 1) == (int)gridDim.x - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int ntok = (int)min((int64_t)TPB, T - t0);
+  for (int i = threadIdx.x; i < ntok * E; i += blockDim.x)
+    s_lg[i] = bf16_bits_to_f32(__ldcg(lg + t0 * E + i));
+  __syncthreads();
+  for (int i = warp; i < ntok; i += RS_WARPS) {
+    const int64_t t = t0 + i;
+    route_token_warp(s_lg + i * E, t, E, K, renorm, lane, idx_out, w_out, probs_out);
+    if (sig_out) shared_gate_warp(x + t * D, D, sg, lane, sig_out + t);
+  }
+}
+
+// Large batches: logits in CTA tiles of 32 tokens x 16 experts staged
+// through shared memory, then a routing kernel (one warp per token). Warp w
+// of a tile owns tokens 8*(w%4) .. +7 and experts 8*(w/4) .. +7; lane j
+// keeps the contract's chain over chunks j, j+32, ... of D for each of its
+// 64 (token, expert) pairs, so each logit is the same fp32 value as in
+// router_fused_kernel. Every 32-chunk block of D is copied to shared memory
+// once per tile (16-byte cp.async, double-buffered) and read by 2 or 4
+// warps, instead of every warp streaming x and the router weight itself.
+constexpr int RT_TT = 32, RT_TE = 16, RT_TILE_THREADS = 256;
+constexpr int RT_ROWB = 32 * 16;                        // bytes of one row's 32-chunk block
+constexpr int RT_STAGE = (RT_TT + RT_TE) * RT_ROWB;     // 24 KB
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__global__ void __launch_bounds__(RT_TILE_THREADS) router_logits_tile_kernel(const uint16_t* __restrict__ x, int64_t T,
+                                                                           int D, const uint16_t* __restrict__ wg,
+                                                                           int E, const float* __restrict__ bias,
+                                                                           uint16_t* __restrict__ lg) {
+  extern __shared__ __align__(16) uint8_t rt_smem[];  // 2 stages of [32 x rows | 16 w rows][512 B]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e0 = blockIdx.x * RT_TE;
+  const int64_t t0 = (int64_t)blockIdx.y * RT_TT;
+  const int nchunks = D / 8;
+  const int nblocks = (nchunks + 31) / 32;
+  const uint32_t sbase = smem_u32(rt_smem);
+  auto stage_in = [&](int m, int st) {
+    // 48 rows x 32 chunks = 1536 copies of 16 B, 6 per thread.
+    for (int q = threadIdx.x; q < (RT_TT + RT_TE) * 32; q += RT_TILE_THREADS) {
+      const int r = q >> 5, cj = q & 31;
+      const int c = m * 32 + cj;
+      const uint32_t dst = sbase + (uint32_t)(st * RT_STAGE + r * RT_ROWB + cj * 16);
+      if (r < RT_TT) {
+        const int64_t t = t0 + r;
+        const bool ok = t < T && c < nchunks;
+        cp_async16(dst, x + (ok ? t : 0) * (int64_t)D + (ok ? c : 0) * 8, ok);
+      } else {
+        const int e = e0 + (r - RT_TT);
+        const bool ok = e < E && c < nchunks;
+        cp_async16(dst, wg + (ok ? e : 0) * (int64_t)D + (ok ? c : 0) * 8, ok);
+      }
+    }
+    cp_async_commit();
+  };
+  const int tg = warp & 3, eg = warp >> 2;
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+  stage_in(0, 0);
+  for (int m = 0; m < nblocks; ++m) {
+    if (m + 1 < nblocks) {
+      stage_in(m + 1, (m + 1) & 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    if (m * 32 + lane < nchunks) {
+      const uint8_t* sx = rt_smem + (m & 1) * RT_STAGE + (tg * 8) * RT_ROWB + lane * 16;
+      const uint8_t* sw = rt_smem + (m & 1) * RT_STAGE + (RT_TT + eg * 8) * RT_ROWB + lane * 16;
+      uint4 xv[8], wv[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) xv[i] = *reinterpret_cast<const uint4*>(sx + i * RT_ROWB);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) wv[j] = *reinterpret_cast<const uint4*>(sw + j * RT_ROWB);
+#pragma unroll
+      for (int el = 0; el < 8; ++el) {
+        float xf[8], wf[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t wd = el < 2 ? xv[i].x : el < 4 ? xv[i].y : el < 6 ? xv[i].z : xv[i].w;
+          xf[i] = (el & 1) ? bf_hi(wd) : bf_lo(wd);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t wd = el < 2 ? wv[j].x : el < 4 ? wv[j].y : el < 6 ? wv[j].z : wv[j].w;
+          wf[j] = (el & 1) ? bf_hi(wd) : bf_lo(wd);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(xf[i], wf[j], acc[i][j]);
+      }
+    }
+    __syncthreads();  // the stage is refilled by the next iteration's copies
+  }
+  float mine[2] = {0.0f, 0.0f};
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float v = acc[i][j];
+#pragma unroll
+      for (int s = 16; s >= 1; s >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, s));
+      const int idx = i * 8 + j;  // lane idx & 31 keeps pair idx
+      if (lane == (idx & 31)) mine[idx >> 5] = v;
+    }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int idx = h * 32 + lane;
+    const int i = idx >> 3, j = idx & 7;
+    const int64_t t = t0 + tg * 8 + i;
+    const int e = e0 + eg * 8 + j;
+    if (t < T && e < E) {
+      const float b = bias ? bias[e] : 0.0f;
+      lg[t * E + e] = f32_to_bf16_bits(__fadd_rn(mine[h], b));
+    }
+  }
+}
+
+// Softmax / top-K / renormalisation (and the shared-expert gate) of one
+// token per warp from the bf16 logits lg [T, E].
+constexpr int RT_ROUTE_WARPS = 8;
+__global__ void __launch_bounds__(RT_ROUTE_WARPS * 32) route_rows_kernel(
+    const uint16_t* __restrict__ lg, const uint16_t* __restrict__ x, int64_t T, int D, int E, int K, int renorm,
+    int32_t* __restrict__ idx_out, uint16_t* __restrict__ w_out, uint16_t* __restrict__ probs_out, SharedGateArgs sg,
+    float* __restrict__ sig_out) {
+  extern __shared__ float s_row[];  // [RT_ROUTE_WARPS][E]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * RT_ROUTE_WARPS + warp;
+  if (t >= T) return;
+  float* row = s_row + warp * E;
+  for (int e = lane; e < E; e += 32) row[e] = bf16_bits_to_f32(lg[t * E + e]);
+  __syncwarp();
+  route_token_warp(row, t, E, K, renorm, lane, idx_out, w_out, probs_out);
+  if (sig_out) shared_gate_warp(x + t * D, D, sg, lane, sig_out + t);
+}
+
 // ------------------------------------------------------- permutation ----
 constexpr int PERM_ROWS = 2048;  // flat rows per permute block (8 warps x 256)
 constexpr int PERM_MAX_E = 1024;
