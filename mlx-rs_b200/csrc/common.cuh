@@ -8,6 +8,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <utility>
 
 #include "../../include/mlxr_moe.h"
 
@@ -33,6 +34,32 @@ inline int ensure_smem_attr(F* func, int bytes, std::atomic<uint64_t>& done) {
   if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
   if (bit) done.fetch_or(bit, std::memory_order_acq_rel);
   return MLXR_CU_OK;
+}
+
+// Programmatic dependent launch. Every kernel of the block is launched with
+// launch_pdl (the launch may begin while the previous kernel in the stream
+// is still running) and starts with pdl_wait() before it touches global
+// memory: griddepcontrol.wait returns once the previous grid has completed
+// and its writes are visible, so the overlap only hides launch latency and
+// prologues (barrier set-up, tensor-memory allocation). pdl_launch_dependents()
+// lets the next kernel begin launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 #define MLXR_CHECK_ARG(cond, ...)                                                  \

@@ -89,7 +89,7 @@ static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
   a.pair = p.pair;
   a.status = p.status;
   const int grid = p.grid > 0 ? p.grid : num_sms_current();
-  kern<<<grid, C::NUM_THREADS, C::SMEM_BYTES, st>>>(ta0, ta1, tb, a);
+  launch_pdl(kern, grid, C::NUM_THREADS, C::SMEM_BYTES, st, ta0, ta1, tb, a);
   MLXR_LAUNCH_CHECK("grouped_dequant_gemm_kernel");
   return MLXR_CU_OK;
 }

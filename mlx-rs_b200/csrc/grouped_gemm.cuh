@@ -244,6 +244,10 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Everything above touched only this CTA's shared and tensor memory; the
+  // tile list and operands come from the previous kernel.
+  pdl_wait();
+  pdl_launch_dependents();
 
   const int n_out = args.n_out;
   const int pair = NMAT == 2 ? args.pair : 0;

@@ -189,8 +189,10 @@ static int run_router(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
   // block routes it. Up to 256 tokens: one token per CTA (latency); beyond,
   // four per CTA (fewer re-reads of the router weight).
   if (L.T <= kSplitRouterMaxT) {
+    // 2 experts per warp; 1, 2 or 4 tokens per block.
     const int tpb = L.T <= 4 ? 1 : L.T <= 16 ? 2 : 4;
-    const int ngroups = (L.E + 7) / 8;
+    constexpr int EPW = 2;
+    const int ngroups = (L.E + EPW - 1) / EPW;
     const dim3 grid((unsigned)((ngroups + RS_WARPS - 1) / RS_WARPS), (unsigned)((L.T + tpb - 1) / tpb));
     uint16_t* lg = logits ? logits : at<uint16_t>(ws, L.logits);
     int* counter = at<int>(ws, L.status) + 1;
@@ -198,15 +200,16 @@ static int run_router(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
     const float* rb = wt->router_bias;
     int32_t* io = at<int32_t>(ws, L.idx);
     uint16_t* wo = at<uint16_t>(ws, L.w);
+    const int rn = c->norm_topk_prob;
     if (tpb == 1)
-      router_split_kernel<1><<<grid, RS_WARPS * 32, smem, st>>>(xp, L.T, L.D, wg, L.E, rb, L.K, c->norm_topk_prob, io, wo,
-                                                                lg, probs, sg, sig, counter);
+      launch_pdl(router_split_kernel<1, EPW, 8>, grid, RS_WARPS * 32, smem, st, xp, L.T, L.D, wg, L.E, rb, L.K, rn, io, wo, lg,
+                                                                        probs, sg, sig, counter);
     else if (tpb == 2)
-      router_split_kernel<2><<<grid, RS_WARPS * 32, smem, st>>>(xp, L.T, L.D, wg, L.E, rb, L.K, c->norm_topk_prob, io, wo,
-                                                                lg, probs, sg, sig, counter);
+      launch_pdl(router_split_kernel<2, EPW, 6>, grid, RS_WARPS * 32, smem, st, xp, L.T, L.D, wg, L.E, rb, L.K, rn, io, wo, lg,
+                                                                        probs, sg, sig, counter);
     else
-      router_split_kernel<4><<<grid, RS_WARPS * 32, smem, st>>>(xp, L.T, L.D, wg, L.E, rb, L.K, c->norm_topk_prob, io, wo,
-                                                                lg, probs, sg, sig, counter);
+      launch_pdl(router_split_kernel<4, EPW, 4>, grid, RS_WARPS * 32, smem, st, xp, L.T, L.D, wg, L.E, rb, L.K, rn, io, wo, lg,
+                                                                        probs, sg, sig, counter);
     MLXR_LAUNCH_CHECK("router_split_kernel");
     return MLXR_CU_OK;
   } else if (L.T > kTileRouterMinT) {
@@ -214,20 +217,19 @@ static int run_router(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
     static std::atomic<uint64_t> attr_done{0};  // 48 KB of dynamic shared memory
     if (int rc = ensure_smem_attr(router_logits_tile_kernel, 2 * RT_STAGE, attr_done)) return rc;
     const dim3 grid((unsigned)((L.E + RT_TE - 1) / RT_TE), (unsigned)((L.T + RT_TT - 1) / RT_TT));
-    router_logits_tile_kernel<<<grid, RT_TILE_THREADS, 2 * RT_STAGE, st>>>(xp, L.T, L.D, wg, L.E, wt->router_bias, lg);
+    launch_pdl(router_logits_tile_kernel, grid, RT_TILE_THREADS, 2 * RT_STAGE, st, xp, L.T, L.D, wg, L.E, wt->router_bias, lg);
     MLXR_LAUNCH_CHECK("router_logits_tile_kernel");
-    route_rows_kernel<<<(unsigned)((L.T + RT_ROUTE_WARPS - 1) / RT_ROUTE_WARPS), RT_ROUTE_WARPS * 32,
-                        RT_ROUTE_WARPS * L.E * sizeof(float), st>>>(lg, xp, L.T, L.D, L.E, L.K, c->norm_topk_prob,
+    launch_pdl(route_rows_kernel, (unsigned)((L.T + RT_ROUTE_WARPS - 1) / RT_ROUTE_WARPS), RT_ROUTE_WARPS * 32, RT_ROUTE_WARPS * L.E * sizeof(float), st, lg, xp, L.T, L.D, L.E, L.K, c->norm_topk_prob,
                                                                     at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w),
                                                                     probs, sg, sig);
     MLXR_LAUNCH_CHECK("route_rows_kernel");
     return MLXR_CU_OK;
   } else if (L.T <= 256) {
-    router_fused_kernel<1><<<(unsigned)L.T, RT_THREADS, L.E * sizeof(float), st>>>(
+    launch_pdl(router_fused_kernel<1>, (unsigned)L.T, RT_THREADS, L.E * sizeof(float), st, 
         xp, L.T, L.D, wg, L.E, wt->router_bias, L.K, c->norm_topk_prob, at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w),
         logits, probs, sg, sig);
   } else {
-    router_fused_kernel<4><<<(unsigned)((L.T + 3) / 4), RT_THREADS, 4 * L.E * sizeof(float), st>>>(
+    launch_pdl(router_fused_kernel<4>, (unsigned)((L.T + 3) / 4), RT_THREADS, 4 * L.E * sizeof(float), st, 
         xp, L.T, L.D, wg, L.E, wt->router_bias, L.K, c->norm_topk_prob, at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w),
         logits, probs, sg, sig);
   }
@@ -244,24 +246,24 @@ static int run_permute(const Layout& L, const int32_t* idx, const void* x, void*
   TileListOut lsh{L.Is > 0 ? at<GemmTile>(ws, L.tsh) : nullptr, at<int32_t>(ws, L.nsh), L.bns, L.max_tsh};
   if (L.nblk == 1) {
     // Every flat row fits one block: count, scan, tile lists and ranks in one CTA.
-    permute_small_kernel<<<1, 1024, 9 * L.E * sizeof(int), st>>>(idx, L.R, L.E, L.T, counts, offsets, sorted, inv, l1,
+    launch_pdl(permute_small_kernel, 1, 1024, 9 * L.E * sizeof(int), st, idx, L.R, L.E, L.T, counts, offsets, sorted, inv, l1,
                                                                   l2, lsh, skip, status);
     MLXR_LAUNCH_CHECK("permute_small_kernel");
   } else {
-    permute_count_kernel<<<L.nblk, 256, L.E * sizeof(int), st>>>(idx, L.R, L.E, at<int32_t>(ws, L.bcounts), skip,
+    launch_pdl(permute_count_kernel, L.nblk, 256, L.E * sizeof(int), st, idx, L.R, L.E, at<int32_t>(ws, L.bcounts), skip,
                                                                  status);
     MLXR_LAUNCH_CHECK("permute_count_kernel");
-    permute_scan_kernel<<<1, 1024, 0, st>>>(at<int32_t>(ws, L.bcounts), L.nblk, L.E, L.T, at<int32_t>(ws, L.bbase),
+    launch_pdl(permute_scan_kernel, 1, 1024, 0, st, at<int32_t>(ws, L.bcounts), L.nblk, L.E, L.T, at<int32_t>(ws, L.bbase),
                                             counts, offsets, l1, l2, lsh);
     MLXR_LAUNCH_CHECK("permute_scan_kernel");
-    permute_scatter_kernel<<<L.nblk, 256, 8 * L.E * sizeof(int), st>>>(idx, L.R, L.E, at<int32_t>(ws, L.bbase),
+    launch_pdl(permute_scatter_kernel, L.nblk, 256, 8 * L.E * sizeof(int), st, idx, L.R, L.E, at<int32_t>(ws, L.bbase),
                                                                        sorted, inv);
     MLXR_LAUNCH_CHECK("permute_scatter_kernel");
   }
   if (L.R > 0 && L.rows > 0) {
     const int64_t gblocks = (L.rows + 7) / 8;
     const int gather_grid = (int)(gblocks < 4 * 148 ? gblocks : 4 * 148);
-    permute_gather_kernel<<<gather_grid, 256, 0, st>>>(sorted, L.rows, L.R, L.K, static_cast<const uint16_t*>(x), L.D,
+    launch_pdl(permute_gather_kernel, gather_grid, 256, 0, st, sorted, L.rows, L.R, L.K, static_cast<const uint16_t*>(x), L.D,
                                                        kperm, xs, skip ? offsets + L.E : nullptr, status);
     MLXR_LAUNCH_CHECK("permute_gather_kernel");
   }
@@ -349,7 +351,7 @@ static int run_shared(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
     // A padded (>= 256 rows) and, for 4-bit weights, K-order-permuted copy.
     const int64_t gblocks = (L.T + 7) / 8;
     const int grid = (int)(gblocks < 4 * 148 ? gblocks : 4 * 148);
-    permute_gather_kernel<<<grid, 256, 0, st>>>(nullptr, L.T, L.T, 1, static_cast<const uint16_t*>(x), L.D, kperm,
+    launch_pdl(permute_gather_kernel, grid, 256, 0, st, nullptr, L.T, L.T, 1, static_cast<const uint16_t*>(x), L.D, kperm,
                                                 at<uint16_t>(ws, L.xpad), nullptr, status);
     MLXR_LAUNCH_CHECK("permute_gather_kernel(shared)");
     act = at<uint16_t>(ws, L.xpad);
@@ -466,7 +468,7 @@ int mlxr_cu_moe_block_forward(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_w
   stage_mark(4, st);
   if (int rc = run_shared(cfg, weights, L, x, ws, st)) return rc;
   stage_mark(5, st);
-  combine_kernel<<<(unsigned)L.T, L.D >= 2048 ? 256 : 128, 0, st>>>(at<uint16_t>(ws, L.y), at<int32_t>(ws, L.inv), at<uint16_t>(ws, L.w),
+  launch_pdl(combine_kernel, (unsigned)L.T, L.D >= 2048 ? 256 : 128, 0, st, at<uint16_t>(ws, L.y), at<int32_t>(ws, L.inv), at<uint16_t>(ws, L.w),
                                                 L.K, L.D, L.T, L.Is > 0 ? at<uint16_t>(ws, L.ysh) : nullptr,
                                                 at<float>(ws, L.sig), static_cast<uint16_t*>(out),
                                                 at<int>(ws, L.status));
@@ -679,7 +681,7 @@ int mlxr_cu_moe_ep_dispatch(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_wei
   const int K = cfg->num_experts_per_tok;
   const int64_t R = L.R;
   int32_t* dest = at<int32_t>(ws, dest_off);
-  ep_pair_dest_kernel<<<(unsigned)((R + 255) / 256), 256, 0, st>>>(at<int32_t>(ws, L.idx), num_tokens, K, world, dest,
+  launch_pdl(ep_pair_dest_kernel, (unsigned)((R + 255) / 256), 256, 0, st, at<int32_t>(ws, L.idx), num_tokens, K, world, dest,
                                                                     at<int>(ws, L.status));
   MLXR_LAUNCH_CHECK("ep_pair_dest_kernel");
   // Stable sort of the pairs by destination rank: the block permutation with
@@ -694,9 +696,9 @@ int mlxr_cu_moe_ep_dispatch(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_wei
   if (int rc = run_permute(P, dest, x, ws, at<int32_t>(ws, L.counts), at<int32_t>(ws, L.offsets),
                            at<int32_t>(ws, L.sorted), pair_pos, static_cast<uint16_t*>(x_send), 0, st, 1))
     return rc;
-  ep_counts_kernel<<<1, 1024, 0, st>>>(at<int32_t>(ws, L.idx), R, world, at<int32_t>(ws, L.counts), send_counts);
+  launch_pdl(ep_counts_kernel, 1, 1024, 0, st, at<int32_t>(ws, L.idx), R, world, at<int32_t>(ws, L.counts), send_counts);
   MLXR_LAUNCH_CHECK("ep_counts_kernel");
-  ep_pair_meta_kernel<<<(unsigned)((num_tokens + 127) / 128), 128, 0, st>>>(
+  launch_pdl(ep_pair_meta_kernel, (unsigned)((num_tokens + 127) / 128), 128, 0, st, 
       at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w), pair_pos, num_tokens, K, world, P.rows, meta_send,
       at<int>(ws, L.status));
   MLXR_LAUNCH_CHECK("ep_pair_meta_kernel");
@@ -722,7 +724,7 @@ int mlxr_cu_moe_ep_experts(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weig
   if (num_pairs == 0) return MLXR_CU_OK;
   MLXR_CHECK_ARG(x_recv && meta_recv && partial && aligned16(x_recv) && aligned16(partial),
                  "moe_ep_experts: NULL or misaligned argument (x_recv and partial need 16-byte alignment)");
-  ep_slot_expert_kernel<<<(unsigned)((L.R + 255) / 256), 256, 0, st>>>(meta_recv, L.R, L.E, at<int32_t>(ws, L.idx),
+  launch_pdl(ep_slot_expert_kernel, (unsigned)((L.R + 255) / 256), 256, 0, st, meta_recv, L.R, L.E, at<int32_t>(ws, L.idx),
                                                                         at<int>(ws, L.status));
   MLXR_LAUNCH_CHECK("ep_slot_expert_kernel");
   if (int rc = run_permute(L, at<int32_t>(ws, L.idx), x_recv, ws, at<int32_t>(ws, L.counts), at<int32_t>(ws, L.offsets),
@@ -733,7 +735,7 @@ int mlxr_cu_moe_ep_experts(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weig
     MLXR_CUDA_TRY(cudaMemsetAsync(partial, 0, (size_t)num_pairs * L.D * 2, st));
     return MLXR_CU_OK;
   }
-  ep_reduce_kernel<<<(unsigned)num_pairs, L.D >= 2048 ? 256 : 128, 0, st>>>(
+  launch_pdl(ep_reduce_kernel, (unsigned)num_pairs, L.D >= 2048 ? 256 : 128, 0, st, 
       at<uint16_t>(ws, L.y), at<int32_t>(ws, L.inv), meta_recv, L.K, L.D, L.rows, static_cast<uint16_t*>(partial),
       at<int>(ws, L.status));
   MLXR_LAUNCH_CHECK("ep_reduce_kernel");
@@ -757,14 +759,14 @@ int mlxr_cu_moe_ep_combine(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weig
   if (L.Is > 0) {
     MLXR_CHECK_ARG(shared_gate != nullptr && weights != nullptr, "moe_ep_combine: shared_gate / weights is NULL");
     // The block forward gets the shared tile list from its permute; here it is built alone.
-    shared_tiles_kernel<<<(unsigned)((L.max_tsh + 255) / 256), 256, 0, st>>>(at<GemmTile>(ws, L.tsh),
+    launch_pdl(shared_tiles_kernel, (unsigned)((L.max_tsh + 255) / 256), 256, 0, st, at<GemmTile>(ws, L.tsh),
                                                                              at<int32_t>(ws, L.nsh), L.T, L.bns,
                                                                              L.max_tsh);
     MLXR_LAUNCH_CHECK("shared_tiles_kernel");
     if (int rc = run_shared(cfg, weights, L, x, ws, st)) return rc;
     ysh = at<uint16_t>(ws, L.ysh);
   }
-  ep_combine_kernel<<<(unsigned)L.T, L.D >= 2048 ? 256 : 128, 0, st>>>(
+  launch_pdl(ep_combine_kernel, (unsigned)L.T, L.D >= 2048 ? 256 : 128, 0, st, 
       static_cast<const uint16_t*>(partial_back), pair_pos, L.K, L.D, num_pairs, ysh, shared_gate,
       static_cast<uint16_t*>(out), at<int>(ws, L.status));
   MLXR_LAUNCH_CHECK("ep_combine_kernel");

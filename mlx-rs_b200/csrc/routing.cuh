@@ -161,6 +161,8 @@ __global__ void __launch_bounds__(RT_THREADS) router_fused_kernel(
     const float* __restrict__ bias, int K, int renorm, int32_t* __restrict__ idx_out, uint16_t* __restrict__ w_out,
     uint16_t* __restrict__ logits_out, uint16_t* __restrict__ probs_out, SharedGateArgs sg,
     float* __restrict__ sig_out) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ float s_lg[];  // [TPB][E]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t t0 = (int64_t)blockIdx.x * TPB;
@@ -234,78 +236,91 @@ __global__ void __launch_bounds__(RT_THREADS) router_fused_kernel(
 }
 
 // Small batches: the logits of TPB tokens are spread over many CTAs (warp w
-// of CTA (gx, gy) computes expert group 4*gx + w for tokens gy*TPB ...), in
-// the same per-logit FMA order as router_fused_kernel, into the bf16 logits
-// buffer lg [T, E]. The CTA that finishes the last expert group of a token
-// block (counter[gy], zero on entry) routes that block's tokens. This keeps
-// every SM streaming a slice of the router weight instead of one CTA per
-// token streaming all of it.
+// of CTA (gx, gy) computes the EPW experts of group RS_WARPS*gx + w for
+// tokens gy*TPB ...), in the same per-logit FMA order as
+// router_fused_kernel, into the bf16 logits buffer lg [T, E]. Each lane
+// issues the loads of UNR chunk steps before using them, so a warp keeps
+// (TPB + EPW) * UNR 16-byte loads in flight: with few tokens the kernel is
+// bound by memory latency, not arithmetic. The CTA that finishes the last
+// expert group of a token block (counter[gy], zero on entry) routes it.
 constexpr int RS_WARPS = 4;
 
-template <int TPB>
+template <int TPB, int EPW, int UNR>
 __global__ void __launch_bounds__(RS_WARPS * 32) router_split_kernel(
     const uint16_t* __restrict__ x, int64_t T, int D, const uint16_t* __restrict__ wg, int E,
     const float* __restrict__ bias, int K, int renorm, int32_t* __restrict__ idx_out, uint16_t* __restrict__ w_out,
     uint16_t* __restrict__ lg, uint16_t* __restrict__ probs_out, SharedGateArgs sg, float* __restrict__ sig_out,
     int* __restrict__ counter) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ float s_lg[];  // [TPB][E] (last CTA of a token block only)
   __shared__ int s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t t0 = (int64_t)blockIdx.y * TPB;
   const int nchunks = D / 8;
-  const int ngroups = (E + 7) / 8;
+  const int ngroups = (E + EPW - 1) / EPW;
   const int g = blockIdx.x * RS_WARPS + warp;
   if (g < ngroups) {
     const uint4* xr[TPB];
 #pragma unroll
     for (int i = 0; i < TPB; ++i) xr[i] = reinterpret_cast<const uint4*>(x + (t0 + i < T ? t0 + i : T - 1) * D);
-    const int e0 = g * 8;
-    const uint4* wr[8];
+    const int e0 = g * EPW;
+    const uint4* wr[EPW];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) wr[j] = reinterpret_cast<const uint4*>(wg + (int64_t)(e0 + j < E ? e0 + j : E - 1) * D);
-    float acc[TPB][8];
+    for (int j = 0; j < EPW; ++j)
+      wr[j] = reinterpret_cast<const uint4*>(wg + (int64_t)(e0 + j < E ? e0 + j : E - 1) * D);
+    float acc[TPB][EPW];
 #pragma unroll
     for (int i = 0; i < TPB; ++i)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
-#pragma unroll 2
-    for (int c = lane; c < nchunks; c += 32) {
-      uint4 xv[TPB], wv[8];
+      for (int j = 0; j < EPW; ++j) acc[i][j] = 0.0f;
+    for (int cb = 0; cb < nchunks; cb += 32 * UNR) {
+      uint4 xv[UNR][TPB], wv[UNR][EPW];
 #pragma unroll
-      for (int i = 0; i < TPB; ++i) xv[i] = __ldg(xr[i] + c);
+      for (int u = 0; u < UNR; ++u) {
+        const int c = cb + 32 * u + lane;
+        if (c < nchunks) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) wv[j] = __ldg(wr[j] + c);
+          for (int i = 0; i < TPB; ++i) xv[u][i] = __ldg(xr[i] + c);
 #pragma unroll
-      for (int el = 0; el < 8; ++el) {
-        float xf[TPB], wf[8];
-#pragma unroll
-        for (int i = 0; i < TPB; ++i) {
-          const uint32_t wd = el < 2 ? xv[i].x : el < 4 ? xv[i].y : el < 6 ? xv[i].z : xv[i].w;
-          xf[i] = (el & 1) ? bf_hi(wd) : bf_lo(wd);
+          for (int j = 0; j < EPW; ++j) wv[u][j] = __ldg(wr[j] + c);
         }
+      }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t wd = el < 2 ? wv[j].x : el < 4 ? wv[j].y : el < 6 ? wv[j].z : wv[j].w;
-          wf[j] = (el & 1) ? bf_hi(wd) : bf_lo(wd);
+      for (int u = 0; u < UNR; ++u) {
+        if (cb + 32 * u + lane >= nchunks) break;
+#pragma unroll
+        for (int el = 0; el < 8; ++el) {
+          float xf[TPB], wf[EPW];
+#pragma unroll
+          for (int i = 0; i < TPB; ++i) {
+            const uint32_t wd = el < 2 ? xv[u][i].x : el < 4 ? xv[u][i].y : el < 6 ? xv[u][i].z : xv[u][i].w;
+            xf[i] = (el & 1) ? bf_hi(wd) : bf_lo(wd);
+          }
+#pragma unroll
+          for (int j = 0; j < EPW; ++j) {
+            const uint32_t wd = el < 2 ? wv[u][j].x : el < 4 ? wv[u][j].y : el < 6 ? wv[u][j].z : wv[u][j].w;
+            wf[j] = (el & 1) ? bf_hi(wd) : bf_lo(wd);
+          }
+#pragma unroll
+          for (int i = 0; i < TPB; ++i)
+#pragma unroll
+            for (int j = 0; j < EPW; ++j) acc[i][j] = __fmaf_rn(xf[i], wf[j], acc[i][j]);
         }
-#pragma unroll
-        for (int i = 0; i < TPB; ++i)
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(xf[i], wf[j], acc[i][j]);
       }
     }
     float mine = 0.0f;
 #pragma unroll
     for (int i = 0; i < TPB; ++i)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < EPW; ++j) {
         float v = acc[i][j];
 #pragma unroll
         for (int s = 16; s >= 1; s >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, s));
-        if (lane == i * 8 + j) mine = v;
+        if (lane == i * EPW + j) mine = v;
       }
-    if (lane < TPB * 8) {
-      const int i = lane >> 3, e = e0 + (lane & 7);
+    if (lane < TPB * EPW) {
+      const int i = lane / EPW, e = e0 + lane % EPW;
       if (e < E && t0 + i < T) {
         const float b = bias ? bias[e] : 0.0f;
         lg[(t0 + i) * E + e] = f32_to_bf16_bits(__fadd_rn(mine, b));
@@ -353,6 +368,8 @@ __global__ void __launch_bounds__(RT_TILE_THREADS) router_logits_tile_kernel(con
                                                                            int D, const uint16_t* __restrict__ wg,
                                                                            int E, const float* __restrict__ bias,
                                                                            uint16_t* __restrict__ lg) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ __align__(16) uint8_t rt_smem[];  // 2 stages of [32 x rows | 16 w rows][512 B]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e0 = blockIdx.x * RT_TE;
@@ -453,6 +470,8 @@ __global__ void __launch_bounds__(RT_ROUTE_WARPS * 32) route_rows_kernel(
     const uint16_t* __restrict__ lg, const uint16_t* __restrict__ x, int64_t T, int D, int E, int K, int renorm,
     int32_t* __restrict__ idx_out, uint16_t* __restrict__ w_out, uint16_t* __restrict__ probs_out, SharedGateArgs sg,
     float* __restrict__ sig_out) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ float s_row[];  // [RT_ROUTE_WARPS][E]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * RT_ROUTE_WARPS + warp;
@@ -472,6 +491,8 @@ constexpr int PERM_MAX_E = 1024;
 // (their inv entry becomes -1); otherwise a negative index is an error.
 __global__ void __launch_bounds__(256) permute_count_kernel(const int32_t* __restrict__ idx, int64_t R, int E,
                                                            int32_t* __restrict__ block_counts, int skip, int* status) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ int hist[];
   for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
   __syncthreads();
@@ -564,6 +585,8 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(const int32_t* __res
                                                            int64_t T, int32_t* __restrict__ block_base,
                                                            int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
                                                            TileListOut l1, TileListOut l2, TileListOut lsh) {
+  pdl_wait();
+  pdl_launch_dependents();
   __shared__ int warp_sums[32];
   __shared__ int total;
   const int e = threadIdx.x;
@@ -623,6 +646,8 @@ __global__ void __launch_bounds__(1024) permute_small_kernel(const int32_t* __re
                                                             int32_t* __restrict__ sorted_rows,
                                                             int32_t* __restrict__ inv, TileListOut l1, TileListOut l2,
                                                             TileListOut lsh, int skip, int* status) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ int sm[];  // hist[E], then wcnt[8][E] (8 row ranges of 256)
   __shared__ int warp_sums[32];
   __shared__ int total;
@@ -671,6 +696,8 @@ __global__ void __launch_bounds__(256) permute_scatter_kernel(const int32_t* __r
                                                              const int32_t* __restrict__ block_base,
                                                              int32_t* __restrict__ sorted_rows,
                                                              int32_t* __restrict__ inv) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ int wcnt[];  // [8][E]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < 8 * E; i += blockDim.x) wcnt[i] = 0;
@@ -705,6 +732,8 @@ __global__ void __launch_bounds__(256) permute_gather_kernel(const int32_t* __re
                                                             int64_t n_flat, int K, const uint16_t* __restrict__ x,
                                                             int D, int kperm, uint16_t* __restrict__ x_sorted,
                                                             const int32_t* __restrict__ count, int* status) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int dvec = D / 8;
   int64_t n = n_rows;
@@ -743,6 +772,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict
                                                      int K, int D, int64_t T, const uint16_t* __restrict__ y_sh,
                                                      const float* __restrict__ sig, uint16_t* __restrict__ out,
                                                      int* status) {
+  pdl_wait();
+  pdl_launch_dependents();
   __shared__ int rows[RT_MAXK];
   __shared__ float wk[RT_MAXK];
   const int64_t t = blockIdx.x;
@@ -812,6 +843,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict
 // entries lists the pairs by rank, then token).
 __global__ void ep_pair_dest_kernel(const int32_t* __restrict__ idx, int64_t T, int K, int world,
                                     int32_t* __restrict__ dest, int* status) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (f >= T * K) return;
   const int64_t t = f / K;
@@ -839,6 +872,8 @@ __global__ void ep_pair_dest_kernel(const int32_t* __restrict__ idx, int64_t T, 
 __global__ void __launch_bounds__(1024) ep_counts_kernel(const int32_t* __restrict__ idx, int64_t R, int world,
                                                         const int32_t* __restrict__ pair_counts,
                                                         int32_t* __restrict__ send_counts) {
+  pdl_wait();
+  pdl_launch_dependents();
   __shared__ int hist[64];
   if (threadIdx.x < 64) hist[threadIdx.x] = 0;
   __syncthreads();
@@ -864,6 +899,8 @@ __device__ __forceinline__ int32_t ep_slot(int local_expert, uint16_t weight_bit
 __global__ void ep_pair_meta_kernel(const int32_t* __restrict__ idx, const uint16_t* __restrict__ w,
                                     const int32_t* __restrict__ pair_pos, int64_t T, int K, int world,
                                     int64_t max_pairs, int32_t* __restrict__ meta, int* status) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
   const int32_t* ti = idx + t * K;
@@ -887,6 +924,8 @@ __global__ void ep_pair_meta_kernel(const int32_t* __restrict__ idx, const uint1
 // Receiving side: idx_local[i] = local expert of slot i, -1 for an empty slot.
 __global__ void ep_slot_expert_kernel(const int32_t* __restrict__ meta, int64_t n, int E_local,
                                       int32_t* __restrict__ idx_local, int* status) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const int32_t m = meta[i];
@@ -940,6 +979,8 @@ __global__ void __launch_bounds__(256) ep_reduce_kernel(const uint16_t* __restri
                                                        const int32_t* __restrict__ inv,
                                                        const int32_t* __restrict__ meta, int K, int D, int64_t rows,
                                                        uint16_t* __restrict__ partial, int* status) {
+  pdl_wait();
+  pdl_launch_dependents();
   __shared__ int rws[RT_MAXK];
   __shared__ float wk[RT_MAXK];
   __shared__ int nk;
@@ -976,6 +1017,8 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const uint16_t* __restr
                                                         int64_t num_pairs, const uint16_t* __restrict__ y_sh,
                                                         const float* __restrict__ sig, uint16_t* __restrict__ out,
                                                         int* status) {
+  pdl_wait();
+  pdl_launch_dependents();
   __shared__ int rws[RT_MAXK + 1];
   __shared__ float wk[RT_MAXK + 1];
   __shared__ int nk;
@@ -1018,6 +1061,8 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const uint16_t* __restr
 // tokens), for callers that run the shared expert without a permute.
 __global__ void shared_tiles_kernel(GemmTile* __restrict__ tiles, int32_t* __restrict__ count, int64_t T, int bn,
                                     int cap) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int nt = (int)((T + bn - 1) / bn);
   for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < nt && j < cap; j += gridDim.x * blockDim.x) {
     GemmTile g;
