@@ -167,6 +167,8 @@ __device__ inline bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* a
   }
 }
 
+__device__ inline void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
 // -------------------------------------------------------------- TMA -----
 __device__ inline void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t c0, int32_t c1) {
   asm volatile(

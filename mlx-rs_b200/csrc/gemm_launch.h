@@ -30,6 +30,10 @@ struct GroupedGemmProblem {
   int pair;                   // nmat 2 only: w[0] rows m and m+128 as the two matrices (plain store)
   int* status;
   int grid;                   // 0 = one CTA per SM
+  int splits;                 // split-K factor (0/1 = none); needs partial and counters
+  int max_split_rows;         // row slices (tile x m-tile) the split buffers hold
+  float* partial;             // fp32 [max_split_rows][splits][4][nmat][bn][32]
+  int32_t* counters;          // [max_split_rows][4], zero before the launch
 };
 
 int launch_grouped_gemm(const GroupedGemmProblem& p, cudaStream_t st);

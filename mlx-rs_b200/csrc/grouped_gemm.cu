@@ -51,7 +51,7 @@ int num_sms_current() {
   return n > 0 ? n : 148;
 }
 
-template <int NMAT, int BN, int BITS>
+template <int NMAT, int BN, int BITS, bool SPLITK>
 static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
   using C = GG<NMAT, BN, BITS>;
   CUtensorMap ta0, ta1, tb;
@@ -69,7 +69,7 @@ static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
   if (int rc = make_map_2d(&tb, p.act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)p.k_dim, (uint64_t)p.act_rows,
                            C::BK, BN, CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
-  auto kern = grouped_dequant_gemm_kernel<NMAT, BN, BITS>;
+  auto kern = grouped_dequant_gemm_kernel<NMAT, BN, BITS, SPLITK>;
   static std::atomic<uint64_t> attr_done{0};  // per instantiation and device
   if (int rc = ensure_smem_attr(kern, C::SMEM_BYTES, attr_done)) return rc;
   GemmArgs a;
@@ -88,6 +88,12 @@ static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
   a.perm_out = p.perm_out;
   a.pair = p.pair;
   a.status = p.status;
+  a.splits = p.splits > 1 ? p.splits : 1;
+  a.max_split_rows = p.max_split_rows;
+  a.partial = p.partial;
+  a.counters = p.counters;
+  if (a.splits > 1 && (!a.partial || !a.counters || a.max_split_rows <= 0))
+    return set_error(MLXR_CU_ERR_INVALID_ARGUMENT, "grouped gemm: split-K needs partial and counter buffers");
   const int grid = p.grid > 0 ? p.grid : num_sms_current();
   launch_pdl(kern, grid, C::NUM_THREADS, C::SMEM_BYTES, st, ta0, ta1, tb, a);
   MLXR_LAUNCH_CHECK("grouped_dequant_gemm_kernel");
@@ -100,8 +106,16 @@ int launch_grouped_gemm(const GroupedGemmProblem& p, cudaStream_t st) {
   if (p.n_out % 128 != 0 || p.k_dim % 64 != 0)
     return set_error(MLXR_CU_ERR_INVALID_ARGUMENT, "grouped gemm: n_out=%d must be a multiple of 128 and K=%d of 64",
                      p.n_out, p.k_dim);
+  // Split-K only for the decode tile widths (few work items come from few tokens).
+  if (p.splits > 1 && p.bn > 32)
+    return set_error(MLXR_CU_ERR_INVALID_ARGUMENT, "grouped gemm: split-K is built for bn <= 32 (bn=%d)", p.bn);
+#define MLXR_GG_SPLIT(NM, BNV, BT) \
+  if (p.splits > 1 && p.nmat == NM && p.bn == BNV && p.bits == BT) return launch_one<NM, BNV, BT, true>(p, st);
+  MLXR_GG_SPLIT(2, 16, 4) MLXR_GG_SPLIT(2, 32, 4) MLXR_GG_SPLIT(1, 16, 4) MLXR_GG_SPLIT(1, 32, 4)
+  MLXR_GG_SPLIT(2, 16, 8) MLXR_GG_SPLIT(2, 32, 8) MLXR_GG_SPLIT(1, 16, 8) MLXR_GG_SPLIT(1, 32, 8)
+#undef MLXR_GG_SPLIT
 #define MLXR_GG_CASE(NM, BNV, BT) \
-  if (p.nmat == NM && p.bn == BNV && p.bits == BT) return launch_one<NM, BNV, BT>(p, st);
+  if (p.nmat == NM && p.bn == BNV && p.bits == BT) return launch_one<NM, BNV, BT, false>(p, st);
   MLXR_GG_CASE(2, 16, 4) MLXR_GG_CASE(2, 32, 4) MLXR_GG_CASE(2, 64, 4) MLXR_GG_CASE(2, 128, 4)
   MLXR_GG_CASE(1, 16, 4) MLXR_GG_CASE(1, 32, 4) MLXR_GG_CASE(1, 64, 4) MLXR_GG_CASE(1, 128, 4) MLXR_GG_CASE(1, 256, 4)
   MLXR_GG_CASE(2, 16, 8) MLXR_GG_CASE(2, 32, 8) MLXR_GG_CASE(2, 64, 8) MLXR_GG_CASE(2, 128, 8)

@@ -123,6 +123,14 @@ struct GemmArgs {
   int pair;                   // NMAT == 2 only: the two matrices are row blocks m and m+128
                               // of one weight (plain epilogue) instead of gate and up (SwiGLU)
   int* status;
+  // Split-K (splits > 1): every (tile, row slice) is split into `splits`
+  // k-ranges; each writes its fp32 accumulators to `partial`, and the last
+  // split to finish (per TMEM lane quarter, counted in `counters`, zero on
+  // entry) adds them up in split order and runs the epilogue.
+  int splits;
+  int max_split_rows;         // row slices `partial` and `counters` hold
+  float* partial;             // [row slices][splits][4 quarters][NMAT][BN][32]
+  int32_t* counters;          // [row slices][4]
 };
 
 // A tile entry is used only if it names a valid expert and a row range inside
@@ -189,7 +197,9 @@ __device__ inline void drain_ring(uint64_t* full, uint32_t issued, volatile int*
   }
 }
 
-template <int NMAT, int BN, int BITS>
+// SPLITK: the split-K variant (args.splits > 1); the plain variant has S = 1
+// folded in at compile time.
+template <int NMAT, int BN, int BITS, bool SPLITK>
 __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
     grouped_dequant_gemm_kernel(const __grid_constant__ CUtensorMap tm_a0, const __grid_constant__ CUtensorMap tm_a1,
                                 const __grid_constant__ CUtensorMap tm_b, const GemmArgs args) {
@@ -256,20 +266,26 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
   const int ksteps = args.k_dim / C::BK;
   int ntiles = *args.num_tiles;
   if (ntiles > args.max_tiles) ntiles = args.max_tiles;
-  const int num_items = ntiles * mt_per_expert;
+  const int S = SPLITK ? (args.splits > 1 ? args.splits : 1) : 1;
+  const int num_items = ntiles * mt_per_expert * S;
+  // Work item -> (row slice `base` = tile * mt_per_expert + m-tile, split);
+  // split s covers k-steps [s*ksteps/S, (s+1)*ksteps/S).
+  auto k_lo_of = [&](int item) { return (item % S) * ksteps / S; };
+  auto k_hi_of = [&](int item) { return (item % S + 1) * ksteps / S; };
 
   if (warp == C::W_RAW) {
     // ---------------------------------------------- raw weight producer --
     if (lane == 0) {
       uint32_t it = 0;
       for (int item = blockIdx.x; item < num_items && !*abort_flag; item += gridDim.x) {
-        const GemmTile t = args.tiles[item / mt_per_expert];
+        const int base = item / S;
+        const GemmTile t = args.tiles[base / mt_per_expert];
         if (!tile_ok(t, args)) {
           atomicCAS(args.status, 0, (int)kDevBadIndex);
           continue;
         }
-        const int a_row = t.expert * n_out + (item % mt_per_expert) * mrows;
-        for (int ks = 0; ks < ksteps; ++ks, ++it) {
+        const int a_row = t.expert * n_out + (base % mt_per_expert) * mrows;
+        for (int ks = k_lo_of(item); ks < k_hi_of(item); ++ks, ++it) {
           const int s = it % C::RS;
           if (!mbar_wait(&raw_empty[s], ((it / C::RS) & 1) ^ 1, abort_flag, args.status)) break;
           mbar_arrive_expect_tx(&raw_full[s], C::RAW_STAGE);
@@ -288,9 +304,9 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       int s = 0;
       uint32_t ph = 0;
       for (int item = blockIdx.x; item < num_items && !*abort_flag; item += gridDim.x) {
-        const GemmTile t = args.tiles[item / mt_per_expert];
+        const GemmTile t = args.tiles[(item / S) / mt_per_expert];
         if (!tile_ok(t, args)) continue;
-        for (int ks = 0; ks < ksteps; ++ks, ++it) {
+        for (int ks = k_lo_of(item); ks < k_hi_of(item); ++ks, ++it) {
           if (!mbar_wait(&op_empty[s], ph ^ 1, abort_flag, args.status)) break;
           mbar_arrive_expect_tx(&b_full[s], C::B_STAGE);
           tma_load_2d(sB + s * C::B_STAGE, &tm_b, &b_full[s], ks * C::BK, t.row_start);
@@ -316,14 +332,15 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       uint32_t ph = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
-        if (!tile_ok(args.tiles[item / mt_per_expert], args)) continue;
+        if (!tile_ok(args.tiles[(item / S) / mt_per_expert], args)) continue;
         const int ab = li % C::AB;
         const uint32_t acc_phase = (li / C::AB) & 1;
         ++li;  // counts valid items only, exactly like the epilogue
         if (!mbar_wait(&acc_empty[ab], acc_phase ^ 1, abort_flag, args.status)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(ab * C::ACC_COLS + mi * BN);
-        for (int ks = 0; ks < ksteps; ++ks) {
+        const int k_lo = k_lo_of(item), k_hi = k_hi_of(item);
+        for (int ks = k_lo; ks < k_hi; ++ks) {
           if (!mbar_wait(&b_full[s], ph, abort_flag, args.status) ||
               !mbar_wait(&op_full[s], ph, abort_flag, args.status)) {
             ok = false;
@@ -331,7 +348,7 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
           }
           tc_fence_after();
           umma_bf16_ts_k64(d, a0 + (uint32_t)(s * C::A_COLS), bdesc0 + (uint64_t)(s * (C::B_STAGE >> 4)), C::IDESC,
-                           ks != 0 ? 1u : 0u);
+                           ks != k_lo ? 1u : 0u);
           umma_commit(&op_empty[s]);
           if (++s == C::OS) {
             s = 0;
@@ -374,9 +391,10 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       it += n;
     };
     for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
-      const GemmTile t = args.tiles[item / mt_per_expert];
+      const GemmTile t = args.tiles[(item / S) / mt_per_expert];
       if (!tile_ok(t, args)) continue;
-      const int64_t srow = (int64_t)t.expert * n_out + (item % mt_per_expert) * mrows + (pair ? mat * C::BM : 0) + row;
+      const int64_t srow =
+          (int64_t)t.expert * n_out + ((item / S) % mt_per_expert) * mrows + (pair ? mat * C::BM : 0) + row;
       // (select, not index: a runtime index into the kernel parameters would
       // copy them to local memory)
       const uint16_t* sbase = mat ? args.scales[1] : args.scales[0];
@@ -384,13 +402,15 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       const uint16_t* sp = sbase + srow * ksteps;
       const uint16_t* bp = bbase + srow * ksteps;
       // First k-step of this item that belongs to the group.
-      int ks = (int)((grp - (int)(it % NGRP) + NGRP) % NGRP);
-      advance(ks < ksteps ? ks : ksteps);
-      if (ks >= ksteps) continue;
+      const int k_lo = k_lo_of(item), k_hi = k_hi_of(item);
+      const int first = (int)((grp - (int)(it % NGRP) + NGRP) % NGRP);
+      int ks = k_lo + first;
+      advance(ks < k_hi ? first : k_hi - k_lo);
+      if (ks >= k_hi) continue;
       uint32_t s_nx = __ldg(sp + ks), b_nx = __ldg(bp + ks);  // one k-step ahead
-      for (; ks < ksteps; ks += NGRP) {
+      for (; ks < k_hi; ks += NGRP) {
         const uint32_t s16 = s_nx, b16 = b_nx;
-        if (ks + NGRP < ksteps) {
+        if (ks + NGRP < k_hi) {
           s_nx = __ldg(sp + ks + NGRP);
           b_nx = __ldg(bp + ks + NGRP);
         }
@@ -445,7 +465,7 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&op_full[os]);
-        const int step = ks + NGRP < ksteps ? NGRP : ksteps - ks;
+        const int step = ks + NGRP < k_hi ? NGRP : k_hi - ks;
         advance(step);
       }
     }
@@ -453,21 +473,79 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
     // ------------------------------------------------------- epilogue ----
     const int q = warp;  // TMEM lane quarter 0..3
     uint32_t li = 0;
+    constexpr int CW = 16;  // TMEM columns per load (keeps the epilogue's registers small)
+    constexpr int PQ = NMAT * BN * 32;  // floats of one quarter's partial accumulators
     for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
-      const GemmTile t = args.tiles[item / mt_per_expert];
+      const int base = item / S, split = item % S;
+      const GemmTile t = args.tiles[base / mt_per_expert];
       if (!tile_ok(t, args)) continue;
       const int ab = li % C::AB;
       const uint32_t acc_phase = (li / C::AB) & 1;
       ++li;
       if (!mbar_wait(&acc_full[ab], acc_phase, abort_flag, args.status)) break;
       tc_fence_after();
-      const int fn = (item % mt_per_expert) * mrows + q * 32 + lane;
+      const int fn = (base % mt_per_expert) * mrows + q * 32 + lane;
       const int f = args.perm_out ? ((fn & ~7) | kperm_pos(fn & 7)) : fn;
       uint16_t* outp2 = args.out + (int64_t)t.row_start * n_out + fn + C::BM;  // pair mode: second row block
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * C::ACC_COLS);
       uint16_t* outp = args.out + (int64_t)t.row_start * n_out + f;
       const int rows = t.row_count < BN ? t.row_count : BN;
-      constexpr int CW = 16;  // TMEM columns per load (keeps the epilogue's registers small)
+      auto store = [&](int col, float gv, float uv) {
+        if (NMAT == 2 && pair) {
+          outp[(int64_t)col * n_out] = f32_to_bf16_bits(gv);
+          outp2[(int64_t)col * n_out] = f32_to_bf16_bits(uv);
+        } else {
+          float v = gv;
+          if (NMAT == 2) v = silu_f32(v) * uv;
+          outp[(int64_t)col * n_out] = f32_to_bf16_bits(v);
+        }
+      };
+      if constexpr (SPLITK) {
+        // Split-K: spill this split's accumulators, release TMEM, and let the
+        // last split of the row slice (per lane quarter) finish it.
+        const bool in_cap = base < args.max_split_rows;
+        if (!in_cap && lane == 0) atomicCAS(args.status, 0, (int)kDevBadIndex);
+        float* pq = args.partial + (((size_t)base * S + split) * 4 + q) * PQ;
+#pragma unroll 1
+        for (int c = 0; c < BN / CW && in_cap; ++c) {
+          if (c * CW >= rows) break;
+          uint32_t g[32];
+          uint32_t u[32];
+          if (NMAT == 2) tmem_ld2_x16_wait(tbase + c * CW, tbase + BN + c * CW, g, u);
+          else tmem_ld_x16_wait(tbase + c * CW, g);
+#pragma unroll
+          for (int j = 0; j < CW; ++j) {
+            pq[(c * CW + j) * 32 + lane] = __uint_as_float(g[j]);
+            if (NMAT == 2) pq[(BN + c * CW + j) * 32 + lane] = __uint_as_float(u[j]);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[ab]);
+        if (!in_cap) continue;
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+          last = atomicAdd(&args.counters[base * 4 + q], 1) == S - 1;
+          if (last) args.counters[base * 4 + q] = 0;  // clean for the next launch
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) continue;
+        __threadfence();
+        const float* p0 = args.partial + ((size_t)base * S * 4 + q) * PQ;
+        const size_t sstride = (size_t)4 * PQ;
+#pragma unroll 1
+        for (int col = 0; col < rows; ++col) {
+          float gv = 0.0f, uv = 0.0f;
+          for (int sp_ = 0; sp_ < S; ++sp_) {
+            gv += __ldcg(p0 + sp_ * sstride + col * 32 + lane);
+            if (NMAT == 2) uv += __ldcg(p0 + sp_ * sstride + (BN + col) * 32 + lane);
+          }
+          store(col, gv, uv);
+        }
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / CW; ++c) {
         if (c * CW >= rows) break;
@@ -476,24 +554,9 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
         if (NMAT == 2) tmem_ld2_x16_wait(tbase + c * CW, tbase + BN + c * CW, g, u);
         else tmem_ld_x16_wait(tbase + c * CW, g);
         const int nvalid = rows - c * CW < CW ? rows - c * CW : CW;
-        if (NMAT == 2 && pair) {
 #pragma unroll
-          for (int j = 0; j < CW; ++j) {
-            if (j < nvalid) {
-              outp[(int64_t)(c * CW + j) * n_out] = f32_to_bf16_bits(__uint_as_float(g[j]));
-              outp2[(int64_t)(c * CW + j) * n_out] = f32_to_bf16_bits(__uint_as_float(u[j]));
-            }
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < CW; ++j) {
-            if (j < nvalid) {
-              float v = __uint_as_float(g[j]);
-              if (NMAT == 2) v = silu_f32(v) * __uint_as_float(u[j]);
-              outp[(int64_t)(c * CW + j) * n_out] = f32_to_bf16_bits(v);
-            }
-          }
-        }
+        for (int j = 0; j < CW; ++j)
+          if (j < nvalid) store(c * CW + j, __uint_as_float(g[j]), NMAT == 2 ? __uint_as_float(u[j]) : 0.0f);
       }
       tc_fence_before();
       __syncwarp();

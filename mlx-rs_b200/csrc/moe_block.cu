@@ -9,6 +9,7 @@
 //   [shared expert: dense GEMMs over x with the same kernels]
 //   combine (+ sigmoid-gated shared expert)
 // All scratch lives in the caller's workspace; nothing is allocated here.
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 
@@ -54,10 +55,12 @@ struct Layout {
   int64_t T = 0, R = 0, rows = 0, rows_pad = 0, sh_rows_pad = 0;
   int E = 0, K = 0, D = 0, I = 0, Is = 0, nblk = 0;
   int bn1 = 0, bn2 = 0, bns = 0;
+  int s1 = 1, s2 = 1;          // split-K factors of the gate/up and down GEMMs
+  int split_rows = 0;          // row slices the split buffers hold
   int max_t1 = 0, max_t2 = 0, max_tsh = 0;
   size_t status = 0, logits = 0, idx = 0, w = 0, sig = 0, bcounts = 0, bbase = 0, counts = 0, offsets = 0,
          sorted = 0, inv = 0, t1 = 0, n1 = 0, t2 = 0, n2 = 0, tsh = 0, nsh = 0, xs = 0, h = 0, y = 0, xpad = 0,
-         hsh = 0, ysh = 0, total = 0;
+         hsh = 0, ysh = 0, part = 0, cnt = 0, total = 0;
 };
 
 // Token-tile width from the mean number of rows per expert.
@@ -95,6 +98,17 @@ static int validate(const mlxr_cu_moe_config* c, int64_t T) {
   return MLXR_CU_OK;
 }
 
+// Split-K factor for a GEMM with `items` work items of `ksteps` k-steps: only
+// when the items would leave more than half of the SMs idle.
+static int pick_splits(int64_t items, int ksteps) {
+  const int sms = num_sms_current();
+  if (items <= 0 || items * 2 > sms) return 1;
+  int sp = (int)(sms / items);
+  if (sp > ksteps / 4) sp = ksteps / 4;
+  if (sp > 8) sp = 8;
+  return sp < 1 ? 1 : sp;
+}
+
 static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T, int64_t rows_cap = -1) {
   Layout L;
   L.T = T;
@@ -116,6 +130,20 @@ static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T, int64_t rows_c
   L.max_t1 = (int)(L.E + (L.rows + L.bn1 - 1) / L.bn1 + 1);
   L.max_t2 = (int)(L.E + (L.rows + L.bn2 - 1) / L.bn2 + 1);
   L.max_tsh = (int)((T + L.bns - 1) / L.bns + 1);
+  // Split-K for small batches (the whole permutation in one CTA, which also
+  // clears the split counters): expected non-empty experts min(E, rows).
+  const int mt1 = L.I / 128, mt2 = (L.D % 256 == 0) ? L.D / 256 : L.D / 128;
+  if (L.nblk == 1 && L.rows > 0) {
+    const int64_t used = L.rows < L.E ? L.rows : L.E;
+    if (L.bn1 <= 32) L.s1 = pick_splits(used * mt1, L.D / 64);
+    if (L.bn2 <= 32) L.s2 = pick_splits(used * mt2, L.I / 64);
+  }
+  if (L.s1 > 1 || L.s2 > 1) {
+    // Tiles per GEMM are at most rows/bn + (non-empty experts) + 1.
+    const int64_t t1 = std::min<int64_t>(L.max_t1, L.rows / L.bn1 + std::min<int64_t>(L.rows, L.E) + 1);
+    const int64_t t2 = std::min<int64_t>(L.max_t2, L.rows / L.bn2 + std::min<int64_t>(L.rows, L.E) + 1);
+    L.split_rows = (int)std::max(t1 * mt1, t2 * mt2);
+  }
   size_t o = 0;
   auto take = [&](size_t bytes) {
     const size_t at = o;
@@ -146,6 +174,12 @@ static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T, int64_t rows_c
     L.xpad = take((T < 256 || c->shared_bits == 4) ? (size_t)L.sh_rows_pad * L.D * 2 : 0);
     L.hsh = take((size_t)L.sh_rows_pad * L.Is * 2);
     L.ysh = take((size_t)T * L.D * 2);
+  }
+  if (L.split_rows > 0) {
+    const int smax = L.s1 > L.s2 ? L.s1 : L.s2;
+    const int bmax = L.bn1 > L.bn2 ? L.bn1 : L.bn2;
+    L.part = take((size_t)L.split_rows * smax * 4 * 2 * bmax * 32 * sizeof(float));
+    L.cnt = take((size_t)L.split_rows * 4 * sizeof(int32_t));
   }
   L.total = o;
   return L;
@@ -247,7 +281,7 @@ static int run_permute(const Layout& L, const int32_t* idx, const void* x, void*
   if (L.nblk == 1) {
     // Every flat row fits one block: count, scan, tile lists and ranks in one CTA.
     launch_pdl(permute_small_kernel, 1, 1024, 9 * L.E * sizeof(int), st, idx, L.R, L.E, L.T, counts, offsets, sorted, inv, l1,
-                                                                  l2, lsh, skip, status);
+               l2, lsh, skip, status, L.split_rows ? at<int32_t>(ws, L.cnt) : (int32_t*)nullptr, L.split_rows * 4);
     MLXR_LAUNCH_CHECK("permute_small_kernel");
   } else {
     launch_pdl(permute_count_kernel, L.nblk, 256, L.E * sizeof(int), st, idx, L.R, L.E, at<int32_t>(ws, L.bcounts), skip,
@@ -308,6 +342,10 @@ static int run_experts(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* w
   p.out_rows = L.rows;
   p.perm_out = c->bits == 4;  // h is the 4-bit down projection's activation operand
   p.status = status;
+  p.splits = L.s1;
+  p.max_split_rows = L.split_rows;
+  p.partial = L.split_rows ? at<float>(ws, L.part) : nullptr;
+  p.counters = L.split_rows ? at<int32_t>(ws, L.cnt) : nullptr;
   if (int rc = launch_grouped_gemm(p, st)) return rc;
   stage_mark(mid_stage, st);
 
@@ -334,6 +372,10 @@ static int run_experts(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* w
   q.out_rows = L.rows;
   q.perm_out = 0;
   q.status = status;
+  q.splits = L.s2;
+  q.max_split_rows = L.split_rows;
+  q.partial = L.split_rows ? at<float>(ws, L.part) : nullptr;
+  q.counters = L.split_rows ? at<int32_t>(ws, L.cnt) : nullptr;
   return launch_grouped_gemm(q, st);
 }
 

@@ -645,9 +645,12 @@ __global__ void __launch_bounds__(1024) permute_small_kernel(const int32_t* __re
                                                             int32_t* __restrict__ offsets,
                                                             int32_t* __restrict__ sorted_rows,
                                                             int32_t* __restrict__ inv, TileListOut l1, TileListOut l2,
-                                                            TileListOut lsh, int skip, int* status) {
+                                                            TileListOut lsh, int skip, int* status,
+                                                            int32_t* __restrict__ zero, int nzero) {
   pdl_wait();
   pdl_launch_dependents();
+  // Counters the GEMMs that follow expect at zero (split-K).
+  for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0;
   extern __shared__ int sm[];  // hist[E], then wcnt[8][E] (8 row ranges of 256)
   __shared__ int warp_sums[32];
   __shared__ int total;
