@@ -334,6 +334,8 @@ __device__ __host__ inline uint32_t sw128_offset(uint32_t r, uint32_t c) {
   return r * 128u + ((c ^ (r & 7u)) << 4);
 }
 
-__device__ inline float silu_f32(float g) { return g / (1.0f + __expf(-g)); }
+// g * sigmoid(g) with the fast exponential and division (a few ulp of fp32;
+// the result is rounded to bf16 right after).
+__device__ inline float silu_f32(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 }  // namespace mlxr
