@@ -345,44 +345,61 @@ __global__ void __launch_bounds__(RS_WARPS * 32) router_split_kernel(
   }
 }
 
-// Large batches: logits in CTA tiles of 32 tokens x 16 experts staged
-// through shared memory, then a routing kernel (one warp per token). Warp w
-// of a tile owns tokens 8*(w%4) .. +7 and experts 8*(w/4) .. +7; lane j
-// keeps the contract's chain over chunks j, j+32, ... of D for each of its
-// 64 (token, expert) pairs, so each logit is the same fp32 value as in
-// router_fused_kernel. Every 32-chunk block of D is copied to shared memory
-// once per tile (16-byte cp.async, double-buffered) and read by 2 or 4
-// warps, instead of every warp streaming x and the router weight itself.
+// Large batches: logits in CTA tiles of 32 tokens x 16 experts. Each
+// 32-chunk block of D (256 elements) of the tile's x rows and router rows is
+// copied to shared memory as bf16 (16-byte cp.async, one block ahead), then
+// converted once to fp32: x as [token][half][chunk][4], the router rows as
+// expert pairs [pair][element pair][chunk][4] = (w_j[e], w_j+1[e], w_j[e+1],
+// w_j+1[e+1]). Warp w owns tokens 8*(w%4) .. +7 and experts 8*(w/4) .. +7;
+// lane j keeps the contract's chain over chunks j, j+32, ... of D for each of
+// its 64 (token, expert) pairs, two experts at a time with the packed fp32x2
+// FMA (two IEEE round-to-nearest FMAs), so each logit is the same fp32 value
+// as in router_fused_kernel while the per-FMA unpacking and operand loads
+// are shared by the warp's tile.
 constexpr int RT_TT = 32, RT_TE = 16, RT_TILE_THREADS = 256;
-constexpr int RT_ROWB = 32 * 16;                        // bytes of one row's 32-chunk block
-constexpr int RT_STAGE = (RT_TT + RT_TE) * RT_ROWB;     // 24 KB
+constexpr int RT_BF_STAGE = (RT_TT + RT_TE) * 32 * 16;        // bf16 staging: 24 KB
+constexpr int RT_X32 = RT_TT * 256 * 4;                        // fp32 x: 32 KB
+constexpr int RT_W32 = RT_TE * 256 * 4;                        // fp32 router rows: 16 KB
+constexpr int RT_TILE_SMEM = RT_BF_STAGE + RT_X32 + RT_W32;    // 72 KB
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-__global__ void __launch_bounds__(RT_TILE_THREADS) router_logits_tile_kernel(const uint16_t* __restrict__ x, int64_t T,
-                                                                           int D, const uint16_t* __restrict__ wg,
-                                                                           int E, const float* __restrict__ bias,
-                                                                           uint16_t* __restrict__ lg) {
-  pdl_wait();
-  pdl_launch_dependents();
-  extern __shared__ __align__(16) uint8_t rt_smem[];  // 2 stages of [32 x rows | 16 w rows][512 B]
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+// d = a * b + d elementwise on two packed fp32 values (two IEEE fmaf).
+__device__ __forceinline__ void ffma2(uint64_t& d, uint64_t a, uint64_t b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b));
+}
+
+__global__ void __launch_bounds__(RT_TILE_THREADS, 2) router_logits_tile_kernel(const uint16_t* __restrict__ x, int64_t T,
+                                                                              int D, const uint16_t* __restrict__ wg,
+                                                                              int E, const float* __restrict__ bias,
+                                                                              uint16_t* __restrict__ lg) {
+  extern __shared__ __align__(16) uint8_t rt_smem[];
+  uint8_t* sbf = rt_smem;                                      // bf16 staging [48 rows][32 chunks][16 B]
+  float* sx = reinterpret_cast<float*>(rt_smem + RT_BF_STAGE);  // [32 tokens][2 halves][32 chunks][4]
+  float* sw = sx + RT_TT * 256;                                 // [8 pairs][4 element pairs][32 chunks][4]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e0 = blockIdx.x * RT_TE;
   const int64_t t0 = (int64_t)blockIdx.y * RT_TT;
   const int nchunks = D / 8;
   const int nblocks = (nchunks + 31) / 32;
-  const uint32_t sbase = smem_u32(rt_smem);
-  auto stage_in = [&](int m, int st) {
-    // 48 rows x 32 chunks = 1536 copies of 16 B, 6 per thread.
+  const uint32_t sbf_u32 = smem_u32(sbf);
+  auto stage_in = [&](int m) {
     for (int q = threadIdx.x; q < (RT_TT + RT_TE) * 32; q += RT_TILE_THREADS) {
       const int r = q >> 5, cj = q & 31;
       const int c = m * 32 + cj;
-      const uint32_t dst = sbase + (uint32_t)(st * RT_STAGE + r * RT_ROWB + cj * 16);
+      const uint32_t dst = sbf_u32 + (uint32_t)(q * 16);
       if (r < RT_TT) {
         const int64_t t = t0 + r;
         const bool ok = t < T && c < nchunks;
@@ -396,69 +413,89 @@ __global__ void __launch_bounds__(RT_TILE_THREADS) router_logits_tile_kernel(con
     cp_async_commit();
   };
   const int tg = warp & 3, eg = warp >> 2;
-  float acc[8][8];
+  uint64_t acc[8][4];  // [token][expert pair]
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
-  stage_in(0, 0);
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0ull;
+  stage_in(0);
   for (int m = 0; m < nblocks; ++m) {
-    if (m + 1 < nblocks) {
-      stage_in(m + 1, (m + 1) & 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
+    cp_async_wait_all();
+    __syncthreads();
+    // bf16 staging -> fp32 compute layout.
+    for (int q = threadIdx.x; q < RT_TT * 32; q += RT_TILE_THREADS) {  // x: (token, chunk)
+      const int r = q >> 5, cj = q & 31;
+      const uint4 v = *reinterpret_cast<const uint4*>(sbf + q * 16);
+      float4* d0 = reinterpret_cast<float4*>(sx + ((r * 2 + 0) * 32 + cj) * 4);
+      float4* d1 = reinterpret_cast<float4*>(sx + ((r * 2 + 1) * 32 + cj) * 4);
+      *d0 = make_float4(bf_lo(v.x), bf_hi(v.x), bf_lo(v.y), bf_hi(v.y));
+      *d1 = make_float4(bf_lo(v.z), bf_hi(v.z), bf_lo(v.w), bf_hi(v.w));
+    }
+    for (int q = threadIdx.x; q < (RT_TE / 2) * 32; q += RT_TILE_THREADS) {  // w: (expert pair, chunk)
+      const int jp = q >> 5, cj = q & 31;
+      const uint4 a = *reinterpret_cast<const uint4*>(sbf + ((RT_TT + 2 * jp) * 32 + cj) * 16);
+      const uint4 b = *reinterpret_cast<const uint4*>(sbf + ((RT_TT + 2 * jp + 1) * 32 + cj) * 16);
+      const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int ep = 0; ep < 4; ++ep)
+        *reinterpret_cast<float4*>(sw + ((jp * 4 + ep) * 32 + cj) * 4) =
+            make_float4(bf_lo(aw[ep]), bf_lo(bw[ep]), bf_hi(aw[ep]), bf_hi(bw[ep]));
     }
     __syncthreads();
+    if (m + 1 < nblocks) stage_in(m + 1);  // the staging buffer is free again
     if (m * 32 + lane < nchunks) {
-      const uint8_t* sx = rt_smem + (m & 1) * RT_STAGE + (tg * 8) * RT_ROWB + lane * 16;
-      const uint8_t* sw = rt_smem + (m & 1) * RT_STAGE + (RT_TT + eg * 8) * RT_ROWB + lane * 16;
-      uint4 xv[8], wv[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) xv[i] = *reinterpret_cast<const uint4*>(sx + i * RT_ROWB);
+      for (int h = 0; h < 2; ++h) {
+        float4 xv[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) wv[j] = *reinterpret_cast<const uint4*>(sw + j * RT_ROWB);
+        for (int i = 0; i < 8; ++i) xv[i] = *reinterpret_cast<const float4*>(sx + (((tg * 8 + i) * 2 + h) * 32 + lane) * 4);
 #pragma unroll
-      for (int el = 0; el < 8; ++el) {
-        float xf[8], wf[8];
+        for (int ep2 = 0; ep2 < 2; ++ep2) {  // element pairs (4h + 2*ep2, +1)
+          float4 wv[4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const uint32_t wd = el < 2 ? xv[i].x : el < 4 ? xv[i].y : el < 6 ? xv[i].z : xv[i].w;
-          xf[i] = (el & 1) ? bf_hi(wd) : bf_lo(wd);
+          for (int jp = 0; jp < 4; ++jp)
+            wv[jp] = *reinterpret_cast<const float4*>(sw + (((eg * 4 + jp) * 4 + (2 * h + ep2)) * 32 + lane) * 4);
+#pragma unroll
+          for (int el = 0; el < 2; ++el) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float xe = (ep2 == 0) ? (el == 0 ? xv[i].x : xv[i].y) : (el == 0 ? xv[i].z : xv[i].w);
+              const uint64_t xx = f2_pack(xe, xe);
+#pragma unroll
+              for (int jp = 0; jp < 4; ++jp)
+                ffma2(acc[i][jp], xx, el == 0 ? f2_pack(wv[jp].x, wv[jp].y) : f2_pack(wv[jp].z, wv[jp].w));
+            }
+          }
         }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t wd = el < 2 ? wv[j].x : el < 4 ? wv[j].y : el < 6 ? wv[j].z : wv[j].w;
-          wf[j] = (el & 1) ? bf_hi(wd) : bf_lo(wd);
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(xf[i], wf[j], acc[i][j]);
       }
     }
-    __syncthreads();  // the stage is refilled by the next iteration's copies
+    __syncthreads();  // the fp32 buffers are rewritten by the next block
   }
   float mine[2] = {0.0f, 0.0f};
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float v = acc[i][j];
+    for (int jp = 0; jp < 4; ++jp) {
+      float va, vb;
+      f2_unpack(acc[i][jp], va, vb);
 #pragma unroll
-      for (int s = 16; s >= 1; s >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, s));
-      const int idx = i * 8 + j;  // lane idx & 31 keeps pair idx
-      if (lane == (idx & 31)) mine[idx >> 5] = v;
+      for (int s = 16; s >= 1; s >>= 1) {
+        va = __fadd_rn(va, __shfl_xor_sync(0xffffffffu, va, s));
+        vb = __fadd_rn(vb, __shfl_xor_sync(0xffffffffu, vb, s));
+      }
+      const int ia = i * 8 + 2 * jp, ib = ia + 1;  // pair index = token * 8 + expert
+      if (lane == (ia & 31)) mine[ia >> 5] = va;
+      if (lane == (ib & 31)) mine[ib >> 5] = vb;
     }
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int idx = h * 32 + lane;
+  for (int hh = 0; hh < 2; ++hh) {
+    const int idx = hh * 32 + lane;
     const int i = idx >> 3, j = idx & 7;
     const int64_t t = t0 + tg * 8 + i;
     const int e = e0 + eg * 8 + j;
     if (t < T && e < E) {
       const float b = bias ? bias[e] : 0.0f;
-      lg[t * E + e] = f32_to_bf16_bits(__fadd_rn(mine[h], b));
+      lg[t * E + e] = f32_to_bf16_bits(__fadd_rn(mine[hh], b));
     }
   }
 }
