@@ -459,7 +459,7 @@ def bench_ep(args, dev, st, world, rank):
     import torch.distributed as dist
 
     from mlxr_moe import synth
-    from mlxr_moe.ep import ExpertParallelMoeBlock, TorchDistExchange
+    from mlxr_moe.ep import ExpertParallelMoeBlock, TorchDistExchange, balanced_placement
 
     ex = TorchDistExchange()
     res = {}
@@ -469,8 +469,16 @@ def bench_ep(args, dev, st, world, rank):
         D, K = cfg.hidden_size, cfg.num_experts_per_tok
         T = T_total // world
         full = synth.make_block(cfg, 0, spec["zipf"], dev)
-        blk = ExpertParallelMoeBlock.from_block(full, rank, world)
         xs = [synth.make_input(T, D, stream_offset=500 + 16 * rank + i, device=dev) for i in range(2)]
+        # Placement from measured expert loads: every rank routes a calibration
+        # batch (its own tokens), the counts are summed over ranks, and the
+        # experts are spread greedily so each rank gets about the same rows.
+        calib = synth.make_input(T, D, stream_offset=900 + rank, device=dev)
+        idx, _ = full.router(calib)
+        loads = torch.bincount(idx.reshape(-1).long(), minlength=cfg.num_experts).to(torch.float64)
+        dist.all_reduce(loads)
+        place = balanced_placement(loads.cpu().tolist(), world)
+        blk = ExpertParallelMoeBlock.from_block(full, rank, world, place)
         bounds = dict(max_recv_pairs=world * T, max_recv_rows=world * T * K)
         n_steps = max(5, args.steps // 2)
         with torch.cuda.stream(st):
@@ -516,7 +524,7 @@ def bench_ep(args, dev, st, world, rank):
         res[name] = dict(tokens=T_total, tokens_per_rank=T, ms=ms, tokens_per_s=T_total / (ms / 1e3),
                          tflops_total=fl / (ms / 1e3) / 1e12, one_gpu_ms=one,
                          speedup_vs_one_gpu=(one / ms) if one else None, zipf=spec["zipf"],
-                         placement="expert e on rank e % world",
+                         placement="balanced: experts spread greedily by loads measured on a calibration batch",
                          exchange="NCCL all_to_all_single: counts, pair rows, slot rows, partial rows")
         del blk, full, xs
         torch.cuda.empty_cache()

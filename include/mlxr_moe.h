@@ -243,9 +243,11 @@ MLXR_CU_API int mlxr_cu_moe_permute(const mlxr_cu_moe_config* cfg, const int32_t
 /* No counterpart in the reference, which runs the whole block on one device
  * (Qwen35MoeBlock::forward, crates/mlxr-lm/src/qwen3_5/text/moe.rs:116-146,
  * has no collective). The block's experts are spread over `world` ranks, one
- * process per GPU: expert e lives on rank e % world as local expert
- * e / world; the router and the shared expert are replicated. A step on each
- * rank, with the caller doing the two exchanges (e.g. NCCL all-to-all):
+ * process per GPU: expert e lives on rank placement[e] >> 16 as that rank's
+ * local expert placement[e] & 0xFFFF (a device int32 table [E]; NULL means
+ * rank e % world, local expert e / world); the router and the shared expert
+ * are replicated. A step on each rank, with the caller doing the two
+ * exchanges (e.g. NCCL all-to-all):
  *   1. mlxr_cu_moe_ep_dispatch: route this rank's T tokens; list one pair per
  *      (token, destination rank) holding one of the token's experts, sorted
  *      by rank then token, with the token's x row and K slots of (local
@@ -266,7 +268,8 @@ MLXR_CU_API int mlxr_cu_moe_permute(const mlxr_cu_moe_config* cfg, const int32_t
 
 /* Workspace for all three steps of one rank: num_tokens of its own tokens,
  * up to max_recv_pairs received pairs carrying up to max_recv_rows filled
- * slots (bounds: world * num_tokens pairs; pairs * K rows). */
+ * slots (bounds: world * num_tokens pairs; pairs * K rows); sized for any
+ * placement. */
 MLXR_CU_API int mlxr_cu_moe_ep_workspace_size(const mlxr_cu_moe_config* cfg, int world, int64_t num_tokens,
                                               int64_t max_recv_pairs, int64_t max_recv_rows, size_t* bytes);
 
@@ -278,17 +281,17 @@ MLXR_CU_API int mlxr_cu_moe_ep_workspace_size(const mlxr_cu_moe_config* cfg, int
  * shared_gate [T] fp32 (sigmoid of the shared-expert gate; NULL without a
  * shared expert) is kept for step 5. */
 MLXR_CU_API int mlxr_cu_moe_ep_dispatch(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights, int world,
-                                        const void* x, int64_t num_tokens, int32_t* send_counts, int32_t* pair_pos,
+                                        const int32_t* placement, const void* x, int64_t num_tokens, int32_t* send_counts, int32_t* pair_pos,
                                         void* x_send, int32_t* meta_send, float* shared_gate, void* workspace,
                                         size_t workspace_bytes, void* stream);
 
 /* Step 3. cfg is the full block's configuration; local_weights hold this
- * rank's E / world experts in local order (switch_* members only). x_recv
+ * rank's num_local_experts experts in local order (switch_* members only). x_recv
  * [num_pairs, D] bf16 and meta_recv [num_pairs, K] int32 as received;
  * num_rows = the filled slots among them (the sum of the received
  * send_counts[.][1]). partial [num_pairs, D] bf16 out. */
 MLXR_CU_API int mlxr_cu_moe_ep_experts(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* local_weights,
-                                       int world, const void* x_recv, const int32_t* meta_recv, int64_t num_pairs,
+                                       int num_local_experts, const void* x_recv, const int32_t* meta_recv, int64_t num_pairs,
                                        int64_t num_rows, void* partial, void* workspace, size_t workspace_bytes,
                                        void* stream);
 

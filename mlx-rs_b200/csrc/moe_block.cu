@@ -456,17 +456,11 @@ static size_t ep_dispatch_bytes(const mlxr_cu_moe_config* c, int64_t T, size_t* 
 }
 
 static int ep_check_world(const mlxr_cu_moe_config* cfg, int world) {
-  MLXR_CHECK_ARG(world >= 1 && world <= 64 && cfg->num_experts % world == 0,
-                 "moe_ep: world=%d must be in [1, 64] and divide num_experts=%d", world, cfg->num_experts);
+  MLXR_CHECK_ARG(world >= 1 && world <= 64 && world <= cfg->num_experts,
+                 "moe_ep: world=%d must be in [1, min(64, num_experts=%d)]", world, cfg->num_experts);
   return MLXR_CU_OK;
 }
 
-static mlxr_cu_moe_config ep_local_config(const mlxr_cu_moe_config* cfg, int world) {
-  mlxr_cu_moe_config lc = *cfg;
-  lc.num_experts = cfg->num_experts / world;
-  lc.shared_expert_intermediate_size = 0;
-  return lc;  // num_experts_per_tok stays K: the number of slots per pair
-}
 
 // Receiving side: num_pairs pairs of K slots (flat rows), num_rows filled slots.
 static Layout ep_experts_layout(const mlxr_cu_moe_config* lc, int64_t num_pairs, int64_t num_rows) {
@@ -685,7 +679,8 @@ int mlxr_cu_moe_ep_workspace_size(const mlxr_cu_moe_config* cfg, int world, int6
   MLXR_CHECK_ARG(bytes != nullptr, "moe_ep_workspace_size: bytes is NULL");
   MLXR_CHECK_ARG(max_recv_pairs >= 0 && max_recv_rows >= 0, "moe_ep_workspace_size: negative receive bound");
   if (int rc = validate(cfg, max_recv_pairs)) return rc;
-  const mlxr_cu_moe_config lc = ep_local_config(cfg, world);
+  mlxr_cu_moe_config lc = *cfg;  // any placement: up to all experts on this rank
+  lc.shared_expert_intermediate_size = 0;
   size_t dest_off = 0;
   size_t need = ep_dispatch_bytes(cfg, num_tokens, &dest_off);
   const size_t e2 = ep_experts_layout(&lc, max_recv_pairs, max_recv_rows).total;
@@ -697,7 +692,7 @@ int mlxr_cu_moe_ep_workspace_size(const mlxr_cu_moe_config* cfg, int world, int6
 }
 
 int mlxr_cu_moe_ep_dispatch(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights, int world,
-                            const void* x, int64_t num_tokens, int32_t* send_counts, int32_t* pair_pos,
+                            const int32_t* placement, const void* x, int64_t num_tokens, int32_t* send_counts, int32_t* pair_pos,
                             void* x_send, int32_t* meta_send, float* shared_gate, void* workspace,
                             size_t workspace_bytes, void* stream) {
   if (int rc = validate(cfg, num_tokens)) return rc;
@@ -723,7 +718,7 @@ int mlxr_cu_moe_ep_dispatch(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_wei
   const int K = cfg->num_experts_per_tok;
   const int64_t R = L.R;
   int32_t* dest = at<int32_t>(ws, dest_off);
-  launch_pdl(ep_pair_dest_kernel, (unsigned)((R + 255) / 256), 256, 0, st, at<int32_t>(ws, L.idx), num_tokens, K, world, dest,
+  launch_pdl(ep_pair_dest_kernel, (unsigned)((R + 255) / 256), 256, 0, st, at<int32_t>(ws, L.idx), num_tokens, K, world, placement, dest,
                                                                     at<int>(ws, L.status));
   MLXR_LAUNCH_CHECK("ep_pair_dest_kernel");
   // Stable sort of the pairs by destination rank: the block permutation with
@@ -738,10 +733,11 @@ int mlxr_cu_moe_ep_dispatch(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_wei
   if (int rc = run_permute(P, dest, x, ws, at<int32_t>(ws, L.counts), at<int32_t>(ws, L.offsets),
                            at<int32_t>(ws, L.sorted), pair_pos, static_cast<uint16_t*>(x_send), 0, st, 1))
     return rc;
-  launch_pdl(ep_counts_kernel, 1, 1024, 0, st, at<int32_t>(ws, L.idx), R, world, at<int32_t>(ws, L.counts), send_counts);
+  launch_pdl(ep_counts_kernel, 1, 1024, 0, st, at<int32_t>(ws, L.idx), R, world, placement, at<int32_t>(ws, L.counts),
+             send_counts);
   MLXR_LAUNCH_CHECK("ep_counts_kernel");
   launch_pdl(ep_pair_meta_kernel, (unsigned)((num_tokens + 127) / 128), 128, 0, st, 
-      at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w), pair_pos, num_tokens, K, world, P.rows, meta_send,
+      at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w), pair_pos, num_tokens, K, world, placement, P.rows, meta_send,
       at<int>(ws, L.status));
   MLXR_LAUNCH_CHECK("ep_pair_meta_kernel");
   if (cfg->shared_expert_intermediate_size > 0)
@@ -750,12 +746,15 @@ int mlxr_cu_moe_ep_dispatch(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_wei
   return MLXR_CU_OK;
 }
 
-int mlxr_cu_moe_ep_experts(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* local_weights, int world,
-                           const void* x_recv, const int32_t* meta_recv, int64_t num_pairs, int64_t num_rows,
-                           void* partial, void* workspace, size_t workspace_bytes, void* stream) {
-  if (int rc = ep_check_world(cfg, world)) return rc;
+int mlxr_cu_moe_ep_experts(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* local_weights,
+                           int num_local_experts, const void* x_recv, const int32_t* meta_recv, int64_t num_pairs,
+                           int64_t num_rows, void* partial, void* workspace, size_t workspace_bytes, void* stream) {
   if (int rc = validate(cfg, num_pairs)) return rc;
-  const mlxr_cu_moe_config lc = ep_local_config(cfg, world);
+  MLXR_CHECK_ARG(num_local_experts >= 1 && num_local_experts <= cfg->num_experts,
+                 "moe_ep_experts: num_local_experts=%d must be in [1, num_experts]", num_local_experts);
+  mlxr_cu_moe_config lc = *cfg;
+  lc.num_experts = num_local_experts;
+  lc.shared_expert_intermediate_size = 0;
   MLXR_CHECK_ARG(local_weights != nullptr, "moe_ep_experts: weights is NULL");
   MLXR_CHECK_ARG(num_rows >= 0 && num_rows <= num_pairs * lc.num_experts_per_tok,
                  "moe_ep_experts: num_rows=%lld must be in [0, num_pairs * K]", (long long)num_rows);

@@ -872,7 +872,9 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict
 }
 
 // ------------------------------------------------- expert parallelism ---
-// Expert e lives on rank e % world as that rank's local expert e / world.
+// Expert e lives on rank placement[e] >> 16 as its local expert
+// placement[e] & 0xFFFF; without a placement table, on rank e % world as
+// local expert e / world.
 // Every token is sent once to each rank that owns at least one of its top-k
 // experts (one "pair" per (token, rank)); the pair carries up to K slots of
 // (local expert, top-k weight), and the receiving rank returns one partial
@@ -881,8 +883,15 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict
 // dest[t*K + k] = rank of expert idx[t*K + k] when k is the first of token t
 // that goes to that rank, -1 otherwise (so a stable sort of the non-negative
 // entries lists the pairs by rank, then token).
+__device__ __forceinline__ int ep_rank_of(int e, int world, const int32_t* placement) {
+  return placement ? (int)((uint32_t)placement[e] >> 16) : e % world;
+}
+__device__ __forceinline__ int ep_local_of(int e, int world, const int32_t* placement) {
+  return placement ? (placement[e] & 0xFFFF) : e / world;
+}
+
 __global__ void ep_pair_dest_kernel(const int32_t* __restrict__ idx, int64_t T, int K, int world,
-                                    int32_t* __restrict__ dest, int* status) {
+                                    const int32_t* __restrict__ placement, int32_t* __restrict__ dest, int* status) {
   pdl_wait();
   pdl_launch_dependents();
   const int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -895,11 +904,16 @@ __global__ void ep_pair_dest_kernel(const int32_t* __restrict__ idx, int64_t T, 
     dest[f] = -1;
     return;
   }
-  const int r = e % world;
+  const int r = ep_rank_of(e, world, placement);
+  if (r < 0 || r >= world) {
+    atomicCAS(status, 0, (int)kDevBadIndex);
+    dest[f] = -1;
+    return;
+  }
   bool first = true;
   for (int j = 0; j < k; ++j) {
     const int ej = idx[t * K + j];
-    if (ej >= 0 && ej % world == r) {
+    if (ej >= 0 && ep_rank_of(ej, world, placement) == r) {
       first = false;
       break;
     }
@@ -910,6 +924,7 @@ __global__ void ep_pair_dest_kernel(const int32_t* __restrict__ idx, int64_t T, 
 // send_counts[2r] = pairs sent to rank r (from the pair permutation),
 // send_counts[2r + 1] = (token, k) rows those pairs carry. One CTA.
 __global__ void __launch_bounds__(1024) ep_counts_kernel(const int32_t* __restrict__ idx, int64_t R, int world,
+                                                        const int32_t* __restrict__ placement,
                                                         const int32_t* __restrict__ pair_counts,
                                                         int32_t* __restrict__ send_counts) {
   pdl_wait();
@@ -919,7 +934,10 @@ __global__ void __launch_bounds__(1024) ep_counts_kernel(const int32_t* __restri
   __syncthreads();
   for (int64_t f = threadIdx.x; f < R; f += blockDim.x) {
     const int e = idx[f];
-    if (e >= 0) atomicAdd(&hist[e % world], 1);
+    if (e >= 0) {
+      const int r = ep_rank_of(e, world, placement);
+      if (r >= 0 && r < world) atomicAdd(&hist[r], 1);
+    }
   }
   __syncthreads();
   if (threadIdx.x < world) {
@@ -938,7 +956,8 @@ __device__ __forceinline__ int32_t ep_slot(int local_expert, uint16_t weight_bit
 // bf16 weight bits; -1 fills the unused slots.
 __global__ void ep_pair_meta_kernel(const int32_t* __restrict__ idx, const uint16_t* __restrict__ w,
                                     const int32_t* __restrict__ pair_pos, int64_t T, int K, int world,
-                                    int64_t max_pairs, int32_t* __restrict__ meta, int* status) {
+                                    const int32_t* __restrict__ placement, int64_t max_pairs,
+                                    int32_t* __restrict__ meta, int* status) {
   pdl_wait();
   pdl_launch_dependents();
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -951,11 +970,12 @@ __global__ void ep_pair_meta_kernel(const int32_t* __restrict__ idx, const uint1
       atomicCAS(status, 0, (int)kDevBadIndex);
       continue;
     }
-    const int r = ti[k] % world;
+    const int r = ep_rank_of(ti[k], world, placement);
     int j = 0;
     for (int k2 = k; k2 < K; ++k2) {
       const int e = ti[k2];
-      if (e >= 0 && e % world == r) meta[pos * K + j++] = ep_slot(e / world, w[t * K + k2]);
+      if (e >= 0 && ep_rank_of(e, world, placement) == r)
+        meta[pos * K + j++] = ep_slot(ep_local_of(e, world, placement), w[t * K + k2]);
     }
     for (; j < K; ++j) meta[pos * K + j] = -1;
   }

@@ -142,7 +142,7 @@ def _load():
     lib.mlxr_cu_synth_normal_bf16.argtypes = [C.c_uint64, C.c_uint64, I64, C.c_float, P, P]
     cfg_p, w_p = C.POINTER(MoeConfig), C.POINTER(MoeWeights)
     lib.mlxr_cu_moe_ep_workspace_size.argtypes = [cfg_p, I32, I64, I64, I64, C.POINTER(C.c_size_t)]
-    lib.mlxr_cu_moe_ep_dispatch.argtypes = [cfg_p, w_p, I32, P, I64, P, P, P, P, P, P, C.c_size_t, P]
+    lib.mlxr_cu_moe_ep_dispatch.argtypes = [cfg_p, w_p, I32, P, P, I64, P, P, P, P, P, P, C.c_size_t, P]
     lib.mlxr_cu_moe_ep_experts.argtypes = [cfg_p, w_p, I32, P, P, I64, I64, P, P, C.c_size_t, P]
     lib.mlxr_cu_moe_ep_combine.argtypes = [cfg_p, w_p, P, I64, P, I64, P, P, P, P, C.c_size_t, P]
     for name in EXPORTS:

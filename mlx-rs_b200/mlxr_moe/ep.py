@@ -3,8 +3,10 @@
 The reference runs the whole block on one device (Qwen35MoeBlock::forward,
 crates/mlxr-lm/src/qwen3_5/text/moe.rs:116-146, has no collective). Here the
 experts of a block are spread over `world` ranks: expert e lives on rank
-e % world as that rank's local expert e // world; the router and the shared
-expert are replicated, so routing is bit-identical to one device. A step on
+placement[e] (by default e % world; `balanced_placement` spreads measured
+expert loads evenly) as that rank's local expert (in increasing expert id);
+the router and the shared expert are replicated, so routing is
+bit-identical to one device. A step on
 each rank:
 
 1. dispatch (`mlxr_cu_moe_ep_dispatch`): route the rank's own tokens and list
@@ -31,12 +33,46 @@ from . import _lib
 from .moe import QuantizedSwitchLinear, Qwen35MoeBlock, SplitSwitchFfn
 
 
-def local_switch(sw: SplitSwitchFfn, rank: int, world: int) -> SplitSwitchFfn:
-    """The experts {e : e % world == rank} of a switch layer, in order e // world."""
+def strided_placement(num_experts: int, world: int) -> list[int]:
+    """Expert e on rank e % world (the default: neighbouring ids on different ranks)."""
+    return [e % world for e in range(num_experts)]
+
+
+def balanced_placement(loads, world: int) -> list[int]:
+    """Longest-processing-time greedy: experts in decreasing load, each to the
+    rank with the least load so far (ties: fewer experts, then lower rank).
+    `loads` are per-expert row counts measured on a calibration batch; with
+    skewed (Zipf) routing this keeps the busiest rank near the mean."""
+    loads = [float(v) for v in loads]
+    order = sorted(range(len(loads)), key=lambda e: (-loads[e], e))
+    tot = [0.0] * world
+    cnt = [0] * world
+    out = [0] * len(loads)
+    for e in order:
+        r = min(range(world), key=lambda q: (tot[q], cnt[q], q))
+        out[e] = r
+        tot[r] += loads[e]
+        cnt[r] += 1
+    return out
+
+
+def placement_table(rank_of: list[int]) -> list[int]:
+    """(rank << 16) | local index, local indices in increasing expert id."""
+    seen: dict[int, int] = {}
+    table = []
+    for r in rank_of:
+        table.append((r << 16) | seen.get(r, 0))
+        seen[r] = seen.get(r, 0) + 1
+    return table
+
+
+def local_switch(sw: SplitSwitchFfn, experts: list[int]) -> SplitSwitchFfn:
+    """The given experts of a switch layer, in that order."""
 
     def take(q: QuantizedSwitchLinear):
-        return QuantizedSwitchLinear(q.weight[rank::world].contiguous(), q.scales[rank::world].contiguous(),
-                                     q.biases[rank::world].contiguous(), q.group_size, q.bits)
+        idx = torch.tensor(experts, dtype=torch.long, device=q.weight.device)
+        return QuantizedSwitchLinear(q.weight.index_select(0, idx).contiguous(), q.scales.index_select(0, idx).contiguous(),
+                                     q.biases.index_select(0, idx).contiguous(), q.group_size, q.bits)
 
     return SplitSwitchFfn(take(sw.gate_proj), take(sw.up_proj), take(sw.down_proj))
 
@@ -56,19 +92,27 @@ class DispatchPlan:
 
 class ExpertParallelMoeBlock:
     """One rank's share of a Qwen35MoeBlock: the router and shared expert
-    (replicated) and the experts e with e % world == rank."""
+    (replicated) and the experts that `placement` (rank of each expert; by
+    default e % world) puts on this rank."""
 
-    def __init__(self, full: Qwen35MoeBlock, rank: int, world: int):
+    def __init__(self, full: Qwen35MoeBlock, rank: int, world: int, placement: list[int] | None = None):
         cfg = full.cfg
-        if world < 1 or cfg.num_experts % world:
-            raise _lib.MlxrError(_lib.ERR_INVALID_ARGUMENT,
-                                 f"world={world} must divide num_experts={cfg.num_experts}")
+        if world < 1:
+            raise _lib.MlxrError(_lib.ERR_INVALID_ARGUMENT, f"world={world} must be >= 1")
+        rank_of = list(placement) if placement is not None else strided_placement(cfg.num_experts, world)
+        if len(rank_of) != cfg.num_experts or any(r < 0 or r >= world for r in rank_of):
+            raise _lib.MlxrError(_lib.ERR_INVALID_ARGUMENT, "placement must give a rank in [0, world) per expert")
+        mine = [e for e in range(cfg.num_experts) if rank_of[e] == rank]
+        if not mine:
+            raise _lib.MlxrError(_lib.ERR_INVALID_ARGUMENT, f"placement leaves rank {rank} without experts")
         self.cfg, self.rank, self.world = cfg, rank, world
+        self.rank_of, self.experts_here = rank_of, mine
+        self.placement = torch.tensor(placement_table(rank_of), dtype=torch.int32, device=full.gate.device)
         self.gate = full.gate
         self.router_bias = full.router_bias
         self.shared_expert = full.shared_expert
         self.shared_expert_gate = full.shared_expert_gate
-        self.switch_mlp = local_switch(full.switch_mlp, rank, world)
+        self.switch_mlp = local_switch(full.switch_mlp, mine)
         self._ccfg = cfg.to_c()
         z = _lib.QLinear(None, None, None)
         se, seg = self.shared_expert, self.shared_expert_gate
@@ -81,8 +125,9 @@ class ExpertParallelMoeBlock:
         self._ws = None
 
     @classmethod
-    def from_block(cls, full: Qwen35MoeBlock, rank: int, world: int) -> "ExpertParallelMoeBlock":
-        return cls(full, rank, world)
+    def from_block(cls, full: Qwen35MoeBlock, rank: int, world: int,
+                   placement: list[int] | None = None) -> "ExpertParallelMoeBlock":
+        return cls(full, rank, world, placement)
 
     def workspace_bytes(self, T: int, max_recv_pairs: int, max_recv_rows: int) -> int:
         n = C.c_size_t(0)
@@ -101,7 +146,8 @@ class ExpertParallelMoeBlock:
         T, K = x.shape[0], self.cfg.num_experts_per_tok
         plan = DispatchPlan(T, K, self.cfg.hidden_size, self.world, self.shared_expert is not None, x.device)
         st = torch.cuda.current_stream(x.device).cuda_stream
-        _lib.call("mlxr_cu_moe_ep_dispatch", C.byref(self._ccfg), C.byref(self._cw_rep), self.world, x.data_ptr(), T,
+        _lib.call("mlxr_cu_moe_ep_dispatch", C.byref(self._ccfg), C.byref(self._cw_rep), self.world,
+                  self.placement.data_ptr(), x.data_ptr(), T,
                   plan.send_counts.data_ptr(), plan.pair_pos.data_ptr(), plan.x_send.data_ptr(),
                   plan.meta_send.data_ptr(), None if plan.shared_gate is None else plan.shared_gate.data_ptr(),
                   ws.data_ptr(), ws.numel(), st)
@@ -111,7 +157,7 @@ class ExpertParallelMoeBlock:
         P = x_recv.shape[0]
         partial = torch.empty((max(P, 1), self.cfg.hidden_size), dtype=torch.bfloat16, device=x_recv.device)
         st = torch.cuda.current_stream(x_recv.device).cuda_stream
-        _lib.call("mlxr_cu_moe_ep_experts", C.byref(self._ccfg), C.byref(self._cw_loc), self.world,
+        _lib.call("mlxr_cu_moe_ep_experts", C.byref(self._ccfg), C.byref(self._cw_loc), len(self.experts_here),
                   x_recv.data_ptr(), meta_recv.data_ptr(), P, num_rows, partial.data_ptr(), ws.data_ptr(), ws.numel(),
                   st)
         return partial[:P]

@@ -101,6 +101,34 @@ def test_ep_loopback_matches_single_device(name, T, world):
         assert_mostly_tight(bf16_np(outs[r]), bf16_np(want), TIGHT_ATOL, TIGHT_RTOL, TIGHT_FRAC, f"rank {r} tight")
 
 
+@pytest.mark.parametrize("name,T,world", [("c3", 256, 4), ("c1", 32, 3)])
+def test_ep_loopback_balanced_placement(name, T, world):
+    """Experts placed by measured load (uneven counts per rank) give the same
+    outputs as one device, and the plan names each expert's rank and local slot."""
+    from mlxr_moe.ep import balanced_placement
+
+    full = block_for(name)
+    cfg = full.cfg
+    xs = [synth.make_input(T, cfg.hidden_size, stream_offset=90 + r) for r in range(world)]
+    loads = np.zeros(cfg.num_experts)
+    for x in xs:
+        idx, _ = full.router(x)
+        loads += np.bincount(idx.cpu().numpy().ravel(), minlength=cfg.num_experts)
+    place = balanced_placement(loads, world)
+    blocks = [ExpertParallelMoeBlock.from_block(full, r, world, place) for r in range(world)]
+    per_rank = [sum(loads[e] for e in range(cfg.num_experts) if place[e] == r) for r in range(world)]
+    assert max(per_rank) <= loads.sum() / world + loads.max()  # the greedy bound
+    outs = loopback_forward(blocks, xs)
+    torch.cuda.synchronize()
+    for b in blocks:
+        b.status()
+    for r in range(world):
+        want = full.forward(xs[r])
+        torch.cuda.synchronize()
+        assert_close_bf16(bf16_np(outs[r]), bf16_np(want), ATOL, RTOL, f"rank {r}")
+        assert_mostly_tight(bf16_np(outs[r]), bf16_np(want), TIGHT_ATOL, TIGHT_RTOL, TIGHT_FRAC, f"rank {r} tight")
+
+
 def test_ep_loopback_matches_oracle():
     full = block_for("c1")
     world, T = 4, 32
