@@ -449,17 +449,18 @@ def bench_extra(args, dev, st, flush, peaks):
 
 
 def bench_ep(args, dev, st, world, rank):
-    """Expert parallelism across the `world` ranks (NCCL all-to-all of the
-    pairs and of the partial rows): the largest BASELINE configurations with
-    their token batch split evenly over the ranks (strong scaling: fixed total
-    tokens). Rank r holds experts e % world == r. Times are max over ranks;
-    the whole batch on rank 0 alone (full block, one GPU) gives the one-GPU
-    time in the same run."""
+    """Expert parallelism across the `world` ranks: the largest BASELINE
+    configurations with their token batch split evenly over the ranks (strong
+    scaling: fixed total tokens). Experts are placed by loads measured on a
+    calibration batch. The step exchanges pairs and partial rows inside the
+    kernels over peer memory (the product path); the same step over NCCL
+    all-to-all is timed beside it. Times are max over ranks; the whole batch on
+    rank 0 alone (full block, one GPU) gives the one-GPU time in the same run."""
     import torch
     import torch.distributed as dist
 
     from mlxr_moe import synth
-    from mlxr_moe.ep import ExpertParallelMoeBlock, TorchDistExchange, balanced_placement
+    from mlxr_moe.ep import ExpertParallelMoeBlock, PeerComm, TorchDistExchange, balanced_placement
 
     ex = TorchDistExchange()
     res = {}
@@ -481,26 +482,37 @@ def bench_ep(args, dev, st, world, rank):
         blk = ExpertParallelMoeBlock.from_block(full, rank, world, place)
         bounds = dict(max_recv_pairs=world * T, max_recv_rows=world * T * K)
         n_steps = max(5, args.steps // 2)
-        with torch.cuda.stream(st):
-            for i in range(3):
-                blk.forward(xs[i % 2], ex, **bounds)
+        comm = PeerComm(rank, world, cap=T, hidden=D, k=K)
+        exp_rows = max(1, T_total * K // world)
+
+        def timed(fn):
+            with torch.cuda.stream(st):
+                for i in range(3):
+                    fn(xs[i % 2])
+                torch.cuda.synchronize(dev)
+                blk.status()
+                dist.barrier()
+                times = []
+                for i in range(n_steps):
+                    a = torch.cuda.Event(enable_timing=True)
+                    b = torch.cuda.Event(enable_timing=True)
+                    a.record(st)
+                    fn(xs[i % 2])
+                    b.record(st)
+                    b.synchronize()
+                    times.append(a.elapsed_time(b))
             torch.cuda.synchronize(dev)
             blk.status()
-            dist.barrier()
-            times = []
-            for i in range(n_steps):
-                a = torch.cuda.Event(enable_timing=True)
-                b = torch.cuda.Event(enable_timing=True)
-                a.record(st)
-                blk.forward(xs[i % 2], ex, **bounds)
-                b.record(st)
-                b.synchronize()
-                times.append(a.elapsed_time(b))
+            t = torch.tensor([statistics.median(times)], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+
+        # Peer-memory exchange (the product path), then the NCCL exchange for reference.
+        ms = timed(lambda xx: blk.forward_p2p(xx, comm, expected_rows=exp_rows))
+        ms_nccl = timed(lambda xx: blk.forward(xx, ex, **bounds))
         torch.cuda.synchronize(dev)
-        blk.status()
-        t = torch.tensor([statistics.median(times)], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        dist.barrier()
+        comm.close()
         one = None
         if rank == 0:  # the whole batch on this GPU alone, for the speed-up
             x1 = synth.make_input(T_total, D, stream_offset=600, device=dev)
@@ -524,8 +536,11 @@ def bench_ep(args, dev, st, world, rank):
         res[name] = dict(tokens=T_total, tokens_per_rank=T, ms=ms, tokens_per_s=T_total / (ms / 1e3),
                          tflops_total=fl / (ms / 1e3) / 1e12, one_gpu_ms=one,
                          speedup_vs_one_gpu=(one / ms) if one else None, zipf=spec["zipf"],
+                         exchange="peer memory: dispatch/combine kernels store into the other ranks' CUDA-IPC "
+                                  "buffers over NVLink, flag waits on the GPU, no host synchronisation",
+                         nccl_ms=ms_nccl, nccl_speedup_vs_one_gpu=(one / ms_nccl) if one else None,
                          placement="balanced: experts spread greedily by loads measured on a calibration batch",
-                         exchange="NCCL all_to_all_single: counts, pair rows, slot rows, partial rows")
+                         nccl_exchange="NCCL all_to_all_single: counts, pair rows, slot rows, partial rows")
         del blk, full, xs
         torch.cuda.empty_cache()
     return res

@@ -303,6 +303,50 @@ MLXR_CU_API int mlxr_cu_moe_ep_combine(const mlxr_cu_moe_config* cfg, const mlxr
                                        const int32_t* pair_pos, const float* shared_gate, void* out,
                                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------- expert parallelism over peer memory -- */
+/* The same steps as above with the exchange done by the kernels over NVLink
+ * (no counterpart in the reference). Every rank creates a communicator with
+ * an exchange buffer sized for `cap` tokens per rank, shares its CUDA IPC
+ * handle (MLXR_CU_IPC_HANDLE_BYTES bytes) with the other ranks (e.g. through
+ * a host all-gather) and connects with all handles in rank order. Per step,
+ * with the same `epoch` on every rank (1, 2, 3, ...):
+ *   dispatch_p2p: route; store each pair straight into its destination's
+ *     buffer; publish counts and a flag there;
+ *   experts_p2p: wait (bounded) for every rank's flag; run the received
+ *     pairs through the local experts; store each partial row straight into
+ *     its owner's buffer; publish a flag there;
+ *   combine_p2p: the shared expert, then wait for every rank's flag and add
+ *     up each token's partial rows.
+ * No host synchronisation is needed between the steps. A rank that never
+ * publishes makes the others' waits expire after 10 s with
+ * MLXR_CU_ERR_TIMEOUT in the status word. Ranks must be on different GPUs. */
+#define MLXR_CU_IPC_HANDLE_BYTES 64
+
+MLXR_CU_API int mlxr_cu_ep_comm_create(int world, int rank, int64_t cap, int hidden, int k, void** comm,
+                                       void* ipc_handle);
+MLXR_CU_API int mlxr_cu_ep_comm_connect(void* comm, const void* ipc_handles);
+MLXR_CU_API int mlxr_cu_ep_comm_destroy(void* comm);
+
+/* Workspace for one rank's three peer-memory steps; expected_rows (the
+ * filled slots a rank usually receives, e.g. T_total * K / world) picks the
+ * tile widths; the buffers hold the worst case. */
+MLXR_CU_API int mlxr_cu_moe_ep_p2p_workspace_size(const mlxr_cu_moe_config* cfg, const void* comm, int64_t num_tokens,
+                                                  int num_local_experts, int64_t expected_rows, size_t* bytes);
+
+/* pair_pos [T*K] int32 out: where each pair's partial row comes back;
+ * shared_gate [T] fp32 out as for mlxr_cu_moe_ep_dispatch. */
+MLXR_CU_API int mlxr_cu_moe_ep_dispatch_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights,
+                                            void* comm, const int32_t* placement, const void* x, int64_t num_tokens,
+                                            int32_t* pair_pos, float* shared_gate, uint32_t epoch, void* workspace,
+                                            size_t workspace_bytes, void* stream);
+MLXR_CU_API int mlxr_cu_moe_ep_experts_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* local_weights,
+                                           int num_local_experts, void* comm, int64_t expected_rows, uint32_t epoch,
+                                           void* workspace, size_t workspace_bytes, void* stream);
+MLXR_CU_API int mlxr_cu_moe_ep_combine_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights,
+                                           void* comm, const void* x, int64_t num_tokens, const int32_t* pair_pos,
+                                           const float* shared_gate, void* out, uint32_t epoch, void* workspace,
+                                           size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------ synthetic inputs -- */
 
 /* Seeded N(0, stddev^2) samples rounded to bf16: Philox4x32-10 keyed by

@@ -109,7 +109,9 @@ static int pick_splits(int64_t items, int ksteps) {
   return sp < 1 ? 1 : sp;
 }
 
-static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T, int64_t rows_cap = -1) {
+// rows_cap: expert rows the buffers hold (default T*K); bn_rows: the rows
+// the tile widths are chosen for (default: rows_cap).
+static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T, int64_t rows_cap = -1, int64_t bn_rows = -1) {
   Layout L;
   L.T = T;
   L.E = c->num_experts;
@@ -123,7 +125,7 @@ static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T, int64_t rows_c
   L.sh_rows_pad = T > 256 ? T : 256;
   L.nblk = (int)((L.R + PERM_ROWS - 1) / PERM_ROWS);
   if (L.nblk < 1) L.nblk = 1;
-  const double avg = L.E > 0 ? (double)L.rows / L.E : 0.0;
+  const double avg = L.E > 0 ? (double)(bn_rows >= 0 ? bn_rows : L.rows) / L.E : 0.0;
   L.bn1 = pick_bn(avg, 128);
   L.bn2 = pick_bn(avg, (L.D % 256 == 0) ? 128 : 256);
   L.bns = pick_bn((double)T, 64);
@@ -294,7 +296,7 @@ static int run_permute(const Layout& L, const int32_t* idx, const void* x, void*
                                                                        sorted, inv);
     MLXR_LAUNCH_CHECK("permute_scatter_kernel");
   }
-  if (L.R > 0 && L.rows > 0) {
+  if (xs && L.R > 0 && L.rows > 0) {
     const int64_t gblocks = (L.rows + 7) / 8;
     const int gather_grid = (int)(gblocks < 4 * 148 ? gblocks : 4 * 148);
     launch_pdl(permute_gather_kernel, gather_grid, 256, 0, st, sorted, L.rows, L.R, L.K, static_cast<const uint16_t*>(x), L.D,
@@ -811,6 +813,284 @@ int mlxr_cu_moe_ep_combine(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weig
       static_cast<const uint16_t*>(partial_back), pair_pos, L.K, L.D, num_pairs, ysh, shared_gate,
       static_cast<uint16_t*>(out), at<int>(ws, L.status));
   MLXR_LAUNCH_CHECK("ep_combine_kernel");
+  return MLXR_CU_OK;
+}
+
+// ----------------------------------------- expert parallelism, peer memory --
+// The same three steps with the exchange done by the kernels themselves
+// over NVLink (see EpBufLayout in routing.cuh): no collective library and no
+// host read of the counts. A communicator holds this rank's exchange buffer
+// and every other rank's buffer mapped through CUDA IPC.
+
+}  // extern "C"
+
+namespace mlxr {
+struct EpComm {
+  int world = 0, rank = 0, D = 0, K = 0, device = -1;
+  int64_t cap = 0;
+  EpBufLayout bl{};
+  uint8_t* local = nullptr;
+  EpPeers peers{};
+  bool opened[EP_MAX_WORLD] = {};
+};
+
+static int ep_comm_check(const void* comm, const mlxr_cu_moe_config* cfg) {
+  MLXR_CHECK_ARG(comm != nullptr, "moe_ep_p2p: comm is NULL");
+  const EpComm* c = static_cast<const EpComm*>(comm);
+  MLXR_CHECK_ARG(c->local != nullptr, "moe_ep_p2p: comm is not initialised");
+  MLXR_CHECK_ARG(cfg->hidden_size == c->D && cfg->num_experts_per_tok == c->K,
+                 "moe_ep_p2p: comm was made for hidden=%d K=%d, block has hidden=%d K=%d", c->D, c->K,
+                 cfg->hidden_size, cfg->num_experts_per_tok);
+  for (int r = 0; r < c->world; ++r)
+    MLXR_CHECK_ARG(c->peers.base[r] != nullptr, "moe_ep_p2p: rank %d's buffer is not connected", r);
+  return MLXR_CU_OK;
+}
+
+// Dispatch scratch on top of the block layout: destinations, slot rows, counts.
+struct EpP2PDispatch {
+  size_t dest, meta, counts, total;
+};
+static EpP2PDispatch ep_p2p_dispatch_layout(const mlxr_cu_moe_config* c, int world, int64_t T) {
+  EpP2PDispatch d{};
+  const Layout L = make_layout(c, T);
+  size_t o = L.total;
+  const int K = c->num_experts_per_tok;
+  auto take = [&](size_t bytes) {
+    const size_t at_ = o;
+    o = align256(o + (bytes ? bytes : 1));
+    return at_;
+  };
+  d.dest = take((size_t)T * K * 4);
+  d.meta = take((size_t)T * (K < world ? K : world) * K * 4);
+  d.counts = take((size_t)world * 2 * 4);
+  d.total = o;
+  return d;
+}
+static Layout ep_p2p_experts_layout(const mlxr_cu_moe_config* c, int num_local, int world, int64_t cap,
+                                    int64_t expected_rows) {
+  mlxr_cu_moe_config lc = *c;
+  lc.num_experts = num_local;
+  lc.shared_expert_intermediate_size = 0;
+  const int K = c->num_experts_per_tok;
+  const int64_t pairs = (int64_t)world * cap;
+  const int64_t rows = pairs * (K < num_local ? K : num_local);
+  return make_layout(&lc, pairs, rows, expected_rows);
+}
+}  // namespace mlxr
+
+extern "C" {
+
+int mlxr_cu_ep_comm_create(int world, int rank, int64_t cap, int hidden, int k, void** comm, void* ipc_handle) {
+  MLXR_CHECK_ARG(world >= 1 && world <= EP_MAX_WORLD && rank >= 0 && rank < world,
+                 "ep_comm_create: world=%d rank=%d (world must be in [1, %d])", world, rank, EP_MAX_WORLD);
+  MLXR_CHECK_ARG(cap >= 1 && hidden > 0 && hidden % 8 == 0 && k >= 1 && k <= RT_MAXK,
+                 "ep_comm_create: cap=%lld hidden=%d k=%d", (long long)cap, hidden, k);
+  MLXR_CHECK_ARG(comm && ipc_handle, "ep_comm_create: NULL output");
+  EpComm* c = new EpComm();
+  c->world = world;
+  c->rank = rank;
+  c->cap = cap;
+  c->D = hidden;
+  c->K = k;
+  c->bl = ep_buf_layout(world, cap, hidden, k);
+  cudaError_t e = cudaGetDevice(&c->device);
+  if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&c->local), (size_t)c->bl.total);
+  if (e == cudaSuccess) e = cudaMemset(c->local, 0, (size_t)c->bl.total);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, c->local);
+  if (e != cudaSuccess) {
+    if (c->local) cudaFree(c->local);
+    delete c;
+    return check_cuda(e, "ep_comm_create");
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == MLXR_CU_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  c->peers.base[rank] = c->local;
+  *comm = c;
+  return MLXR_CU_OK;
+}
+
+int mlxr_cu_ep_comm_connect(void* comm, const void* ipc_handles) {
+  MLXR_CHECK_ARG(comm && ipc_handles, "ep_comm_connect: NULL argument");
+  EpComm* c = static_cast<EpComm*>(comm);
+  for (int r = 0; r < c->world; ++r) {
+    if (r == c->rank || c->opened[r]) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, static_cast<const uint8_t*>(ipc_handles) + (size_t)r * sizeof(h), sizeof(h));
+    void* p = nullptr;
+    MLXR_CUDA_TRY(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+    c->peers.base[r] = static_cast<uint8_t*>(p);
+    c->opened[r] = true;
+  }
+  return MLXR_CU_OK;
+}
+
+int mlxr_cu_ep_comm_destroy(void* comm) {
+  if (!comm) return MLXR_CU_OK;
+  EpComm* c = static_cast<EpComm*>(comm);
+  int rc = MLXR_CU_OK;
+  for (int r = 0; r < c->world; ++r)
+    if (c->opened[r]) {
+      const cudaError_t e = cudaIpcCloseMemHandle(c->peers.base[r]);
+      if (e != cudaSuccess && rc == MLXR_CU_OK) rc = check_cuda(e, "cudaIpcCloseMemHandle");
+    }
+  if (c->local) {
+    const cudaError_t e = cudaFree(c->local);
+    if (e != cudaSuccess && rc == MLXR_CU_OK) rc = check_cuda(e, "cudaFree(exchange buffer)");
+  }
+  delete c;
+  return rc;
+}
+
+int mlxr_cu_moe_ep_p2p_workspace_size(const mlxr_cu_moe_config* cfg, const void* comm, int64_t num_tokens,
+                                      int num_local_experts, int64_t expected_rows, size_t* bytes) {
+  if (int rc = validate(cfg, num_tokens)) return rc;
+  if (int rc = ep_comm_check(comm, cfg)) return rc;
+  MLXR_CHECK_ARG(bytes && num_local_experts >= 1 && num_local_experts <= cfg->num_experts,
+                 "moe_ep_p2p_workspace_size: bad num_local_experts=%d", num_local_experts);
+  const EpComm* c = static_cast<const EpComm*>(comm);
+  MLXR_CHECK_ARG(num_tokens <= c->cap, "moe_ep_p2p: %lld tokens exceed the comm capacity %lld",
+                 (long long)num_tokens, (long long)c->cap);
+  size_t need = ep_p2p_dispatch_layout(cfg, c->world, num_tokens).total;
+  const size_t e2 = ep_p2p_experts_layout(cfg, num_local_experts, c->world, c->cap, expected_rows).total;
+  const size_t e3 = make_layout(cfg, num_tokens).total;
+  if (e2 > need) need = e2;
+  if (e3 > need) need = e3;
+  *bytes = need;
+  return MLXR_CU_OK;
+}
+
+int mlxr_cu_moe_ep_dispatch_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights, void* comm,
+                                const int32_t* placement, const void* x, int64_t num_tokens, int32_t* pair_pos,
+                                float* shared_gate, uint32_t epoch, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+  if (int rc = validate(cfg, num_tokens)) return rc;
+  if (int rc = ep_comm_check(comm, cfg)) return rc;
+  EpComm* c = static_cast<EpComm*>(comm);
+  const int world = c->world;
+  MLXR_CHECK_ARG(num_tokens <= c->cap, "moe_ep_dispatch_p2p: %lld tokens exceed the comm capacity %lld",
+                 (long long)num_tokens, (long long)c->cap);
+  MLXR_CHECK_ARG(weights != nullptr, "moe_ep_dispatch_p2p: weights is NULL");
+  const EpP2PDispatch dl = ep_p2p_dispatch_layout(cfg, world, num_tokens);
+  MLXR_CHECK_ARG(workspace && (reinterpret_cast<uintptr_t>(workspace) & 255) == 0 && workspace_bytes >= dl.total,
+                 "moe_ep_dispatch_p2p: workspace NULL, not 256-byte aligned or smaller than %zu bytes", dl.total);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* ws = workspace;
+  const Layout L = make_layout(cfg, num_tokens);
+  MLXR_CUDA_TRY(cudaMemsetAsync(at<int>(ws, L.status), 0, kStatusSlotBytes, st));
+  const int K = cfg->num_experts_per_tok;
+  const int64_t R = L.R;
+  int32_t* offsets = at<int32_t>(ws, L.offsets);
+  int32_t* send_counts = at<int32_t>(ws, dl.counts);
+  if (num_tokens == 0) {
+    MLXR_CUDA_TRY(cudaMemsetAsync(offsets, 0, (size_t)(world + 1) * 4, st));
+    MLXR_CUDA_TRY(cudaMemsetAsync(send_counts, 0, (size_t)world * 2 * 4, st));
+  } else {
+    MLXR_CHECK_ARG(x && pair_pos && aligned16(x), "moe_ep_dispatch_p2p: NULL or misaligned x / pair_pos");
+    MLXR_CHECK_ARG(cfg->shared_expert_intermediate_size == 0 || shared_gate, "moe_ep_dispatch_p2p: shared_gate is NULL");
+    if (int rc = run_router(cfg, weights, L, x, ws, nullptr, nullptr, st)) return rc;
+    int32_t* dest = at<int32_t>(ws, dl.dest);
+    launch_pdl(ep_pair_dest_kernel, (unsigned)((R + 255) / 256), 256, 0, st, at<int32_t>(ws, L.idx), num_tokens, K,
+               world, placement, dest, at<int>(ws, L.status));
+    MLXR_LAUNCH_CHECK("ep_pair_dest_kernel");
+    Layout P = L;
+    P.E = world;
+    P.Is = 0;
+    P.rows = num_tokens * (K < world ? K : world);
+    P.bn1 = P.bn2 = 1 << 30;
+    P.max_t1 = P.max_t2 = world + 1;
+    if (int rc = run_permute(P, dest, x, ws, at<int32_t>(ws, L.counts), offsets, at<int32_t>(ws, L.sorted), pair_pos,
+                             nullptr, 0, st, 1))
+      return rc;
+    launch_pdl(ep_counts_kernel, 1, 1024, 0, st, at<int32_t>(ws, L.idx), R, world, placement, at<int32_t>(ws, L.counts),
+               send_counts);
+    MLXR_LAUNCH_CHECK("ep_counts_kernel");
+    launch_pdl(ep_pair_meta_kernel, (unsigned)((num_tokens + 127) / 128), 128, 0, st, at<int32_t>(ws, L.idx),
+               at<uint16_t>(ws, L.w), pair_pos, num_tokens, K, world, placement, P.rows, at<int32_t>(ws, dl.meta),
+               at<int>(ws, L.status));
+    MLXR_LAUNCH_CHECK("ep_pair_meta_kernel");
+    if (cfg->shared_expert_intermediate_size > 0)
+      MLXR_CUDA_TRY(cudaMemcpyAsync(shared_gate, at<float>(ws, L.sig), (size_t)num_tokens * 4,
+                                    cudaMemcpyDeviceToDevice, st));
+  }
+  const int64_t pairs_max = num_tokens * (K < world ? K : world);
+  int grid = (int)((pairs_max + 7) / 8);
+  if (grid > 4 * 148) grid = 4 * 148;
+  if (grid < 1) grid = 1;
+  launch_pdl(ep_send_kernel, grid, 256, 0, st, c->peers, c->bl, c->rank, world, c->cap,
+             static_cast<const uint16_t*>(x), c->D, K, at<int32_t>(ws, L.sorted), offsets, at<int32_t>(ws, dl.meta),
+             send_counts, pair_pos, epoch, reinterpret_cast<int*>(c->local + c->bl.done), at<int>(ws, L.status));
+  MLXR_LAUNCH_CHECK("ep_send_kernel");
+  return MLXR_CU_OK;
+}
+
+int mlxr_cu_moe_ep_experts_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* local_weights,
+                               int num_local_experts, void* comm, int64_t expected_rows, uint32_t epoch,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = ep_comm_check(comm, cfg)) return rc;
+  EpComm* c = static_cast<EpComm*>(comm);
+  MLXR_CHECK_ARG(local_weights != nullptr && num_local_experts >= 1 && num_local_experts <= cfg->num_experts,
+                 "moe_ep_experts_p2p: weights NULL or num_local_experts=%d out of range", num_local_experts);
+  if (int rc = validate(cfg, (int64_t)c->world * c->cap)) return rc;
+  mlxr_cu_moe_config lc = *cfg;
+  lc.num_experts = num_local_experts;
+  lc.shared_expert_intermediate_size = 0;
+  const Layout L = ep_p2p_experts_layout(cfg, num_local_experts, c->world, c->cap, expected_rows);
+  if (int rc = check_ws(L, workspace, workspace_bytes)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* ws = workspace;  // the status word was cleared by this step's dispatch
+  int* status = at<int>(ws, L.status);
+  const uint8_t* b = c->local;
+  launch_pdl(ep_wait_flags_kernel, 1, 64, 0, st, reinterpret_cast<const uint32_t*>(b + c->bl.flag_disp), c->world,
+             epoch, 5 * kWaitLimitNs, status);
+  MLXR_LAUNCH_CHECK("ep_wait_flags_kernel(dispatch)");
+  const int32_t* meta = reinterpret_cast<const int32_t*>(b + c->bl.recv_meta);
+  const int32_t* counts = reinterpret_cast<const int32_t*>(b + c->bl.counts);
+  launch_pdl(ep_slot_expert_p2p_kernel, (unsigned)((L.R + 255) / 256 < 4096 ? (L.R + 255) / 256 : 4096), 256, 0, st,
+             meta, counts, c->world, c->cap, c->K, num_local_experts, at<int32_t>(ws, L.idx), status);
+  MLXR_LAUNCH_CHECK("ep_slot_expert_p2p_kernel");
+  if (int rc = run_permute(L, at<int32_t>(ws, L.idx), b + c->bl.recv_x, ws, at<int32_t>(ws, L.counts),
+                           at<int32_t>(ws, L.offsets), at<int32_t>(ws, L.sorted), at<int32_t>(ws, L.inv),
+                           at<uint16_t>(ws, L.xs), lc.bits == 4, st, 1))
+    return rc;
+  if (int rc = run_experts(&lc, local_weights, L, ws, st, 7)) return rc;
+  int grid = (int)(c->world * c->cap < 8 * 148 ? c->world * c->cap : 8 * 148);
+  launch_pdl(ep_reduce_send_kernel, grid, L.D >= 2048 ? 256 : 128, 0, st, c->peers, c->bl, c->rank, c->world, c->cap,
+             at<uint16_t>(ws, L.y), at<int32_t>(ws, L.inv), meta, counts, c->K, c->D, L.rows, epoch,
+             reinterpret_cast<int*>(c->local + c->bl.done), status);
+  MLXR_LAUNCH_CHECK("ep_reduce_send_kernel");
+  return MLXR_CU_OK;
+}
+
+int mlxr_cu_moe_ep_combine_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights, void* comm,
+                               const void* x, int64_t num_tokens, const int32_t* pair_pos, const float* shared_gate,
+                               void* out, uint32_t epoch, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = validate(cfg, num_tokens)) return rc;
+  if (int rc = ep_comm_check(comm, cfg)) return rc;
+  EpComm* c = static_cast<EpComm*>(comm);
+  const Layout L = make_layout(cfg, num_tokens);
+  if (int rc = check_ws(L, workspace, workspace_bytes)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* ws = workspace;  // the status word was cleared by this step's dispatch
+  const uint16_t* ysh = nullptr;
+  if (num_tokens > 0 && L.Is > 0) {
+    MLXR_CHECK_ARG(x && shared_gate && weights && aligned16(x), "moe_ep_combine_p2p: x / shared_gate / weights");
+    // The shared expert runs before the wait: it overlaps the other ranks' experts.
+    launch_pdl(shared_tiles_kernel, (unsigned)((L.max_tsh + 255) / 256), 256, 0, st, at<GemmTile>(ws, L.tsh),
+               at<int32_t>(ws, L.nsh), L.T, L.bns, L.max_tsh);
+    MLXR_LAUNCH_CHECK("shared_tiles_kernel");
+    if (int rc = run_shared(cfg, weights, L, x, ws, st)) return rc;
+    ysh = at<uint16_t>(ws, L.ysh);
+  }
+  launch_pdl(ep_wait_flags_kernel, 1, 64, 0, st, reinterpret_cast<const uint32_t*>(c->local + c->bl.flag_back),
+             c->world, epoch, 5 * kWaitLimitNs, at<int>(ws, L.status));
+  MLXR_LAUNCH_CHECK("ep_wait_flags_kernel(combine)");
+  if (num_tokens == 0) return MLXR_CU_OK;
+  MLXR_CHECK_ARG(pair_pos && out && aligned16(out), "moe_ep_combine_p2p: NULL or misaligned argument");
+  launch_pdl(ep_combine_kernel, (unsigned)L.T, L.D >= 2048 ? 256 : 128, 0, st,
+             reinterpret_cast<const uint16_t*>(c->local + c->bl.back), pair_pos, L.K, L.D,
+             (int64_t)c->world * c->cap, ysh, shared_gate, static_cast<uint16_t*>(out), at<int>(ws, L.status));
+  MLXR_LAUNCH_CHECK("ep_combine_kernel(p2p)");
   return MLXR_CU_OK;
 }
 

@@ -792,7 +792,7 @@ __global__ void __launch_bounds__(256) permute_gather_kernel(const int32_t* __re
     const uint4* src = reinterpret_cast<const uint4*>(x + src_row * D);
     uint4* dst = reinterpret_cast<uint4*>(x_sorted + pos * D);
     for (int v = lane; v < dvec; v += 32) {
-      uint4 a = __ldg(src + v);
+      uint4 a = __ldcg(src + v);  // through L2: the rows may have been stored there by a peer GPU
       if (kperm) {
         uint4 b;
         b.x = __byte_perm(a.x, a.z, 0x5410);
@@ -1008,7 +1008,7 @@ __device__ __forceinline__ void weighted_rows_acc(const uint16_t* __restrict__ b
     uint4 yv[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j)
-      if (k0 + j < n) yv[j] = __ldg(reinterpret_cast<const uint4*>(base + (int64_t)rows[k0 + j] * D) + v);
+      if (k0 + j < n) yv[j] = __ldcg(reinterpret_cast<const uint4*>(base + (int64_t)rows[k0 + j] * D) + v);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       if (k0 + j < n) {
@@ -1133,6 +1133,215 @@ __global__ void shared_tiles_kernel(GemmTile* __restrict__ tiles, int32_t* __res
     tiles[j] = g;
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) *count = min(nt, cap);
+}
+
+// ------------------------------------------------ peer-memory exchange ---
+// Expert parallelism without a collective library: every rank owns one
+// exchange buffer of the same layout, mapped into every other rank's address
+// space (CUDA IPC over NVLink). Rank `me` stores the pairs it sends to rank r
+// into r's buffer (recv_x / recv_meta block `me`), then the pair and slot
+// counts and finally an epoch flag; r stores the partial rows it returns into
+// me's buffer (back block r) and then a flag. Readers wait on the flags
+// (bounded) and read the data through L2.
+struct EpBufLayout {
+  int64_t recv_x, recv_meta, back, counts, rows, flag_disp, flag_back, done, total;
+};
+
+__host__ __device__ inline EpBufLayout ep_buf_layout(int world, int64_t cap, int D, int K) {
+  EpBufLayout b{};
+  int64_t o = 0;
+  auto take = [&](int64_t bytes) {
+    const int64_t at = o;
+    o += (bytes + 255) & ~(int64_t)255;
+    return at;
+  };
+  b.recv_x = take((int64_t)world * cap * D * 2);
+  b.recv_meta = take((int64_t)world * cap * K * 4);
+  b.back = take((int64_t)world * cap * D * 2);
+  b.counts = take((int64_t)world * 4);
+  b.rows = take((int64_t)world * 4);
+  b.flag_disp = take((int64_t)world * 4);
+  b.flag_back = take((int64_t)world * 4);
+  b.done = take(16);
+  b.total = o;
+  return b;
+}
+
+constexpr int EP_MAX_WORLD = 64;
+struct EpPeers {
+  uint8_t* base[EP_MAX_WORLD];  // every rank's exchange buffer as seen from this GPU
+};
+
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Dispatch over peer memory: one warp per pair in destination order (pos in
+// [offsets[r], offsets[r+1]) for rank r). The pair's x row and slot row go to
+// rank r's recv block `me` at index pos - offsets[r]; pair_pos[f] (f = the
+// pair's first (token, k)) becomes r * cap + that index, where the partial
+// row will come back. The last CTA to finish publishes the counts and the
+// flag on every rank.
+__global__ void __launch_bounds__(256) ep_send_kernel(EpPeers peers, EpBufLayout bl, int me, int world, int64_t cap,
+                                                      const uint16_t* __restrict__ x, int D, int K,
+                                                      const int32_t* __restrict__ sorted,
+                                                      const int32_t* __restrict__ offsets,
+                                                      const int32_t* __restrict__ meta_local,
+                                                      const int32_t* __restrict__ send_counts,
+                                                      int32_t* __restrict__ pair_pos, uint32_t epoch,
+                                                      int* __restrict__ done, int* status) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ int s_off[EP_MAX_WORLD + 1];
+  __shared__ int s_last;
+  for (int i = threadIdx.x; i <= world; i += blockDim.x) s_off[i] = offsets[i];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t npairs = s_off[world];
+  for (int64_t pos = (int64_t)blockIdx.x * 8 + warp; pos < npairs; pos += (int64_t)gridDim.x * 8) {
+    int r = 0;
+    while (r + 1 < world && s_off[r + 1] <= pos) ++r;
+    const int64_t pr = pos - s_off[r];
+    const int32_t f = sorted[pos];
+    if (pr >= cap || f < 0) {
+      if (lane == 0) atomicCAS(status, 0, (int)kDevBadIndex);
+      continue;
+    }
+    const int64_t t = f / K;
+    if (lane == 0) pair_pos[f] = (int32_t)(r * cap + pr);
+    const uint4* src = reinterpret_cast<const uint4*>(x + t * D);
+    uint4* dst = reinterpret_cast<uint4*>(peers.base[r] + bl.recv_x + ((int64_t)me * cap + pr) * D * 2);
+    for (int v = lane; v < D / 8; v += 32) dst[v] = __ldg(src + v);
+    int32_t* dm = reinterpret_cast<int32_t*>(peers.base[r] + bl.recv_meta) + ((int64_t)me * cap + pr) * K;
+    if (lane < K) dm[lane] = meta_local[pos * K + lane];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(done, 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence_system();
+  if (threadIdx.x < world) {
+    const int r = threadIdx.x;
+    uint8_t* b = peers.base[r];
+    reinterpret_cast<volatile int32_t*>(b + bl.counts)[me] = s_off[r + 1] - s_off[r];
+    reinterpret_cast<volatile int32_t*>(b + bl.rows)[me] = send_counts[2 * r + 1];
+    __threadfence_system();
+    st_release_sys_u32(reinterpret_cast<uint32_t*>(b + bl.flag_disp) + me, epoch);
+  }
+  if (threadIdx.x == 0) *done = 0;
+}
+
+// One CTA: wait until every rank has published `epoch` in flags[0..world)
+// (bounded; on expiry the status records a timeout and the data is not used).
+__global__ void ep_wait_flags_kernel(const uint32_t* __restrict__ flags, int world, uint32_t epoch,
+                                     unsigned long long limit_ns, int* status) {
+  pdl_wait();
+  pdl_launch_dependents();
+  if (threadIdx.x < world) {
+    const unsigned long long t0 = global_ns();
+    for (uint32_t it = 0;; ++it) {
+      if ((int32_t)(ld_acquire_sys_u32(flags + threadIdx.x) - epoch) >= 0) break;
+      if ((it & 63u) == 63u && global_ns() - t0 > limit_ns) {
+        atomicCAS(status, 0, (int)kDevTimeout);
+        break;
+      }
+    }
+  }
+  __threadfence_system();
+}
+
+// Receiving side over peer memory: slot f of the [world][cap][K] receive
+// area is used when its pair index is below that source's count and the slot
+// is filled; idx_local[f] = local expert or -1.
+__global__ void ep_slot_expert_p2p_kernel(const int32_t* __restrict__ meta, const int32_t* __restrict__ counts,
+                                          int world, int64_t cap, int K, int E_local,
+                                          int32_t* __restrict__ idx_local, int* status) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t n = (int64_t)world * cap * K;
+  for (int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; f < n; f += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t q = f / K;
+    const int s = (int)(q / cap);
+    const int64_t p = q - (int64_t)s * cap;
+    int le = -1;
+    const int c = __ldcg(counts + s);
+    if (c < 0 || c > cap) {
+      if (f == (int64_t)s * cap * K) atomicCAS(status, 0, (int)kDevBadIndex);
+    } else if (p < c) {
+      const int32_t m = __ldcg(meta + f);
+      if (m >= 0) {
+        le = m >> 16;
+        if (le >= E_local) {
+          atomicCAS(status, 0, (int)kDevBadIndex);
+          le = -1;
+        }
+      }
+    }
+    idx_local[f] = le;
+  }
+}
+
+// Pre-reduce each received pair and store the partial row straight into the
+// owner's back block; the last CTA publishes the back flag on every rank.
+__global__ void __launch_bounds__(256) ep_reduce_send_kernel(EpPeers peers, EpBufLayout bl, int me, int world,
+                                                             int64_t cap, const uint16_t* __restrict__ y_sorted,
+                                                             const int32_t* __restrict__ inv,
+                                                             const int32_t* __restrict__ meta,
+                                                             const int32_t* __restrict__ counts, int K, int D,
+                                                             int64_t rows, uint32_t epoch, int* __restrict__ done,
+                                                             int* status) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ int rws[RT_MAXK];
+  __shared__ float wk[RT_MAXK];
+  __shared__ int nk;
+  __shared__ int s_last;
+  const int64_t npairs = (int64_t)world * cap;
+  for (int64_t q = blockIdx.x; q < npairs; q += gridDim.x) {
+    const int s = (int)(q / cap);
+    const int64_t p = q - (int64_t)s * cap;
+    if (p >= __ldcg(counts + s)) continue;  // uniform over the CTA
+    if (threadIdx.x == 0) {
+      int n = 0;
+      for (int j = 0; j < K; ++j) {
+        const int32_t m = __ldcg(meta + q * K + j);
+        if (m < 0) continue;
+        const int r = inv[q * K + j];
+        if (r < 0 || (int64_t)r >= rows) {
+          atomicCAS(status, 0, (int)kDevBadIndex);
+          continue;
+        }
+        rws[n] = r;
+        wk[n] = bf16_bits_to_f32((uint16_t)(m & 0xFFFF));
+        ++n;
+      }
+      nk = n;
+    }
+    __syncthreads();
+    const int n = nk;
+    uint16_t* dst = reinterpret_cast<uint16_t*>(peers.base[s] + bl.back) + ((int64_t)me * cap + p) * D;
+    for (int v = threadIdx.x; v < D / 8; v += blockDim.x) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      weighted_rows_acc(y_sorted, rws, wk, n, D, v, acc);
+      store_bf16x8(dst + 8 * v, acc);
+    }
+    __syncthreads();
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(done, 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence_system();
+  if (threadIdx.x < world)
+    st_release_sys_u32(reinterpret_cast<uint32_t*>(peers.base[threadIdx.x] + bl.flag_back) + me, epoch);
+  if (threadIdx.x == 0) *done = 0;
 }
 
 }  // namespace mlxr

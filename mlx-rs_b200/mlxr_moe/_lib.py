@@ -49,6 +49,13 @@ EXPORTS = (
     "mlxr_cu_moe_ep_dispatch",
     "mlxr_cu_moe_ep_experts",
     "mlxr_cu_moe_ep_combine",
+    "mlxr_cu_ep_comm_create",
+    "mlxr_cu_ep_comm_connect",
+    "mlxr_cu_ep_comm_destroy",
+    "mlxr_cu_moe_ep_p2p_workspace_size",
+    "mlxr_cu_moe_ep_dispatch_p2p",
+    "mlxr_cu_moe_ep_experts_p2p",
+    "mlxr_cu_moe_ep_combine_p2p",
 )
 
 
@@ -145,6 +152,14 @@ def _load():
     lib.mlxr_cu_moe_ep_dispatch.argtypes = [cfg_p, w_p, I32, P, P, I64, P, P, P, P, P, P, C.c_size_t, P]
     lib.mlxr_cu_moe_ep_experts.argtypes = [cfg_p, w_p, I32, P, P, I64, I64, P, P, C.c_size_t, P]
     lib.mlxr_cu_moe_ep_combine.argtypes = [cfg_p, w_p, P, I64, P, I64, P, P, P, P, C.c_size_t, P]
+    U32 = C.c_uint32
+    lib.mlxr_cu_ep_comm_create.argtypes = [I32, I32, I64, I32, I32, C.POINTER(C.c_void_p), P]
+    lib.mlxr_cu_ep_comm_connect.argtypes = [P, P]
+    lib.mlxr_cu_ep_comm_destroy.argtypes = [P]
+    lib.mlxr_cu_moe_ep_p2p_workspace_size.argtypes = [cfg_p, P, I64, I32, I64, C.POINTER(C.c_size_t)]
+    lib.mlxr_cu_moe_ep_dispatch_p2p.argtypes = [cfg_p, w_p, P, P, P, I64, P, P, U32, P, C.c_size_t, P]
+    lib.mlxr_cu_moe_ep_experts_p2p.argtypes = [cfg_p, w_p, I32, P, I64, U32, P, C.c_size_t, P]
+    lib.mlxr_cu_moe_ep_combine_p2p.argtypes = [cfg_p, w_p, P, P, I64, P, P, P, U32, P, C.c_size_t, P]
     for name in EXPORTS:
         f = getattr(lib, name)
         if f.restype is C.c_int or name not in ("mlxr_cu_last_error", "mlxr_cu_clear_error"):

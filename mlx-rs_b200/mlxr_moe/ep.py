@@ -21,7 +21,10 @@ each rank:
 
 `TorchDistExchange` moves the pairs with `torch.distributed` all-to-all
 (NCCL over NVLink on GPUs, gloo on CPU for the host-side tests);
-`loopback_forward` runs several virtual ranks inside one process (one GPU).
+`PeerComm` + `ExpertParallelMoeBlock.forward_p2p` do the exchange inside the
+kernels over peer memory (CUDA IPC buffers, no collective library and no host
+synchronisation per step); `loopback_forward` runs several virtual ranks
+inside one process (one GPU).
 """
 from __future__ import annotations
 
@@ -203,6 +206,36 @@ class ExpertParallelMoeBlock:
         back = exchange.rows(partial, recv_pairs, send_pairs)
         return self.combine(x, back, plan, ws)
 
+    def forward_p2p(self, x: torch.Tensor, comm: "PeerComm", expected_rows: int | None = None,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+        """One step over peer memory; every rank calls it together (same order of
+        steps on every rank, each GPU one rank)."""
+        x = x.reshape(-1, self.cfg.hidden_size).contiguous()
+        T, K = x.shape[0], self.cfg.num_experts_per_tok
+        if expected_rows is None:
+            expected_rows = max(1, comm.cap * K)
+        n = C.c_size_t(0)
+        _lib.call("mlxr_cu_moe_ep_p2p_workspace_size", C.byref(self._ccfg), comm.comm, T, len(self.experts_here),
+                  expected_rows, C.byref(n))
+        if self._ws is None or self._ws.numel() < n.value:
+            self._ws = torch.empty(max(int(n.value), 256), dtype=torch.uint8, device=x.device)
+        ws = self._ws
+        comm.epoch += 1
+        ep = comm.epoch & 0xFFFFFFFF
+        st = torch.cuda.current_stream(x.device).cuda_stream
+        pair_pos = torch.empty(max(T * K, 1), dtype=torch.int32, device=x.device)
+        sg = torch.empty(max(T, 1), dtype=torch.float32, device=x.device) if self.shared_expert is not None else None
+        out = torch.empty_like(x) if out is None else out
+        _lib.call("mlxr_cu_moe_ep_dispatch_p2p", C.byref(self._ccfg), C.byref(self._cw_rep), comm.comm,
+                  self.placement.data_ptr(), x.data_ptr() if T else None, T, pair_pos.data_ptr(),
+                  None if sg is None else sg.data_ptr(), ep, ws.data_ptr(), ws.numel(), st)
+        _lib.call("mlxr_cu_moe_ep_experts_p2p", C.byref(self._ccfg), C.byref(self._cw_loc), len(self.experts_here),
+                  comm.comm, expected_rows, ep, ws.data_ptr(), ws.numel(), st)
+        _lib.call("mlxr_cu_moe_ep_combine_p2p", C.byref(self._ccfg), C.byref(self._cw_rep), comm.comm,
+                  x.data_ptr() if T else None, T, pair_pos.data_ptr(), None if sg is None else sg.data_ptr(),
+                  out.data_ptr() if T else None, ep, ws.data_ptr(), ws.numel(), st)
+        return out
+
 
 class TorchDistExchange:
     """All-to-all of pair rows through torch.distributed (NCCL or gloo).
@@ -262,3 +295,29 @@ def loopback_forward(blocks: list[ExpertParallelMoeBlock], xs: list[torch.Tensor
         back = torch.cat(parts).contiguous()
         outs.append(blocks[s].combine(xs[s], back, plans[s], wss[s]))
     return outs
+
+
+class PeerComm:
+    """This rank's exchange buffer plus every other rank's, mapped through
+    CUDA IPC (`mlxr_cu_ep_comm_create/connect`). The IPC handles travel over
+    the `torch.distributed` group (host all-gather, once). `cap` = the most
+    tokens any rank feeds a step."""
+
+    def __init__(self, rank: int, world: int, cap: int, hidden: int, k: int, group=None):
+        import torch.distributed as dist
+
+        self.rank, self.world, self.cap = rank, world, cap
+        self.comm = C.c_void_p()
+        handle = (C.c_uint8 * 64)()
+        _lib.call("mlxr_cu_ep_comm_create", world, rank, cap, hidden, k, C.byref(self.comm), handle)
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        buf = (C.c_uint8 * (64 * world)).from_buffer_copy(b"".join(handles))
+        _lib.call("mlxr_cu_ep_comm_connect", self.comm, buf)
+        dist.barrier(group=group)  # every rank has mapped every buffer before the first step
+        self.epoch = 0
+
+    def close(self):
+        if self.comm:
+            _lib.call("mlxr_cu_ep_comm_destroy", self.comm)
+            self.comm = C.c_void_p()

@@ -202,3 +202,65 @@ def test_ep_nccl_two_gpus(tmp_path):
     mp.spawn(_nccl_worker, args=(2, 29517, str(res)), nprocs=2, join=True)
     ok, err = res.read_text().split()
     assert ok == "1", f"max abs err {err}"
+
+
+def _p2p_worker(rank, world, port, result_path):
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    from mlxr_moe.ep import PeerComm, balanced_placement
+
+    worst = 0.0
+    ok = 1
+    for name, zipf in (("c4", False), ("c3", True)):
+        spec = synth.CONFIGS[name]
+        cfg = spec["cfg"]
+        full = synth.make_block(cfg, 0, spec["zipf"], device="cuda")
+        place = None
+        if zipf:  # placement from the loads of a calibration batch
+            idx, _ = full.router(synth.make_input(64, cfg.hidden_size, stream_offset=7 + rank, device="cuda"))
+            loads = torch.bincount(idx.reshape(-1).long(), minlength=cfg.num_experts).to(torch.float64)
+            dist.all_reduce(loads)
+            place = balanced_placement(loads.cpu().tolist(), world)
+        blk = ExpertParallelMoeBlock.from_block(full, rank, world, place)
+        comm = PeerComm(rank, world, cap=96, hidden=cfg.hidden_size, k=cfg.num_experts_per_tok)
+        # ragged: different token counts per rank and per step, one step with an empty rank
+        for step, T in enumerate([48 + 16 * rank, 96 - 40 * rank, 0 if rank == 1 else 33]):
+            x = (synth.make_input(T, cfg.hidden_size, stream_offset=100 + 4 * rank + step, device="cuda") if T
+                 else torch.empty((0, cfg.hidden_size), dtype=torch.bfloat16, device="cuda"))
+            out = blk.forward_p2p(x, comm)
+            torch.cuda.synchronize()
+            blk.status()
+            if T:
+                want = full.forward(x)
+                torch.cuda.synchronize()
+                err = (out.float() - want.float()).abs()
+                worst = max(worst, err.max().item())
+                ok &= int(bool((err <= ATOL + RTOL * want.float().abs()).all()))
+        torch.cuda.synchronize()
+        dist.barrier()
+        comm.close()
+        del blk, full
+    t = torch.tensor([ok], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    if rank == 0:
+        with open(result_path, "w") as f:
+            f.write(f"{int(t.item())} {worst}\n")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_p2p_two_gpus(tmp_path):
+    """Exchange inside the kernels over peer memory (CUDA IPC), two GPUs:
+    matches the one-device block, ragged and empty batches included."""
+    import torch.multiprocessing as mp
+
+    res = tmp_path / "p2p.txt"
+    mp.spawn(_p2p_worker, args=(2, 29519, str(res)), nprocs=2, join=True)
+    ok, err = res.read_text().split()
+    assert ok == "1", f"max abs err {err}"
