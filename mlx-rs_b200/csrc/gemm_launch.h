@@ -34,6 +34,20 @@ struct GroupedGemmProblem {
   int max_split_rows;         // row slices (tile x m-tile) the split buffers hold
   float* partial;             // fp32 [max_split_rows][splits][4][nmat][bn][32]
   int32_t* counters;          // [max_split_rows][4], zero before the launch
+  // Fused launch (nmat 2, not split): after this problem (gate|up + SwiGLU),
+  // the down projection in row pairs over the same tiles: weights w2
+  // [w2_rows, k_dim2*bits/32] (+ s2, b2), activations act2 = this problem's
+  // out, output out2 [out_rows, n_out2]; tile_ready [max_tiles] zeroed.
+  int fused;
+  const uint32_t* w2;
+  const uint16_t* s2;
+  const uint16_t* b2;
+  int64_t w2_rows;
+  int n_out2;
+  int k_dim2;
+  int64_t act2_rows;
+  uint16_t* out2;
+  int32_t* tile_ready;
 };
 
 int launch_grouped_gemm(const GroupedGemmProblem& p, cudaStream_t st);

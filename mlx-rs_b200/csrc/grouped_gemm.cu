@@ -51,10 +51,10 @@ int num_sms_current() {
   return n > 0 ? n : 148;
 }
 
-template <int NMAT, int BN, int BITS, bool SPLITK>
+template <int NMAT, int BN, int BITS, bool SPLITK, bool FUSED>
 static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
   using C = GG<NMAT, BN, BITS>;
-  CUtensorMap ta0, ta1, tb;
+  CUtensorMap ta0, ta1, tb, ta2, tb2;
   const uint64_t kw = (uint64_t)p.k_dim * BITS / 32;
   if (int rc = make_map_2d(&ta0, p.w[0], CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, kw, (uint64_t)p.w_rows, C::KW, C::BM,
                            CU_TENSOR_MAP_SWIZZLE_NONE))
@@ -69,7 +69,18 @@ static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
   if (int rc = make_map_2d(&tb, p.act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)p.k_dim, (uint64_t)p.act_rows,
                            C::BK, BN, CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
-  auto kern = grouped_dequant_gemm_kernel<NMAT, BN, BITS, SPLITK>;
+  if (FUSED) {
+    if (int rc = make_map_2d(&ta2, p.w2, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)p.k_dim2 * BITS / 32,
+                             (uint64_t)p.w2_rows, C::KW, C::BM, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+    if (int rc = make_map_2d(&tb2, p.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)p.k_dim2,
+                             (uint64_t)p.act2_rows, C::BK, BN, CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  } else {
+    ta2 = ta0;
+    tb2 = tb;
+  }
+  auto kern = grouped_dequant_gemm_kernel<NMAT, BN, BITS, SPLITK, FUSED>;
   static std::atomic<uint64_t> attr_done{0};  // per instantiation and device
   if (int rc = ensure_smem_attr(kern, C::SMEM_BYTES, attr_done)) return rc;
   GemmArgs a;
@@ -94,8 +105,17 @@ static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
   a.counters = p.counters;
   if (a.splits > 1 && (!a.partial || !a.counters || a.max_split_rows <= 0))
     return set_error(MLXR_CU_ERR_INVALID_ARGUMENT, "grouped gemm: split-K needs partial and counter buffers");
+  a.scales2 = p.s2;
+  a.biases2 = p.b2;
+  a.out2 = p.out2;
+  a.n_out2 = p.n_out2;
+  a.k_dim2 = p.k_dim2;
+  a.tile_ready = p.tile_ready;
+  if (FUSED && (!p.w2 || !p.s2 || !p.b2 || !p.out2 || !p.tile_ready || p.n_out2 % 256 != 0 || p.k_dim2 % 64 != 0 ||
+                p.k_dim2 != p.n_out))
+    return set_error(MLXR_CU_ERR_INVALID_ARGUMENT, "grouped gemm: bad fused second phase");
   const int grid = p.grid > 0 ? p.grid : num_sms_current();
-  launch_pdl(kern, grid, C::NUM_THREADS, C::SMEM_BYTES, st, ta0, ta1, tb, a);
+  launch_pdl(kern, grid, C::NUM_THREADS, C::SMEM_BYTES, st, ta0, ta1, tb, ta2, tb2, a);
   MLXR_LAUNCH_CHECK("grouped_dequant_gemm_kernel");
   return MLXR_CU_OK;
 }
@@ -109,13 +129,20 @@ int launch_grouped_gemm(const GroupedGemmProblem& p, cudaStream_t st) {
   // Split-K only for the decode tile widths (few work items come from few tokens).
   if (p.splits > 1 && p.bn > 32)
     return set_error(MLXR_CU_ERR_INVALID_ARGUMENT, "grouped gemm: split-K is built for bn <= 32 (bn=%d)", p.bn);
+  if (p.fused && (p.nmat != 2 || p.splits > 1 || p.pair))
+    return set_error(MLXR_CU_ERR_INVALID_ARGUMENT, "grouped gemm: the fused launch needs nmat 2, no split, no pair");
+#define MLXR_GG_FUSED(BNV, BT) \
+  if (p.fused && p.bn == BNV && p.bits == BT) return launch_one<2, BNV, BT, false, true>(p, st);
+  MLXR_GG_FUSED(16, 4) MLXR_GG_FUSED(32, 4) MLXR_GG_FUSED(64, 4) MLXR_GG_FUSED(128, 4)
+  MLXR_GG_FUSED(16, 8) MLXR_GG_FUSED(32, 8) MLXR_GG_FUSED(64, 8) MLXR_GG_FUSED(128, 8)
+#undef MLXR_GG_FUSED
 #define MLXR_GG_SPLIT(NM, BNV, BT) \
-  if (p.splits > 1 && p.nmat == NM && p.bn == BNV && p.bits == BT) return launch_one<NM, BNV, BT, true>(p, st);
+  if (p.splits > 1 && p.nmat == NM && p.bn == BNV && p.bits == BT) return launch_one<NM, BNV, BT, true, false>(p, st);
   MLXR_GG_SPLIT(2, 16, 4) MLXR_GG_SPLIT(2, 32, 4) MLXR_GG_SPLIT(1, 16, 4) MLXR_GG_SPLIT(1, 32, 4)
   MLXR_GG_SPLIT(2, 16, 8) MLXR_GG_SPLIT(2, 32, 8) MLXR_GG_SPLIT(1, 16, 8) MLXR_GG_SPLIT(1, 32, 8)
 #undef MLXR_GG_SPLIT
 #define MLXR_GG_CASE(NM, BNV, BT) \
-  if (p.nmat == NM && p.bn == BNV && p.bits == BT) return launch_one<NM, BNV, BT, false>(p, st);
+  if (p.nmat == NM && p.bn == BNV && p.bits == BT) return launch_one<NM, BNV, BT, false, false>(p, st);
   MLXR_GG_CASE(2, 16, 4) MLXR_GG_CASE(2, 32, 4) MLXR_GG_CASE(2, 64, 4) MLXR_GG_CASE(2, 128, 4)
   MLXR_GG_CASE(1, 16, 4) MLXR_GG_CASE(1, 32, 4) MLXR_GG_CASE(1, 64, 4) MLXR_GG_CASE(1, 128, 4) MLXR_GG_CASE(1, 256, 4)
   MLXR_GG_CASE(2, 16, 8) MLXR_GG_CASE(2, 32, 8) MLXR_GG_CASE(2, 64, 8) MLXR_GG_CASE(2, 128, 8)

@@ -131,6 +131,17 @@ struct GemmArgs {
   int max_split_rows;         // row slices `partial` and `counters` hold
   float* partial;             // [row slices][splits][4 quarters][NMAT][BN][32]
   int32_t* counters;          // [row slices][4]
+  // Fused launch (second phase): after the gate|up items (phase 1), the same
+  // CTAs run the down projection items (phase 2: row pairs of the down weight,
+  // plain epilogue) over the same tile list. A phase-2 item of tile j loads
+  // its activation rows (h) once all phase-1 items of tile j have stored
+  // them: tile_ready[j] counts their epilogue warps (zero on entry).
+  const uint16_t* scales2;
+  const uint16_t* biases2;
+  uint16_t* out2;             // bf16 [rows, n_out2]
+  int32_t n_out2;             // multiple of 256
+  int32_t k_dim2;             // multiple of 64
+  int32_t* tile_ready;        // [max_tiles]
 };
 
 // A tile entry is used only if it names a valid expert and a row range inside
@@ -197,12 +208,33 @@ __device__ inline void drain_ring(uint64_t* full, uint32_t issued, volatile int*
   }
 }
 
-// SPLITK: the split-K variant (args.splits > 1); the plain variant has S = 1
-// folded in at compile time.
-template <int NMAT, int BN, int BITS, bool SPLITK>
+// Bounded wait until *p >= target (a counter other CTAs of this grid raise).
+__device__ inline bool wait_counter_geq(const int32_t* p, int target, volatile int* abort_flag, int* status) {
+  const unsigned long long t0 = global_ns();
+  for (uint32_t it = 0;; ++it) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    if (v >= target) return true;
+    if ((it & 63u) == 63u) {
+      if (*abort_flag) return false;
+      if (global_ns() - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        atomicCAS(status, 0, (int)kDevTimeout);
+        return false;
+      }
+    }
+  }
+}
+
+// SPLITK: the split-K variant (args.splits > 1). FUSED: gate|up then down in
+// one launch (NMAT == 2). The plain variant has both folded out.
+template <int NMAT, int BN, int BITS, bool SPLITK, bool FUSED>
 __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
     grouped_dequant_gemm_kernel(const __grid_constant__ CUtensorMap tm_a0, const __grid_constant__ CUtensorMap tm_a1,
-                                const __grid_constant__ CUtensorMap tm_b, const GemmArgs args) {
+                                const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_a2,
+                                const __grid_constant__ CUtensorMap tm_b2, const GemmArgs args) {
+  static_assert(!(SPLITK && FUSED), "split-K and the fused launch are separate variants");
+  static_assert(!FUSED || NMAT == 2, "the fused launch pairs gate|up with row pairs of down");
   using C = GG<NMAT, BN, BITS>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -249,6 +281,10 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
     prefetch_tmap(&tm_a0);
     if (NMAT == 2) prefetch_tmap(&tm_a1);
     prefetch_tmap(&tm_b);
+    if (FUSED) {
+      prefetch_tmap(&tm_a2);
+      prefetch_tmap(&tm_b2);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -259,40 +295,77 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
   pdl_wait();
   pdl_launch_dependents();
 
-  const int n_out = args.n_out;
-  const int pair = NMAT == 2 ? args.pair : 0;
-  const int mrows = pair ? 2 * C::BM : C::BM;  // output rows per work item
-  const int mt_per_expert = n_out / mrows;
-  const int ksteps = args.k_dim / C::BK;
+  const int pair1 = NMAT == 2 ? args.pair : 0;
+  const int mrows1 = pair1 ? 2 * C::BM : C::BM;  // output rows per work item
+  const int mt1 = args.n_out / mrows1;
+  const int ks1 = args.k_dim / C::BK;
   int ntiles = *args.num_tiles;
   if (ntiles > args.max_tiles) ntiles = args.max_tiles;
   const int S = SPLITK ? (args.splits > 1 ? args.splits : 1) : 1;
-  const int num_items = ntiles * mt_per_expert * S;
-  // Work item -> (row slice `base` = tile * mt_per_expert + m-tile, split);
-  // split s covers k-steps [s*ksteps/S, (s+1)*ksteps/S).
-  auto k_lo_of = [&](int item) { return (item % S) * ksteps / S; };
-  auto k_hi_of = [&](int item) { return (item % S + 1) * ksteps / S; };
+  const int n1 = ntiles * mt1 * S;
+  const int mt2 = FUSED ? args.n_out2 / (2 * C::BM) : 1;
+  const int ks2 = FUSED ? args.k_dim2 / C::BK : 0;
+  const int num_items = n1 + (FUSED ? ntiles * mt2 : 0);
+  // Work item -> tile, m-tile, k-range and phase. Phase 1: row slice
+  // base = tile * mt1 + m, split s covers k-steps [s*ks1/S, (s+1)*ks1/S).
+  // Phase 2 (fused launch): down row pairs of the same tiles.
+  struct Item {
+    int tile, m, base, split, k_lo, k_hi, ksteps, n_out, mrows, pair;
+    bool ph2;
+  };
+  auto item_of = [&](int item) {
+    Item d;
+    if (!FUSED || item < n1) {
+      d.base = item / S;
+      d.split = item % S;
+      d.tile = d.base / mt1;
+      d.m = d.base % mt1;
+      d.ksteps = ks1;
+      d.k_lo = d.split * ks1 / S;
+      d.k_hi = (d.split + 1) * ks1 / S;
+      d.n_out = args.n_out;
+      d.mrows = mrows1;
+      d.pair = pair1;
+      d.ph2 = false;
+    } else {
+      const int l = item - n1;
+      d.base = l;
+      d.split = 0;
+      d.tile = l / mt2;
+      d.m = l % mt2;
+      d.ksteps = ks2;
+      d.k_lo = 0;
+      d.k_hi = ks2;
+      d.n_out = args.n_out2;
+      d.mrows = 2 * C::BM;
+      d.pair = 1;
+      d.ph2 = true;
+    }
+    return d;
+  };
 
   if (warp == C::W_RAW) {
     // ---------------------------------------------- raw weight producer --
     if (lane == 0) {
       uint32_t it = 0;
       for (int item = blockIdx.x; item < num_items && !*abort_flag; item += gridDim.x) {
-        const int base = item / S;
-        const GemmTile t = args.tiles[base / mt_per_expert];
+        const Item d = item_of(item);
+        const GemmTile t = args.tiles[d.tile];
         if (!tile_ok(t, args)) {
           atomicCAS(args.status, 0, (int)kDevBadIndex);
           continue;
         }
-        const int a_row = t.expert * n_out + (base % mt_per_expert) * mrows;
-        for (int ks = k_lo_of(item); ks < k_hi_of(item); ++ks, ++it) {
+        const int a_row = t.expert * d.n_out + d.m * d.mrows;
+        const CUtensorMap* ma = (FUSED && d.ph2) ? &tm_a2 : &tm_a0;
+        const CUtensorMap* mb = (FUSED && d.ph2) ? &tm_a2 : &tm_a1;
+        for (int ks = d.k_lo; ks < d.k_hi; ++ks, ++it) {
           const int s = it % C::RS;
           if (!mbar_wait(&raw_empty[s], ((it / C::RS) & 1) ^ 1, abort_flag, args.status)) break;
           mbar_arrive_expect_tx(&raw_full[s], C::RAW_STAGE);
-          tma_load_2d(sRaw + s * C::RAW_STAGE, &tm_a0, &raw_full[s], ks * C::KW, a_row);
+          tma_load_2d(sRaw + s * C::RAW_STAGE, ma, &raw_full[s], ks * C::KW, a_row);
           if (NMAT == 2)
-            tma_load_2d(sRaw + s * C::RAW_STAGE + C::RAW_MAT, &tm_a1, &raw_full[s], ks * C::KW,
-                        a_row + (pair ? C::BM : 0));
+            tma_load_2d(sRaw + s * C::RAW_STAGE + C::RAW_MAT, mb, &raw_full[s], ks * C::KW,
+                        a_row + (d.pair ? C::BM : 0));
         }
       }
       drain_ring<C::RS>(raw_full, it, abort_flag, args.status);
@@ -304,12 +377,23 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       int s = 0;
       uint32_t ph = 0;
       for (int item = blockIdx.x; item < num_items && !*abort_flag; item += gridDim.x) {
-        const GemmTile t = args.tiles[(item / S) / mt_per_expert];
+        const Item d = item_of(item);
+        const GemmTile t = args.tiles[d.tile];
         if (!tile_ok(t, args)) continue;
-        for (int ks = k_lo_of(item); ks < k_hi_of(item); ++ks, ++it) {
+        const CUtensorMap* mbt = &tm_b;
+        if constexpr (FUSED) {
+          if (d.ph2) {
+            // The tile's h rows come from phase-1 epilogues (generic stores,
+            // possibly in other CTAs); order them before these TMA reads.
+            if (!wait_counter_geq(args.tile_ready + d.tile, 4 * mt1, abort_flag, args.status)) break;
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            mbt = &tm_b2;
+          }
+        }
+        for (int ks = d.k_lo; ks < d.k_hi; ++ks, ++it) {
           if (!mbar_wait(&op_empty[s], ph ^ 1, abort_flag, args.status)) break;
           mbar_arrive_expect_tx(&b_full[s], C::B_STAGE);
-          tma_load_2d(sB + s * C::B_STAGE, &tm_b, &b_full[s], ks * C::BK, t.row_start);
+          tma_load_2d(sB + s * C::B_STAGE, mbt, &b_full[s], ks * C::BK, t.row_start);
           if (++s == C::OS) {
             s = 0;
             ph ^= 1;
@@ -332,14 +416,15 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       uint32_t ph = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
-        if (!tile_ok(args.tiles[(item / S) / mt_per_expert], args)) continue;
+        const Item di = item_of(item);
+        if (!tile_ok(args.tiles[di.tile], args)) continue;
         const int ab = li % C::AB;
         const uint32_t acc_phase = (li / C::AB) & 1;
         ++li;  // counts valid items only, exactly like the epilogue
         if (!mbar_wait(&acc_empty[ab], acc_phase ^ 1, abort_flag, args.status)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(ab * C::ACC_COLS + mi * BN);
-        const int k_lo = k_lo_of(item), k_hi = k_hi_of(item);
+        const int k_lo = di.k_lo, k_hi = di.k_hi;
         for (int ks = k_lo; ks < k_hi; ++ks) {
           if (!mbar_wait(&b_full[s], ph, abort_flag, args.status) ||
               !mbar_wait(&op_full[s], ph, abort_flag, args.status)) {
@@ -391,18 +476,18 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       it += n;
     };
     for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
-      const GemmTile t = args.tiles[(item / S) / mt_per_expert];
+      const Item d = item_of(item);
+      const GemmTile t = args.tiles[d.tile];
       if (!tile_ok(t, args)) continue;
-      const int64_t srow =
-          (int64_t)t.expert * n_out + ((item / S) % mt_per_expert) * mrows + (pair ? mat * C::BM : 0) + row;
+      const int64_t srow = (int64_t)t.expert * d.n_out + d.m * d.mrows + (d.pair ? mat * C::BM : 0) + row;
       // (select, not index: a runtime index into the kernel parameters would
       // copy them to local memory)
-      const uint16_t* sbase = mat ? args.scales[1] : args.scales[0];
-      const uint16_t* bbase = mat ? args.biases[1] : args.biases[0];
-      const uint16_t* sp = sbase + srow * ksteps;
-      const uint16_t* bp = bbase + srow * ksteps;
+      const uint16_t* sbase = (FUSED && d.ph2) ? args.scales2 : (mat ? args.scales[1] : args.scales[0]);
+      const uint16_t* bbase = (FUSED && d.ph2) ? args.biases2 : (mat ? args.biases[1] : args.biases[0]);
+      const uint16_t* sp = sbase + srow * d.ksteps;
+      const uint16_t* bp = bbase + srow * d.ksteps;
       // First k-step of this item that belongs to the group.
-      const int k_lo = k_lo_of(item), k_hi = k_hi_of(item);
+      const int k_lo = d.k_lo, k_hi = d.k_hi;
       const int first = (int)((grp - (int)(it % NGRP) + NGRP) % NGRP);
       int ks = k_lo + first;
       advance(ks < k_hi ? first : k_hi - k_lo);
@@ -476,22 +561,26 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
     constexpr int CW = 16;  // TMEM columns per load (keeps the epilogue's registers small)
     constexpr int PQ = NMAT * BN * 32;  // floats of one quarter's partial accumulators
     for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
-      const int base = item / S, split = item % S;
-      const GemmTile t = args.tiles[base / mt_per_expert];
+      const Item d = item_of(item);
+      const int base = d.base, split = d.split;
+      const GemmTile t = args.tiles[d.tile];
       if (!tile_ok(t, args)) continue;
       const int ab = li % C::AB;
       const uint32_t acc_phase = (li / C::AB) & 1;
       ++li;
       if (!mbar_wait(&acc_full[ab], acc_phase, abort_flag, args.status)) break;
       tc_fence_after();
-      const int fn = (base % mt_per_expert) * mrows + q * 32 + lane;
-      const int f = args.perm_out ? ((fn & ~7) | kperm_pos(fn & 7)) : fn;
-      uint16_t* outp2 = args.out + (int64_t)t.row_start * n_out + fn + C::BM;  // pair mode: second row block
+      const int n_out = d.n_out;
+      const int fn = d.m * d.mrows + q * 32 + lane;
+      const int perm = (FUSED && d.ph2) ? 0 : args.perm_out;
+      const int f = perm ? ((fn & ~7) | kperm_pos(fn & 7)) : fn;
+      uint16_t* outb = (FUSED && d.ph2) ? args.out2 : args.out;
+      uint16_t* outp2 = outb + (int64_t)t.row_start * n_out + fn + C::BM;  // pair mode: second row block
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * C::ACC_COLS);
-      uint16_t* outp = args.out + (int64_t)t.row_start * n_out + f;
+      uint16_t* outp = outb + (int64_t)t.row_start * n_out + f;
       const int rows = t.row_count < BN ? t.row_count : BN;
       auto store = [&](int col, float gv, float uv) {
-        if (NMAT == 2 && pair) {
+        if (NMAT == 2 && d.pair) {
           outp[(int64_t)col * n_out] = f32_to_bf16_bits(gv);
           outp2[(int64_t)col * n_out] = f32_to_bf16_bits(uv);
         } else {
@@ -561,6 +650,13 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[ab]);
+      if constexpr (FUSED) {
+        if (!d.ph2) {  // this warp's h rows of the tile are stored: count them
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) atomicAdd(args.tile_ready + d.tile, 1);
+        }
+      }
     }
   }
 

@@ -57,10 +57,11 @@ struct Layout {
   int bn1 = 0, bn2 = 0, bns = 0;
   int s1 = 1, s2 = 1;          // split-K factors of the gate/up and down GEMMs
   int split_rows = 0;          // row slices the split buffers hold
+  int fuse = 0;                // gate/up and down in one launch (same tile list, no split)
   int max_t1 = 0, max_t2 = 0, max_tsh = 0;
   size_t status = 0, logits = 0, idx = 0, w = 0, sig = 0, bcounts = 0, bbase = 0, counts = 0, offsets = 0,
          sorted = 0, inv = 0, t1 = 0, n1 = 0, t2 = 0, n2 = 0, tsh = 0, nsh = 0, xs = 0, h = 0, y = 0, xpad = 0,
-         hsh = 0, ysh = 0, part = 0, cnt = 0, total = 0;
+         hsh = 0, ysh = 0, part = 0, cnt = 0, ready = 0, total = 0;
 };
 
 // Token-tile width from the mean number of rows per expert.
@@ -140,6 +141,11 @@ static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T, int64_t rows_c
     if (L.bn1 <= 32) L.s1 = pick_splits(used * mt1, L.D / 64);
     if (L.bn2 <= 32) L.s2 = pick_splits(used * mt2, L.I / 64);
   }
+  // One launch for both GEMMs when they share the tile list (equal token-tile
+  // widths), the down weight goes in row pairs, and neither is split; only
+  // for decode-width tiles, where the gate|up tail and the second launch's
+  // ramp are a visible share of the time (measured: no gain for prefill).
+  L.fuse = (L.s1 == 1 && L.s2 == 1 && L.D % 256 == 0 && L.bn1 <= 32 && L.bn1 == (L.bn2 < 128 ? L.bn2 : 128)) ? 1 : 0;
   if (L.s1 > 1 || L.s2 > 1) {
     // Tiles per GEMM are at most rows/bn + (non-empty experts) + 1.
     const int64_t t1 = std::min<int64_t>(L.max_t1, L.rows / L.bn1 + std::min<int64_t>(L.rows, L.E) + 1);
@@ -177,6 +183,7 @@ static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T, int64_t rows_c
     L.hsh = take((size_t)L.sh_rows_pad * L.Is * 2);
     L.ysh = take((size_t)T * L.D * 2);
   }
+  if (L.fuse) L.ready = take((size_t)L.max_t1 * sizeof(int32_t));
   if (L.split_rows > 0) {
     const int smax = L.s1 > L.s2 ? L.s1 : L.s2;
     const int bmax = L.bn1 > L.bn2 ? L.bn1 : L.bn2;
@@ -275,21 +282,33 @@ static int run_router(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
 
 // skip != 0: rows with a negative index are left out (see permute_count_kernel).
 static int run_permute(const Layout& L, const int32_t* idx, const void* x, void* ws, int32_t* counts, int32_t* offsets,
-                       int32_t* sorted, int32_t* inv, uint16_t* xs, int kperm, cudaStream_t st, int skip = 0) {
+                       int32_t* sorted, int32_t* inv, uint16_t* xs, int kperm, cudaStream_t st, int skip = 0,
+                       int coherent = 0) {
   int* status = at<int>(ws, L.status);
   TileListOut l1{at<GemmTile>(ws, L.t1), at<int32_t>(ws, L.n1), L.bn1, L.max_t1};
   TileListOut l2{at<GemmTile>(ws, L.t2), at<int32_t>(ws, L.n2), L.bn2, L.max_t2};
   TileListOut lsh{L.Is > 0 ? at<GemmTile>(ws, L.tsh) : nullptr, at<int32_t>(ws, L.nsh), L.bns, L.max_tsh};
+  // Counters the expert GEMMs expect at zero: split-K arrivals or the fused
+  // launch's per-tile readiness.
+  int32_t* zero = nullptr;
+  int nzero = 0;
+  if (L.split_rows > 0) {
+    zero = at<int32_t>(ws, L.cnt);
+    nzero = L.split_rows * 4;
+  } else if (L.fuse) {
+    zero = at<int32_t>(ws, L.ready);
+    nzero = L.max_t1;
+  }
   if (L.nblk == 1) {
     // Every flat row fits one block: count, scan, tile lists and ranks in one CTA.
     launch_pdl(permute_small_kernel, 1, 1024, 9 * L.E * sizeof(int), st, idx, L.R, L.E, L.T, counts, offsets, sorted, inv, l1,
-               l2, lsh, skip, status, L.split_rows ? at<int32_t>(ws, L.cnt) : (int32_t*)nullptr, L.split_rows * 4);
+               l2, lsh, skip, status, zero, nzero);
     MLXR_LAUNCH_CHECK("permute_small_kernel");
   } else {
     launch_pdl(permute_count_kernel, L.nblk, 256, L.E * sizeof(int), st, idx, L.R, L.E, at<int32_t>(ws, L.bcounts), skip,
                                                                  status);
     MLXR_LAUNCH_CHECK("permute_count_kernel");
-    launch_pdl(permute_scan_kernel, 1, 1024, 0, st, at<int32_t>(ws, L.bcounts), L.nblk, L.E, L.T, at<int32_t>(ws, L.bbase),
+    launch_pdl(permute_scan_kernel, 1, 1024, 0, st, zero, nzero, at<int32_t>(ws, L.bcounts), L.nblk, L.E, L.T, at<int32_t>(ws, L.bbase),
                                             counts, offsets, l1, l2, lsh);
     MLXR_LAUNCH_CHECK("permute_scan_kernel");
     launch_pdl(permute_scatter_kernel, L.nblk, 256, 8 * L.E * sizeof(int), st, idx, L.R, L.E, at<int32_t>(ws, L.bbase),
@@ -300,7 +319,7 @@ static int run_permute(const Layout& L, const int32_t* idx, const void* x, void*
     const int64_t gblocks = (L.rows + 7) / 8;
     const int gather_grid = (int)(gblocks < 4 * 148 ? gblocks : 4 * 148);
     launch_pdl(permute_gather_kernel, gather_grid, 256, 0, st, sorted, L.rows, L.R, L.K, static_cast<const uint16_t*>(x), L.D,
-                                                       kperm, xs, skip ? offsets + L.E : nullptr, status);
+                                                       kperm, xs, skip ? offsets + L.E : nullptr, status, coherent);
     MLXR_LAUNCH_CHECK("permute_gather_kernel");
   }
   return MLXR_CU_OK;
@@ -348,6 +367,22 @@ static int run_experts(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* w
   p.max_split_rows = L.split_rows;
   p.partial = L.split_rows ? at<float>(ws, L.part) : nullptr;
   p.counters = L.split_rows ? at<int32_t>(ws, L.cnt) : nullptr;
+  if (L.fuse) {
+    // gate|up then down (row pairs) in one launch over the same tiles.
+    p.fused = 1;
+    p.w2 = wt->switch_down.weight;
+    p.s2 = static_cast<const uint16_t*>(wt->switch_down.scales);
+    p.b2 = static_cast<const uint16_t*>(wt->switch_down.biases);
+    p.w2_rows = (int64_t)L.E * L.D;
+    p.n_out2 = L.D;
+    p.k_dim2 = L.I;
+    p.act2_rows = L.rows_pad;
+    p.out2 = at<uint16_t>(ws, L.y);
+    p.tile_ready = at<int32_t>(ws, L.ready);
+    if (int rc = launch_grouped_gemm(p, st)) return rc;
+    stage_mark(mid_stage, st);
+    return MLXR_CU_OK;
+  }
   if (int rc = launch_grouped_gemm(p, st)) return rc;
   stage_mark(mid_stage, st);
 
@@ -396,7 +431,7 @@ static int run_shared(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
     const int64_t gblocks = (L.T + 7) / 8;
     const int grid = (int)(gblocks < 4 * 148 ? gblocks : 4 * 148);
     launch_pdl(permute_gather_kernel, grid, 256, 0, st, nullptr, L.T, L.T, 1, static_cast<const uint16_t*>(x), L.D, kperm,
-                                                at<uint16_t>(ws, L.xpad), nullptr, status);
+                                                at<uint16_t>(ws, L.xpad), nullptr, status, 0);
     MLXR_LAUNCH_CHECK("permute_gather_kernel(shared)");
     act = at<uint16_t>(ws, L.xpad);
     act_rows = L.sh_rows_pad;
@@ -1051,7 +1086,7 @@ int mlxr_cu_moe_ep_experts_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_
   MLXR_LAUNCH_CHECK("ep_slot_expert_p2p_kernel");
   if (int rc = run_permute(L, at<int32_t>(ws, L.idx), b + c->bl.recv_x, ws, at<int32_t>(ws, L.counts),
                            at<int32_t>(ws, L.offsets), at<int32_t>(ws, L.sorted), at<int32_t>(ws, L.inv),
-                           at<uint16_t>(ws, L.xs), lc.bits == 4, st, 1))
+                           at<uint16_t>(ws, L.xs), lc.bits == 4, st, 1, 1))
     return rc;
   if (int rc = run_experts(&lc, local_weights, L, ws, st, 7)) return rc;
   int grid = (int)(c->world * c->cap < 8 * 148 ? c->world * c->cap : 8 * 148);

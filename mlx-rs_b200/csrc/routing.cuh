@@ -618,12 +618,14 @@ __device__ inline void build_tile_lists(int e, int E, int tot, int off, int64_t 
 
 // Single CTA of 1024 threads: expert totals, offsets, per-block bases and
 // the GEMM tile lists (one per tile width) plus the dense shared-expert list.
-__global__ void __launch_bounds__(1024) permute_scan_kernel(const int32_t* __restrict__ block_counts, int nblk, int E,
+__global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t* __restrict__ zero, int nzero,
+                                                           const int32_t* __restrict__ block_counts, int nblk, int E,
                                                            int64_t T, int32_t* __restrict__ block_base,
                                                            int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
                                                            TileListOut l1, TileListOut l2, TileListOut lsh) {
   pdl_wait();
   pdl_launch_dependents();
+  for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0;  // counters the GEMMs expect at zero
   __shared__ int warp_sums[32];
   __shared__ int total;
   const int e = threadIdx.x;
@@ -771,7 +773,8 @@ __global__ void __launch_bounds__(256) permute_scatter_kernel(const int32_t* __r
 __global__ void __launch_bounds__(256) permute_gather_kernel(const int32_t* __restrict__ sorted_rows, int64_t n_rows,
                                                             int64_t n_flat, int K, const uint16_t* __restrict__ x,
                                                             int D, int kperm, uint16_t* __restrict__ x_sorted,
-                                                            const int32_t* __restrict__ count, int* status) {
+                                                            const int32_t* __restrict__ count, int* status,
+                                                            int coherent) {
   pdl_wait();
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -792,7 +795,9 @@ __global__ void __launch_bounds__(256) permute_gather_kernel(const int32_t* __re
     const uint4* src = reinterpret_cast<const uint4*>(x + src_row * D);
     uint4* dst = reinterpret_cast<uint4*>(x_sorted + pos * D);
     for (int v = lane; v < dvec; v += 32) {
-      uint4 a = __ldcg(src + v);  // through L2: the rows may have been stored there by a peer GPU
+      // coherent: through L2 only (the rows were stored by a peer GPU);
+      // otherwise the read-only path, which keeps rows gathered K times in L1.
+      uint4 a = coherent ? __ldcg(src + v) : __ldg(src + v);
       if (kperm) {
         uint4 b;
         b.x = __byte_perm(a.x, a.z, 0x5410);
