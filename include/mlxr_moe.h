@@ -239,6 +239,28 @@ MLXR_CU_API int mlxr_cu_moe_permute(const mlxr_cu_moe_config* cfg, const int32_t
                         int32_t* counts, int32_t* offsets, int32_t* sorted_rows, int32_t* inverse, void* x_sorted,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* Routed experts alone (SplitSwitchFfn::forward, switch.rs:417-442: gather_qmm
+ * gate_proj and up_proj, swiglu, gather_qmm down_proj, without the sort and
+ * unsort): y_rows[r] = down_e(silu(gate_e(x_rows[r])) * up_e(x_rows[r])), the
+ * un-weighted output of expert e = row_experts[r], for the T*K rows
+ * (num_tokens = T). Rows may come in any order; the natural input is the
+ * permute step's x_sorted with the sorted experts, which keeps the expert
+ * order. The workspace is the block forward's (mlxr_cu_moe_workspace_size). */
+MLXR_CU_API int mlxr_cu_moe_experts(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights,
+                        const int32_t* row_experts, int64_t num_tokens, const void* x_rows, void* y_rows,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* Combine alone (scatter_unsort and the weighted sum over k, switch.rs:437-439
+ * and 223-234, plus the shared branch, qwen3_5/text/moe.rs:118-120,144):
+ * out[t] = sum_k topk_weights[t,k] * y_sorted[inverse[t*K+k]] (fp32 in k order)
+ * + sigmoid(x[t] . shared_expert_gate) * shared_expert(x[t]); x may be NULL
+ * without a shared expert. An inverse entry outside [0, T*K) is reported by
+ * mlxr_cu_moe_status as MLXR_CU_ERR_DEVICE_INDEX. */
+MLXR_CU_API int mlxr_cu_moe_combine(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights, const void* x,
+                        int64_t num_tokens, const void* y_sorted, const int32_t* inverse,
+                        const void* topk_weights, void* out, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
 /* ---------------------------------------------- expert parallelism -- */
 /* No counterpart in the reference, which runs the whole block on one device
  * (Qwen35MoeBlock::forward, crates/mlxr-lm/src/qwen3_5/text/moe.rs:116-146,

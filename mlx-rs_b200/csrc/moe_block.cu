@@ -698,6 +698,75 @@ int mlxr_cu_moe_permute(const mlxr_cu_moe_config* cfg, const int32_t* indices, i
                      0, st);
 }
 
+int mlxr_cu_moe_experts(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights, const int32_t* row_experts,
+                        int64_t num_tokens, const void* x_rows, void* y_rows, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  if (int rc = validate(cfg, num_tokens)) return rc;
+  MLXR_CHECK_ARG(weights != nullptr, "moe_experts: weights is NULL");
+  const Layout L = make_layout(cfg, num_tokens);
+  if (int rc = check_ws(L, workspace, workspace_bytes)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  MLXR_CUDA_TRY(cudaMemsetAsync(at<int>(workspace, L.status), 0, kStatusSlotBytes, st));
+  if (num_tokens == 0) return MLXR_CU_OK;
+  MLXR_CHECK_ARG(row_experts && x_rows && y_rows, "moe_experts: NULL argument");
+  MLXR_CHECK_ARG(aligned16(x_rows) && aligned16(y_rows), "moe_experts: x_rows and y_rows must be 16-byte aligned");
+  void* ws = workspace;
+  // The T*K rows are grouped by expert as single-slot tokens (a stable sort:
+  // the identity when they already are), gathered into the GEMM operand
+  // buffer, run through the experts, and written back in the caller's order.
+  Layout P = L;
+  P.K = 1;
+  P.T = L.R;
+  P.Is = 0;
+  if (int rc = run_permute(P, row_experts, x_rows, ws, at<int32_t>(ws, L.counts), at<int32_t>(ws, L.offsets),
+                           at<int32_t>(ws, L.sorted), at<int32_t>(ws, L.inv), at<uint16_t>(ws, L.xs), cfg->bits == 4, st))
+    return rc;
+  if (int rc = run_experts(cfg, weights, L, ws, st, 3)) return rc;
+  const int64_t gblocks = (L.R + 7) / 8;
+  const int grid = (int)(gblocks < 4 * 148 ? gblocks : 4 * 148);
+  launch_pdl(permute_gather_kernel, grid, 256, 0, st, at<int32_t>(ws, L.inv), L.R, L.R, 1, at<uint16_t>(ws, L.y), L.D, 0,
+             static_cast<uint16_t*>(y_rows), nullptr, at<int>(ws, L.status), 0);
+  MLXR_LAUNCH_CHECK("permute_gather_kernel(unsort)");
+  return MLXR_CU_OK;
+}
+
+int mlxr_cu_moe_combine(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights, const void* x,
+                        int64_t num_tokens, const void* y_sorted, const int32_t* inverse, const void* topk_weights,
+                        void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = validate(cfg, num_tokens)) return rc;
+  const Layout L = make_layout(cfg, num_tokens);
+  if (int rc = check_ws(L, workspace, workspace_bytes)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  MLXR_CUDA_TRY(cudaMemsetAsync(at<int>(workspace, L.status), 0, kStatusSlotBytes, st));
+  if (num_tokens == 0) return MLXR_CU_OK;
+  MLXR_CHECK_ARG(y_sorted && inverse && topk_weights && out, "moe_combine: NULL argument");
+  MLXR_CHECK_ARG(aligned16(y_sorted) && aligned16(out), "moe_combine: y_sorted and out must be 16-byte aligned");
+  void* ws = workspace;
+  const uint16_t* ysh = nullptr;
+  if (L.Is > 0) {
+    MLXR_CHECK_ARG(weights != nullptr && x != nullptr && aligned16(x), "moe_combine: weights / x is NULL or misaligned");
+    MLXR_CHECK_ARG(weights->shared_expert_gate.weight && weights->shared_expert_gate.scales &&
+                       weights->shared_expert_gate.biases,
+                   "moe_combine: shared_expert_gate is NULL");
+    SharedGateArgs sg{weights->shared_expert_gate.weight,
+                      static_cast<const uint16_t*>(weights->shared_expert_gate.scales),
+                      static_cast<const uint16_t*>(weights->shared_expert_gate.biases), cfg->shared_bits};
+    launch_pdl(shared_gate_kernel, (unsigned)((L.T + 7) / 8), 256, 0, st, static_cast<const uint16_t*>(x), L.T, L.D, sg,
+               at<float>(ws, L.sig));
+    MLXR_LAUNCH_CHECK("shared_gate_kernel");
+    launch_pdl(shared_tiles_kernel, (unsigned)((L.max_tsh + 255) / 256), 256, 0, st, at<GemmTile>(ws, L.tsh),
+               at<int32_t>(ws, L.nsh), L.T, L.bns, L.max_tsh);
+    MLXR_LAUNCH_CHECK("shared_tiles_kernel");
+    if (int rc = run_shared(cfg, weights, L, x, ws, st)) return rc;
+    ysh = at<uint16_t>(ws, L.ysh);
+  }
+  launch_pdl(combine_kernel, (unsigned)L.T, L.D >= 2048 ? 256 : 128, 0, st, static_cast<const uint16_t*>(y_sorted), inverse,
+             static_cast<const uint16_t*>(topk_weights), L.K, L.D, L.T, ysh, at<float>(ws, L.sig),
+             static_cast<uint16_t*>(out), at<int>(ws, L.status));
+  MLXR_LAUNCH_CHECK("combine_kernel");
+  return MLXR_CU_OK;
+}
+
 // ------------------------------------------------ expert parallelism ---
 // One rank's share of the block when its experts are spread over `world`
 // ranks (expert e on rank e % world as local expert e / world). Per step:

@@ -1124,6 +1124,17 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const uint16_t* __restr
 
 // The dense shared-expert tile list alone (row tiles of width bn over T
 // tokens), for callers that run the shared expert without a permute.
+// sig[t] = sigmoid(x[t] . dequant(shared_expert_gate)) alone, one warp per
+// token, for callers that run the combine without the router (the routers
+// compute it in their own pass over x, with the same helper).
+__global__ void __launch_bounds__(256) shared_gate_kernel(const uint16_t* __restrict__ x, int64_t T, int D,
+                                                         SharedGateArgs sg, float* __restrict__ sig) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t t = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t < T) shared_gate_warp(x + t * D, D, sg, threadIdx.x & 31, sig + t);
+}
+
 __global__ void shared_tiles_kernel(GemmTile* __restrict__ tiles, int32_t* __restrict__ count, int64_t T, int bn,
                                     int cap) {
   pdl_wait();

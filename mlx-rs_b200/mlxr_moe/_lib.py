@@ -44,6 +44,8 @@ EXPORTS = (
     "mlxr_cu_op_status",
     "mlxr_cu_moe_router",
     "mlxr_cu_moe_permute",
+    "mlxr_cu_moe_experts",
+    "mlxr_cu_moe_combine",
     "mlxr_cu_synth_normal_bf16",
     "mlxr_cu_moe_ep_workspace_size",
     "mlxr_cu_moe_ep_dispatch",
@@ -146,6 +148,9 @@ def _load():
     lib.mlxr_cu_moe_router.argtypes = [C.POINTER(MoeConfig), C.POINTER(MoeWeights), P, I64, P, P, P, P, P,
                                        C.c_size_t, P]
     lib.mlxr_cu_moe_permute.argtypes = [C.POINTER(MoeConfig), P, I64, P, P, P, P, P, P, P, C.c_size_t, P]
+    lib.mlxr_cu_moe_experts.argtypes = [C.POINTER(MoeConfig), C.POINTER(MoeWeights), P, I64, P, P, P, C.c_size_t, P]
+    lib.mlxr_cu_moe_combine.argtypes = [C.POINTER(MoeConfig), C.POINTER(MoeWeights), P, I64, P, P, P, P, P,
+                                        C.c_size_t, P]
     lib.mlxr_cu_synth_normal_bf16.argtypes = [C.c_uint64, C.c_uint64, I64, C.c_float, P, P]
     cfg_p, w_p = C.POINTER(MoeConfig), C.POINTER(MoeWeights)
     lib.mlxr_cu_moe_ep_workspace_size.argtypes = [cfg_p, I32, I64, I64, I64, C.POINTER(C.c_size_t)]

@@ -244,6 +244,36 @@ class Qwen35MoeBlock:
                   ws.numel(), st)
         return counts, offsets, srt, inv, xs[: T * K]
 
+    def experts(self, row_experts: torch.Tensor, x_rows: torch.Tensor) -> torch.Tensor:
+        """y_rows [T*K, D]: each row through its expert's SwiGLU FFN, un-weighted (switch.rs:417-442)."""
+        K, D = self.cfg.num_experts_per_tok, self.cfg.hidden_size
+        R = row_experts.numel()
+        if R % K:
+            raise ValueError(f"experts: {R} rows is not a multiple of num_experts_per_tok={K}")
+        T, dev = R // K, x_rows.device
+        xr = x_rows.reshape(R, D).contiguous()
+        y = torch.empty((max(R, 1), D), dtype=torch.bfloat16, device=dev)
+        ws = self.workspace(T, dev)
+        st = torch.cuda.current_stream(dev).cuda_stream
+        _lib.call("mlxr_cu_moe_experts", C.byref(self._ccfg), C.byref(self._cw),
+                  row_experts.to(torch.int32).contiguous().data_ptr(), T, xr.data_ptr(), y.data_ptr(), ws.data_ptr(),
+                  ws.numel(), st)
+        return y[:R]
+
+    def combine(self, x: torch.Tensor, y_sorted: torch.Tensor, inverse: torch.Tensor,
+                topk_weights: torch.Tensor) -> torch.Tensor:
+        """out [T, D]: the weighted sum of each token's expert rows plus the gated shared expert."""
+        x2 = x.reshape(-1, x.shape[-1]).contiguous()
+        T, dev = x2.shape[0], x.device
+        out = torch.empty_like(x2)
+        ws = self.workspace(T, dev)
+        st = torch.cuda.current_stream(dev).cuda_stream
+        _lib.call("mlxr_cu_moe_combine", C.byref(self._ccfg), C.byref(self._cw), x2.data_ptr(), T,
+                  y_sorted.contiguous().data_ptr(), inverse.to(torch.int32).contiguous().data_ptr(),
+                  topk_weights.to(torch.bfloat16).contiguous().data_ptr(), out.data_ptr(), ws.data_ptr(), ws.numel(),
+                  st)
+        return out.reshape(x.shape)
+
     def forward_ops(self, x: torch.Tensor) -> torch.Tensor:
         """The reference's op-by-op chain (moe.rs:116-146) through the op family."""
         idx, w = self.router(x)

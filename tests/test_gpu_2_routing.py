@@ -20,7 +20,7 @@ def _router_block(D, E, K, zipf=False, seed=0):
     cfg = MoeConfig(D, E, K, 128, bits=4)
     router = ops.synth_normal_bf16(seed, synth.STREAM_ROUTER, (E, D), 0.02)
     dummy = QuantizedSwitchLinear.from_switch_linear(ops.synth_normal_bf16(seed, 1, (1, 128, D), 0.02), 64, 4)
-    bias = synth.zipf_bias(E, seed) if zipf else None
+    bias = synth.zipf_bias(E, D, seed) if zipf else None
     return Qwen35MoeBlock(cfg, router, SplitSwitchFfn(dummy, dummy, dummy), router_bias=bias)
 
 

@@ -169,3 +169,57 @@ def test_determinism_and_op_level_chain():
     # the reference's op-by-op chain through the op family agrees with the fused block
     c = blk.forward_ops(x)
     assert_close_bf16(bf16_np(c), bf16_np(a), ATOL, RTOL, "op-level chain vs fused block")
+
+
+def _substep_chain(blk, x):
+    idx, w = blk.router(x)
+    counts, offsets, srt, inv, xs = blk.permute(idx, x)
+    row_experts = idx.reshape(-1)[srt.long()]
+    ys = blk.experts(row_experts, xs)
+    return blk.combine(x, ys, inv, w), row_experts, xs, ys
+
+
+@pytest.mark.parametrize("name,T", [("c1", 32), ("c2", 8), ("c2", 64), ("c4", 300)])
+def test_substeps_chain_equals_block(name, T):
+    """router -> permute -> experts -> combine through the sub-step entry points
+    gives the block forward's output bit for bit (same kernels, same order)."""
+    blk, _ = block_for(name)
+    x = synth.make_input(T, blk.cfg.hidden_size, stream_offset=5)
+    out_blk, _ = run_gpu_block(blk, x)
+    out, _, _, _ = _substep_chain(blk, x)
+    blk.status()
+    assert torch.equal(out, out_blk)
+
+
+def test_substep_experts_rows_any_order_and_vs_oracle():
+    blk, ow = block_for("c1")
+    cfg, W = ow
+    x = synth.make_input(32, 2048, stream_offset=6)
+    _, row_experts, xs, ys = _substep_chain(blk, x)
+    # a shuffled row order returns the same rows, shuffled
+    perm = torch.randperm(row_experts.numel(), generator=torch.Generator().manual_seed(0)).cuda()
+    ys2 = blk.experts(row_experts[perm], xs[perm].contiguous())
+    assert torch.equal(ys2, ys[perm])
+    # each row against the oracle's gather_qmm chain (bf16 gate/up and h, fp32 accumulation)
+    xo, re = bf16_np(xs)[:, None, :], row_experts.cpu().numpy()
+    g = O.gather_qmm(xo, *W["gate"], rhs=re, bits=4)
+    u = O.gather_qmm(xo, *W["up"], rhs=re, bits=4)
+    g32 = O.bf16_to_f32(O.f32_to_bf16(g))
+    h = O.f32_to_bf16(g32 / (1.0 + np.exp(-g32)) * O.bf16_to_f32(O.f32_to_bf16(u)))
+    y = O.f32_to_bf16(O.gather_qmm(h, *W["down"], rhs=re, bits=4))[:, 0, :]
+    assert_close_bf16(bf16_np(ys), y, ATOL, RTOL, "experts sub-step vs oracle rows")
+
+
+def test_substep_combine_reports_bad_inverse():
+    blk, _ = block_for("c1")
+    x = synth.make_input(8, 2048, stream_offset=7)
+    idx, w = blk.router(x)
+    _, _, srt, inv, xs = blk.permute(idx, x)
+    ys = blk.experts(idx.reshape(-1)[srt.long()], xs)
+    bad = inv.clone()
+    bad[3] = 8 * 8  # one past the last row
+    blk.combine(x, ys, bad, w)
+    from mlxr_moe import _lib
+
+    with pytest.raises(_lib.MlxrError):
+        blk.status()
