@@ -114,6 +114,10 @@ static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
   if (FUSED && (!p.w2 || !p.s2 || !p.b2 || !p.out2 || !p.tile_ready || p.n_out2 % 256 != 0 || p.k_dim2 % 64 != 0 ||
                 p.k_dim2 != p.n_out))
     return set_error(MLXR_CU_ERR_INVALID_ARGUMENT, "grouped gemm: bad fused second phase");
+  // k-parity accumulators: every work item needs a k-step of each parity.
+  if (C::KP == 2 && ((p.k_dim / C::BK) / a.splits < 2 || (FUSED && p.k_dim2 / C::BK < 2)))
+    return set_error(MLXR_CU_ERR_INVALID_ARGUMENT, "grouped gemm: K=%d over %d splits leaves a work item one k-step",
+                     p.k_dim, a.splits);
   const int grid = p.grid > 0 ? p.grid : num_sms_current();
   launch_pdl(kern, grid, C::NUM_THREADS, C::SMEM_BYTES, st, ta0, ta1, tb, ta2, tb2, a);
   MLXR_LAUNCH_CHECK("grouped_dequant_gemm_kernel");

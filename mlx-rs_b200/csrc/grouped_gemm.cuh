@@ -19,7 +19,7 @@
 // D[128, BN] lives in TMEM too: lane = output feature, column = token.
 // Decode batches use small BN (16/32), prefill BN = 128 (gate/up) or 256 (down).
 //
-// Warp roles (736 threads, 768 with two weight matrices):
+// Warp roles (736 threads, 768 with two weight matrices or narrow tiles):
 //   warps 0-3   epilogue: TMEM -> registers -> SwiGLU / plain -> bf16 global
 //   warps 4-19  dequant: packed uint32 tile (smem) -> bf16 A stage in TMEM;
 //               NGRP = 2 (two matrices) or 4 (one) groups of warps take
@@ -28,9 +28,10 @@
 //               other's barrier, fence and TMEM-store latencies
 //   warp 20     TMA producer for packed weight tiles (raw ring)
 //   warp 21     TMA producer for activation tiles (B ring)
-//   warps 22-   one single-thread tcgen05.mma issuer per weight matrix
+//   warps 22-   single-thread tcgen05.mma issuers: one per weight matrix, or
+//               for narrow tiles (BN <= 32) one per k-step parity
 //               (warp 22 also allocates TMEM)
-// TMEM columns: [0, AB*NMAT*BN) accumulators (double-buffered when they fit,
+// TMEM columns: [0, AB*NMAT*BN*KP) accumulators (double-buffered when they fit,
 // so the epilogue of item i overlaps the main loop of item i+1), then OS
 // stages of NMAT x 32 columns (128 rows x 64 bf16) of dequantised A.
 #pragma once
@@ -56,8 +57,14 @@ struct GG {
   static constexpr int RAW_MAT = BM * RAW_ROW;
   static constexpr int RAW_STAGE = NMAT * RAW_MAT;
   static constexpr int B_STAGE = BN * BK * 2;
+  // Narrow (decode) tiles split every accumulator by k-step parity: two
+  // issuers, one per parity, each issue all NMAT matrices' MMAs of their own
+  // k-steps into their own accumulators, and the epilogue adds the halves.
+  // The fixed cost a thread pays per tcgen05.mma, commit and barrier wait,
+  // not the tensor pipe, bounds a single issuer's k-step rate at these widths.
+  static constexpr int KP = BN <= 32 ? 2 : 1;
   // Tensor memory: accumulators, then the A stages.
-  static constexpr int ACC_COLS = NMAT * BN;
+  static constexpr int ACC_COLS = NMAT * BN * KP;
   static constexpr int A_COLS = NMAT * 32;                // one A stage: NMAT x (128 x 64 bf16)
   static constexpr int AB = (2 * ACC_COLS + 2 * A_COLS <= 512) ? 2 : 1;
   static constexpr int OS_FIT = (512 - AB * ACC_COLS) / A_COLS;
@@ -85,7 +92,8 @@ struct GG {
   // One MMA-issuing thread per matrix: issuing a tcgen05.mma costs the issuing
   // thread tens of cycles whatever N is, so with narrow decode tiles a single
   // issuer, not the tensor pipe, bounds the k-step rate.
-  static constexpr int ISSUERS = NMAT;
+  static constexpr int ISSUERS = KP == 2 ? 2 : NMAT;
+  static constexpr int STAGE_COMMITS = KP == 2 ? 1 : ISSUERS;  // commits that release one stage
   static constexpr int DQ_WARPS = 16;
   static constexpr int W_RAW = 4 + DQ_WARPS;  // raw weight producer warp
   static constexpr int W_B = W_RAW + 1;       // activation producer warp
@@ -262,7 +270,7 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
     }
     for (int i = 0; i < C::OS; ++i) {
       mbar_init(&op_full[i], C::GRP_WARPS);
-      mbar_init(&op_empty[i], C::ISSUERS);
+      mbar_init(&op_empty[i], C::STAGE_COMMITS);
     }
     for (int i = 0; i < C::OS; ++i) mbar_init(&b_full[i], 1);
     for (int i = 0; i < C::AB; ++i) {
@@ -408,7 +416,53 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
     // accumulator; every stage and accumulator barrier expects one commit
     // per issuer.
     const int mi = warp - C::W_MMA;
-    if (lane == 0) {
+    if (C::KP == 2 && lane == 0) {
+      // Issuer mi takes the k-steps of global parity mi (the same split as the
+      // dequant groups) for every matrix, into accumulator half mi.
+      const uint64_t bdesc0 = umma_desc_sw128(smem_u32(sB));
+      const uint32_t a0 = tmem_base + (uint32_t)C::A_BASE;
+      uint32_t li = 0, git = 0;
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
+        const Item di = item_of(item);
+        if (!tile_ok(args.tiles[di.tile], args)) continue;
+        const int ab = li % C::AB;
+        const uint32_t acc_phase = (li / C::AB) & 1;
+        ++li;
+        if (!mbar_wait(&acc_empty[ab], acc_phase ^ 1, abort_flag, args.status)) break;
+        tc_fence_after();
+        const uint32_t d0 = tmem_base + (uint32_t)(ab * C::ACC_COLS + mi * BN);
+        uint32_t acc = 0;
+        for (int ks = di.k_lo; ks < di.k_hi; ++ks, ++git) {
+          if ((git & 1u) == (uint32_t)mi) {
+            if (!mbar_wait(&b_full[s], ph, abort_flag, args.status) ||
+                !mbar_wait(&op_full[s], ph, abort_flag, args.status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t bd = bdesc0 + (uint64_t)(s * (C::B_STAGE >> 4));
+            const uint32_t as = a0 + (uint32_t)(s * C::A_COLS);
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m)
+              umma_bf16_ts_k64(d0 + (uint32_t)(m * 2 * BN), as + (uint32_t)(m * 32), bd, C::IDESC, acc);
+            acc = 1;
+            umma_commit(&op_empty[s]);
+          }
+          if (++s == C::OS) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        // (with no k-step of its parity in the item the commit arrives at once
+        // and the half is never read: items have at least two k-steps)
+        if (ok) umma_commit(&acc_full[ab]);
+      }
+      umma_commit(fin_bar);
+      mbar_wait(fin_bar, 0, abort_flag, args.status);
+    } else if (C::KP == 1 && lane == 0) {
       const uint64_t bdesc0 = umma_desc_sw128(smem_u32(sB));
       const uint32_t a0 = tmem_base + (uint32_t)(C::A_BASE + mi * 32);
       uint32_t li = 0;
@@ -558,7 +612,8 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
     // ------------------------------------------------------- epilogue ----
     const int q = warp;  // TMEM lane quarter 0..3
     uint32_t li = 0;
-    constexpr int CW = 16;  // TMEM columns per load (keeps the epilogue's registers small)
+    // TMEM columns per load (keeps the epilogue's registers small).
+    constexpr int CW = C::KP == 2 ? 8 : 16;
     constexpr int PQ = NMAT * BN * 32;  // floats of one quarter's partial accumulators
     for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
       const Item d = item_of(item);
@@ -579,6 +634,31 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * C::ACC_COLS);
       uint16_t* outp = outb + (int64_t)t.row_start * n_out + f;
       const int rows = t.row_count < BN ? t.row_count : BN;
+      // Columns [c*CW, c*CW + CW) of both matrices' accumulators (halves added
+      // for k-parity accumulators: half 0 + half 1, in that order).
+      auto load_cols = [&](int c, float (&gv)[16], float (&uv)[16]) {
+        const uint32_t tc = tbase + (uint32_t)(c * CW);
+        if constexpr (C::KP == 2) {
+          uint32_t r[32];
+          if (NMAT == 2) tmem_ld4_x8_wait(tc, tc + BN, tc + 2 * BN, tc + 3 * BN, r);
+          else tmem_ld2_x8_wait(tc, tc + BN, r);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            gv[j] = __uint_as_float(r[j]) + __uint_as_float(r[8 + j]);
+            uv[j] = NMAT == 2 ? __uint_as_float(r[16 + j]) + __uint_as_float(r[24 + j]) : 0.0f;
+          }
+        } else {
+          uint32_t g[32];
+          uint32_t u[32];
+          if (NMAT == 2) tmem_ld2_x16_wait(tc, tc + BN, g, u);
+          else tmem_ld_x16_wait(tc, g);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            gv[j] = __uint_as_float(g[j]);
+            uv[j] = NMAT == 2 ? __uint_as_float(u[j]) : 0.0f;
+          }
+        }
+      };
       auto store = [&](int col, float gv, float uv) {
         if (NMAT == 2 && d.pair) {
           outp[(int64_t)col * n_out] = f32_to_bf16_bits(gv);
@@ -598,14 +678,12 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
 #pragma unroll 1
         for (int c = 0; c < BN / CW && in_cap; ++c) {
           if (c * CW >= rows) break;
-          uint32_t g[32];
-          uint32_t u[32];
-          if (NMAT == 2) tmem_ld2_x16_wait(tbase + c * CW, tbase + BN + c * CW, g, u);
-          else tmem_ld_x16_wait(tbase + c * CW, g);
+          float gv[16], uv[16];
+          load_cols(c, gv, uv);
 #pragma unroll
           for (int j = 0; j < CW; ++j) {
-            pq[(c * CW + j) * 32 + lane] = __uint_as_float(g[j]);
-            if (NMAT == 2) pq[(BN + c * CW + j) * 32 + lane] = __uint_as_float(u[j]);
+            pq[(c * CW + j) * 32 + lane] = gv[j];
+            if (NMAT == 2) pq[(BN + c * CW + j) * 32 + lane] = uv[j];
           }
         }
         tc_fence_before();
@@ -638,14 +716,12 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
 #pragma unroll 1
       for (int c = 0; c < BN / CW; ++c) {
         if (c * CW >= rows) break;
-        uint32_t g[32];
-        uint32_t u[32];
-        if (NMAT == 2) tmem_ld2_x16_wait(tbase + c * CW, tbase + BN + c * CW, g, u);
-        else tmem_ld_x16_wait(tbase + c * CW, g);
+        float gv[16], uv[16];
+        load_cols(c, gv, uv);
         const int nvalid = rows - c * CW < CW ? rows - c * CW : CW;
 #pragma unroll
         for (int j = 0; j < CW; ++j)
-          if (j < nvalid) store(c * CW + j, __uint_as_float(g[j]), NMAT == 2 ? __uint_as_float(u[j]) : 0.0f);
+          if (j < nvalid) store(c * CW + j, gv[j], uv[j]);
       }
       tc_fence_before();
       __syncwarp();
