@@ -148,6 +148,23 @@ __device__ inline bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes or `ns` nanoseconds pass, instead of spinning. A spinning waiter
+// takes issue slots from the warps that share its SM sub-partition: in the
+// grouped GEMM a spinning producer warp left the dequant warps beside it
+// thousands of cycles behind the others.
+__device__ inline bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait on an mbarrier phase. Returns false (and raises the CTA's
 // abort flag and the global status) when the limit expires or when another
 // thread of the CTA has already aborted.
@@ -155,14 +172,12 @@ __device__ inline bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* a
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 0) {
-      if (*abort_flag) return false;
-      if (global_ns() - t0 > kWaitLimitNs) {
-        *abort_flag = 1;
-        atomicCAS(status, 0, (int)kDevTimeout);
-        return false;
-      }
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (*abort_flag) return false;
+    if ((it & 15u) == 0 && global_ns() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      atomicCAS(status, 0, (int)kDevTimeout);
+      return false;
     }
   }
 }
