@@ -608,11 +608,13 @@ def run_reference(args):
     sec = time.perf_counter() - t0
     value = sum(BATCHES) * args.steps / sec
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 0, "steps": args.steps,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * sec / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (Philox seed 0), same configuration as the GPU arm",
-        "config": {"workload": "c2 decode sweep: one block forward at T=1, 8, 64 per step", "batches": BATCHES},
+        "config": {"workload": "c2 decode sweep: one block forward at T=1, 8, 64 per step",
+                   "hidden": 2048, "experts": 128, "top_k": 8, "moe_intermediate": 768, "bits": 4, "group_size": 64,
+                   "batches": BATCHES, "host": f"CPU, {cores} threads (rank 0 only; the GPUs are unused)"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": f"{args.steps} full sweeps on the oracle (CPU restatement; MLX unbuildable here)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
