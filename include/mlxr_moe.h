@@ -126,8 +126,11 @@ typedef struct mlxr_cu_moe_config {
   int32_t shared_expert_intermediate_size; /* Is; 0 = no shared expert */
   int32_t group_size;                      /* 64 */
   int32_t bits;                            /* routed experts: 4 or 8 */
-  int32_t shared_bits;                     /* shared expert + its gate: 4 or 8 */
+  int32_t shared_bits;                     /* shared expert: 4 or 8 */
   int32_t norm_topk_prob;                  /* 1 = renormalise top-k (moe.rs:136-138) */
+  int32_t shared_gate_bits;                /* shared_expert_gate: 4 or 8; 0 = shared_bits. Converted
+                                              checkpoints pin it at 8 (mlxr-convert/src/qwen3_5.rs:
+                                              classify_default) while the body is 4-bit */
 } mlxr_cu_moe_config;
 
 /* One quantised projection: packed weight, scales, biases (bf16). */

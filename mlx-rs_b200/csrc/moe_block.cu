@@ -75,6 +75,10 @@ static int pick_bn(double avg_rows, int max_bn) {
   return bn < max_bn ? bn : max_bn;
 }
 
+static int shared_gate_bits(const mlxr_cu_moe_config* c) {
+  return c->shared_gate_bits ? c->shared_gate_bits : c->shared_bits;
+}
+
 static int validate(const mlxr_cu_moe_config* c, int64_t T) {
   MLXR_CHECK_ARG(c != nullptr, "moe: null config");
   MLXR_CHECK_ARG(T >= 0, "moe: negative token count");
@@ -94,6 +98,10 @@ static int validate(const mlxr_cu_moe_config* c, int64_t T) {
   if (c->bits != 4 && c->bits != 8) return set_error(MLXR_CU_ERR_UNSUPPORTED, "moe: bits=%d is not supported (4, 8)", c->bits);
   if (c->shared_expert_intermediate_size > 0 && c->shared_bits != 4 && c->shared_bits != 8)
     return set_error(MLXR_CU_ERR_UNSUPPORTED, "moe: shared_bits=%d is not supported (4, 8)", c->shared_bits);
+  if (c->shared_expert_intermediate_size > 0 && c->shared_gate_bits != 0 && c->shared_gate_bits != 4 &&
+      c->shared_gate_bits != 8)
+    return set_error(MLXR_CU_ERR_UNSUPPORTED, "moe: shared_gate_bits=%d is not supported (0, 4, 8)",
+                     c->shared_gate_bits);
   MLXR_CHECK_ARG(T * (int64_t)c->num_experts_per_tok < (int64_t)1 << 30, "moe: T*K=%lld too large",
                  (long long)(T * c->num_experts_per_tok));
   return MLXR_CU_OK;
@@ -223,7 +231,7 @@ static int run_router(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
     sg.w = wt->shared_expert_gate.weight;
     sg.s = static_cast<const uint16_t*>(wt->shared_expert_gate.scales);
     sg.b = static_cast<const uint16_t*>(wt->shared_expert_gate.biases);
-    sg.bits = c->shared_bits;
+    sg.bits = shared_gate_bits(c);
     sig = at<float>(ws, L.sig);
   }
   const uint16_t* xp = static_cast<const uint16_t*>(x);
@@ -750,7 +758,7 @@ int mlxr_cu_moe_combine(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights
                    "moe_combine: shared_expert_gate is NULL");
     SharedGateArgs sg{weights->shared_expert_gate.weight,
                       static_cast<const uint16_t*>(weights->shared_expert_gate.scales),
-                      static_cast<const uint16_t*>(weights->shared_expert_gate.biases), cfg->shared_bits};
+                      static_cast<const uint16_t*>(weights->shared_expert_gate.biases), shared_gate_bits(cfg)};
     launch_pdl(shared_gate_kernel, (unsigned)((L.T + 7) / 8), 256, 0, st, static_cast<const uint16_t*>(x), L.T, L.D, sg,
                at<float>(ws, L.sig));
     MLXR_LAUNCH_CHECK("shared_gate_kernel");

@@ -90,6 +90,7 @@ class MoeConfig(C.Structure):
         ("bits", I32),
         ("shared_bits", I32),
         ("norm_topk_prob", I32),
+        ("shared_gate_bits", I32),
     ]
 
 

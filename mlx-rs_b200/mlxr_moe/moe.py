@@ -34,12 +34,14 @@ class MoeConfig:
     bits: int = 4
     shared_bits: int | None = None
     norm_topk_prob: bool = True
+    shared_gate_bits: int | None = None  # None: shared_bits
 
     def to_c(self) -> _lib.MoeConfig:
         return _lib.MoeConfig(
             self.hidden_size, self.num_experts, self.num_experts_per_tok, self.moe_intermediate_size,
             self.shared_expert_intermediate_size, self.group_size, self.bits,
             self.shared_bits if self.shared_bits is not None else self.bits, int(self.norm_topk_prob),
+            self.shared_gate_bits or 0,
         )
 
 

@@ -538,8 +538,9 @@ struct OrcMoeConfig {
   int shared_intermediate;  // Is (0 = no shared expert)
   int group_size;
   int bits;
-  int shared_bits;  // bits of the shared expert and its gate
+  int shared_bits;  // bits of the shared expert
   int renorm;
+  int shared_gate_bits;  // bits of shared_expert_gate; 0 = shared_bits
 };
 
 struct OrcMoeWeights {
@@ -618,8 +619,8 @@ ORC_API int orc_moe_block(const OrcMoeConfig* c, const OrcMoeWeights* wt, const 
     dense_weight(wt->sh_gate.w, wt->sh_gate.s, wt->sh_gate.b, DT_BF16, 0, Is, D, 1, gs, sbits, sg.data());
     dense_weight(wt->sh_up.w, wt->sh_up.s, wt->sh_up.b, DT_BF16, 0, Is, D, 1, gs, sbits, su.data());
     dense_weight(wt->sh_down.w, wt->sh_down.s, wt->sh_down.b, DT_BF16, 0, D, Is, 1, gs, sbits, sd.data());
-    dense_weight(wt->sh_expert_gate.w, wt->sh_expert_gate.s, wt->sh_expert_gate.b, DT_BF16, 0, 1, D, 1, gs, sbits,
-                 gw.data());
+    dense_weight(wt->sh_expert_gate.w, wt->sh_expert_gate.s, wt->sh_expert_gate.b, DT_BF16, 0, 1, D, 1, gs,
+                 c->shared_gate_bits ? c->shared_gate_bits : sbits, gw.data());
     if (fused) {
       for (auto& v : sg) v = rbf(v);
       for (auto& v : su) v = rbf(v);

@@ -63,6 +63,7 @@ class OrcMoeConfig(C.Structure):
         ("bits", I32),
         ("shared_bits", I32),
         ("renorm", I32),
+        ("shared_gate_bits", I32),
     ]
 
 
@@ -285,7 +286,7 @@ def moe_block(cfg: dict, weights: dict, x: np.ndarray, mode: str = "fused"):
     c = OrcMoeConfig(
         cfg["hidden"], cfg["num_experts"], cfg["top_k"], cfg["moe_intermediate"], cfg.get("shared_intermediate", 0),
         cfg.get("group_size", 64), cfg.get("bits", 4), cfg.get("shared_bits", cfg.get("bits", 4)),
-        int(cfg.get("renorm", True)),
+        int(cfg.get("renorm", True)), int(cfg.get("shared_gate_bits", 0) or 0),
     )
     keep = []
 

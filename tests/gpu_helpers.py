@@ -20,7 +20,7 @@ def block_to_oracle(block):
     cfg = dict(hidden=c.hidden_size, num_experts=c.num_experts, top_k=c.num_experts_per_tok,
                moe_intermediate=c.moe_intermediate_size, shared_intermediate=c.shared_expert_intermediate_size,
                group_size=c.group_size, bits=c.bits, shared_bits=c.shared_bits if c.shared_bits else c.bits,
-               renorm=c.norm_topk_prob)
+               renorm=c.norm_topk_prob, shared_gate_bits=c.shared_gate_bits or 0)
     sm = block.switch_mlp
     W = {"router": bf16_np(block.gate), "gate": qtriple(sm.gate_proj), "up": qtriple(sm.up_proj),
          "down": qtriple(sm.down_proj)}
