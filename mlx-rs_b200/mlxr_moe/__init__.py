@@ -3,8 +3,9 @@
 Importing this package loads libmlxr_moe.so; it raises if the library is
 missing (there is no CPU fallback).
 """
-from . import _lib, ops, synth
+from . import _lib, checkpoint, ops, synth
 from ._lib import MlxrError
+from .checkpoint import load_qwen35_moe_block
 from .moe import (MoeConfig, QuantizedLinear, QuantizedSwitchLinear, Qwen35MoeBlock, Routing, SplitSwitchFfn,
                   SwigluMlp)
 from .ops import dequantize, gather_mm, gather_qmm, quantize, quantized_matmul
@@ -12,5 +13,5 @@ from .ops import dequantize, gather_mm, gather_qmm, quantize, quantized_matmul
 __all__ = [
     "MlxrError", "MoeConfig", "QuantizedLinear", "QuantizedSwitchLinear", "Qwen35MoeBlock", "Routing",
     "SplitSwitchFfn", "SwigluMlp", "dequantize", "gather_mm", "gather_qmm", "quantize", "quantized_matmul",
-    "ops", "synth", "_lib",
+    "ops", "synth", "_lib", "checkpoint", "load_qwen35_moe_block",
 ]
