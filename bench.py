@@ -568,7 +568,7 @@ def cpu_baseline(blk, graphs, args):
     cfg, W = block_to_oracle(blk)
     cores = O.max_threads()
     times = []
-    reps = 3
+    reps = 5
     for rep in range(reps):
         t0 = time.perf_counter()
         for T in BATCHES:
