@@ -141,11 +141,39 @@ def smi_id(torch, dev) -> str:
         return str(dev.index)
 
 
-def kernels_per_forward(cfg) -> int:
-    # router (logits, top-k) + permute (count, scan, scatter, gather) + gate/up + down + combine
-    n = 1 + 2 + 2 + 1  # router, permute (small path: ranks + gather), gate|up, down, combine
+def kernels_per_forward(cfg, T: int, sms: int = 148) -> int:
+    """Library kernels one block forward launches at T tokens (the launch
+    choices of csrc/moe_block.cu: router variant, one-CTA or three-kernel
+    permute with or without a separate row gather, split-K / fused / plain
+    expert GEMMs, combine, shared expert)."""
+    D, E, K, I = cfg.hidden_size, cfg.num_experts, cfg.num_experts_per_tok, cfg.moe_intermediate_size
+    R = T * K
+    if T == 0:
+        return 0
+    n = 2 if T > 256 else 1                                    # router (tile + route rows above 256 tokens)
+    small = R <= 2048
+    n += 1 if small else 3                                     # permute
+    n += 0 if (small and R <= 16) else 1                       # row gather (in the one-CTA permute up to 16 rows)
+
+    def pick_bn(avg, cap):
+        bn = 16 if avg <= 12 else 32 if avg <= 24 else 64 if avg <= 48 else 128 if avg <= 160 else 256
+        return min(bn, cap)
+
+    def splits(items, ksteps):
+        if items <= 0 or items * 2 > sms:
+            return 1
+        return max(1, min(sms // items, ksteps // 4, 8))
+    bn1 = pick_bn(R / E, 128)
+    bn2 = pick_bn(R / E, 128 if D % 256 == 0 else 256)
+    used = min(R, E)
+    s1 = splits(used * (I // 128), D // 64) if small and bn1 <= 32 else 1
+    s2 = splits(used * (D // 256 if D % 256 == 0 else D // 128), I // 64) if small and bn2 <= 32 else 1
+    fuse = s1 == 1 and s2 == 1 and D % 256 == 0 and bn1 <= 32 and bn1 == min(bn2, 128)
+    n += 1 if fuse else 2                                      # expert GEMMs
+    n += 1                                                     # combine
     if cfg.shared_expert_intermediate_size:
-        n += 2
+        sb = cfg.shared_bits or cfg.bits
+        n += 2 + (1 if (T < 256 or sb == 4) else 0)            # shared gate|up, down (+ padded copy)
     return n
 
 
@@ -387,7 +415,7 @@ def run_gpu(args):
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "note": "pinned host x -> device, graph replay, out -> pinned host, per forward"},
-            "gpu_launches": kernels_per_forward(cfg) * len(BATCHES) * args.steps,
+            "gpu_launches": sum(kernels_per_forward(cfg, T) for T in BATCHES) * args.steps,
             "clocks": clk,
             "sweep": sweep,
             "extra": extra,

@@ -307,11 +307,18 @@ static int run_permute(const Layout& L, const int32_t* idx, const void* x, void*
     zero = at<int32_t>(ws, L.ready);
     nzero = L.max_t1;
   }
+  // Up to this many rows the one-CTA permute also gathers them (one launch
+  // fewer on the decode path).
+  constexpr int64_t kGatherInSmall = 16;
+  bool gathered = false;
   if (L.nblk == 1) {
     // Every flat row fits one block: count, scan, tile lists and ranks in one CTA.
+    const bool g = xs && !skip && L.R > 0 && L.rows == L.R && L.R <= kGatherInSmall;
     launch_pdl(permute_small_kernel, 1, 1024, 9 * L.E * sizeof(int), st, idx, L.R, L.E, L.T, counts, offsets, sorted, inv, l1,
-               l2, lsh, skip, status, zero, nzero);
+               l2, lsh, skip, status, zero, nzero, g ? static_cast<const uint16_t*>(x) : nullptr, L.D, L.K, kperm,
+               g ? xs : nullptr);
     MLXR_LAUNCH_CHECK("permute_small_kernel");
+    gathered = g;
   } else {
     launch_pdl(permute_count_kernel, L.nblk, 256, L.E * sizeof(int), st, idx, L.R, L.E, at<int32_t>(ws, L.bcounts), skip,
                                                                  status);
@@ -323,7 +330,7 @@ static int run_permute(const Layout& L, const int32_t* idx, const void* x, void*
                                                                        sorted, inv);
     MLXR_LAUNCH_CHECK("permute_scatter_kernel");
   }
-  if (xs && L.R > 0 && L.rows > 0) {
+  if (xs && !gathered && L.R > 0 && L.rows > 0) {
     const int64_t gblocks = (L.rows + 7) / 8;
     const int gather_grid = (int)(gblocks < 4 * 148 ? gblocks : 4 * 148);
     launch_pdl(permute_gather_kernel, gather_grid, 256, 0, st, sorted, L.rows, L.R, L.K, static_cast<const uint16_t*>(x), L.D,

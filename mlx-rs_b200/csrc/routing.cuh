@@ -685,7 +685,9 @@ __global__ void __launch_bounds__(1024) permute_small_kernel(const int32_t* __re
                                                             int32_t* __restrict__ sorted_rows,
                                                             int32_t* __restrict__ inv, TileListOut l1, TileListOut l2,
                                                             TileListOut lsh, int skip, int* status,
-                                                            int32_t* __restrict__ zero, int nzero) {
+                                                            int32_t* __restrict__ zero, int nzero,
+                                                            const uint16_t* __restrict__ gx, int D, int K, int kperm,
+                                                            uint16_t* __restrict__ x_sorted) {
   pdl_wait();
   pdl_launch_dependents();
   // Counters the GEMMs that follow expect at zero (split-K).
@@ -729,6 +731,30 @@ __global__ void __launch_bounds__(1024) permute_small_kernel(const int32_t* __re
     const int64_t wbeg = (int64_t)warp * (PERM_ROWS / 8);
     const int64_t wend = min(wbeg + PERM_ROWS / 8, R);
     rank_rows_warp(idx, wbeg, wend, R, E, wcnt + warp * E, lane, sorted_rows, inv);
+  }
+  if (x_sorted == nullptr) return;
+  // Few rows (decode): the row gather here rather than in a second launch,
+  // the same copy as permute_gather_kernel (one warp per row, 16-byte
+  // accesses, 4-bit K order when kperm).
+  __syncthreads();
+  const int dvec = D / 8;
+  for (int64_t pos = warp; pos < R; pos += 32) {
+    const int32_t f = sorted_rows[pos];
+    if (f < 0 || (int64_t)f >= R) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(gx + (int64_t)(f / K) * D);
+    uint4* dst = reinterpret_cast<uint4*>(x_sorted + pos * D);
+    for (int v = lane; v < dvec; v += 32) {
+      uint4 a = __ldg(src + v);
+      if (kperm) {
+        uint4 b;
+        b.x = __byte_perm(a.x, a.z, 0x5410);
+        b.y = __byte_perm(a.x, a.z, 0x7632);
+        b.z = __byte_perm(a.y, a.w, 0x5410);
+        b.w = __byte_perm(a.y, a.w, 0x7632);
+        a = b;
+      }
+      dst[v] = a;
+    }
   }
 }
 
