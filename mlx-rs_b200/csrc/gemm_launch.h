@@ -48,6 +48,7 @@ struct GroupedGemmProblem {
   int64_t act2_rows;
   uint16_t* out2;
   int32_t* tile_ready;
+  int32_t* sched;             // 2 ints, zero before the launch (work queue; left zero after it)
 };
 
 int launch_grouped_gemm(const GroupedGemmProblem& p, cudaStream_t st);

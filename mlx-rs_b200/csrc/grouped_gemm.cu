@@ -111,6 +111,8 @@ static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
   a.n_out2 = p.n_out2;
   a.k_dim2 = p.k_dim2;
   a.tile_ready = p.tile_ready;
+  a.sched = p.sched;
+  if (!a.sched) return set_error(MLXR_CU_ERR_INVALID_ARGUMENT, "grouped gemm: no work-queue counters");
   if (FUSED && (!p.w2 || !p.s2 || !p.b2 || !p.out2 || !p.tile_ready || p.n_out2 % 256 != 0 || p.k_dim2 % 64 != 0 ||
                 p.k_dim2 != p.n_out))
     return set_error(MLXR_CU_ERR_INVALID_ARGUMENT, "grouped gemm: bad fused second phase");

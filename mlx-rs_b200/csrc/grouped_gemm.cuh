@@ -108,9 +108,10 @@ struct GG {
   static constexpr int OFF_RAW = OFF_B + OS * B_STAGE;
   static constexpr int OFF_BAR = OFF_RAW + RS * RAW_STAGE;
   static constexpr int NUM_BARS = 2 * RS + 3 * OS + 2 * AB + 1;
+  static constexpr int SCHED_Q = 16;  // work-queue entries published ahead (shared-memory ring)
   // At least 120 KB so that two CTAs never share an SM: each CTA holds its
   // tensor memory for its whole (persistent) lifetime.
-  static constexpr int SMEM_USED = OFF_BAR + NUM_BARS * 8 + 16 + 1024;  // + alignment slack
+  static constexpr int SMEM_USED = OFF_BAR + NUM_BARS * 8 + 16 + (SCHED_Q + 2) * 4 + 1024;  // + alignment slack
   static constexpr int SMEM_BYTES = SMEM_USED > 120 * 1024 ? SMEM_USED : 120 * 1024;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory exceeded");
   static constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN);
@@ -150,6 +151,10 @@ struct GemmArgs {
   int32_t n_out2;             // multiple of 256
   int32_t k_dim2;             // multiple of 64
   int32_t* tile_ready;        // [max_tiles]
+  // Work queue: sched[0] counts the items handed out beyond each CTA's
+  // first (item blockIdx.x), sched[1] the CTAs that finished; zero before the
+  // launch, and the last CTA to finish zeroes both again.
+  int32_t* sched;
 };
 
 // A tile entry is used only if it names a valid expert and a row range inside
@@ -259,6 +264,11 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
   uint64_t* fin_bar = acc_empty + C::AB;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // Work-queue ring: entry n of this CTA's item sequence in s_ring[n % Q];
+  // s_pub = entries published, s_cons = entries the epilogue has finished.
+  volatile int* s_ring = reinterpret_cast<volatile int*>(tmem_slot + 4);
+  volatile int* s_pub = s_ring + C::SCHED_Q;
+  volatile int* s_cons = s_pub + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -279,6 +289,8 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
     }
     mbar_init(fin_bar, C::ISSUERS);
     *abort_flag = 0;
+    *s_pub = 1;  // entry 0 is blockIdx.x, known to every role
+    *s_cons = 0;
     fence_mbar_init();
   }
   if (warp == C::W_MMA) {
@@ -352,11 +364,66 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
     return d;
   };
 
+  // Entry n of this CTA's work sequence (-1: no more). Entry 0 is item
+  // blockIdx.x. Decode-width launches (their items are uneven: 32-k-step
+  // gate|up items and 12-k-step down items, and a static round-robin left
+  // whole gate|up items on a few CTAs at the end) take later entries from the
+  // shared counter, fetched and published by the weight producer; wide tiles
+  // keep the static round-robin (measured slightly faster there).
+  const bool dynamic = C::KP == 2 && (int)gridDim.x < num_items;
+  auto sched_item = [&](int n) -> int {
+    if (!dynamic) {
+      const int64_t it = (int64_t)blockIdx.x + (int64_t)n * gridDim.x;
+      return it < num_items ? (int)it : -1;
+    }
+    if (n == 0) return (int)blockIdx.x < num_items ? (int)blockIdx.x : -1;
+    if (*s_pub <= n) {
+      const unsigned long long t0 = global_ns();
+      for (uint32_t k = 1; *s_pub <= n; ++k) {
+        __nanosleep(64);
+        if ((k & 63u) == 0) {
+          if (*abort_flag) return -1;
+          if (global_ns() - t0 > kWaitLimitNs) {
+            *abort_flag = 1;
+            atomicCAS(args.status, 0, (int)kDevTimeout);
+            return -1;
+          }
+        }
+      }
+    }
+    __threadfence_block();
+    return s_ring[n % C::SCHED_Q];
+  };
+
   if (warp == C::W_RAW) {
     // ---------------------------------------------- raw weight producer --
     if (lane == 0) {
       uint32_t it = 0;
-      for (int item = blockIdx.x; item < num_items && !*abort_flag; item += gridDim.x) {
+      for (int n = 0; !*abort_flag; ++n) {
+        int item;
+        if (n == 0 || !dynamic) {
+          item = sched_item(n);
+        } else {
+          // Reuse ring slot n % Q once the epilogue has started entry n - Q + 1.
+          const unsigned long long t0 = global_ns();
+          bool ok = true;
+          for (uint32_t k = 1; *s_cons < n - C::SCHED_Q + 1; ++k) {
+            __nanosleep(64);
+            if ((k & 63u) == 0 && (*abort_flag || global_ns() - t0 > kWaitLimitNs)) {
+              if (!*abort_flag) atomicCAS(args.status, 0, (int)kDevTimeout);
+              *abort_flag = 1;
+              ok = false;
+              break;
+            }
+          }
+          if (!ok) break;
+          item = (int)gridDim.x + atomicAdd(&args.sched[0], 1);
+          if (item >= num_items) item = -1;
+          s_ring[n % C::SCHED_Q] = item;
+          __threadfence_block();
+          *s_pub = n + 1;
+        }
+        if (item < 0) break;
         const Item d = item_of(item);
         const GemmTile t = args.tiles[d.tile];
         if (!tile_ok(t, args)) {
@@ -384,7 +451,9 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       uint32_t it = 0;
       int s = 0;
       uint32_t ph = 0;
-      for (int item = blockIdx.x; item < num_items && !*abort_flag; item += gridDim.x) {
+      for (int n = 0; !*abort_flag; ++n) {
+        const int item = sched_item(n);
+        if (item < 0) break;
         const Item d = item_of(item);
         const GemmTile t = args.tiles[d.tile];
         if (!tile_ok(t, args)) continue;
@@ -425,7 +494,9 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
+      for (int n = 0; ok; ++n) {
+        const int item = sched_item(n);
+        if (item < 0) break;
         const Item di = item_of(item);
         if (!tile_ok(args.tiles[di.tile], args)) continue;
         const int ab = li % C::AB;
@@ -469,7 +540,9 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
+      for (int n = 0; ok; ++n) {
+        const int item = sched_item(n);
+        if (item < 0) break;
         const Item di = item_of(item);
         if (!tile_ok(args.tiles[di.tile], args)) continue;
         const int ab = li % C::AB;
@@ -529,7 +602,9 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       }
       it += n;
     };
-    for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
+    for (int n = 0; ok; ++n) {
+      const int item = sched_item(n);
+      if (item < 0) break;
       const Item d = item_of(item);
       const GemmTile t = args.tiles[d.tile];
       if (!tile_ok(t, args)) continue;
@@ -615,7 +690,10 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
     // TMEM columns per load (keeps the epilogue's registers small).
     constexpr int CW = C::KP == 2 ? 8 : 16;
     constexpr int PQ = NMAT * BN * 32;  // floats of one quarter's partial accumulators
-    for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
+    for (int n = 0;; ++n) {
+      if (q == 0 && lane == 0) *s_cons = n;  // entries before n are finished
+      const int item = sched_item(n);
+      if (item < 0) break;
       const Item d = item_of(item);
       const int base = d.base, split = d.split;
       const GemmTile t = args.tiles[d.tile];
@@ -738,6 +816,13 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (dynamic && threadIdx.x == 0) {  // (a launch with no queued items never touches the counters)
+    __threadfence();
+    if (atomicAdd(&args.sched[1], 1) == (int)gridDim.x - 1) {  // last CTA: clean for the next launch
+      args.sched[0] = 0;
+      args.sched[1] = 0;
+    }
+  }
   if (warp == C::W_MMA) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);

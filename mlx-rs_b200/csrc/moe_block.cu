@@ -44,8 +44,11 @@ static inline void stage_mark(int i, cudaStream_t st) {
 static inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 // The first 256 bytes of every workspace: the device status word, then the
-// split router's per-token-block counters (both cleared by each call).
+// split router's per-token-block counters (ints 1..16), then the grouped
+// GEMM launches' work-queue counters (ints 32..39), all cleared by the call
+// that starts a forward (or an expert-parallel step).
 constexpr size_t kStatusSlotBytes = 256;
+constexpr int kSchedExperts1 = 32, kSchedExperts2 = 34, kSchedShared1 = 36, kSchedShared2 = 38;
 constexpr int kSplitRouterMaxT = 64;   // batches up to this size use router_split_kernel
 constexpr int kTileRouterMinT = 256;   // batches above this size use router_logits_tile_kernel
 
@@ -382,6 +385,7 @@ static int run_experts(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* w
   p.max_split_rows = L.split_rows;
   p.partial = L.split_rows ? at<float>(ws, L.part) : nullptr;
   p.counters = L.split_rows ? at<int32_t>(ws, L.cnt) : nullptr;
+  p.sched = at<int32_t>(ws, L.status) + kSchedExperts1;
   if (L.fuse) {
     // gate|up then down (row pairs) in one launch over the same tiles.
     p.fused = 1;
@@ -428,6 +432,7 @@ static int run_experts(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* w
   q.max_split_rows = L.split_rows;
   q.partial = L.split_rows ? at<float>(ws, L.part) : nullptr;
   q.counters = L.split_rows ? at<int32_t>(ws, L.cnt) : nullptr;
+  q.sched = at<int32_t>(ws, L.status) + kSchedExperts2;
   return launch_grouped_gemm(q, st);
 }
 
@@ -474,6 +479,7 @@ static int run_shared(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
   p.out_rows = L.T;
   p.perm_out = c->shared_bits == 4;
   p.status = status;
+  p.sched = at<int32_t>(ws, L.status) + kSchedShared1;
   if (int rc = launch_grouped_gemm(p, st)) return rc;
   GroupedGemmProblem q{};
   q.pair = (L.D % 256 == 0) ? 1 : 0;
@@ -496,6 +502,7 @@ static int run_shared(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
   q.out_rows = L.T;
   q.perm_out = 0;
   q.status = status;
+  q.sched = at<int32_t>(ws, L.status) + kSchedShared2;
   return launch_grouped_gemm(q, st);
 }
 
