@@ -26,6 +26,13 @@
 //   * op family: crates/mlxr/src/ops/quantization.rs:47-221 (quantize,
 //     quantized_matmul, dequantize, gather_qmm) and gather_mm
 //     crates/mlxr/src/ops/arithmetic.rs:1577-1609
+//   * Gemma 4 MoE branch (orc_gemma4_block): Router::forward
+//     crates/mlxr-lm/src/gemma4/text/text.rs:622-664 with router_post
+//     crates/mlxr-lm/src/activations.rs:309-331, the experts input norm
+//     pre_feedforward_layernorm_2 (text.rs:907-911), PackedSwitchFfn
+//     crates/mlxr-lm/src/nn/switch.rs:242-345 (gate_up_proj [E, 2I, D]) with
+//     GegluActivation (switch.rs:195-206; gelu_approximate
+//     crates/mlxr/src/layers/activation.rs:170-174)
 //
 // Two block modes:
 //   mode 0 "mlx-staged": rounds to bf16 at every reference op boundary
@@ -671,5 +678,150 @@ ORC_API int orc_moe_block(const OrcMoeConfig* c, const OrcMoeWeights* wt, const 
       out[t * D + d] = f2bf(o);
     }
   }
+  return 0;
+}
+
+// ------------------------------------------------------------ Gemma 4 ----
+// Routing contract of the Gemma 4 MoE branch (bit-exact with the CUDA
+// router), restating Router::forward (gemma4/text/text.rs:622-664):
+//  1. inv(t) = 1 / sqrt(ss / D + eps) in IEEE fp32, where ss is the sum of
+//     x[t][d]^2 in the logit order (lane j folds chunks j, j+32, ... with
+//     fmaf, then the xor butterfly): fast::rms_norm's inverse RMS.
+//  2. router input  xr[d] = bf16((x[d] * inv) * wr[d]), wr = Router.scale *
+//     hidden^-0.5 (pre-multiplied once, text.rs:628-639);
+//     experts input xe[d] = bf16((x[d] * inv) * we[d]), we =
+//     pre_feedforward_layernorm_2.weight (text.rs:907-911).
+//  3. scores = route_logit(xr, Wr[e]) (no bias): the bf16 scores.
+//  4. top-K by (score desc, expert asc) in place of argpartition (text.rs:
+//     647-651, order undefined there).
+//  5. router_post (activations.rs:325-331): softmax over the K scores
+//     (max = the first; exp_route; the sum in top-K order; IEEE division;
+//     bf16), times per_expert_scale[idx] (bf16 x bf16 in fp32, bf16).
+float gemma4_inv_rms(const uint16_t* xr, int D, float eps) {
+  float lane[32];
+  const int nchunks = D / 8;
+  for (int j = 0; j < 32; ++j) {
+    float acc = 0.0f;
+    for (int c = j; c < nchunks; c += 32)
+      for (int i = 0; i < 8; ++i) {
+        const float v = bf2f(xr[c * 8 + i]);
+        acc = std::fma(v, v, acc);
+      }
+    lane[j] = acc;
+  }
+  for (int s = 16; s >= 1; s >>= 1) {
+    float nv[32];
+    for (int j = 0; j < 32; ++j) nv[j] = lane[j] + lane[j ^ s];
+    std::memcpy(lane, nv, sizeof(lane));
+  }
+  const float ms = lane[0] / (float)D;
+  return 1.0f / std::sqrt(ms + eps);
+}
+
+// Order-preserving 16-bit key of a bf16 value (larger value, larger key).
+inline uint32_t bf16_order_key(uint16_t b) { return (b & 0x8000u) ? (uint32_t)(uint16_t)~b : (uint32_t)(b | 0x8000u); }
+
+void gemma4_route_token(const uint16_t* scores, const uint16_t* expert_scale, int E, int K, int32_t* idx, uint16_t* w) {
+  std::vector<uint32_t> key(E);
+  for (int e = 0; e < E; ++e) key[e] = (bf16_order_key(scores[e]) << 16) | (uint32_t)(0xffff - e);
+  std::vector<uint32_t> top(K);
+  std::partial_sort_copy(key.begin(), key.end(), top.begin(), top.end(), [](uint32_t a, uint32_t b) { return a > b; });
+  std::vector<float> ex(K);
+  float mx = 0.0f, sum = 0.0f;
+  for (int k = 0; k < K; ++k) {
+    idx[k] = 0xffff - (int)(top[k] & 0xffff);
+    const float sc = bf2f(scores[idx[k]]);
+    if (k == 0) mx = sc;
+    ex[k] = exp_route(sc - mx);
+    sum = sum + ex[k];
+  }
+  for (int k = 0; k < K; ++k) w[k] = f2bf(bf2f(f2bf(ex[k] / sum)) * bf2f(expert_scale[idx[k]]));
+}
+
+// gelu_approximate (activation.rs:170): 0.5 g (1 + tanh(sqrt(2/pi) (g + 0.044715 g^3))).
+inline float gelu_tanh(float g) {
+  const float y = 0.7978845608028654f * (g + 0.044715f * g * g * g);
+  return 0.5f * g * (1.0f + std::tanh(y));
+}
+
+struct OrcGemma4Config {
+  int hidden;            // D
+  int num_experts;       // E
+  int top_k;             // K
+  int moe_intermediate;  // I (gate_up_proj has 2I rows per expert)
+  int group_size;
+  int bits;
+  float eps;
+};
+
+struct OrcGemma4Weights {
+  const uint16_t* router;        // Router.proj [E, D] bf16
+  const uint16_t* router_norm;   // [D] bf16: Router.scale * hidden^-0.5
+  const uint16_t* expert_scale;  // [E] bf16: Router.per_expert_scale
+  const uint16_t* experts_norm;  // [D] bf16: pre_feedforward_layernorm_2.weight
+  OrcQuant gate_up;              // [E, 2I, D*b/32]
+  OrcQuant down;                 // [E, D, I*b/32]
+};
+
+// Gemma 4 MoE branch in the kernels' contract (fused-fp32: weights
+// dequantised to bf16, fp32 accumulation, h and y stored bf16, fp32
+// combine). x [T, D] is the router input h (text.rs:901-916); out [T, D] =
+// sum_k w_k * down_k(geglu(gate_up_k(pre_ff_2(h)))), before
+// post_feedforward_layernorm_2. out may be NULL (routing only).
+ORC_API int orc_gemma4_block(const OrcGemma4Config* c, const OrcGemma4Weights* wt, const uint16_t* x, int64_t T,
+                             uint16_t* out, int32_t* idx_out, uint16_t* w_out) {
+  const int D = c->hidden, E = c->num_experts, K = c->top_k, I = c->moe_intermediate;
+  const int gs = c->group_size, bits = c->bits;
+  if (D % 8 || D % gs || I % gs || !bits_ok(bits) || !gs_ok(gs) || K < 1 || K > E || E > 0xffff) return 1;
+  const int64_t R = T * K;
+  std::vector<int32_t> idx(R), counts(E), offsets(E + 1), sorted(R), inv(R);
+  std::vector<uint16_t> wk(R), xe((size_t)T * D);
+#pragma omp parallel num_threads(nthreads())
+  {
+    std::vector<uint16_t> xr(D), sc(E);
+#pragma omp for schedule(static)
+    for (int64_t t = 0; t < T; ++t) {
+      const uint16_t* xt = x + t * D;
+      const float iv = gemma4_inv_rms(xt, D, c->eps);
+      for (int d = 0; d < D; ++d) {
+        const float a = bf2f(xt[d]) * iv;
+        xr[d] = f2bf(a * bf2f(wt->router_norm[d]));
+        xe[t * D + d] = f2bf(a * bf2f(wt->experts_norm[d]));
+      }
+      for (int e = 0; e < E; ++e) sc[e] = f2bf(route_logit(xr.data(), wt->router + (int64_t)e * D, D, 0.0f));
+      gemma4_route_token(sc.data(), wt->expert_scale, E, K, &idx[t * K], &wk[t * K]);
+    }
+  }
+  if (idx_out) std::memcpy(idx_out, idx.data(), sizeof(int32_t) * R);
+  if (w_out) std::memcpy(w_out, wk.data(), sizeof(uint16_t) * R);
+  if (!out) return 0;
+  orc_permute(idx.data(), T, K, E, counts.data(), offsets.data(), sorted.data(), inv.data());
+
+  std::vector<uint16_t> y(R * (int64_t)D);
+#pragma omp parallel num_threads(nthreads())
+  {
+    std::vector<float> Wb, xin, gu, h, yy;
+#pragma omp for schedule(dynamic)
+    for (int e = 0; e < E; ++e) {
+      const int64_t n = counts[e], o = offsets[e];
+      if (!n) continue;
+      xin.resize(n * D);
+      for (int64_t r = 0; r < n; ++r)
+        for (int d = 0; d < D; ++d) xin[r * D + d] = bf2f(xe[(sorted[o + r] / K) * D + d]);
+      gu.resize(n * 2 * I); h.resize(n * I); yy.resize(n * D);
+      proj_rows(wt->gate_up, e, 2 * I, D, gs, bits, xin.data(), n, gu.data(), true, Wb);
+      for (int64_t r = 0; r < n; ++r)
+        for (int i = 0; i < I; ++i) h[r * I + i] = rbf(gelu_tanh(gu[r * 2 * I + i]) * gu[r * 2 * I + I + i]);
+      proj_rows(wt->down, e, D, I, gs, bits, h.data(), n, yy.data(), true, Wb);
+      for (int64_t i = 0; i < n * D; ++i) y[o * D + i] = f2bf(yy[i]);
+    }
+  }
+#pragma omp parallel for schedule(static) num_threads(nthreads())
+  for (int64_t t = 0; t < T; ++t)
+    for (int d = 0; d < D; ++d) {
+      float acc = 0.0f;
+      for (int k = 0; k < K; ++k) acc += bf2f(wk[t * K + k]) * bf2f(y[(int64_t)inv[t * K + k] * D + d]);
+      out[t * D + d] = f2bf(acc);
+    }
   return 0;
 }

@@ -81,6 +81,29 @@ class OrcMoeWeights(C.Structure):
     ]
 
 
+class OrcGemma4Config(C.Structure):
+    _fields_ = [
+        ("hidden", I32),
+        ("num_experts", I32),
+        ("top_k", I32),
+        ("moe_intermediate", I32),
+        ("group_size", I32),
+        ("bits", I32),
+        ("eps", C.c_float),
+    ]
+
+
+class OrcGemma4Weights(C.Structure):
+    _fields_ = [
+        ("router", P),
+        ("router_norm", P),
+        ("expert_scale", P),
+        ("experts_norm", P),
+        ("gate_up", OrcQuant),
+        ("down", OrcQuant),
+    ]
+
+
 def _declare(L):
     L.orc_normal_bf16.argtypes = [C.c_uint64, C.c_uint64, I64, C.c_float, P]
     L.orc_normal_bf16.restype = None
@@ -94,6 +117,7 @@ def _declare(L):
     L.orc_router.argtypes = [P, I64, I32, P, I32, P, I32, I32, P, P, P, P]
     L.orc_permute.argtypes = [P, I64, I32, I32, P, P, P, P]
     L.orc_moe_block.argtypes = [C.POINTER(OrcMoeConfig), C.POINTER(OrcMoeWeights), P, I64, I32, P, P, P]
+    L.orc_gemma4_block.argtypes = [C.POINTER(OrcGemma4Config), C.POINTER(OrcGemma4Weights), P, I64, P, P, P]
     L.orc_set_threads.argtypes = [I32]
     L.orc_max_threads.restype = I32
 
@@ -313,4 +337,41 @@ def moe_block(cfg: dict, weights: dict, x: np.ndarray, mode: str = "fused"):
     rc = lib().orc_moe_block(C.byref(c), C.byref(w), _p(x), T, 1 if mode == "fused" else 0, _p(out), _p(idx), _p(wk))
     if rc:
         raise ValueError(f"orc_moe_block rc={rc}")
+    return out, idx, wk
+
+
+def gemma4_block(cfg: dict, weights: dict, x: np.ndarray, routing_only: bool = False):
+    """Gemma 4 MoE branch (gemma4/text/text.rs:622-664 router, text.rs:901-916
+    experts on pre_feedforward_layernorm_2(h); nn/switch.rs:242-345 packed
+    gate_up_proj with GeGLU) in the kernels' fused-fp32 contract.
+
+    cfg: hidden, num_experts, top_k, moe_intermediate, group_size, bits, eps.
+    weights: router [E,D] u16, router_norm [D] u16 (Router.scale *
+    hidden^-0.5), expert_scale [E] u16, experts_norm [D] u16, gate_up
+    [E,2I,..] and down [E,D,..] as (wq, scales, biases) triples.
+    Returns (out [T,D] u16 or None, idx [T,K] i32, w [T,K] u16).
+    """
+    x = np.ascontiguousarray(x, np.uint16)
+    T = x.shape[0]
+    c = OrcGemma4Config(cfg["hidden"], cfg["num_experts"], cfg["top_k"], cfg["moe_intermediate"],
+                        cfg.get("group_size", 64), cfg.get("bits", 4), float(cfg.get("eps", 1e-6)))
+    keep = []
+
+    def cont(a):
+        a = np.ascontiguousarray(a)
+        keep.append(a)
+        return a
+
+    def trip(name):
+        return tuple(cont(v) for v in weights[name])
+
+    w = OrcGemma4Weights(_p(cont(weights["router"])), _p(cont(weights["router_norm"])),
+                         _p(cont(weights["expert_scale"])), _p(cont(weights["experts_norm"])),
+                         _q(None if routing_only else trip("gate_up")), _q(None if routing_only else trip("down")))
+    out = None if routing_only else np.empty_like(x)
+    idx = np.empty((T, c.top_k), np.int32)
+    wk = np.empty((T, c.top_k), np.uint16)
+    rc = lib().orc_gemma4_block(C.byref(c), C.byref(w), _p(x), T, _p(out) if out is not None else None, _p(idx), _p(wk))
+    if rc:
+        raise ValueError(f"orc_gemma4_block rc={rc}")
     return out, idx, wk
