@@ -131,6 +131,13 @@ typedef struct mlxr_cu_moe_config {
   int32_t shared_gate_bits;                /* shared_expert_gate: 4 or 8; 0 = shared_bits. Converted
                                               checkpoints pin it at 8 (mlxr-convert/src/qwen3_5.rs:
                                               classify_default) while the body is 4-bit */
+  int32_t model_kind;                      /* 0 = Qwen 3.5/3.6 MoE block (above); 1 = Gemma 4 MoE branch
+                                              (crates/mlxr-lm/src/gemma4/text/text.rs:568-664, 901-916):
+                                              RMS-normed router, top-k of the scores, softmax over the k
+                                              times per-expert scales, experts on the RMS-normed input
+                                              with a packed gate_up_proj and GeGLU; no shared expert
+                                              (the layer's dense MLP is outside the branch) */
+  float rms_norm_eps;                      /* model_kind 1: eps of both RMS norms (config rms_norm_eps) */
 } mlxr_cu_moe_config;
 
 /* One quantised projection: packed weight, scales, biases (bf16). */
@@ -155,6 +162,14 @@ typedef struct mlxr_cu_moe_weights {
   mlxr_cu_qlinear shared_up;
   mlxr_cu_qlinear shared_down;
   mlxr_cu_qlinear shared_expert_gate;
+  /* model_kind 1 (Gemma 4): router_weight = Router.proj [E, D] bf16 (router_bias NULL);
+   * switch_gate_up = experts.switch_glu.gate_up_proj [E, 2I, D*b/32] (gate rows 0..I-1, up rows
+   * I..2I-1 of each expert; nn/switch.rs:242-345); switch_down as above; the shared_* and
+   * switch_gate / switch_up members are unused. */
+  mlxr_cu_qlinear switch_gate_up;
+  const void* router_norm;   /* [D] bf16: Router.scale * hidden_size^-0.5 (text.rs:628-639) */
+  const void* expert_scale;  /* [E] bf16: Router.per_expert_scale */
+  const void* experts_norm;  /* [D] bf16: pre_feedforward_layernorm_2.weight (text.rs:907-911) */
 } mlxr_cu_moe_weights;
 
 /* Optional routing outputs (any member may be NULL). indices/weights are the

@@ -325,5 +325,12 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
 // g * sigmoid(g) with the fast exponential and division (a few ulp of fp32;
 // the result is rounded to bf16 right after).
 __device__ inline float silu_f32(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
+// gelu_approximate (crates/mlxr/src/layers/activation.rs:170-174):
+// 0.5 g (1 + tanh(y)), y = sqrt(2/pi) (g + 0.044715 g^3), evaluated as the
+// equal g / (1 + exp(-2y)).
+__device__ inline float gelu_tanh_f32(float g) {
+  const float y = 0.7978845608028654f * (g + 0.044715f * g * g * g);
+  return __fdividef(g, 1.0f + __expf(-2.0f * y));
+}
 
 }  // namespace mlxr

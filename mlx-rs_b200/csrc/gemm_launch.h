@@ -28,6 +28,10 @@ struct GroupedGemmProblem {
   int64_t out_rows;
   int perm_out;               // 1: write out's feature axis in the 4-bit chunk K order
   int pair;                   // nmat 2 only: w[0] rows m and m+128 as the two matrices (plain store)
+  int w_expert_rows;          // weight rows per expert (0 = n_out; 2*n_out for a packed gate|up
+                              // whose w[1], s[1], b[1] point n_out rows into the same tensor)
+  int64_t w_rows1;            // rows of matrix 1's tensor view (0 = w_rows)
+  int glu;                    // nmat 2, not pair: 0 = SwiGLU, 1 = GeGLU (gelu_approx(gate) * up)
   int* status;
   int grid;                   // 0 = one CTA per SM
   int splits;                 // split-K factor (0/1 = none); needs partial and counters

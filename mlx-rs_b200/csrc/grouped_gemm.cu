@@ -60,7 +60,8 @@ static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
                            CU_TENSOR_MAP_SWIZZLE_NONE))
     return rc;
   if (NMAT == 2) {
-    if (int rc = make_map_2d(&ta1, p.w[1], CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, kw, (uint64_t)p.w_rows, C::KW, C::BM,
+    if (int rc = make_map_2d(&ta1, p.w[1], CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, kw,
+                             (uint64_t)(p.w_rows1 > 0 ? p.w_rows1 : p.w_rows), C::KW, C::BM,
                              CU_TENSOR_MAP_SWIZZLE_NONE))
       return rc;
   } else {
@@ -98,6 +99,8 @@ static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
   a.out_rows = p.out_rows;
   a.perm_out = p.perm_out;
   a.pair = p.pair;
+  a.w_rows1 = p.w_expert_rows > 0 ? p.w_expert_rows : p.n_out;
+  a.glu = p.glu;
   a.status = p.status;
   a.splits = p.splits > 1 ? p.splits : 1;
   a.max_split_rows = p.max_split_rows;

@@ -131,6 +131,9 @@ struct GemmArgs {
   int perm_out;               // store out's feature axis in the 4-bit chunk K order
   int pair;                   // NMAT == 2 only: the two matrices are row blocks m and m+128
                               // of one weight (plain epilogue) instead of gate and up (SwiGLU)
+  int32_t w_rows1;            // weight rows per expert of the first phase: Nout, or 2*Nout
+                              // for a packed gate|up [E, 2*Nout, K] (up = rows Nout..)
+  int glu;                    // NMAT == 2, not pair: 0 = silu(gate)*up, 1 = gelu_approx(gate)*up
   int* status;
   // Split-K (splits > 1): every (tile, row slice) is split into `splits`
   // k-ranges; each writes its fp32 accumulators to `partial`, and the last
@@ -330,7 +333,7 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
   // base = tile * mt1 + m, split s covers k-steps [s*ks1/S, (s+1)*ks1/S).
   // Phase 2 (fused launch): down row pairs of the same tiles.
   struct Item {
-    int tile, m, base, split, k_lo, k_hi, ksteps, n_out, mrows, pair;
+    int tile, m, base, split, k_lo, k_hi, ksteps, n_out, mrows, pair, wstride;
     bool ph2;
   };
   auto item_of = [&](int item) {
@@ -344,6 +347,7 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       d.k_lo = d.split * ks1 / S;
       d.k_hi = (d.split + 1) * ks1 / S;
       d.n_out = args.n_out;
+      d.wstride = args.w_rows1;
       d.mrows = mrows1;
       d.pair = pair1;
       d.ph2 = false;
@@ -357,6 +361,7 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       d.k_lo = 0;
       d.k_hi = ks2;
       d.n_out = args.n_out2;
+      d.wstride = args.n_out2;
       d.mrows = 2 * C::BM;
       d.pair = 1;
       d.ph2 = true;
@@ -430,7 +435,7 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
           atomicCAS(args.status, 0, (int)kDevBadIndex);
           continue;
         }
-        const int a_row = t.expert * d.n_out + d.m * d.mrows;
+        const int a_row = t.expert * d.wstride + d.m * d.mrows;
         const CUtensorMap* ma = (FUSED && d.ph2) ? &tm_a2 : &tm_a0;
         const CUtensorMap* mb = (FUSED && d.ph2) ? &tm_a2 : &tm_a1;
         for (int ks = d.k_lo; ks < d.k_hi; ++ks, ++it) {
@@ -608,7 +613,7 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       const Item d = item_of(item);
       const GemmTile t = args.tiles[d.tile];
       if (!tile_ok(t, args)) continue;
-      const int64_t srow = (int64_t)t.expert * d.n_out + d.m * d.mrows + (d.pair ? mat * C::BM : 0) + row;
+      const int64_t srow = (int64_t)t.expert * d.wstride + d.m * d.mrows + (d.pair ? mat * C::BM : 0) + row;
       // (select, not index: a runtime index into the kernel parameters would
       // copy them to local memory)
       const uint16_t* sbase = (FUSED && d.ph2) ? args.scales2 : (mat ? args.scales[1] : args.scales[0]);
@@ -743,7 +748,7 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
           outp2[(int64_t)col * n_out] = f32_to_bf16_bits(uv);
         } else {
           float v = gv;
-          if (NMAT == 2) v = silu_f32(v) * uv;
+          if (NMAT == 2) v = (args.glu ? gelu_tanh_f32(v) : silu_f32(v)) * uv;
           outp[(int64_t)col * n_out] = f32_to_bf16_bits(v);
         }
       };

@@ -61,10 +61,11 @@ struct Layout {
   int s1 = 1, s2 = 1;          // split-K factors of the gate/up and down GEMMs
   int split_rows = 0;          // row slices the split buffers hold
   int fuse = 0;                // gate/up and down in one launch (same tile list, no split)
+  int kind = 0;                // config model_kind (1 = Gemma 4 branch)
   int max_t1 = 0, max_t2 = 0, max_tsh = 0;
   size_t status = 0, logits = 0, idx = 0, w = 0, sig = 0, bcounts = 0, bbase = 0, counts = 0, offsets = 0,
          sorted = 0, inv = 0, t1 = 0, n1 = 0, t2 = 0, n2 = 0, tsh = 0, nsh = 0, xs = 0, h = 0, y = 0, xpad = 0,
-         hsh = 0, ysh = 0, part = 0, cnt = 0, ready = 0, total = 0;
+         hsh = 0, ysh = 0, part = 0, cnt = 0, ready = 0, gxr = 0, gxe = 0, total = 0;
 };
 
 // Token-tile width from the mean number of rows per expert.
@@ -98,6 +99,16 @@ static int validate(const mlxr_cu_moe_config* c, int64_t T) {
                  "moe: shared_expert_intermediate_size=%d must be a multiple of 128", c->shared_expert_intermediate_size);
   if (c->group_size != 64)
     return set_error(MLXR_CU_ERR_UNSUPPORTED, "moe: group_size=%d is not supported (64)", c->group_size);
+  if (c->model_kind != 0 && c->model_kind != 1)
+    return set_error(MLXR_CU_ERR_UNSUPPORTED, "moe: model_kind=%d is not supported (0 Qwen 3.5/3.6, 1 Gemma 4)",
+                     c->model_kind);
+  if (c->model_kind == 1) {
+    MLXR_CHECK_ARG(c->shared_expert_intermediate_size == 0,
+                   "moe: the Gemma 4 branch has no shared expert (shared_expert_intermediate_size=%d)",
+                   c->shared_expert_intermediate_size);
+    MLXR_CHECK_ARG(c->rms_norm_eps >= 0.0f && c->rms_norm_eps < 1.0f, "moe: rms_norm_eps=%g out of range",
+                   (double)c->rms_norm_eps);
+  }
   if (c->bits != 4 && c->bits != 8) return set_error(MLXR_CU_ERR_UNSUPPORTED, "moe: bits=%d is not supported (4, 8)", c->bits);
   if (c->shared_expert_intermediate_size > 0 && c->shared_bits != 4 && c->shared_bits != 8)
     return set_error(MLXR_CU_ERR_UNSUPPORTED, "moe: shared_bits=%d is not supported (4, 8)", c->shared_bits);
@@ -131,6 +142,7 @@ static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T, int64_t rows_c
   L.D = c->hidden_size;
   L.I = c->moe_intermediate_size;
   L.Is = c->shared_expert_intermediate_size;
+  L.kind = c->model_kind;
   L.R = T * L.K;
   L.rows = rows_cap >= 0 && rows_cap < L.R ? rows_cap : L.R;
   L.rows_pad = L.rows > 256 ? L.rows : 256;
@@ -195,6 +207,10 @@ static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T, int64_t rows_c
     L.ysh = take((size_t)T * L.D * 2);
   }
   if (L.fuse) L.ready = take((size_t)L.max_t1 * sizeof(int32_t));
+  if (L.kind == 1) {  // Gemma 4: the router's and the experts' RMS-normed inputs
+    L.gxr = take((size_t)T * L.D * 2);
+    L.gxe = take((size_t)T * L.D * 2);
+  }
   if (L.split_rows > 0) {
     const int smax = L.s1 > L.s2 ? L.s1 : L.s2;
     const int bmax = L.bn1 > L.bn2 ? L.bn1 : L.bn2;
@@ -239,6 +255,24 @@ static int run_router(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
   }
   const uint16_t* xp = static_cast<const uint16_t*>(x);
   const uint16_t* wg = static_cast<const uint16_t*>(wt->router_weight);
+  // Gemma 4: route the RMS-normed input (no bias) and write the experts'
+  // normed input beside it; the routing ends in router_post.
+  const float* rbias = wt->router_bias;
+  const uint16_t* es = nullptr;
+  if (c->model_kind == 1) {
+    MLXR_CHECK_ARG(wt->router_norm && wt->expert_scale && wt->experts_norm,
+                   "moe: Gemma 4 router_norm / expert_scale / experts_norm is NULL");
+    MLXR_CHECK_ARG(aligned16(wt->router_norm) && aligned16(wt->experts_norm),
+                   "moe: Gemma 4 router_norm and experts_norm must be 16-byte aligned");
+    uint16_t* gxr = at<uint16_t>(ws, L.gxr);
+    launch_pdl(gemma4_norm_kernel, (unsigned)((L.T + G4_NORM_WARPS - 1) / G4_NORM_WARPS), G4_NORM_WARPS * 32, 0, st, xp,
+               L.T, L.D, c->rms_norm_eps, static_cast<const uint16_t*>(wt->router_norm),
+               static_cast<const uint16_t*>(wt->experts_norm), gxr, at<uint16_t>(ws, L.gxe));
+    MLXR_LAUNCH_CHECK("gemma4_norm_kernel");
+    xp = gxr;
+    rbias = nullptr;
+    es = static_cast<const uint16_t*>(wt->expert_scale);
+  }
   // Small batches: logits spread over many CTAs, the last CTA of each token
   // block routes it. Up to 256 tokens: one token per CTA (latency); beyond,
   // four per CTA (fewer re-reads of the router weight).
@@ -251,19 +285,19 @@ static int run_router(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
     uint16_t* lg = logits ? logits : at<uint16_t>(ws, L.logits);
     int* counter = at<int>(ws, L.status) + 1;
     const size_t smem = (size_t)tpb * L.E * sizeof(float);
-    const float* rb = wt->router_bias;
+    const float* rb = rbias;
     int32_t* io = at<int32_t>(ws, L.idx);
     uint16_t* wo = at<uint16_t>(ws, L.w);
     const int rn = c->norm_topk_prob;
     if (tpb == 1)
       launch_pdl(router_split_kernel<1, EPW, 8>, grid, RS_WARPS * 32, smem, st, xp, L.T, L.D, wg, L.E, rb, L.K, rn, io, wo, lg,
-                                                                        probs, sg, sig, counter);
+                                                                        probs, sg, sig, counter, es);
     else if (tpb == 2)
       launch_pdl(router_split_kernel<2, EPW, 6>, grid, RS_WARPS * 32, smem, st, xp, L.T, L.D, wg, L.E, rb, L.K, rn, io, wo, lg,
-                                                                        probs, sg, sig, counter);
+                                                                        probs, sg, sig, counter, es);
     else
       launch_pdl(router_split_kernel<4, EPW, 4>, grid, RS_WARPS * 32, smem, st, xp, L.T, L.D, wg, L.E, rb, L.K, rn, io, wo, lg,
-                                                                        probs, sg, sig, counter);
+                                                                        probs, sg, sig, counter, es);
     MLXR_LAUNCH_CHECK("router_split_kernel");
     return MLXR_CU_OK;
   } else if (L.T > kTileRouterMinT) {
@@ -271,21 +305,21 @@ static int run_router(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
     static std::atomic<uint64_t> attr_done{0};  // 72 KB of dynamic shared memory
     if (int rc = ensure_smem_attr(router_logits_tile_kernel, RT_TILE_SMEM, attr_done)) return rc;
     const dim3 grid((unsigned)((L.E + RT_TE - 1) / RT_TE), (unsigned)((L.T + RT_TT - 1) / RT_TT));
-    launch_pdl(router_logits_tile_kernel, grid, RT_TILE_THREADS, RT_TILE_SMEM, st, xp, L.T, L.D, wg, L.E, wt->router_bias, lg);
+    launch_pdl(router_logits_tile_kernel, grid, RT_TILE_THREADS, RT_TILE_SMEM, st, xp, L.T, L.D, wg, L.E, rbias, lg);
     MLXR_LAUNCH_CHECK("router_logits_tile_kernel");
     launch_pdl(route_rows_kernel, (unsigned)((L.T + RT_ROUTE_WARPS - 1) / RT_ROUTE_WARPS), RT_ROUTE_WARPS * 32, RT_ROUTE_WARPS * L.E * sizeof(float), st, lg, xp, L.T, L.D, L.E, L.K, c->norm_topk_prob,
                                                                     at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w),
-                                                                    probs, sg, sig);
+                                                                    probs, sg, sig, es);
     MLXR_LAUNCH_CHECK("route_rows_kernel");
     return MLXR_CU_OK;
   } else if (L.T <= 256) {
     launch_pdl(router_fused_kernel<1>, (unsigned)L.T, RT_THREADS, L.E * sizeof(float), st, 
-        xp, L.T, L.D, wg, L.E, wt->router_bias, L.K, c->norm_topk_prob, at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w),
-        logits, probs, sg, sig);
+        xp, L.T, L.D, wg, L.E, rbias, L.K, c->norm_topk_prob, at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w),
+        logits, probs, sg, sig, es);
   } else {
     launch_pdl(router_fused_kernel<4>, (unsigned)((L.T + 3) / 4), RT_THREADS, 4 * L.E * sizeof(float), st, 
-        xp, L.T, L.D, wg, L.E, wt->router_bias, L.K, c->norm_topk_prob, at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w),
-        logits, probs, sg, sig);
+        xp, L.T, L.D, wg, L.E, rbias, L.K, c->norm_topk_prob, at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w),
+        logits, probs, sg, sig, es);
   }
   MLXR_LAUNCH_CHECK("router_fused_kernel");
   return MLXR_CU_OK;
@@ -354,21 +388,43 @@ static int check_qlinear(const mlxr_cu_qlinear& q, const char* name) {
 static int run_experts(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt, const Layout& L, void* ws,
                        cudaStream_t st, int mid_stage) {
   if (L.rows == 0) return MLXR_CU_OK;
-  if (int rc = check_qlinear(wt->switch_gate, "switch_mlp.gate_proj")) return rc;
-  if (int rc = check_qlinear(wt->switch_up, "switch_mlp.up_proj")) return rc;
+  const bool packed = c->model_kind == 1;  // Gemma 4: one gate_up_proj [E, 2I, D*b/32]
+  if (packed) {
+    if (int rc = check_qlinear(wt->switch_gate_up, "switch_glu.gate_up_proj")) return rc;
+  } else {
+    if (int rc = check_qlinear(wt->switch_gate, "switch_mlp.gate_proj")) return rc;
+    if (int rc = check_qlinear(wt->switch_up, "switch_mlp.up_proj")) return rc;
+  }
   if (int rc = check_qlinear(wt->switch_down, "switch_mlp.down_proj")) return rc;
   int* status = at<int>(ws, L.status);
   GroupedGemmProblem p{};
   p.nmat = 2;
   p.bn = L.bn1;
   p.bits = c->bits;
-  p.w[0] = wt->switch_gate.weight;
-  p.w[1] = wt->switch_up.weight;
-  p.s[0] = static_cast<const uint16_t*>(wt->switch_gate.scales);
-  p.s[1] = static_cast<const uint16_t*>(wt->switch_up.scales);
-  p.b[0] = static_cast<const uint16_t*>(wt->switch_gate.biases);
-  p.b[1] = static_cast<const uint16_t*>(wt->switch_up.biases);
-  p.w_rows = (int64_t)L.E * L.I;
+  if (packed) {
+    // Gate = rows 0..I-1 and up = rows I..2I-1 of each expert's 2I rows: the
+    // second matrix's views start I rows into the same tensors.
+    const auto& gu = wt->switch_gate_up;
+    const int64_t wpr = (int64_t)L.D * c->bits / 32, gpr = L.D / 64;
+    p.w[0] = gu.weight;
+    p.w[1] = gu.weight + (int64_t)L.I * wpr;
+    p.s[0] = static_cast<const uint16_t*>(gu.scales);
+    p.s[1] = static_cast<const uint16_t*>(gu.scales) + (int64_t)L.I * gpr;
+    p.b[0] = static_cast<const uint16_t*>(gu.biases);
+    p.b[1] = static_cast<const uint16_t*>(gu.biases) + (int64_t)L.I * gpr;
+    p.w_rows = (int64_t)L.E * 2 * L.I;
+    p.w_rows1 = (int64_t)L.E * 2 * L.I - L.I;
+    p.w_expert_rows = 2 * L.I;
+    p.glu = 1;  // GeGLU (nn/switch.rs:195-206)
+  } else {
+    p.w[0] = wt->switch_gate.weight;
+    p.w[1] = wt->switch_up.weight;
+    p.s[0] = static_cast<const uint16_t*>(wt->switch_gate.scales);
+    p.s[1] = static_cast<const uint16_t*>(wt->switch_up.scales);
+    p.b[0] = static_cast<const uint16_t*>(wt->switch_gate.biases);
+    p.b[1] = static_cast<const uint16_t*>(wt->switch_up.biases);
+    p.w_rows = (int64_t)L.E * L.I;
+  }
   p.n_out = L.I;
   p.k_dim = L.D;
   p.num_experts = L.E;
@@ -514,6 +570,13 @@ static size_t ep_dispatch_bytes(const mlxr_cu_moe_config* c, int64_t T, size_t* 
   return L.total + align256((size_t)(T * c->num_experts_per_tok) * 4 + 4);
 }
 
+// The Gemma 4 branch runs on one device only.
+static int ep_reject_gemma4(const mlxr_cu_moe_config* cfg) {
+  if (cfg && cfg->model_kind == 1)
+    return set_error(MLXR_CU_ERR_UNSUPPORTED, "moe_ep: the Gemma 4 branch has no expert-parallel path");
+  return MLXR_CU_OK;
+}
+
 static int ep_check_world(const mlxr_cu_moe_config* cfg, int world) {
   MLXR_CHECK_ARG(world >= 1 && world <= 64 && world <= cfg->num_experts,
                  "moe_ep: world=%d must be in [1, min(64, num_experts=%d)]", world, cfg->num_experts);
@@ -555,7 +618,8 @@ int mlxr_cu_moe_block_forward(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_w
   stage_mark(0, st);
   if (int rc = run_router(cfg, weights, L, x, ws, nullptr, nullptr, st)) return rc;
   stage_mark(1, st);
-  if (int rc = run_permute(L, at<int32_t>(ws, L.idx), x, ws, at<int32_t>(ws, L.counts), at<int32_t>(ws, L.offsets),
+  const void* xe = L.kind == 1 ? static_cast<const void*>(at<uint16_t>(ws, L.gxe)) : x;  // the experts' input
+  if (int rc = run_permute(L, at<int32_t>(ws, L.idx), xe, ws, at<int32_t>(ws, L.counts), at<int32_t>(ws, L.offsets),
                            at<int32_t>(ws, L.sorted), at<int32_t>(ws, L.inv), at<uint16_t>(ws, L.xs), cfg->bits == 4, st))
     return rc;
   stage_mark(2, st);
@@ -802,6 +866,7 @@ int mlxr_cu_moe_combine(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights
 
 int mlxr_cu_moe_ep_workspace_size(const mlxr_cu_moe_config* cfg, int world, int64_t num_tokens,
                                   int64_t max_recv_pairs, int64_t max_recv_rows, size_t* bytes) {
+  if (int rc = ep_reject_gemma4(cfg)) return rc;
   if (int rc = validate(cfg, num_tokens)) return rc;
   if (int rc = ep_check_world(cfg, world)) return rc;
   MLXR_CHECK_ARG(bytes != nullptr, "moe_ep_workspace_size: bytes is NULL");
@@ -823,6 +888,7 @@ int mlxr_cu_moe_ep_dispatch(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_wei
                             const int32_t* placement, const void* x, int64_t num_tokens, int32_t* send_counts, int32_t* pair_pos,
                             void* x_send, int32_t* meta_send, float* shared_gate, void* workspace,
                             size_t workspace_bytes, void* stream) {
+  if (int rc = ep_reject_gemma4(cfg)) return rc;
   if (int rc = validate(cfg, num_tokens)) return rc;
   if (int rc = ep_check_world(cfg, world)) return rc;
   MLXR_CHECK_ARG(weights != nullptr, "moe_ep_dispatch: weights is NULL");
@@ -877,6 +943,7 @@ int mlxr_cu_moe_ep_dispatch(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_wei
 int mlxr_cu_moe_ep_experts(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* local_weights,
                            int num_local_experts, const void* x_recv, const int32_t* meta_recv, int64_t num_pairs,
                            int64_t num_rows, void* partial, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = ep_reject_gemma4(cfg)) return rc;
   if (int rc = validate(cfg, num_pairs)) return rc;
   MLXR_CHECK_ARG(num_local_experts >= 1 && num_local_experts <= cfg->num_experts,
                  "moe_ep_experts: num_local_experts=%d must be in [1, num_experts]", num_local_experts);
@@ -915,6 +982,7 @@ int mlxr_cu_moe_ep_combine(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weig
                            int64_t num_tokens, const void* partial_back, int64_t num_pairs, const int32_t* pair_pos,
                            const float* shared_gate, void* out, void* workspace, size_t workspace_bytes,
                            void* stream) {
+  if (int rc = ep_reject_gemma4(cfg)) return rc;
   if (int rc = validate(cfg, num_tokens)) return rc;
   const Layout L = make_layout(cfg, num_tokens);
   if (int rc = check_ws(L, workspace, workspace_bytes)) return rc;
@@ -1070,6 +1138,7 @@ int mlxr_cu_ep_comm_destroy(void* comm) {
 
 int mlxr_cu_moe_ep_p2p_workspace_size(const mlxr_cu_moe_config* cfg, const void* comm, int64_t num_tokens,
                                       int num_local_experts, int64_t expected_rows, size_t* bytes) {
+  if (int rc = ep_reject_gemma4(cfg)) return rc;
   if (int rc = validate(cfg, num_tokens)) return rc;
   if (int rc = ep_comm_check(comm, cfg)) return rc;
   MLXR_CHECK_ARG(bytes && num_local_experts >= 1 && num_local_experts <= cfg->num_experts,
@@ -1090,6 +1159,7 @@ int mlxr_cu_moe_ep_dispatch_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe
                                 const int32_t* placement, const void* x, int64_t num_tokens, int32_t* pair_pos,
                                 float* shared_gate, uint32_t epoch, void* workspace, size_t workspace_bytes,
                                 void* stream) {
+  if (int rc = ep_reject_gemma4(cfg)) return rc;
   if (int rc = validate(cfg, num_tokens)) return rc;
   if (int rc = ep_comm_check(comm, cfg)) return rc;
   EpComm* c = static_cast<EpComm*>(comm);
@@ -1153,6 +1223,7 @@ int mlxr_cu_moe_ep_dispatch_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe
 int mlxr_cu_moe_ep_experts_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* local_weights,
                                int num_local_experts, void* comm, int64_t expected_rows, uint32_t epoch,
                                void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = ep_reject_gemma4(cfg)) return rc;
   if (int rc = ep_comm_check(comm, cfg)) return rc;
   EpComm* c = static_cast<EpComm*>(comm);
   MLXR_CHECK_ARG(local_weights != nullptr && num_local_experts >= 1 && num_local_experts <= cfg->num_experts,
@@ -1191,6 +1262,7 @@ int mlxr_cu_moe_ep_experts_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_
 int mlxr_cu_moe_ep_combine_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights, void* comm,
                                const void* x, int64_t num_tokens, const int32_t* pair_pos, const float* shared_gate,
                                void* out, uint32_t epoch, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = ep_reject_gemma4(cfg)) return rc;
   if (int rc = validate(cfg, num_tokens)) return rc;
   if (int rc = ep_comm_check(comm, cfg)) return rc;
   EpComm* c = static_cast<EpComm*>(comm);

@@ -69,9 +69,60 @@ struct SharedGateArgs {
 
 // Softmax + top-K + renormalisation of one token by one warp, from its bf16
 // logits held as floats in shared memory (lrow[0..E)).
+// Order-preserving 16-bit key of a bf16 value (larger value, larger key).
+__device__ inline uint32_t bf16_order_key(uint32_t b) { return (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u); }
+
+// Gemma 4 routing of one token by one warp from its bf16 scores (router_post,
+// crates/mlxr-lm/src/activations.rs:325-331, after the top-k of
+// gemma4/text/text.rs:647-651): top-K by (score desc, expert asc); softmax
+// over the K picked scores (max = the first pick, exp_route, the sum in pick
+// order, IEEE division, bf16); times per_expert_scale[e] (bf16).
+__device__ inline void route_token_warp_gemma4(const float* lrow, int64_t t, int E, int K, int lane,
+                                               int32_t* __restrict__ idx_out, uint16_t* __restrict__ w_out,
+                                               const uint16_t* __restrict__ expert_scale) {
+  uint32_t key[RT_MAXV];
+#pragma unroll
+  for (int m = 0; m < RT_MAXV; ++m) {
+    const int e = lane + 32 * m;
+    key[m] = e < E ? (bf16_order_key(f32_to_bf16_bits(lrow[e])) << 16) | (uint32_t)(0xFFFF - e) : 0u;
+  }
+  int my_e = 0;
+  float my_x = 0.0f, mx = 0.0f, denom = 0.0f;
+  for (int k = 0; k < K; ++k) {
+    uint32_t best = 0u;
+#pragma unroll
+    for (int m = 0; m < RT_MAXV; ++m) best = best > key[m] ? best : key[m];
+    best = __reduce_max_sync(0xffffffffu, best);
+    const int e = 0xFFFF - (int)(best & 0xFFFFu);
+    const float sc = lrow[e];
+    if (lane == (e & 31)) {
+#pragma unroll
+      for (int m = 0; m < RT_MAXV; ++m)
+        if (m == (e >> 5)) key[m] = 0u;
+    }
+    if (k == 0) mx = sc;
+    const float ex = exp_route(__fsub_rn(sc, mx));
+    denom = __fadd_rn(denom, ex);
+    if (lane == k) {
+      my_e = e;
+      my_x = ex;
+    }
+  }
+  if (lane < K) {
+    const float p = bf16_bits_to_f32(f32_to_bf16_bits(__fdiv_rn(my_x, denom)));
+    idx_out[t * K + lane] = my_e;
+    w_out[t * K + lane] = f32_to_bf16_bits(__fmul_rn(p, bf16_bits_to_f32(expert_scale[my_e])));
+  }
+}
+
+// expert_scale != NULL: the Gemma 4 routing above instead of this one.
 __device__ inline void route_token_warp(const float* lrow, int64_t t, int E, int K, int renorm, int lane,
                                         int32_t* __restrict__ idx_out, uint16_t* __restrict__ w_out,
-                                        uint16_t* __restrict__ probs_out) {
+                                        uint16_t* __restrict__ probs_out, const uint16_t* __restrict__ expert_scale) {
+  if (expert_scale) {
+    route_token_warp_gemma4(lrow, t, E, K, lane, idx_out, w_out, expert_scale);
+    return;
+  }
   float lv[RT_MAXV];
   float mx = -INFINITY;
 #pragma unroll
@@ -160,7 +211,7 @@ __global__ void __launch_bounds__(RT_THREADS) router_fused_kernel(
     const uint16_t* __restrict__ x, int64_t T, int D, const uint16_t* __restrict__ wg, int E,
     const float* __restrict__ bias, int K, int renorm, int32_t* __restrict__ idx_out, uint16_t* __restrict__ w_out,
     uint16_t* __restrict__ logits_out, uint16_t* __restrict__ probs_out, SharedGateArgs sg,
-    float* __restrict__ sig_out) {
+    float* __restrict__ sig_out, const uint16_t* __restrict__ expert_scale) {
   pdl_wait();
   pdl_launch_dependents();
   extern __shared__ float s_lg[];  // [TPB][E]
@@ -230,7 +281,7 @@ __global__ void __launch_bounds__(RT_THREADS) router_fused_kernel(
   __syncthreads();
   if (warp < TPB && t0 + warp < T) {
     const int64_t t = t0 + warp;
-    route_token_warp(s_lg + warp * E, t, E, K, renorm, lane, idx_out, w_out, probs_out);
+    route_token_warp(s_lg + warp * E, t, E, K, renorm, lane, idx_out, w_out, probs_out, expert_scale);
     if (sig_out) shared_gate_warp(x + t * D, D, sg, lane, sig_out + t);
   }
 }
@@ -250,7 +301,7 @@ __global__ void __launch_bounds__(RS_WARPS * 32) router_split_kernel(
     const uint16_t* __restrict__ x, int64_t T, int D, const uint16_t* __restrict__ wg, int E,
     const float* __restrict__ bias, int K, int renorm, int32_t* __restrict__ idx_out, uint16_t* __restrict__ w_out,
     uint16_t* __restrict__ lg, uint16_t* __restrict__ probs_out, SharedGateArgs sg, float* __restrict__ sig_out,
-    int* __restrict__ counter) {
+    int* __restrict__ counter, const uint16_t* __restrict__ expert_scale) {
   pdl_wait();
   pdl_launch_dependents();
   extern __shared__ float s_lg[];  // [TPB][E] (last CTA of a token block only)
@@ -340,7 +391,7 @@ __global__ void __launch_bounds__(RS_WARPS * 32) router_split_kernel(
   __syncthreads();
   for (int i = warp; i < ntok; i += RS_WARPS) {
     const int64_t t = t0 + i;
-    route_token_warp(s_lg + i * E, t, E, K, renorm, lane, idx_out, w_out, probs_out);
+    route_token_warp(s_lg + i * E, t, E, K, renorm, lane, idx_out, w_out, probs_out, expert_scale);
     if (sig_out) shared_gate_warp(x + t * D, D, sg, lane, sig_out + t);
   }
 }
@@ -500,13 +551,65 @@ __global__ void __launch_bounds__(RT_TILE_THREADS, 2) router_logits_tile_kernel(
   }
 }
 
+// Gemma 4 input norms of one token per warp (fast::rms_norm of the router,
+// gemma4/text/text.rs:622-639, and pre_feedforward_layernorm_2, :907-911):
+// inv = 1 / sqrt(ss / D + eps) in IEEE fp32, ss = sum of x^2 in the logit
+// order (lane j folds chunks j, j+32, ... of 8 elements with fmaf, then the
+// xor butterfly); xr = bf16((x * inv) * wr), xe = bf16((x * inv) * we).
+// x, xr, xe 16-byte aligned, D a multiple of 8.
+constexpr int G4_NORM_WARPS = 8;
+__global__ void __launch_bounds__(G4_NORM_WARPS * 32) gemma4_norm_kernel(
+    const uint16_t* __restrict__ x, int64_t T, int D, float eps, const uint16_t* __restrict__ wr,
+    const uint16_t* __restrict__ we, uint16_t* __restrict__ xr, uint16_t* __restrict__ xe) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * G4_NORM_WARPS + warp;
+  if (t >= T) return;
+  const uint4* row = reinterpret_cast<const uint4*>(x + t * D);
+  const int nchunks = D / 8;
+  float acc = 0.0f;
+  for (int c = lane; c < nchunks; c += 32) {
+    const uint4 v = row[c];
+    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float a = bf_lo(w4[i]), b = bf_hi(w4[i]);
+      acc = __fmaf_rn(a, a, acc);
+      acc = __fmaf_rn(b, b, acc);
+    }
+  }
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, s));
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)D), eps)));
+  const uint4* wr4 = reinterpret_cast<const uint4*>(wr);
+  const uint4* we4 = reinterpret_cast<const uint4*>(we);
+  uint4* xr4 = reinterpret_cast<uint4*>(xr + t * D);
+  uint4* xe4 = reinterpret_cast<uint4*>(xe + t * D);
+  for (int c = lane; c < nchunks; c += 32) {
+    const uint4 v = row[c], a4 = __ldg(wr4 + c), b4 = __ldg(we4 + c);
+    const uint32_t xv[4] = {v.x, v.y, v.z, v.w}, av[4] = {a4.x, a4.y, a4.z, a4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
+    uint32_t ro[4], eo[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float x0 = __fmul_rn(bf_lo(xv[i]), inv), x1 = __fmul_rn(bf_hi(xv[i]), inv);
+      ro[i] = (uint32_t)f32_to_bf16_bits(__fmul_rn(x0, bf_lo(av[i]))) |
+              ((uint32_t)f32_to_bf16_bits(__fmul_rn(x1, bf_hi(av[i]))) << 16);
+      eo[i] = (uint32_t)f32_to_bf16_bits(__fmul_rn(x0, bf_lo(bv[i]))) |
+              ((uint32_t)f32_to_bf16_bits(__fmul_rn(x1, bf_hi(bv[i]))) << 16);
+    }
+    xr4[c] = make_uint4(ro[0], ro[1], ro[2], ro[3]);
+    xe4[c] = make_uint4(eo[0], eo[1], eo[2], eo[3]);
+  }
+}
+
 // Softmax / top-K / renormalisation (and the shared-expert gate) of one
 // token per warp from the bf16 logits lg [T, E].
 constexpr int RT_ROUTE_WARPS = 8;
 __global__ void __launch_bounds__(RT_ROUTE_WARPS * 32) route_rows_kernel(
     const uint16_t* __restrict__ lg, const uint16_t* __restrict__ x, int64_t T, int D, int E, int K, int renorm,
     int32_t* __restrict__ idx_out, uint16_t* __restrict__ w_out, uint16_t* __restrict__ probs_out, SharedGateArgs sg,
-    float* __restrict__ sig_out) {
+    float* __restrict__ sig_out, const uint16_t* __restrict__ expert_scale) {
   pdl_wait();
   pdl_launch_dependents();
   extern __shared__ float s_row[];  // [RT_ROUTE_WARPS][E]
@@ -516,7 +619,7 @@ __global__ void __launch_bounds__(RT_ROUTE_WARPS * 32) route_rows_kernel(
   float* row = s_row + warp * E;
   for (int e = lane; e < E; e += 32) row[e] = bf16_bits_to_f32(lg[t * E + e]);
   __syncwarp();
-  route_token_warp(row, t, E, K, renorm, lane, idx_out, w_out, probs_out);
+  route_token_warp(row, t, E, K, renorm, lane, idx_out, w_out, probs_out, expert_scale);
   if (sig_out) shared_gate_warp(x + t * D, D, sg, lane, sig_out + t);
 }
 

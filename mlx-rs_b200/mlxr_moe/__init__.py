@@ -6,12 +6,12 @@ missing (there is no CPU fallback).
 from . import _lib, checkpoint, ops, synth
 from ._lib import MlxrError
 from .checkpoint import load_qwen35_moe_block
-from .moe import (MoeConfig, QuantizedLinear, QuantizedSwitchLinear, Qwen35MoeBlock, Routing, SplitSwitchFfn,
-                  SwigluMlp)
+from .moe import (Gemma4MoeBranch, MoeConfig, PackedSwitchFfn, QuantizedLinear, QuantizedSwitchLinear,
+                  Qwen35MoeBlock, Routing, SplitSwitchFfn, SwigluMlp)
 from .ops import dequantize, gather_mm, gather_qmm, quantize, quantized_matmul
 
 __all__ = [
-    "MlxrError", "MoeConfig", "QuantizedLinear", "QuantizedSwitchLinear", "Qwen35MoeBlock", "Routing",
+    "Gemma4MoeBranch", "MlxrError", "MoeConfig", "PackedSwitchFfn", "QuantizedLinear", "QuantizedSwitchLinear", "Qwen35MoeBlock", "Routing",
     "SplitSwitchFfn", "SwigluMlp", "dequantize", "gather_mm", "gather_qmm", "quantize", "quantized_matmul",
     "ops", "synth", "_lib", "checkpoint", "load_qwen35_moe_block",
 ]

@@ -91,6 +91,8 @@ class MoeConfig(C.Structure):
         ("shared_bits", I32),
         ("norm_topk_prob", I32),
         ("shared_gate_bits", I32),
+        ("model_kind", I32),
+        ("rms_norm_eps", C.c_float),
     ]
 
 
@@ -105,6 +107,10 @@ class MoeWeights(C.Structure):
         ("shared_up", QLinear),
         ("shared_down", QLinear),
         ("shared_expert_gate", QLinear),
+        ("switch_gate_up", QLinear),
+        ("router_norm", P),
+        ("expert_scale", P),
+        ("experts_norm", P),
     ]
 
 

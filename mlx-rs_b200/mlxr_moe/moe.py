@@ -35,13 +35,15 @@ class MoeConfig:
     shared_bits: int | None = None
     norm_topk_prob: bool = True
     shared_gate_bits: int | None = None  # None: shared_bits
+    model_kind: int = 0                  # 0 Qwen 3.5/3.6 block, 1 Gemma 4 MoE branch (Gemma4MoeBranch)
+    rms_norm_eps: float = 1e-6           # model_kind 1: eps of the router and experts-input RMS norms
 
     def to_c(self) -> _lib.MoeConfig:
         return _lib.MoeConfig(
             self.hidden_size, self.num_experts, self.num_experts_per_tok, self.moe_intermediate_size,
             self.shared_expert_intermediate_size, self.group_size, self.bits,
             self.shared_bits if self.shared_bits is not None else self.bits, int(self.norm_topk_prob),
-            self.shared_gate_bits or 0,
+            self.shared_gate_bits or 0, int(self.model_kind), float(self.rms_norm_eps),
         )
 
 
@@ -287,3 +289,44 @@ class Qwen35MoeBlock:
             routed = (sh.float() * sg.float()).to(sh.dtype).float() + routed.float()
             routed = routed.to(torch.bfloat16)
         return routed.reshape(x.shape)
+
+
+class PackedSwitchFfn:
+    """Gemma 4 routed experts (nn/switch.rs:242-345): one gate_up_proj switch
+    linear [E, 2I, D*b/32] (gate rows 0..I-1, up rows I..2I-1 of each expert)
+    and down_proj [E, D, I*b/32], with GeGLU (gelu_approx(gate) * up)."""
+
+    def __init__(self, gate_up_proj: QuantizedSwitchLinear, down_proj: QuantizedSwitchLinear):
+        self.gate_up_proj, self.down_proj = gate_up_proj, down_proj
+
+
+class Gemma4MoeBranch(Qwen35MoeBlock):
+    """The Gemma 4 MoE branch of a decoder layer (gemma4/text/text.rs:901-916):
+    Router::forward(h) (text.rs:622-664: RMS norm with `router_norm` =
+    Router.scale * hidden^-0.5, scores = h_normed . proj, top-k, softmax over
+    the k times per_expert_scale) and Experts::forward on
+    pre_feedforward_layernorm_2(h) (`experts_norm`), returning the weighted sum
+    before post_feedforward_layernorm_2. Same entry points as Qwen35MoeBlock;
+    cfg.model_kind must be 1 and there is no shared expert."""
+
+    def __init__(self, cfg: MoeConfig, proj: torch.Tensor, router_norm: torch.Tensor, expert_scale: torch.Tensor,
+                 experts_norm: torch.Tensor, switch_glu: PackedSwitchFfn):
+        if cfg.model_kind != 1 or cfg.shared_expert_intermediate_size:
+            raise ValueError("Gemma4MoeBranch needs model_kind=1 and no shared expert")
+        self.router_norm = router_norm.to(torch.bfloat16).contiguous()
+        self.expert_scale = expert_scale.to(torch.bfloat16).contiguous()
+        self.experts_norm = experts_norm.to(torch.bfloat16).contiguous()
+        self.switch_glu = switch_glu
+        super().__init__(cfg, proj, None)
+
+    def _weights_c(self) -> _lib.MoeWeights:
+        z = _lib.QLinear(None, None, None)
+        w = _lib.MoeWeights(self.gate.data_ptr(), None, z, z, self.switch_glu.down_proj.c(), z, z, z, z)
+        w.switch_gate_up = self.switch_glu.gate_up_proj.c()
+        w.router_norm = self.router_norm.data_ptr()
+        w.expert_scale = self.expert_scale.data_ptr()
+        w.experts_norm = self.experts_norm.data_ptr()
+        return w
+
+    def forward_ops(self, x: torch.Tensor) -> torch.Tensor:
+        raise NotImplementedError("the op-by-op chain is restated for the Qwen block only")

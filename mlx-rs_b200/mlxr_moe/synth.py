@@ -16,11 +16,13 @@ import numpy as np
 import torch
 
 from . import ops
-from .moe import MoeConfig, QuantizedLinear, QuantizedSwitchLinear, Qwen35MoeBlock, SplitSwitchFfn, SwigluMlp
+from .moe import (Gemma4MoeBranch, MoeConfig, PackedSwitchFfn, QuantizedLinear, QuantizedSwitchLinear, Qwen35MoeBlock,
+                  SplitSwitchFfn, SwigluMlp)
 
 STREAM_ROUTER, STREAM_GATE, STREAM_UP, STREAM_DOWN = 0, 1, 2, 3
 STREAM_SH_GATE, STREAM_SH_UP, STREAM_SH_DOWN, STREAM_SH_EXPERT_GATE = 4, 5, 6, 7
 STREAM_X, STREAM_RANK = 8, 9
+STREAM_G4_ROUTER_NORM, STREAM_G4_EXPERT_SCALE, STREAM_G4_EXPERTS_NORM = 10, 11, 12
 
 # BASELINE configurations (shapes only; the same block is reused across a
 # config's token counts).
@@ -123,3 +125,24 @@ def algorithmic_flops(cfg: MoeConfig, num_tokens: int) -> int:
     if Is:
         f += 2 * 3 * Is * D + 2 * D
     return num_tokens * f
+
+
+def make_gemma4_branch(cfg: MoeConfig, seed: int = 0, device="cuda") -> Gemma4MoeBranch:
+    """A seeded Gemma 4 MoE branch (no checkpoint is available here): router
+    proj N(0, 0.5) bf16 (scores of order one on the RMS-normed input),
+    router_norm = bf16(hidden^-0.5 * (1 + N(0, 0.1))), per_expert_scale
+    1 + N(0, 0.2), experts_norm 1 + N(0, 0.1), gate_up_proj [E, 2I, D] and
+    down_proj [E, D, I] N(0, 0.02) affine-quantised. Streams: router 0,
+    gate_up 1, down 3, the three norm/scale vectors 10-12."""
+    D, E, I = cfg.hidden_size, cfg.num_experts, cfg.moe_intermediate_size
+    gs, b = cfg.group_size, cfg.bits
+    proj = ops.synth_normal_bf16(seed, STREAM_ROUTER, (E, D), 0.5, device)
+
+    def around_one(stream, n, sd):
+        return (1.0 + ops.synth_normal_bf16(seed, stream, (n,), sd, device).float()).to(torch.bfloat16)
+
+    router_norm = (around_one(STREAM_G4_ROUTER_NORM, D, 0.1).float() * D ** -0.5).to(torch.bfloat16)
+    ffn = PackedSwitchFfn(_qswitch(seed, STREAM_GATE, (E, 2 * I, D), b, gs, device),
+                          _qswitch(seed, STREAM_DOWN, (E, D, I), b, gs, device))
+    return Gemma4MoeBranch(cfg, proj, router_norm, around_one(STREAM_G4_EXPERT_SCALE, E, 0.2),
+                           around_one(STREAM_G4_EXPERTS_NORM, D, 0.1), ffn)
