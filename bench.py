@@ -426,6 +426,14 @@ def run_gpu(args):
         dist.destroy_process_group()
 
 
+# The Gemma 4 MoE branch (model_kind 1) on a synthetic block of the C2
+# sizes (no Gemma 4 checkpoint or BASELINE configuration exists here):
+# hidden 2048, 128 experts, top-8, expert intermediate 768, 4-bit gs64.
+def _gemma4_cfg():
+    from mlxr_moe.moe import MoeConfig
+    return MoeConfig(2048, 128, 8, 768, bits=4, model_kind=1, rms_norm_eps=1e-6)
+
+
 def bench_extra(args, dev, st, flush, peaks):
     """The other BASELINE configurations on this GPU (informational lines)."""
     import ctypes as C
@@ -437,12 +445,22 @@ def bench_extra(args, dev, st, flush, peaks):
     from mlxr_moe import synth
     from mlxr_moe.moe import Routing
 
+    GEMMA4_CFG = _gemma4_cfg()
     res = {}
-    for name, T in (("c1", 32), ("c3", 4096), ("c5_decode", 256), ("c5_prefill", 8192), ("c4", 16384)):
-        key = name.split("_")[0]
+
+    def baseline(key):
         spec = synth.CONFIGS[key]
-        cfg = spec["cfg"]
-        blk = synth.make_block(cfg, 0, spec["zipf"], dev)
+        return synth.make_block(spec["cfg"], 0, spec["zipf"], dev), spec["zipf"]
+
+    def gemma4():
+        return synth.make_gemma4_branch(GEMMA4_CFG, 0, dev), False
+
+    for name, T, make in (("c1", 32, lambda: baseline("c1")), ("c3", 4096, lambda: baseline("c3")),
+                          ("c5_decode", 256, lambda: baseline("c5")), ("c5_prefill", 8192, lambda: baseline("c5")),
+                          ("c4", 16384, lambda: baseline("c4")), ("gemma4_decode", 64, gemma4),
+                          ("gemma4_prefill", 4096, gemma4)):
+        blk, zipf = make()
+        cfg = blk.cfg
         x = synth.make_input(T, cfg.hidden_size, stream_offset=7, device=dev)
         out = torch.empty_like(x)
         ws = torch.empty(blk.workspace_bytes(T), dtype=torch.uint8, device=dev)
@@ -477,7 +495,7 @@ def bench_extra(args, dev, st, flush, peaks):
         res[name] = dict(tokens=T, ms=ms, tokens_per_s=T / (ms / 1e3), tflops=tfl, gbs=gbs,
                          bound="tensor" if prefill else "hbm",
                          frac=(tfl / peaks["bf16_tflops"]) if prefill else (gbs / peaks["hbm_gbs"]),
-                         distinct_experts=U, zipf=spec["zipf"],
+                         distinct_experts=U, zipf=zipf,
                          stages_ms={k: round(v, 5) for k, v in stg.items()})
         del g, blk, ws, out, x
         torch.cuda.empty_cache()

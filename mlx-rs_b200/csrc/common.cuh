@@ -329,8 +329,8 @@ __device__ inline float silu_f32(float g) { return __fdividef(g, 1.0f + __expf(-
 // 0.5 g (1 + tanh(y)), y = sqrt(2/pi) (g + 0.044715 g^3), evaluated as the
 // equal g / (1 + exp(-2y)).
 __device__ inline float gelu_tanh_f32(float g) {
-  const float y = 0.7978845608028654f * (g + 0.044715f * g * g * g);
-  return __fdividef(g, 1.0f + __expf(-2.0f * y));
+  const float z = 1.5957691216057308f * (g + 0.044715f * g * g * g);
+  return __fdividef(g, 1.0f + __expf(-z));
 }
 
 }  // namespace mlxr

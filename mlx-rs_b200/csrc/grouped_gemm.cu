@@ -51,7 +51,7 @@ int num_sms_current() {
   return n > 0 ? n : 148;
 }
 
-template <int NMAT, int BN, int BITS, bool SPLITK, bool FUSED>
+template <int NMAT, int BN, int BITS, bool SPLITK, bool FUSED, bool GLU = false>
 static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
   using C = GG<NMAT, BN, BITS>;
   CUtensorMap ta0, ta1, tb, ta2, tb2;
@@ -81,7 +81,7 @@ static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
     ta2 = ta0;
     tb2 = tb;
   }
-  auto kern = grouped_dequant_gemm_kernel<NMAT, BN, BITS, SPLITK, FUSED>;
+  auto kern = grouped_dequant_gemm_kernel<NMAT, BN, BITS, SPLITK, FUSED, GLU>;
   static std::atomic<uint64_t> attr_done{0};  // per instantiation and device
   if (int rc = ensure_smem_attr(kern, C::SMEM_BYTES, attr_done)) return rc;
   GemmArgs a;
@@ -100,7 +100,6 @@ static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
   a.perm_out = p.perm_out;
   a.pair = p.pair;
   a.w_rows1 = p.w_expert_rows > 0 ? p.w_expert_rows : p.n_out;
-  a.glu = p.glu;
   a.status = p.status;
   a.splits = p.splits > 1 ? p.splits : 1;
   a.max_split_rows = p.max_split_rows;
@@ -140,6 +139,19 @@ int launch_grouped_gemm(const GroupedGemmProblem& p, cudaStream_t st) {
     return set_error(MLXR_CU_ERR_INVALID_ARGUMENT, "grouped gemm: split-K is built for bn <= 32 (bn=%d)", p.bn);
   if (p.fused && (p.nmat != 2 || p.splits > 1 || p.pair))
     return set_error(MLXR_CU_ERR_INVALID_ARGUMENT, "grouped gemm: the fused launch needs nmat 2, no split, no pair");
+  if (p.glu && (p.nmat != 2 || p.pair))
+    return set_error(MLXR_CU_ERR_INVALID_ARGUMENT, "grouped gemm: GeGLU needs a gate|up pair (nmat 2, no pair)");
+  if (p.glu) {  // GeGLU gate|up instantiations (the Gemma 4 experts)
+#define MLXR_GG_GLU(BNV, BT)                                                                                     \
+  if (p.fused && p.bn == BNV && p.bits == BT) return launch_one<2, BNV, BT, false, true, true>(p, st);        \
+  if (!p.fused && p.splits > 1 && p.bn == BNV && p.bits == BT && BNV <= 32)                                   \
+    return launch_one<2, BNV, BT, (BNV <= 32), false, true>(p, st);                                           \
+  if (!p.fused && p.splits <= 1 && p.bn == BNV && p.bits == BT) return launch_one<2, BNV, BT, false, false, true>(p, st);
+    MLXR_GG_GLU(16, 4) MLXR_GG_GLU(32, 4) MLXR_GG_GLU(64, 4) MLXR_GG_GLU(128, 4)
+    MLXR_GG_GLU(16, 8) MLXR_GG_GLU(32, 8) MLXR_GG_GLU(64, 8) MLXR_GG_GLU(128, 8)
+#undef MLXR_GG_GLU
+    return set_error(MLXR_CU_ERR_UNSUPPORTED, "grouped gemm: no GeGLU kernel for bn=%d bits=%d", p.bn, p.bits);
+  }
 #define MLXR_GG_FUSED(BNV, BT) \
   if (p.fused && p.bn == BNV && p.bits == BT) return launch_one<2, BNV, BT, false, true>(p, st);
   MLXR_GG_FUSED(16, 4) MLXR_GG_FUSED(32, 4) MLXR_GG_FUSED(64, 4) MLXR_GG_FUSED(128, 4)

@@ -133,7 +133,6 @@ struct GemmArgs {
                               // of one weight (plain epilogue) instead of gate and up (SwiGLU)
   int32_t w_rows1;            // weight rows per expert of the first phase: Nout, or 2*Nout
                               // for a packed gate|up [E, 2*Nout, K] (up = rows Nout..)
-  int glu;                    // NMAT == 2, not pair: 0 = silu(gate)*up, 1 = gelu_approx(gate)*up
   int* status;
   // Split-K (splits > 1): every (tile, row slice) is split into `splits`
   // k-ranges; each writes its fp32 accumulators to `partial`, and the last
@@ -243,8 +242,9 @@ __device__ inline bool wait_counter_geq(const int32_t* p, int target, volatile i
 }
 
 // SPLITK: the split-K variant (args.splits > 1). FUSED: gate|up then down in
-// one launch (NMAT == 2). The plain variant has both folded out.
-template <int NMAT, int BN, int BITS, bool SPLITK, bool FUSED>
+// one launch (NMAT == 2). The plain variant has both folded out. GLU: the
+// gate|up epilogue applies gelu_approx (GeGLU) instead of silu (SwiGLU).
+template <int NMAT, int BN, int BITS, bool SPLITK, bool FUSED, bool GLU>
 __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
     grouped_dequant_gemm_kernel(const __grid_constant__ CUtensorMap tm_a0, const __grid_constant__ CUtensorMap tm_a1,
                                 const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_a2,
@@ -748,7 +748,7 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
           outp2[(int64_t)col * n_out] = f32_to_bf16_bits(uv);
         } else {
           float v = gv;
-          if (NMAT == 2) v = (args.glu ? gelu_tanh_f32(v) : silu_f32(v)) * uv;
+          if constexpr (NMAT == 2) v = (GLU ? gelu_tanh_f32(v) : silu_f32(v)) * uv;
           outp[(int64_t)col * n_out] = f32_to_bf16_bits(v);
         }
       };
