@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define MLXR_CU_ABI_VERSION 1
+#define MLXR_CU_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define MLXR_CU_API __attribute__((visibility("default")))

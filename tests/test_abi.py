@@ -40,7 +40,7 @@ def test_library_exports_every_declared_symbol():
 def test_abi_version_and_clean_error_state():
     from mlxr_moe import _lib
 
-    assert _lib.LIB.mlxr_cu_abi_version() == 1
+    assert _lib.LIB.mlxr_cu_abi_version() == 2
     _lib.LIB.mlxr_cu_clear_error()
     assert _lib.last_error() is None
 
