@@ -675,9 +675,12 @@ def run_case(args):
     from mlxr_moe import synth
 
     name, T = args.case.split(":")
-    spec = synth.CONFIGS[name]
-    blk = synth.make_block(spec["cfg"], 0, spec["zipf"])
-    x = synth.make_input(int(T), spec["cfg"].hidden_size)
+    if name == "gemma4":
+        blk = synth.make_gemma4_branch(_gemma4_cfg(), 0)
+    else:
+        spec = synth.CONFIGS[name]
+        blk = synth.make_block(spec["cfg"], 0, spec["zipf"])
+    x = synth.make_input(int(T), blk.cfg.hidden_size)
     for _ in range(args.iters):
         blk.forward(x)
     torch.cuda.synchronize()
@@ -694,7 +697,7 @@ def main():
     ap.add_argument("--no-extra", action="store_true", help="skip the other BASELINE configurations")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--case", default=None,
-                    help="profiling driver: CONFIG:TOKENS (e.g. c2:64); runs only block forwards, prints nothing timed")
+                    help="profiling driver: CONFIG:TOKENS (e.g. c2:64, gemma4:64); runs only block forwards, prints nothing timed")
     ap.add_argument("--iters", type=int, default=3, help="forwards for --case")
     args = ap.parse_args()
     if args.case:
