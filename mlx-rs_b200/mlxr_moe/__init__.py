@@ -5,7 +5,7 @@ missing (there is no CPU fallback).
 """
 from . import _lib, checkpoint, ops, synth
 from ._lib import MlxrError
-from .checkpoint import load_qwen35_moe_block
+from .checkpoint import load_gemma4_moe_branch, load_qwen35_moe_block
 from .moe import (Gemma4MoeBranch, MoeConfig, PackedSwitchFfn, QuantizedLinear, QuantizedSwitchLinear,
                   Qwen35MoeBlock, Routing, SplitSwitchFfn, SwigluMlp)
 from .ops import dequantize, gather_mm, gather_qmm, quantize, quantized_matmul
@@ -13,5 +13,5 @@ from .ops import dequantize, gather_mm, gather_qmm, quantize, quantized_matmul
 __all__ = [
     "Gemma4MoeBranch", "MlxrError", "MoeConfig", "PackedSwitchFfn", "QuantizedLinear", "QuantizedSwitchLinear", "Qwen35MoeBlock", "Routing",
     "SplitSwitchFfn", "SwigluMlp", "dequantize", "gather_mm", "gather_qmm", "quantize", "quantized_matmul",
-    "ops", "synth", "_lib", "checkpoint", "load_qwen35_moe_block",
+    "ops", "synth", "_lib", "checkpoint", "load_qwen35_moe_block", "load_gemma4_moe_branch",
 ]

@@ -1,4 +1,5 @@
-"""Qwen 3.5 / 3.6 MoE blocks from an mlxr-convert checkpoint directory.
+"""Qwen 3.5 / 3.6 MoE blocks (and the Gemma 4 MoE branch, see below) from
+a converted checkpoint directory.
 
 The converter (crates/mlxr-convert) writes:
   * sharded safetensors files plus `model.safetensors.index.json`, whose
@@ -31,7 +32,8 @@ import numpy as np
 import torch
 
 from . import ops
-from .moe import MoeConfig, QuantizedLinear, QuantizedSwitchLinear, Qwen35MoeBlock, SplitSwitchFfn, SwigluMlp
+from .moe import (Gemma4MoeBranch, MoeConfig, PackedSwitchFfn, QuantizedLinear, QuantizedSwitchLinear, Qwen35MoeBlock,
+                  SplitSwitchFfn, SwigluMlp)
 
 # ------------------------------------------------------------ config -----
 
@@ -240,5 +242,116 @@ def load_qwen35_moe_block(model_dir: str | Checkpoint, layer: int, device="cuda"
     return Qwen35MoeBlock(cfg, router, sw, shared, shared_gate)
 
 
+# ------------------------------------------------------------ Gemma 4 ----
+# Gemma 4 checkpoints (gemma4/text/weights.rs:1-16, 60-180 of the reference's
+# loader): keys under `model.language_model.layers.N` (a VLM envelope; also
+# accepted: `model.layers.N`, `language_model.model.layers.N`), the router at
+# `router.{proj.weight, scale, per_expert_scale}`, the experts' input norm at
+# `pre_feedforward_layernorm_2.weight`, and the experts either as one
+# `experts.gate_up_proj` [E, 2I, D] (dense, or quantised with
+# .weight/.scales/.biases) or, as pre-quantised mlx-community checkpoints ship
+# them, as `experts.{gate,up}_proj.{weight,scales,biases}`, which the
+# reference concatenates along the row axis into `switch_glu.gate_up_proj`
+# (merge_gate_up, weights.rs:155-180); `experts.down_proj` likewise.
+
+_GEMMA4_PREFIXES = ("model.language_model.layers.{}", "model.layers.{}", "language_model.model.layers.{}")
+
+
+def gemma4_layer_prefix(ck: "Checkpoint", layer: int) -> str:
+    for f in _GEMMA4_PREFIXES:
+        p = f.format(layer)
+        if f"{p}.router.proj.weight" in ck:
+            return p
+    raise KeyError(f"layer {layer}: no Gemma 4 router (router.proj.weight) under {[f.format(layer) for f in _GEMMA4_PREFIXES]}")
+
+
+def gemma4_moe_config(config: dict, bits: int, group_size: int = 64) -> MoeConfig:
+    """MoeConfig (model_kind 1) of the MoE branch from config.json's text
+    fields (gemma4/text/config.rs: hidden_size, num_experts, top_k_experts,
+    moe_intermediate_size, rms_norm_eps)."""
+    tc = text_config(config)
+    if not tc.get("num_experts") or not tc.get("top_k_experts") or not tc.get("moe_intermediate_size"):
+        raise ValueError("config.json describes no Gemma 4 MoE block (num_experts / top_k_experts / moe_intermediate_size)")
+    if group_size != 64:
+        raise ValueError(f"group size {group_size} is not supported by the block (64)")
+    return MoeConfig(hidden_size=int(tc["hidden_size"]), num_experts=int(tc["num_experts"]),
+                     num_experts_per_tok=int(tc["top_k_experts"]), moe_intermediate_size=int(tc["moe_intermediate_size"]),
+                     group_size=group_size, bits=bits, model_kind=1, rms_norm_eps=float(tc.get("rms_norm_eps", 1e-6)))
+
+
+def _bf16_vector(ck: "Checkpoint", key: str, n: int, device) -> torch.Tensor:
+    t = ck.tensor(key, device)
+    if tuple(t.shape) != (n,):
+        raise ValueError(f"{key}: shape {tuple(t.shape)}, expected {(n,)}")
+    return t.to(torch.bfloat16)
+
+
+def load_gemma4_moe_branch(model_dir: str | Checkpoint, layer: int, device="cuda", bits: int = 4) -> Gemma4MoeBranch:
+    """Gemma4MoeBranch of decoder layer `layer`. Quantised experts keep the
+    checkpoint's group size and bits (from config.json's quantisation block);
+    dense experts are quantised at load with the library's affine quantiser
+    (`bits`, group 64). A quantised router projection is expanded once to
+    bf16(scale * q + bias)."""
+    ck = model_dir if isinstance(model_dir, Checkpoint) else Checkpoint(model_dir)
+    p = gemma4_layer_prefix(ck, layer)
+    q = quantization_config(ck.config)
+    ex = f"{p}.experts"
+    packed_q = f"{ex}.gate_up_proj.scales" in ck
+    split_q = f"{ex}.gate_proj.scales" in ck
+    if packed_q or split_q:
+        if q is None:
+            raise ValueError("quantised experts but config.json has no quantization block")
+        gs, bits = q.for_path(f"{ex}.gate_up_proj" if packed_q else f"{ex}.gate_proj")
+    else:
+        gs = 64
+    cfg = gemma4_moe_config(ck.config, bits, gs)
+    E, D, I = cfg.num_experts, cfg.hidden_size, cfg.moe_intermediate_size
+    # router projection
+    if f"{p}.router.proj.scales" in ck:
+        rgs, rbits = q.for_path(f"{p}.router.proj") if q is not None else (64, 8)
+        rq = _qlinear(ck, f"{p}.router.proj", rgs, rbits, device)
+        proj = ops.dequantize(rq.weight, rq.scales, rq.biases, rgs, rbits, dtype=torch.bfloat16)
+    else:
+        proj = ck.tensor(f"{p}.router.proj.weight", device).to(torch.bfloat16)
+    if tuple(proj.shape) != (E, D):
+        raise ValueError(f"{p}.router.proj: shape {tuple(proj.shape)}, expected {(E, D)}")
+    # Router.scale * hidden^-0.5 in the scale's dtype (text.rs:628-639: the
+    # scalar is staged into that dtype first), then bf16 for the kernel.
+    scale = ck.tensor(f"{p}.router.scale", device)
+    if tuple(scale.shape) != (D,):
+        raise ValueError(f"{p}.router.scale: shape {tuple(scale.shape)}, expected {(D,)}")
+    root = torch.tensor(D ** -0.5, dtype=torch.float32).to(scale.dtype).to(device)
+    router_norm = (scale * root).to(torch.bfloat16)
+    expert_scale = _bf16_vector(ck, f"{p}.router.per_expert_scale", E, device)
+    experts_norm = _bf16_vector(ck, f"{p}.pre_feedforward_layernorm_2.weight", D, device)
+    # experts
+    if packed_q:
+        gu = _qlinear(ck, f"{ex}.gate_up_proj", gs, bits, device, QuantizedSwitchLinear)
+    elif split_q:
+        g = _qlinear(ck, f"{ex}.gate_proj", gs, bits, device, QuantizedSwitchLinear)
+        u = _qlinear(ck, f"{ex}.up_proj", gs, bits, device, QuantizedSwitchLinear)
+        gu = QuantizedSwitchLinear(torch.cat([g.weight, u.weight], 1).contiguous(),
+                                   torch.cat([g.scales, u.scales], 1).contiguous(),
+                                   torch.cat([g.biases, u.biases], 1).contiguous(), gs, bits)
+    else:
+        w = ck.tensor(f"{ex}.gate_up_proj", device).to(torch.bfloat16)
+        if tuple(w.shape) != (E, 2 * I, D):
+            raise ValueError(f"{ex}.gate_up_proj: shape {tuple(w.shape)}, expected {(E, 2 * I, D)}")
+        gu = QuantizedSwitchLinear.from_switch_linear(w, gs, bits)
+    if f"{ex}.down_proj.scales" in ck:
+        dn = _qlinear(ck, f"{ex}.down_proj", gs, bits, device, QuantizedSwitchLinear)
+    else:
+        w = ck.tensor(f"{ex}.down_proj", device).to(torch.bfloat16)
+        if tuple(w.shape) != (E, D, I):
+            raise ValueError(f"{ex}.down_proj: shape {tuple(w.shape)}, expected {(E, D, I)}")
+        dn = QuantizedSwitchLinear.from_switch_linear(w, gs, bits)
+    for name, m, rows, kin in (("gate_up_proj", gu, 2 * I, D), ("down_proj", dn, D, I)):
+        want = (E, rows, kin * bits // 32)
+        if tuple(m.weight.shape) != want:
+            raise ValueError(f"{ex}.{name}.weight: shape {tuple(m.weight.shape)}, expected {want}")
+    return Gemma4MoeBranch(cfg, proj, router_norm, expert_scale, experts_norm, PackedSwitchFfn(gu, dn))
+
+
 __all__ = ["QuantizationConfig", "Checkpoint", "moe_config", "load_qwen35_moe_block", "write_safetensors",
-           "read_header", "layer_prefix", "text_config", "quantization_config"]
+           "read_header", "layer_prefix", "text_config", "quantization_config", "gemma4_moe_config",
+           "gemma4_layer_prefix", "load_gemma4_moe_branch"]

@@ -107,3 +107,34 @@ def test_single_file_checkpoint(tmp_path):
     os.remove(tmp_path / "model.safetensors")
     with pytest.raises(FileNotFoundError):
         ck.Checkpoint(str(tmp_path))
+
+
+def _gemma4_config():
+    return {"model_type": "gemma4", "text_config": {"hidden_size": 2048, "num_experts": 128, "top_k_experts": 8,
+                                                    "moe_intermediate_size": 768, "rms_norm_eps": 1e-6,
+                                                    "enable_moe_block": True},
+            "quantization": {"group_size": 64, "bits": 4, "mode": "affine"}}
+
+
+def test_gemma4_moe_config():
+    cfg = ck.gemma4_moe_config(_gemma4_config(), bits=4)
+    assert (cfg.hidden_size, cfg.num_experts, cfg.num_experts_per_tok, cfg.moe_intermediate_size) == (2048, 128, 8, 768)
+    assert cfg.model_kind == 1 and cfg.shared_expert_intermediate_size == 0 and abs(cfg.rms_norm_eps - 1e-6) < 1e-12
+    c = cfg.to_c()
+    assert c.model_kind == 1 and abs(c.rms_norm_eps - 1e-6) < 1e-9
+    with pytest.raises(ValueError):
+        ck.gemma4_moe_config({"text_config": {"hidden_size": 2048}}, bits=4)  # a dense-MLP model
+    with pytest.raises(ValueError):
+        ck.gemma4_moe_config(_gemma4_config(), bits=4, group_size=32)
+
+
+@pytest.mark.parametrize("prefix", ["model.language_model.layers.5", "model.layers.5", "language_model.model.layers.5"])
+def test_gemma4_layer_prefix(tmp_path, prefix):
+    ck.write_safetensors(str(tmp_path / "model.safetensors"),
+                         {f"{prefix}.router.proj.weight": np.zeros((4, 8), np.uint16)}, {f"{prefix}.router.proj.weight": "BF16"})
+    with open(tmp_path / "config.json", "w") as f:
+        json.dump(_gemma4_config(), f)
+    m = ck.Checkpoint(str(tmp_path))
+    assert ck.gemma4_layer_prefix(m, 5) == prefix
+    with pytest.raises(KeyError):
+        ck.gemma4_layer_prefix(m, 6)
