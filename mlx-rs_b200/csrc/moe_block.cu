@@ -570,11 +570,10 @@ static size_t ep_dispatch_bytes(const mlxr_cu_moe_config* c, int64_t T, size_t* 
   return L.total + align256((size_t)(T * c->num_experts_per_tok) * 4 + 4);
 }
 
-// The Gemma 4 branch runs on one device only.
-static int ep_reject_gemma4(const mlxr_cu_moe_config* cfg) {
-  if (cfg && cfg->model_kind == 1)
-    return set_error(MLXR_CU_ERR_UNSUPPORTED, "moe_ep: the Gemma 4 branch has no expert-parallel path");
-  return MLXR_CU_OK;
+// The rows a dispatch sends: x, or for the Gemma 4 branch the experts'
+// RMS-normed input that run_router wrote beside the routing.
+static const void* ep_send_rows(const Layout& L, const void* x, void* ws) {
+  return L.kind == 1 ? static_cast<const void*>(at<uint16_t>(ws, L.gxe)) : x;
 }
 
 static int ep_check_world(const mlxr_cu_moe_config* cfg, int world) {
@@ -866,7 +865,6 @@ int mlxr_cu_moe_combine(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights
 
 int mlxr_cu_moe_ep_workspace_size(const mlxr_cu_moe_config* cfg, int world, int64_t num_tokens,
                                   int64_t max_recv_pairs, int64_t max_recv_rows, size_t* bytes) {
-  if (int rc = ep_reject_gemma4(cfg)) return rc;
   if (int rc = validate(cfg, num_tokens)) return rc;
   if (int rc = ep_check_world(cfg, world)) return rc;
   MLXR_CHECK_ARG(bytes != nullptr, "moe_ep_workspace_size: bytes is NULL");
@@ -888,7 +886,6 @@ int mlxr_cu_moe_ep_dispatch(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_wei
                             const int32_t* placement, const void* x, int64_t num_tokens, int32_t* send_counts, int32_t* pair_pos,
                             void* x_send, int32_t* meta_send, float* shared_gate, void* workspace,
                             size_t workspace_bytes, void* stream) {
-  if (int rc = ep_reject_gemma4(cfg)) return rc;
   if (int rc = validate(cfg, num_tokens)) return rc;
   if (int rc = ep_check_world(cfg, world)) return rc;
   MLXR_CHECK_ARG(weights != nullptr, "moe_ep_dispatch: weights is NULL");
@@ -924,7 +921,7 @@ int mlxr_cu_moe_ep_dispatch(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_wei
   P.rows = num_tokens * (K < world ? K : world);
   P.bn1 = P.bn2 = 1 << 30;  // tile lists are not used here
   P.max_t1 = P.max_t2 = world + 1;
-  if (int rc = run_permute(P, dest, x, ws, at<int32_t>(ws, L.counts), at<int32_t>(ws, L.offsets),
+  if (int rc = run_permute(P, dest, ep_send_rows(L, x, ws), ws, at<int32_t>(ws, L.counts), at<int32_t>(ws, L.offsets),
                            at<int32_t>(ws, L.sorted), pair_pos, static_cast<uint16_t*>(x_send), 0, st, 1))
     return rc;
   launch_pdl(ep_counts_kernel, 1, 1024, 0, st, at<int32_t>(ws, L.idx), R, world, placement, at<int32_t>(ws, L.counts),
@@ -943,7 +940,6 @@ int mlxr_cu_moe_ep_dispatch(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_wei
 int mlxr_cu_moe_ep_experts(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* local_weights,
                            int num_local_experts, const void* x_recv, const int32_t* meta_recv, int64_t num_pairs,
                            int64_t num_rows, void* partial, void* workspace, size_t workspace_bytes, void* stream) {
-  if (int rc = ep_reject_gemma4(cfg)) return rc;
   if (int rc = validate(cfg, num_pairs)) return rc;
   MLXR_CHECK_ARG(num_local_experts >= 1 && num_local_experts <= cfg->num_experts,
                  "moe_ep_experts: num_local_experts=%d must be in [1, num_experts]", num_local_experts);
@@ -982,7 +978,6 @@ int mlxr_cu_moe_ep_combine(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weig
                            int64_t num_tokens, const void* partial_back, int64_t num_pairs, const int32_t* pair_pos,
                            const float* shared_gate, void* out, void* workspace, size_t workspace_bytes,
                            void* stream) {
-  if (int rc = ep_reject_gemma4(cfg)) return rc;
   if (int rc = validate(cfg, num_tokens)) return rc;
   const Layout L = make_layout(cfg, num_tokens);
   if (int rc = check_ws(L, workspace, workspace_bytes)) return rc;
@@ -1138,7 +1133,6 @@ int mlxr_cu_ep_comm_destroy(void* comm) {
 
 int mlxr_cu_moe_ep_p2p_workspace_size(const mlxr_cu_moe_config* cfg, const void* comm, int64_t num_tokens,
                                       int num_local_experts, int64_t expected_rows, size_t* bytes) {
-  if (int rc = ep_reject_gemma4(cfg)) return rc;
   if (int rc = validate(cfg, num_tokens)) return rc;
   if (int rc = ep_comm_check(comm, cfg)) return rc;
   MLXR_CHECK_ARG(bytes && num_local_experts >= 1 && num_local_experts <= cfg->num_experts,
@@ -1159,7 +1153,6 @@ int mlxr_cu_moe_ep_dispatch_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe
                                 const int32_t* placement, const void* x, int64_t num_tokens, int32_t* pair_pos,
                                 float* shared_gate, uint32_t epoch, void* workspace, size_t workspace_bytes,
                                 void* stream) {
-  if (int rc = ep_reject_gemma4(cfg)) return rc;
   if (int rc = validate(cfg, num_tokens)) return rc;
   if (int rc = ep_comm_check(comm, cfg)) return rc;
   EpComm* c = static_cast<EpComm*>(comm);
@@ -1214,7 +1207,8 @@ int mlxr_cu_moe_ep_dispatch_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe
   if (grid > 4 * 148) grid = 4 * 148;
   if (grid < 1) grid = 1;
   launch_pdl(ep_send_kernel, grid, 256, 0, st, c->peers, c->bl, c->rank, world, c->cap,
-             static_cast<const uint16_t*>(x), c->D, K, at<int32_t>(ws, L.sorted), offsets, at<int32_t>(ws, dl.meta),
+             static_cast<const uint16_t*>(ep_send_rows(L, x, ws)), c->D, K, at<int32_t>(ws, L.sorted), offsets,
+             at<int32_t>(ws, dl.meta),
              send_counts, pair_pos, epoch, reinterpret_cast<int*>(c->local + c->bl.done), at<int>(ws, L.status));
   MLXR_LAUNCH_CHECK("ep_send_kernel");
   return MLXR_CU_OK;
@@ -1223,7 +1217,6 @@ int mlxr_cu_moe_ep_dispatch_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe
 int mlxr_cu_moe_ep_experts_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* local_weights,
                                int num_local_experts, void* comm, int64_t expected_rows, uint32_t epoch,
                                void* workspace, size_t workspace_bytes, void* stream) {
-  if (int rc = ep_reject_gemma4(cfg)) return rc;
   if (int rc = ep_comm_check(comm, cfg)) return rc;
   EpComm* c = static_cast<EpComm*>(comm);
   MLXR_CHECK_ARG(local_weights != nullptr && num_local_experts >= 1 && num_local_experts <= cfg->num_experts,
@@ -1262,7 +1255,6 @@ int mlxr_cu_moe_ep_experts_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_
 int mlxr_cu_moe_ep_combine_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights, void* comm,
                                const void* x, int64_t num_tokens, const int32_t* pair_pos, const float* shared_gate,
                                void* out, uint32_t epoch, void* workspace, size_t workspace_bytes, void* stream) {
-  if (int rc = ep_reject_gemma4(cfg)) return rc;
   if (int rc = validate(cfg, num_tokens)) return rc;
   if (int rc = ep_comm_check(comm, cfg)) return rc;
   EpComm* c = static_cast<EpComm*>(comm);

@@ -33,7 +33,7 @@ import ctypes as C
 import torch
 
 from . import _lib
-from .moe import QuantizedSwitchLinear, Qwen35MoeBlock, SplitSwitchFfn
+from .moe import Gemma4MoeBranch, PackedSwitchFfn, QuantizedSwitchLinear, Qwen35MoeBlock, SplitSwitchFfn
 
 
 def strided_placement(num_experts: int, world: int) -> list[int]:
@@ -69,15 +69,18 @@ def placement_table(rank_of: list[int]) -> list[int]:
     return table
 
 
-def local_switch(sw: SplitSwitchFfn, experts: list[int]) -> SplitSwitchFfn:
-    """The given experts of a switch layer, in that order."""
+def _take_experts(q: QuantizedSwitchLinear, experts: list[int]) -> QuantizedSwitchLinear:
+    idx = torch.tensor(experts, dtype=torch.long, device=q.weight.device)
+    return QuantizedSwitchLinear(q.weight.index_select(0, idx).contiguous(), q.scales.index_select(0, idx).contiguous(),
+                                 q.biases.index_select(0, idx).contiguous(), q.group_size, q.bits)
 
-    def take(q: QuantizedSwitchLinear):
-        idx = torch.tensor(experts, dtype=torch.long, device=q.weight.device)
-        return QuantizedSwitchLinear(q.weight.index_select(0, idx).contiguous(), q.scales.index_select(0, idx).contiguous(),
-                                     q.biases.index_select(0, idx).contiguous(), q.group_size, q.bits)
 
-    return SplitSwitchFfn(take(sw.gate_proj), take(sw.up_proj), take(sw.down_proj))
+def local_switch(sw, experts: list[int]):
+    """The given experts of a switch layer (SplitSwitchFfn, or the Gemma 4
+    PackedSwitchFfn), in that order."""
+    if isinstance(sw, PackedSwitchFfn):
+        return PackedSwitchFfn(_take_experts(sw.gate_up_proj, experts), _take_experts(sw.down_proj, experts))
+    return SplitSwitchFfn(*(_take_experts(q, experts) for q in (sw.gate_proj, sw.up_proj, sw.down_proj)))
 
 
 class DispatchPlan:
@@ -94,9 +97,10 @@ class DispatchPlan:
 
 
 class ExpertParallelMoeBlock:
-    """One rank's share of a Qwen35MoeBlock: the router and shared expert
-    (replicated) and the experts that `placement` (rank of each expert; by
-    default e % world) puts on this rank."""
+    """One rank's share of a Qwen35MoeBlock (or a Gemma4MoeBranch): the router
+    and shared expert, or the Gemma 4 router and norms (replicated), and the
+    experts that `placement` (rank of each expert; by default e % world) puts
+    on this rank."""
 
     def __init__(self, full: Qwen35MoeBlock, rank: int, world: int, placement: list[int] | None = None):
         cfg = full.cfg
@@ -115,7 +119,6 @@ class ExpertParallelMoeBlock:
         self.router_bias = full.router_bias
         self.shared_expert = full.shared_expert
         self.shared_expert_gate = full.shared_expert_gate
-        self.switch_mlp = local_switch(full.switch_mlp, mine)
         self._ccfg = cfg.to_c()
         z = _lib.QLinear(None, None, None)
         se, seg = self.shared_expert, self.shared_expert_gate
@@ -123,8 +126,18 @@ class ExpertParallelMoeBlock:
             self.gate.data_ptr(), None if self.router_bias is None else self.router_bias.data_ptr(), z, z, z,
             se.gate_proj.c() if se else z, se.up_proj.c() if se else z, se.down_proj.c() if se else z,
             seg.c() if seg else z)
-        sm = self.switch_mlp
-        self._cw_loc = _lib.MoeWeights(None, None, sm.gate_proj.c(), sm.up_proj.c(), sm.down_proj.c(), z, z, z, z)
+        if isinstance(full, Gemma4MoeBranch):
+            self._norms = (full.router_norm, full.expert_scale, full.experts_norm)  # kept alive with the pointers
+            self._cw_rep.router_norm, self._cw_rep.expert_scale, self._cw_rep.experts_norm = (
+                t.data_ptr() for t in self._norms)
+            self.switch_mlp = local_switch(full.switch_glu, mine)
+            sm = self.switch_mlp
+            self._cw_loc = _lib.MoeWeights(None, None, z, z, sm.down_proj.c(), z, z, z, z)
+            self._cw_loc.switch_gate_up = sm.gate_up_proj.c()
+        else:
+            self.switch_mlp = local_switch(full.switch_mlp, mine)
+            sm = self.switch_mlp
+            self._cw_loc = _lib.MoeWeights(None, None, sm.gate_proj.c(), sm.up_proj.c(), sm.down_proj.c(), z, z, z, z)
         self._ws = None
 
     @classmethod

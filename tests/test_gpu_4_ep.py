@@ -264,3 +264,24 @@ def test_ep_p2p_two_gpus(tmp_path):
     mp.spawn(_p2p_worker, args=(2, 29519, str(res)), nprocs=2, join=True)
     ok, err = res.read_text().split()
     assert ok == "1", f"max abs err {err}"
+
+
+@pytest.mark.parametrize("T,world", [(32, 2), (64, 8)])
+def test_ep_loopback_gemma4_branch(T, world):
+    """The Gemma 4 branch sharded over `world` virtual ranks: the dispatch
+    sends the experts' RMS-normed rows, each rank runs its slice of the packed
+    gate_up_proj with GeGLU; the outputs match the one-device branch."""
+    from mlxr_moe.moe import MoeConfig
+    cfg = MoeConfig(1024, 64, 4, 512, bits=4, model_kind=1, rms_norm_eps=1e-6)
+    full = synth.make_gemma4_branch(cfg, 0)
+    blocks = [ExpertParallelMoeBlock.from_block(full, r, world) for r in range(world)]
+    xs = [synth.make_input(T, cfg.hidden_size, stream_offset=60 + r) for r in range(world)]
+    outs = loopback_forward(blocks, xs)
+    torch.cuda.synchronize()
+    for b in blocks:
+        b.status()
+    for r in range(world):
+        want = full.forward(xs[r])
+        torch.cuda.synchronize()
+        assert_close_bf16(bf16_np(outs[r]), bf16_np(want), ATOL, RTOL, f"rank {r}")
+        assert_mostly_tight(bf16_np(outs[r]), bf16_np(want), TIGHT_ATOL, TIGHT_RTOL, TIGHT_FRAC, f"rank {r} tight")
