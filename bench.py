@@ -497,9 +497,39 @@ def bench_extra(args, dev, st, flush, peaks):
                          frac=(tfl / peaks["bf16_tflops"]) if prefill else (gbs / peaks["hbm_gbs"]),
                          distinct_experts=U, zipf=zipf,
                          stages_ms={k: round(v, 5) for k, v in stg.items()})
+        if name == "gemma4_decode" and not args.no_cpu:
+            res[name]["cpu_baseline"] = gemma4_cpu_baseline(blk, x)
         del g, blk, ws, out, x
         torch.cuda.empty_cache()
     return res
+
+
+def gemma4_cpu_baseline(branch, x):
+    """The oracle's Gemma 4 branch (fused-fp32 contract, OpenMP on every host
+    core) on the same 64 decode tokens, median of 2 forwards."""
+    import numpy as np
+    import torch
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    u16 = lambda t: t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+    q3 = lambda q: (q.weight.detach().cpu().numpy().view(np.uint32), u16(q.scales), u16(q.biases))  # noqa: E731
+    c = branch.cfg
+    cfg = dict(hidden=c.hidden_size, num_experts=c.num_experts, top_k=c.num_experts_per_tok,
+               moe_intermediate=c.moe_intermediate_size, group_size=c.group_size, bits=c.bits, eps=c.rms_norm_eps)
+    W = {"router": u16(branch.gate), "router_norm": u16(branch.router_norm), "expert_scale": u16(branch.expert_scale),
+         "experts_norm": u16(branch.experts_norm), "gate_up": q3(branch.switch_glu.gate_up_proj),
+         "down": q3(branch.switch_glu.down_proj)}
+    xs = u16(x)
+    times = []
+    for _ in range(2):
+        t0 = time.perf_counter()
+        O.gemma4_block(cfg, W, xs)
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    return {"tokens_per_s": xs.shape[0] / sec, "cores": O.max_threads(), "kind": "port",
+            "sample": f"2 forwards of {xs.shape[0]} tokens, median; oracle fused-fp32, OpenMP {O.max_threads()} threads"}
 
 
 def bench_ep(args, dev, st, world, rank):
