@@ -1,4 +1,5 @@
-// CPU oracle for the Qwen 3.5/3.6 MoE block hot path.
+// CPU oracle for the Qwen 3.5/3.6 MoE block hot path (and the Gemma 4 MoE
+// branch that runs on the same kernels, orc_gemma4_block).
 //
 // TEST INFRASTRUCTURE ONLY. This file is the checker the tests compare the
 // CUDA library against; it is never linked into, called by, or shipped with
