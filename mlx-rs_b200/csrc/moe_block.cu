@@ -302,7 +302,7 @@ static int run_router(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
     return MLXR_CU_OK;
   } else if (L.T > kTileRouterMinT) {
     uint16_t* lg = logits ? logits : at<uint16_t>(ws, L.logits);
-    static std::atomic<uint64_t> attr_done{0};  // 72 KB of dynamic shared memory
+    static std::atomic<uint64_t> attr_done{0};  // 48 KB of dynamic shared memory
     if (int rc = ensure_smem_attr(router_logits_tile_kernel, RT_TILE_SMEM, attr_done)) return rc;
     const dim3 grid((unsigned)((L.E + RT_TE - 1) / RT_TE), (unsigned)((L.T + RT_TT - 1) / RT_TT));
     launch_pdl(router_logits_tile_kernel, grid, RT_TILE_THREADS, RT_TILE_SMEM, st, xp, L.T, L.D, wg, L.E, rbias, lg);

@@ -398,23 +398,24 @@ __global__ void __launch_bounds__(RS_WARPS * 32) router_split_kernel(
 
 // Large batches: logits in CTA tiles of 32 tokens x 16 experts. Each
 // 32-chunk block of D (256 elements) of the tile's x rows and router rows is
-// copied to shared memory as bf16 (16-byte cp.async, one block ahead), then
-// converted once to fp32: x as [token][half][chunk][4], the router rows as
-// expert pairs [pair][element pair][chunk][4] = (w_j[e], w_j+1[e], w_j[e+1],
-// w_j+1[e+1]). Warp w owns tokens 8*(w%4) .. +7 and experts 8*(w/4) .. +7;
-// lane j keeps the contract's chain over chunks j, j+32, ... of D for each of
-// its 64 (token, expert) pairs, two experts at a time with the packed fp32x2
-// FMA (two IEEE round-to-nearest FMAs), so each logit is the same fp32 value
-// as in router_fused_kernel while the per-FMA unpacking and operand loads
-// are shared by the warp's tile.
+// copied to shared memory as bf16 by 8-byte cp.async into two planes, the low
+// and the high half of every 16-byte chunk ([plane][row][chunk][8 B]), double
+// buffered one block ahead. Warp w owns tokens 8*(w%4) .. +7 and experts
+// 8*(w/4) .. +7; lane j keeps the contract's chain over chunks j, j+32, ... of
+// D for each of its 64 (token, expert) pairs, two experts at a time with the
+// packed fp32x2 FMA (two IEEE round-to-nearest FMAs). Per half chunk a lane
+// loads the four elements of its 8 tokens and 8 experts (8-byte loads; a warp
+// reads 256 contiguous bytes, conflict-free) and widens them to fp32 in
+// registers (exact), so each logit is the same fp32 value as in
+// router_fused_kernel. (A layout that staged fp32 copies in shared memory
+// read twice the bytes per FMA and was bound by shared-memory bandwidth.)
 constexpr int RT_TT = 32, RT_TE = 16, RT_TILE_THREADS = 256;
-constexpr int RT_BF_STAGE = (RT_TT + RT_TE) * 32 * 16;        // bf16 staging: 24 KB
-constexpr int RT_X32 = RT_TT * 256 * 4;                        // fp32 x: 32 KB
-constexpr int RT_W32 = RT_TE * 256 * 4;                        // fp32 router rows: 16 KB
-constexpr int RT_TILE_SMEM = RT_BF_STAGE + RT_X32 + RT_W32;    // 72 KB
+constexpr int RT_PLANE = (RT_TT + RT_TE) * 32 * 8;  // one half-chunk plane of a block: 12 KB
+constexpr int RT_BF_STAGE = 2 * RT_PLANE;           // one block: 24 KB
+constexpr int RT_TILE_SMEM = 2 * RT_BF_STAGE;       // double buffered: 48 KB
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(valid ? 8 : 0) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
@@ -431,35 +432,41 @@ __device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
 __device__ __forceinline__ void ffma2(uint64_t& d, uint64_t a, uint64_t b) {
   asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b));
 }
+// Element el (0..3) of a half chunk held as two bf16x2 words, as fp32.
+__device__ __forceinline__ float bf_el(const uint2& v, int el) {
+  const uint32_t w = el < 2 ? v.x : v.y;
+  return (el & 1) ? bf_hi(w) : bf_lo(w);
+}
 
 __global__ void __launch_bounds__(RT_TILE_THREADS, 2) router_logits_tile_kernel(const uint16_t* __restrict__ x, int64_t T,
                                                                               int D, const uint16_t* __restrict__ wg,
                                                                               int E, const float* __restrict__ bias,
                                                                               uint16_t* __restrict__ lg) {
   extern __shared__ __align__(16) uint8_t rt_smem[];
-  uint8_t* sbf = rt_smem;                                      // bf16 staging [48 rows][32 chunks][16 B]
-  float* sx = reinterpret_cast<float*>(rt_smem + RT_BF_STAGE);  // [32 tokens][2 halves][32 chunks][4]
-  float* sw = sx + RT_TT * 256;                                 // [8 pairs][4 element pairs][32 chunks][4]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e0 = blockIdx.x * RT_TE;
   const int64_t t0 = (int64_t)blockIdx.y * RT_TT;
   const int nchunks = D / 8;
   const int nblocks = (nchunks + 31) / 32;
-  const uint32_t sbf_u32 = smem_u32(sbf);
+  const uint32_t sbase = smem_u32(rt_smem);
   auto stage_in = [&](int m) {
+    const uint32_t buf = sbase + (uint32_t)((m & 1) * RT_BF_STAGE);
     for (int q = threadIdx.x; q < (RT_TT + RT_TE) * 32; q += RT_TILE_THREADS) {
       const int r = q >> 5, cj = q & 31;
       const int c = m * 32 + cj;
-      const uint32_t dst = sbf_u32 + (uint32_t)(q * 16);
+      const uint16_t* src;
+      bool ok;
       if (r < RT_TT) {
         const int64_t t = t0 + r;
-        const bool ok = t < T && c < nchunks;
-        cp_async16(dst, x + (ok ? t : 0) * (int64_t)D + (ok ? c : 0) * 8, ok);
+        ok = t < T && c < nchunks;
+        src = x + (ok ? t : 0) * (int64_t)D + (ok ? c : 0) * 8;
       } else {
         const int e = e0 + (r - RT_TT);
-        const bool ok = e < E && c < nchunks;
-        cp_async16(dst, wg + (ok ? e : 0) * (int64_t)D + (ok ? c : 0) * 8, ok);
+        ok = e < E && c < nchunks;
+        src = wg + (ok ? e : 0) * (int64_t)D + (ok ? c : 0) * 8;
       }
+      cp_async8(buf + (uint32_t)(q * 8), src, ok);                 // plane 0: elements 0..3 of the chunk
+      cp_async8(buf + (uint32_t)(RT_PLANE + q * 8), src + 4, ok);  // plane 1: elements 4..7
     }
     cp_async_commit();
   };
@@ -472,55 +479,34 @@ __global__ void __launch_bounds__(RT_TILE_THREADS, 2) router_logits_tile_kernel(
   stage_in(0);
   for (int m = 0; m < nblocks; ++m) {
     cp_async_wait_all();
-    __syncthreads();
-    // bf16 staging -> fp32 compute layout.
-    for (int q = threadIdx.x; q < RT_TT * 32; q += RT_TILE_THREADS) {  // x: (token, chunk)
-      const int r = q >> 5, cj = q & 31;
-      const uint4 v = *reinterpret_cast<const uint4*>(sbf + q * 16);
-      float4* d0 = reinterpret_cast<float4*>(sx + ((r * 2 + 0) * 32 + cj) * 4);
-      float4* d1 = reinterpret_cast<float4*>(sx + ((r * 2 + 1) * 32 + cj) * 4);
-      *d0 = make_float4(bf_lo(v.x), bf_hi(v.x), bf_lo(v.y), bf_hi(v.y));
-      *d1 = make_float4(bf_lo(v.z), bf_hi(v.z), bf_lo(v.w), bf_hi(v.w));
-    }
-    for (int q = threadIdx.x; q < (RT_TE / 2) * 32; q += RT_TILE_THREADS) {  // w: (expert pair, chunk)
-      const int jp = q >> 5, cj = q & 31;
-      const uint4 a = *reinterpret_cast<const uint4*>(sbf + ((RT_TT + 2 * jp) * 32 + cj) * 16);
-      const uint4 b = *reinterpret_cast<const uint4*>(sbf + ((RT_TT + 2 * jp + 1) * 32 + cj) * 16);
-      const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-      for (int ep = 0; ep < 4; ++ep)
-        *reinterpret_cast<float4*>(sw + ((jp * 4 + ep) * 32 + cj) * 4) =
-            make_float4(bf_lo(aw[ep]), bf_lo(bw[ep]), bf_hi(aw[ep]), bf_hi(bw[ep]));
-    }
-    __syncthreads();
-    if (m + 1 < nblocks) stage_in(m + 1);  // the staging buffer is free again
+    __syncthreads();  // block m has landed for every thread, and block m-1's buffer is no longer read
+    if (m + 1 < nblocks) stage_in(m + 1);
     if (m * 32 + lane < nchunks) {
+      const uint8_t* buf = rt_smem + (m & 1) * RT_BF_STAGE;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        float4 xv[8];
+      for (int h = 0; h < 2; ++h) {  // elements 4h .. 4h+3 of the chunk
+        const uint8_t* pl = buf + h * RT_PLANE;
+        uint2 xv[8], wv[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) xv[i] = *reinterpret_cast<const float4*>(sx + (((tg * 8 + i) * 2 + h) * 32 + lane) * 4);
+        for (int i = 0; i < 8; ++i) xv[i] = *reinterpret_cast<const uint2*>(pl + ((tg * 8 + i) * 32 + lane) * 8);
 #pragma unroll
-        for (int ep2 = 0; ep2 < 2; ++ep2) {  // element pairs (4h + 2*ep2, +1)
-          float4 wv[4];
+        for (int e = 0; e < 8; ++e)
+          wv[e] = *reinterpret_cast<const uint2*>(pl + ((RT_TT + eg * 8 + e) * 32 + lane) * 8);
 #pragma unroll
-          for (int jp = 0; jp < 4; ++jp)
-            wv[jp] = *reinterpret_cast<const float4*>(sw + (((eg * 4 + jp) * 4 + (2 * h + ep2)) * 32 + lane) * 4);
+        for (int el = 0; el < 4; ++el) {
+          uint64_t wp[4];
 #pragma unroll
-          for (int el = 0; el < 2; ++el) {
+          for (int jp = 0; jp < 4; ++jp) wp[jp] = f2_pack(bf_el(wv[2 * jp], el), bf_el(wv[2 * jp + 1], el));
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float xe = (ep2 == 0) ? (el == 0 ? xv[i].x : xv[i].y) : (el == 0 ? xv[i].z : xv[i].w);
-              const uint64_t xx = f2_pack(xe, xe);
+          for (int i = 0; i < 8; ++i) {
+            const float xe = bf_el(xv[i], el);
+            const uint64_t xx = f2_pack(xe, xe);
 #pragma unroll
-              for (int jp = 0; jp < 4; ++jp)
-                ffma2(acc[i][jp], xx, el == 0 ? f2_pack(wv[jp].x, wv[jp].y) : f2_pack(wv[jp].z, wv[jp].w));
-            }
+            for (int jp = 0; jp < 4; ++jp) ffma2(acc[i][jp], xx, wp[jp]);
           }
         }
       }
     }
-    __syncthreads();  // the fp32 buffers are rewritten by the next block
   }
   float mine[2] = {0.0f, 0.0f};
 #pragma unroll
