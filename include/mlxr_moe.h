@@ -246,7 +246,11 @@ MLXR_CU_API int mlxr_cu_op_status(void* stream);
 /* Router alone (moe.rs:123-138): logits = x @ gate^T (+bias) rounded to
  * bf16, softmax (fp32 inside, bf16 probabilities), top-k by (prob desc,
  * expert asc), renormalised bf16 weights. logits / probs [T, E] bf16 may be
- * NULL. Bit-exact with the routing contract the oracle states. */
+ * NULL. Bit-exact with the routing contract the oracle states.
+ * model_kind 1 (Gemma 4, text.rs:622-664): x is the layer's h; logits are
+ * the scores of its RMS-normed input, top-k by (score desc, expert asc),
+ * weights = softmax over the k scores times per_expert_scale; probs is not
+ * written (the branch has no softmax over all experts). */
 MLXR_CU_API int mlxr_cu_moe_router(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights, const void* x,
                        int64_t num_tokens, int32_t* indices, void* topk_weights, void* logits, void* probs,
                        void* workspace, size_t workspace_bytes, void* stream);
