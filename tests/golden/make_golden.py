@@ -6,7 +6,8 @@ blocks (D=256, E=16, K=4, I=128, 4-bit gs64; an 8-bit block with a shared
 expert; a skewed-router block) so that any change to the oracle is visible,
 and give the GPU tests fixed inputs with known outputs. Weights are not
 stored: they are regenerated from the seeded generator by `small_block` and
-pinned by SHA-256 digests.
+pinned by SHA-256 digests. `gemma4_small.npz` pins the Gemma 4 branch
+(orc_gemma4_block) the same way.
 """
 import hashlib
 import os
@@ -36,6 +37,22 @@ def small_block(seed, D, E, K, I, T, bits, Is=0, zipf=False):
                bits=bits, shared_bits=bits)
     return cfg, W, x
 
+
+def small_gemma4(seed, D, E, K, I, T, bits=4):
+    """A small Gemma 4 MoE branch (the oracle's orc_gemma4_block inputs)."""
+    f = lambda a: O.bf16_to_f32(a)  # noqa: E731
+    W = {"router": O.normal_bf16(seed, 0, (E, D), 0.5),
+         "router_norm": O.f32_to_bf16(np.float32(D ** -0.5) * (1.0 + f(O.normal_bf16(seed, 10, (D,), 0.1)))),
+         "expert_scale": O.f32_to_bf16(1.0 + f(O.normal_bf16(seed, 11, (E,), 0.2))),
+         "experts_norm": O.f32_to_bf16(1.0 + f(O.normal_bf16(seed, 12, (D,), 0.1))),
+         "gate_up": O.quantize(O.normal_bf16(seed, 1, (E, 2 * I, D), 0.02), 64, bits),
+         "down": O.quantize(O.normal_bf16(seed, 3, (E, D, I), 0.02), 64, bits)}
+    x = O.normal_bf16(seed, 8, (T, D), 1.0)
+    cfg = dict(hidden=D, num_experts=E, top_k=K, moe_intermediate=I, group_size=64, bits=bits, eps=1e-6)
+    return cfg, W, x
+
+
+GEMMA4 = {"g4": dict(seed=0, D=256, E=16, K=4, I=128, T=12)}
 
 BLOCKS = {
     "q4": dict(seed=0, D=256, E=16, K=4, I=128, T=10, bits=4),
@@ -87,6 +104,16 @@ def main():
         fx[f"normal/seed0_stream{st}"] = O.normal_bf16(0, st, (4096,), 1.0)
     np.savez_compressed(os.path.join(HERE, "moe_small.npz"), **fx)
     print("wrote", os.path.join(HERE, "moe_small.npz"), len(fx), "arrays")
+    # The Gemma 4 branch (orc_gemma4_block) in its own file.
+    gx = {}
+    for name, args in GEMMA4.items():
+        cfg, W, x = small_gemma4(**args)
+        out, idx, w = O.gemma4_block(cfg, W, x)
+        for k, v in flat(f"{name}/", W).items():
+            gx[k + ".sha256"] = np.array(digest(v))
+        gx[f"{name}/x"], gx[f"{name}/out"], gx[f"{name}/idx"], gx[f"{name}/w"] = x, out, idx, w
+    np.savez_compressed(os.path.join(HERE, "gemma4_small.npz"), **gx)
+    print("wrote", os.path.join(HERE, "gemma4_small.npz"), len(gx), "arrays")
 
 
 if __name__ == "__main__":

@@ -123,3 +123,26 @@ def test_empty_batch():
     w = weights()
     out, idx, wk = O.gemma4_block(CFG, w, np.zeros((0, D), np.uint16))
     assert out.shape == (0, D) and idx.shape == (0, K)
+
+
+def test_golden_gemma4_branch():
+    """The committed fixture (tests/golden/make_golden.py, `gemma4_small.npz`):
+    the generator, the quantiser and the branch's routing and outputs are
+    unchanged."""
+    import os
+    import sys
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, os.path.join(here, "golden"))
+    import make_golden as G
+
+    fx = np.load(os.path.join(here, "golden", "gemma4_small.npz"))
+    for name, args in G.GEMMA4.items():
+        cfg, W, x = G.small_gemma4(**args)
+        for k, v in G.flat(f"{name}/", W).items():
+            assert G.digest(v) == str(fx[k + ".sha256"]), f"generator/quantiser drifted for {k}"
+        np.testing.assert_array_equal(x, fx[f"{name}/x"])
+        out, idx, w = O.gemma4_block(cfg, W, x)
+        np.testing.assert_array_equal(idx, fx[f"{name}/idx"])
+        np.testing.assert_array_equal(w, fx[f"{name}/w"])
+        np.testing.assert_array_equal(out, fx[f"{name}/out"])
