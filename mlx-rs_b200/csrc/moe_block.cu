@@ -8,6 +8,11 @@
 //   grouped GEMM down              (h_sorted -> y_sorted)
 //   [shared expert: dense GEMMs over x with the same kernels]
 //   combine (+ sigmoid-gated shared expert)
+// model_kind 1 runs the Gemma 4 MoE branch (gemma4/text/text.rs:901-916) on
+// the same stages: the input RMS norms first (router input, experts input),
+// Gemma routing (top-k of the scores, softmax over k x per-expert scale),
+// the experts' normed rows permuted, packed gate_up_proj with GeGLU, no
+// shared expert.
 // All scratch lives in the caller's workspace; nothing is allocated here.
 #include <algorithm>
 #include <cstring>
