@@ -75,7 +75,14 @@ MLXR_CU_API int mlxr_cu_abi_version(void);
  * w [rows, cols] in dtype -> wq uint32 [rows, cols*bits/32],
  * scales/biases [rows, cols/group_size] in dtype. mode must be "affine" or
  * NULL. group_size 0 / bits 0 select the reference defaults 64 / 4
- * (quantization.rs:11-13). */
+ * (quantization.rs:11-13). The arithmetic is MLX's affine quantiser, so the
+ * bytes match mlxr-convert output (crates/mlxr-convert/src/quantize.rs:44):
+ * per group, the end of larger magnitude is the edge, the scale is
+ * (max - min) / (2^bits - 1) (at least 1e-7) with the edge's sign flipped
+ * (negative when the edge is the max), snapped to edge / rint(edge / scale)
+ * so that 0 is exact, the bias is the edge (0 when rint(edge / scale) = 0),
+ * and the codes rint((w - bias) / scale) clamped to [0, 2^bits - 1] come from
+ * the fp32 pair before it is rounded to dtype. Halves round to even. */
 MLXR_CU_API int mlxr_cu_quantize(const void* w, mlxr_cu_dtype dtype, int64_t rows, int64_t cols, int group_size, int bits,
                      const char* mode, uint32_t* wq, void* scales, void* biases, void* stream);
 

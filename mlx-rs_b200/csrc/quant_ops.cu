@@ -76,9 +76,17 @@ __device__ inline uint32_t get_code(const uint32_t* row, int64_t k, int bits) {
 }
 
 // ----------------------------------------------------------- quantize ---
-// One thread per (row, group). Affine: scale = (max-min)/(2^bits-1) and
-// bias = min, both rounded to the weight dtype; q = clamp(rint((w - bias) /
-// scale), 0, 2^bits-1) computed from the rounded pair (0 when scale == 0).
+// One thread per (row, group). MLX's affine quantiser (ml-explore/mlx
+// v0.31.2, `affine_quantize` in mlx/ops.cpp and the CPU kernel in
+// mlx/backend/cpu/quantized.cpp), in fp32 with explicitly rounded IEEE
+// operations so that the bytes do not depend on the compiler's contraction
+// or fast-math choices:
+//   scale = max((max - min) / n_bins, 1e-7), negated unless |min| > |max|;
+//   edge = min when |min| > |max|, else max;
+//   q0 = rint(edge / scale); q0 != 0: scale = edge / q0, bias = edge (zero is
+//   then exactly representable); q0 == 0: bias = 0;
+//   q = clamp(rint((w - bias) / scale), 0, n_bins) from the fp32 pair; the
+//   pair is rounded to the weight dtype only when stored.
 template <int DT>
 __global__ void quantize_kernel(const void* __restrict__ w, int64_t rows, int64_t cols, int gs, int bits,
                                 uint32_t* __restrict__ wq, void* __restrict__ scales, void* __restrict__ biases) {
@@ -94,22 +102,29 @@ __global__ void quantize_kernel(const void* __restrict__ w, int64_t rows, int64_
     mx = fmaxf(mx, v);
   }
   const float nbins = (float)((1 << bits) - 1);
-  const float sc = IO<DT>::round(__fdiv_rn(__fsub_rn(mx, mn), nbins));
-  const float bi = IO<DT>::round(mn);
-  IO<DT>::store(scales, gid, sc);
-  IO<DT>::store(biases, gid, bi);
+  const bool min_edge = fabsf(mn) > fabsf(mx);
+  float sc = fmaxf(__fdiv_rn(__fsub_rn(mx, mn), nbins), 1e-7f);
+  if (!min_edge) sc = -sc;
+  const float edge = min_edge ? mn : mx;
+  const float q0 = rintf(__fdiv_rn(edge, sc));
+  float bi = 0.0f;
+  if (q0 != 0.0f) {
+    sc = __fdiv_rn(edge, q0);
+    bi = edge;
+  }
   const int per = 32 / bits;
   uint32_t* qrow = wq + r * (cols / per) + g * gs / per;
   for (int wi = 0; wi < gs / per; ++wi) {
     uint32_t word = 0;
     for (int j = 0; j < per; ++j) {
       const float v = IO<DT>::load(w, base + wi * per + j);
-      float q = 0.0f;
-      if (sc != 0.0f) q = fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(v, bi), sc)), 0.0f), nbins);
+      const float q = fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(v, bi), sc)), 0.0f), nbins);
       word |= ((uint32_t)q) << (j * bits);
     }
     qrow[wi] = word;
   }
+  IO<DT>::store(scales, gid, sc);
+  IO<DT>::store(biases, gid, bi);
 }
 
 // --------------------------------------------------------- dequantize ---

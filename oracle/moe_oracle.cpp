@@ -127,13 +127,6 @@ inline void store_from_f32(void* p, int dt, int64_t i, float v) {
     default: ((float*)p)[i] = v;
   }
 }
-inline float round_to(int dt, float v) {
-  switch (dt) {
-    case DT_BF16: return rbf(v);
-    case DT_F16: return h2f(f2h(v));
-    default: return v;
-  }
-}
 
 // -------------------------------------------------------------- Philox ----
 // Philox4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel random numbers: as
@@ -266,10 +259,22 @@ void route_token(const float* logit, int E, int K, int renorm, int32_t* idx, uin
 // ------------------------------------------------------ affine packing ----
 // Packing: element j of a uint32 word sits in bits [bits*j, bits*j + bits)
 // (the [E, N, Kin*bits/32] layout pinned by quantization.rs:307).
-// Quantiser (quantization.rs:47, mode "affine"): per row, per group of gs
-// consecutive elements: scale = (max - min) / (2^bits - 1), bias = min, both
-// stored in the weight dtype; codes use the stored (rounded) scale and bias:
-// q = clamp(rint((w - bias) / scale), 0, 2^bits - 1), 0 when scale == 0.
+// Quantiser (quantization.rs:47-70 -> mlx_quantize, mode "affine"; the
+// converter calls it at crates/mlxr-convert/src/quantize.rs:44). The
+// arithmetic is MLX's published affine quantiser (ml-explore/mlx v0.31.2,
+// `affine_quantize` in mlx/ops.cpp and its CPU kernel in
+// mlx/backend/cpu/quantized.cpp), restated per group of gs consecutive
+// elements of a row, all in fp32:
+//   n_bins = 2^bits - 1; scale = max((max - min) / n_bins, 1e-7)
+//   edge = the end (min or max) of larger magnitude; the scale is negative
+//     when |min| <= |max| (edge = max), positive otherwise (edge = min)
+//   q0 = rint(edge / scale); if q0 != 0: scale = edge / q0, bias = edge
+//     (so that 0 = scale * (-q0) + bias is exactly representable);
+//     else bias = 0
+//   q = clamp(rint((w - bias) / scale), 0, n_bins) from the fp32 pair,
+//   and only then scale and bias are rounded to the weight dtype.
+// rint rounds halves to even (MLX's CPU kernel; its Metal kernel rounds
+// halves away from zero, which differs only on exact .5 quotients).
 // Dequantisation: w' = fmaf(scale, q, bias) in fp32.
 inline bool bits_ok(int bits) { return bits == 2 || bits == 4 || bits == 8; }
 inline bool gs_ok(int gs) { return gs == 32 || gs == 64 || gs == 128; }
@@ -377,17 +382,24 @@ ORC_API int orc_quantize(const void* w, int dt, int64_t rows, int64_t cols, int 
         mn = std::min(mn, v);
         mx = std::max(mx, v);
       }
-      const float sc = round_to(dt, (mx - mn) / nbins);
-      const float bi = round_to(dt, mn);
-      store_from_f32(scales, dt, r * ngroups + g, sc);
-      store_from_f32(biases, dt, r * ngroups + g, bi);
+      const bool min_edge = std::fabs(mn) > std::fabs(mx);
+      float sc = std::max((mx - mn) / nbins, 1e-7f);
+      if (!min_edge) sc = -sc;
+      const float edge = min_edge ? mn : mx;
+      const float q0 = std::rint(edge / sc);
+      float bi = 0.0f;
+      if (q0 != 0.0f) {
+        sc = edge / q0;
+        bi = edge;
+      }
       for (int i = 0; i < gs; ++i) {
         const float v = load_as_f32(w, dt, r * cols + g * gs + i);
-        float q = 0.0f;
-        if (sc != 0.0f) q = std::min(std::max(std::rint((v - bi) / sc), 0.0f), nbins);
+        const float q = std::min(std::max(std::rint((v - bi) / sc), 0.0f), nbins);
         const int64_t k = g * gs + i;
         qrow[k / per] |= ((uint32_t)q) << ((k % per) * bits);
       }
+      store_from_f32(scales, dt, r * ngroups + g, sc);
+      store_from_f32(biases, dt, r * ngroups + g, bi);
     }
   }
   return 0;

@@ -51,6 +51,43 @@ def test_quantize_dequantize_reference_case_f32():
         assert (x - xh).abs().max().item() <= 127.0 / (1 << bits)
 
 
+@pytest.mark.parametrize("bits", [2, 4, 8])
+def test_quantize_mlx_edge_groups_bitexact(bits):
+    """MLX's affine quantiser on the GPU: groups that are all zero, constant,
+    one-signed, spanning zero or with |min| == |max|, in bf16 and f32, equal
+    the oracle byte for byte; the scale's sign follows the larger-magnitude
+    end and the bias is that end (or 0)."""
+    from mlxr_moe import ops
+
+    w = O.bf16_to_f32(O.normal_bf16(0, 170 + bits, (32, 256), 0.02)).copy()
+    w[0, :64] = 0.0
+    w[1, :64] = 0.03125
+    w[2, :64] = -np.abs(w[2, :64])
+    w[3, :64] = np.abs(w[3, :64])
+    w[4, :64] = np.linspace(-0.5, 0.5, 64)
+    w[5, :64] = np.linspace(-1.0, 0.875, 64)
+    w[5, 1] = 0.0
+    wb = O.f32_to_bf16(w.astype(np.float32))
+    for host in (wb, O.bf16_to_f32(wb).astype(np.float32)):
+        dev = np_bf16_to_torch(host) if host.dtype == np.uint16 else torch.from_numpy(host).cuda()
+        wq, s, b = ops.quantize(dev, 64, bits)
+        oq, os_, ob = O.quantize(host, 64, bits)
+        np.testing.assert_array_equal(u32(wq), oq)
+        if host.dtype == np.uint16:
+            np.testing.assert_array_equal(bf16_np(s), os_)
+            np.testing.assert_array_equal(bf16_np(b), ob)
+            sf, bf = to_f32(os_), to_f32(ob)
+        else:
+            np.testing.assert_array_equal(s.cpu().numpy(), os_)
+            np.testing.assert_array_equal(b.cpu().numpy(), ob)
+            sf, bf = os_, ob
+        g = O.bf16_to_f32(wb).reshape(32, 4, 64)
+        mn, mx = g.min(-1), g.max(-1)
+        assert ((sf < 0) == (np.abs(mx) >= np.abs(mn))).all()
+        edge = np.where(np.abs(mn) > np.abs(mx), mn, mx)
+        assert ((bf == edge) | (bf == 0)).all()
+
+
 def test_dequantize_bf16_out_bitexact():
     from mlxr_moe import ops
 

@@ -32,6 +32,112 @@ def test_quantize_dequantize_reference_bound():
         assert np.abs(x - xh).max() <= 127.0 / (1 << bits)
 
 
+def mlx_affine_quantize_np(w32, gs, bits):
+    """Independent numpy restatement of MLX's affine quantiser (ml-explore/mlx
+    v0.31.2 `affine_quantize`, mlx/ops.cpp, CPU kernel in
+    mlx/backend/cpu/quantized.cpp), every step an IEEE fp32 operation:
+    returns codes [rows, cols] and the fp32 (scale, bias) per group."""
+    f = np.float32
+    rows, cols = w32.shape
+    g = w32.reshape(rows, cols // gs, gs).astype(f)
+    mn, mx = g.min(-1), g.max(-1)
+    nbins = f((1 << bits) - 1)
+    min_edge = np.abs(mn) > np.abs(mx)
+    sc = np.maximum((mx - mn) / nbins, f(1e-7)).astype(f)
+    sc = np.where(min_edge, sc, -sc).astype(f)
+    edge = np.where(min_edge, mn, mx).astype(f)
+    q0 = np.rint(edge / sc).astype(f)
+    nz = q0 != 0
+    with np.errstate(divide="ignore", invalid="ignore"):
+        sc = np.where(nz, edge / np.where(nz, q0, f(1)), sc).astype(f)
+    bi = np.where(nz, edge, f(0)).astype(f)
+    q = np.clip(np.rint((g - bi[..., None]) / sc[..., None]), 0, nbins).astype(np.uint32)
+    return q.reshape(rows, cols), sc, bi, q0
+
+
+def pack_codes(q, bits):
+    per = 32 // bits
+    r, c = q.shape
+    q = q.reshape(r, c // per, per).astype(np.uint64)
+    sh = (np.arange(per, dtype=np.uint64) * bits)[None, None, :]
+    return (q << sh).sum(-1).astype(np.uint32)
+
+
+@pytest.mark.parametrize("bits", [2, 4, 8])
+@pytest.mark.parametrize("gs", [32, 64, 128])
+def test_quantize_is_mlx_affine_quantize(bits, gs):
+    """The oracle's bytes equal an independent restatement of MLX's
+    affine_quantize on random bf16 groups plus edge groups (all zero,
+    constant, one-signed, spanning zero, |min| == |max|)."""
+    w = O.normal_bf16(0, 150 + bits, (64, 512), 0.02)
+    wf = O.bf16_to_f32(w).copy()
+    wf[0, :gs] = 0.0                                  # all zero: q0 == 0, bias 0
+    wf[1, :gs] = 0.03125                              # constant positive
+    wf[2, :gs] = -np.abs(wf[2, :gs])                  # all non-positive
+    wf[3, :gs] = np.abs(wf[3, :gs])                   # all non-negative
+    wf[4, :gs] = np.linspace(-0.5, 0.5, gs)           # |min| == |max|
+    wf[5, :gs] = np.linspace(-1.0, 0.875, gs)
+    wf[5, 1] = 0.0                                    # spans zero, holds a 0
+    wb = O.f32_to_bf16(wf.astype(np.float32))
+    q, s, b = O.quantize(wb, gs, bits)
+    rq, rs, rb, _ = mlx_affine_quantize_np(O.bf16_to_f32(wb), gs, bits)
+    np.testing.assert_array_equal(q, pack_codes(rq, bits))
+    np.testing.assert_array_equal(s, O.f32_to_bf16(rs))
+    np.testing.assert_array_equal(b, O.f32_to_bf16(rb))
+    # float32 input: the pair is stored unrounded
+    q32, s32, b32 = O.quantize(O.bf16_to_f32(wb).astype(np.float32), gs, bits)
+    np.testing.assert_array_equal(q32, pack_codes(rq, bits))
+    np.testing.assert_array_equal(s32, rs)
+    np.testing.assert_array_equal(b32, rb)
+
+
+def test_quantize_mlx_hand_computed_groups():
+    """Groups worked by hand (4-bit, group 8, float32 in and out)."""
+    w = np.array([
+        [-1.0, 0.0, 0.125, 0.25, 0.5, 0.625, 0.75, 0.875],   # |min| > |max|
+        [-0.5, -0.25, 0.0, 0.25, 0.5, 1.0, 1.25, 1.5],       # |max| > |min|
+        [0.0] * 8,                                           # all zero
+    ], np.float32)
+    w32 = np.tile(w, (1, 4))  # group size 32 (the smallest the ABI takes): 4 copies
+    q, s, b = O.quantize(w32, 32, 4)
+    codes = ((q[:, :, None] >> (np.arange(8, dtype=np.uint32) * 4)) & 15).reshape(3, 32)[:, :8]
+    # Row 0: scale = (0.875 + 1) / 15 = 0.125 > 0, edge = min = -1, q0 = -8,
+    # scale = -1 / -8 = 0.125, bias = -1; codes (w + 1) / 0.125; 0 -> 8 -> 0.0.
+    assert s[0, 0] == np.float32(0.125) and b[0, 0] == np.float32(-1.0)
+    np.testing.assert_array_equal(codes[0], [0, 8, 9, 10, 12, 13, 14, 15])
+    # Row 1: |max| >= |min| -> scale = -(2 / 15), edge = max = 1.5,
+    # q0 = rint(1.5 / -0.1333) = rint(-11.25) = -11, scale = 1.5 / -11 < 0,
+    # bias = 1.5; the code of 0 is rint(-1.5 / scale) = 11.
+    assert s[1, 0] == np.float32(1.5) / np.float32(-11.0) and b[1, 0] == np.float32(1.5)
+    assert codes[1, 2] == 11 and codes[1, 7] == 0
+    # Row 2: scale = -max(0, 1e-7) = -1e-7, q0 = 0 -> bias 0, codes 0.
+    assert s[2, 0] == -np.float32(1e-7) and b[2, 0] == 0.0
+    assert (codes[2] == 0).all()
+    # The code of 0 dequantises to 0 within the fp32 rounding of scale * q0.
+    for r, c0 in ((0, 8), (1, 11)):
+        assert abs(np.float32(s[r, 0]) * np.float32(c0) + b[r, 0]) <= 4 * np.finfo(np.float32).eps
+
+
+def test_quantize_mlx_properties_random():
+    """On N(0, 0.02) bf16 groups: the scale is negative exactly when
+    |max| >= |min|, the bias is the edge, and the element 0 dequantises to
+    within the bf16 rounding of the scale times |q0| of zero."""
+    w = O.normal_bf16(0, 160, (256, 1024), 0.02)
+    wf = O.bf16_to_f32(w).copy()
+    wf[:, ::64] = 0.0  # every group holds a 0
+    wb = O.f32_to_bf16(wf.astype(np.float32))
+    q, s, b = O.quantize(wb, 64, 4)
+    g = O.bf16_to_f32(wb).reshape(256, 16, 64)
+    mn, mx = g.min(-1), g.max(-1)
+    sf, bf = O.bf16_to_f32(s), O.bf16_to_f32(b)
+    assert ((sf < 0) == (np.abs(mx) >= np.abs(mn))).all()
+    edge = np.where(np.abs(mn) > np.abs(mx), mn, mx)
+    np.testing.assert_array_equal(bf, edge)
+    wh = O.dequantize(q, s, b, 64, 4).reshape(256, 16, 64)[..., 0]
+    _, rs, _, q0 = mlx_affine_quantize_np(O.bf16_to_f32(wb), 64, 4)
+    assert (np.abs(wh) <= np.abs(q0) * np.abs(rs) * 2.0**-8 + 1e-12).all()
+
+
 def test_quantized_matmul_reference_relation():
     """quantization.rs:318-341: qmm(x, w) == x @ dequant(w) within 1e-3 (transpose=false)."""
     m, n, k = 32, 128, 128
