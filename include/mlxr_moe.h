@@ -223,8 +223,11 @@ MLXR_CU_API int mlxr_cu_moe_block_forward(const mlxr_cu_moe_config* cfg, const m
  * before any stream capture. All calls share the one array, so calls that
  * overlap on the GPU (different streams or threads) race: serialise them.
  * device_status (device int, may be NULL) receives the device-side status
- * word (0 ok, 1 wait timeout, 2 index out of range) when the forward ends.
- * Nothing on this path calls cudaMalloc, cudaFree or an allocating routine. */
+ * word (0 ok, 1 wait timeout, 2 index out of range) when the forward ends;
+ * it is written (by a copy queued on the stream) only when the call returns
+ * MLXR_CU_OK, so after an error it still holds what it held before. The
+ * array's address is cached per device and driver context. Nothing on this
+ * path calls cudaMalloc, cudaFree or an allocating routine. */
 MLXR_CU_API int mlxr_cu_moe_block_forward_noalloc(const mlxr_cu_moe_config* cfg,
                                                   const mlxr_cu_moe_weights* weights, const void* x,
                                                   int64_t num_tokens, void* out,
@@ -247,7 +250,12 @@ MLXR_CU_API int mlxr_cu_moe_status(const void* workspace, void* stream);
 /* Reads and clears (synchronising on stream) the device status word the op
  * family (quantize ... gather_mm) shares on the current device:
  * MLXR_CU_ERR_DEVICE_INDEX when an lhs/rhs index was outside its batch (the
- * affected output blocks are left unwritten). */
+ * affected output blocks are left unwritten). There is one such word per
+ * device for all host threads and streams: when ops run concurrently on
+ * several streams, a status raised by one of them may be reported to (and
+ * cleared by) a caller checking another, so check it with those streams
+ * serialised. The block entry points keep their status in their own
+ * workspace instead. */
 MLXR_CU_API int mlxr_cu_op_status(void* stream);
 
 /* Router alone (moe.rs:123-138): logits = x @ gate^T (+bias) rounded to
@@ -370,7 +378,13 @@ MLXR_CU_API int mlxr_cu_moe_ep_combine(const mlxr_cu_moe_config* cfg, const mlxr
  *     up each token's partial rows.
  * No host synchronisation is needed between the steps. A rank that never
  * publishes makes the others' waits expire after 10 s with
- * MLXR_CU_ERR_TIMEOUT in the status word. Ranks must be on different GPUs. */
+ * MLXR_CU_ERR_TIMEOUT in the status word. A rank whose own status word is
+ * already non-zero when it publishes (a wait of its own expired, or it
+ * skipped a bad index) publishes a poisoned flag instead, and every rank that
+ * waits on it records the failure (mlxr_cu_moe_status then returns
+ * MLXR_CU_ERR_TIMEOUT with a message naming a failed peer) instead of using
+ * the rows. epoch must be in [1, 2^31) and grow by step; the top bit marks
+ * the poison. Ranks must be on different GPUs. */
 #define MLXR_CU_IPC_HANDLE_BYTES 64
 
 MLXR_CU_API int mlxr_cu_ep_comm_create(int world, int rank, int64_t cap, int hidden, int k, void** comm,

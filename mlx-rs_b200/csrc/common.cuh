@@ -83,6 +83,7 @@ enum DeviceStatus : int {
   kDevTimeout = 1,      // a bounded wait gave up
   kDevBadIndex = 2,     // an index outside [0, E) or a row outside its range
   kDevTmemAlloc = 3,    // tensor-memory allocation failed
+  kDevPeerFailed = 4,   // another rank published a poisoned flag: its side of the step failed
 };
 
 // ------------------------------------------------------------- bf16 -----

@@ -675,11 +675,31 @@ constexpr size_t kNoAllocScratchBytes = size_t(24) << 20;  // 24 MiB
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
 // Host code cannot use g_noalloc_scratch as a device address (in host code it
-// names a host-side stand-in). The device address is looked up once per
-// device, with that device current, and cached.
+// names a host-side stand-in). The device address is looked up with
+// cudaGetSymbolAddress once per device, with that device current, and cached
+// together with the driver context it belongs to: the module (and with it the
+// array) is loaded per context, so a caller that switches to another context
+// on the same device (or recreates the primary one after cudaDeviceReset)
+// gets a fresh lookup instead of a stale address.
+typedef int (*PFN_ctx_get_current)(void**);
+
+static PFN_ctx_get_current ctx_get_current_fn() {
+  static PFN_ctx_get_current fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_ctx_get_current>(p);
+  });
+  return fn;
+}
+
 static void* noalloc_scratch(int* rc) {
   static std::mutex mu;
   static void* ptrs[128] = {};
+  static void* ctxs[128] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) {
@@ -690,8 +710,23 @@ static void* noalloc_scratch(int* rc) {
     *rc = set_error(MLXR_CU_ERR_CUDA, "moe_noalloc: device ordinal %d out of range", dev);
     return nullptr;
   }
+  // Which driver context is current (cudaSetDevice makes the device's
+  // primary context current when none is).
+  void* ctx = nullptr;
+  PFN_ctx_get_current get_ctx = ctx_get_current_fn();
+  if (!get_ctx || get_ctx(&ctx) != 0) {
+    *rc = set_error(MLXR_CU_ERR_CUDA, "moe_noalloc: cuCtxGetCurrent is not available from the driver");
+    return nullptr;
+  }
+  if (!ctx) {
+    e = cudaSetDevice(dev);
+    if (e != cudaSuccess || get_ctx(&ctx) != 0 || !ctx) {
+      *rc = check_cuda(e != cudaSuccess ? e : cudaErrorDeviceUninitialized, "cudaSetDevice (no current context)");
+      return nullptr;
+    }
+  }
   std::lock_guard<std::mutex> lock(mu);
-  if (!ptrs[dev]) {
+  if (!ptrs[dev] || ctxs[dev] != ctx) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) {
@@ -699,6 +734,7 @@ static void* noalloc_scratch(int* rc) {
       return nullptr;
     }
     ptrs[dev] = p;
+    ctxs[dev] = ctx;
   }
   *rc = MLXR_CU_OK;
   return ptrs[dev];
@@ -736,6 +772,10 @@ int mlxr_cu_moe_status(const void* workspace, void* stream) {
     case kDevOk: return MLXR_CU_OK;
     case kDevTimeout: return set_error(MLXR_CU_ERR_TIMEOUT, "moe: a device-side wait timed out");
     case kDevBadIndex: return set_error(MLXR_CU_ERR_DEVICE_INDEX, "moe: an expert index was outside [0, num_experts)");
+    case kDevPeerFailed:
+      return set_error(MLXR_CU_ERR_TIMEOUT,
+                       "moe: another rank reported a failed step (its wait timed out or it skipped a bad index); "
+                       "the rows it exchanged in this step are not valid");
     default: return set_error(MLXR_CU_ERR_CUDA, "moe: device status %d", v);
   }
 }
@@ -1158,6 +1198,7 @@ int mlxr_cu_moe_ep_dispatch_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe
                                 const int32_t* placement, const void* x, int64_t num_tokens, int32_t* pair_pos,
                                 float* shared_gate, uint32_t epoch, void* workspace, size_t workspace_bytes,
                                 void* stream) {
+  MLXR_CHECK_ARG(epoch >= 1 && epoch < EP_FLAG_POISON, "moe_ep: epoch=%u must be in [1, 2^31)", epoch);
   if (int rc = validate(cfg, num_tokens)) return rc;
   if (int rc = ep_comm_check(comm, cfg)) return rc;
   EpComm* c = static_cast<EpComm*>(comm);
@@ -1222,6 +1263,7 @@ int mlxr_cu_moe_ep_dispatch_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe
 int mlxr_cu_moe_ep_experts_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* local_weights,
                                int num_local_experts, void* comm, int64_t expected_rows, uint32_t epoch,
                                void* workspace, size_t workspace_bytes, void* stream) {
+  MLXR_CHECK_ARG(epoch >= 1 && epoch < EP_FLAG_POISON, "moe_ep: epoch=%u must be in [1, 2^31)", epoch);
   if (int rc = ep_comm_check(comm, cfg)) return rc;
   EpComm* c = static_cast<EpComm*>(comm);
   MLXR_CHECK_ARG(local_weights != nullptr && num_local_experts >= 1 && num_local_experts <= cfg->num_experts,
@@ -1260,6 +1302,7 @@ int mlxr_cu_moe_ep_experts_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_
 int mlxr_cu_moe_ep_combine_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights, void* comm,
                                const void* x, int64_t num_tokens, const int32_t* pair_pos, const float* shared_gate,
                                void* out, uint32_t epoch, void* workspace, size_t workspace_bytes, void* stream) {
+  MLXR_CHECK_ARG(epoch >= 1 && epoch < EP_FLAG_POISON, "moe_ep: epoch=%u must be in [1, 2^31)", epoch);
   if (int rc = validate(cfg, num_tokens)) return rc;
   if (int rc = ep_comm_check(comm, cfg)) return rc;
   EpComm* c = static_cast<EpComm*>(comm);

@@ -282,8 +282,11 @@ __global__ void synth_normal_kernel(uint64_t seed, uint64_t stream_id, int64_t n
   if (2 * p + 1 < n) out[2 * p + 1] = f32_to_bf16_bits((float)(rad * sin(th) * (double)stddev));
 }
 
-// Per-thread status word for the op family (no workspace in these ABIs):
-// a small device allocation made once per device by the first call.
+// Device address of the op family's status word (these ABIs take no
+// workspace): one file-scope __device__ int per device, shared by every host
+// thread and stream that calls the op family on that device. Ops running
+// concurrently on several streams race on it: a bad index seen by one can be
+// read (and cleared) by mlxr_cu_op_status called for another.
 int* op_status_word();
 
 }  // namespace mlxr

@@ -1303,6 +1303,14 @@ struct EpPeers {
   uint8_t* base[EP_MAX_WORLD];  // every rank's exchange buffer as seen from this GPU
 };
 
+// Flag values. A rank publishes the step's epoch (1 <= epoch < 2^31) when
+// its side of the step went well, and the epoch with the top bit set (a
+// poisoned flag) when its own status word was already non-zero: a wait that
+// expired, or an index it skipped. Receivers that see a poisoned flag record
+// kDevPeerFailed instead of reading the rows, so one rank's failure reaches
+// every rank's status word rather than passing partial rows on as valid.
+constexpr uint32_t EP_FLAG_POISON = 0x80000000u;
+
 __device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -1363,13 +1371,16 @@ __global__ void __launch_bounds__(256) ep_send_kernel(EpPeers peers, EpBufLayout
     reinterpret_cast<volatile int32_t*>(b + bl.counts)[me] = s_off[r + 1] - s_off[r];
     reinterpret_cast<volatile int32_t*>(b + bl.rows)[me] = send_counts[2 * r + 1];
     __threadfence_system();
-    st_release_sys_u32(reinterpret_cast<uint32_t*>(b + bl.flag_disp) + me, epoch);
+    const uint32_t failed = *reinterpret_cast<volatile int*>(status) != 0 ? EP_FLAG_POISON : 0u;
+    st_release_sys_u32(reinterpret_cast<uint32_t*>(b + bl.flag_disp) + me, epoch | failed);
   }
   if (threadIdx.x == 0) *done = 0;
 }
 
 // One CTA: wait until every rank has published `epoch` in flags[0..world)
 // (bounded; on expiry the status records a timeout and the data is not used).
+// A poisoned flag of this epoch ends the wait for that rank with
+// kDevPeerFailed in the status word.
 __global__ void ep_wait_flags_kernel(const uint32_t* __restrict__ flags, int world, uint32_t epoch,
                                      unsigned long long limit_ns, int* status) {
   pdl_wait();
@@ -1377,7 +1388,12 @@ __global__ void ep_wait_flags_kernel(const uint32_t* __restrict__ flags, int wor
   if (threadIdx.x < world) {
     const unsigned long long t0 = global_ns();
     for (uint32_t it = 0;; ++it) {
-      if ((int32_t)(ld_acquire_sys_u32(flags + threadIdx.x) - epoch) >= 0) break;
+      const uint32_t v = ld_acquire_sys_u32(flags + threadIdx.x);
+      const uint32_t e = v & ~EP_FLAG_POISON;
+      if (e >= epoch) {
+        if (v & EP_FLAG_POISON) atomicCAS(status, 0, (int)kDevPeerFailed);
+        break;
+      }
       if ((it & 63u) == 63u && global_ns() - t0 > limit_ns) {
         atomicCAS(status, 0, (int)kDevTimeout);
         break;
@@ -1470,8 +1486,10 @@ __global__ void __launch_bounds__(256) ep_reduce_send_kernel(EpPeers peers, EpBu
   __syncthreads();
   if (!s_last) return;
   __threadfence_system();
-  if (threadIdx.x < world)
-    st_release_sys_u32(reinterpret_cast<uint32_t*>(peers.base[threadIdx.x] + bl.flag_back) + me, epoch);
+  if (threadIdx.x < world) {
+    const uint32_t failed = *reinterpret_cast<volatile int*>(status) != 0 ? EP_FLAG_POISON : 0u;
+    st_release_sys_u32(reinterpret_cast<uint32_t*>(peers.base[threadIdx.x] + bl.flag_back) + me, epoch | failed);
+  }
   if (threadIdx.x == 0) *done = 0;
 }
 

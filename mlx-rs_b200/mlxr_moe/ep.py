@@ -234,7 +234,9 @@ class ExpertParallelMoeBlock:
             self._ws = torch.empty(max(int(n.value), 256), dtype=torch.uint8, device=x.device)
         ws = self._ws
         comm.epoch += 1
-        ep = comm.epoch & 0xFFFFFFFF
+        if comm.epoch >= 1 << 31:  # the flag's top bit marks a failed step
+            raise _lib.MlxrError(_lib.ERR_INVALID_ARGUMENT, "peer communicator ran out of epochs; recreate it")
+        ep = comm.epoch
         st = torch.cuda.current_stream(x.device).cuda_stream
         pair_pos = torch.empty(max(T * K, 1), dtype=torch.int32, device=x.device)
         sg = torch.empty(max(T, 1), dtype=torch.float32, device=x.device) if self.shared_expert is not None else None

@@ -115,31 +115,58 @@ def test_c3_prefill_zipf_full_size():
     assert c.sum() == 4096 * 8 and c.max() > 4 * c.mean()
 
 
-def test_c4_wide_experts_with_shared_subset_and_full_properties():
+def check_full_batch_prefix(blk, ow, x, n, staged=False):
+    """Runs the whole batch x on the GPU (so the tile widths and kernel
+    variants are those of the full size) and compares its first n rows
+    directly with the oracle run on x[:n]: tokens are independent, so the
+    oracle's cost depends on n only. Routing is checked for every token."""
+    cfg, W = ow
+    out_full, r = run_gpu_block(blk, x)
+    xo = bf16_np(x)
+    oi, ow_ = O.router(xo, W["router"], cfg["top_k"], W.get("router_bias"))
+    np.testing.assert_array_equal(r.indices.cpu().numpy(), oi)
+    np.testing.assert_array_equal(bf16_np(r.weights), ow_)
+    o_fu, idx, _ = O.moe_block(cfg, W, xo[:n], "fused")
+    np.testing.assert_array_equal(oi[:n], idx)
+    got = bf16_np(out_full[:n])
+    assert_close_bf16(got, o_fu, ATOL, RTOL, "full batch prefix vs fused oracle")
+    assert_mostly_tight(got, o_fu, FUSED_ATOL, FUSED_RTOL, FUSED_MAX_FRAC, "full batch prefix vs fused oracle (tight)")
+    if staged:
+        o_st, _, _ = O.moe_block(cfg, W, xo[:n], "staged")
+        assert_close_bf16(got, o_st, ATOL, RTOL, "full batch prefix vs staged oracle")
+    assert torch.isfinite(out_full.float()).all()
+    return out_full, r
+
+
+def test_c4_wide_experts_with_shared_full_size():
+    """C4 at its full 16384 tokens (8-bit, E=512, 320 rows per expert: the
+    128-token prefill tiles) against the oracle on its first 1024 tokens, and
+    a 1024-token batch alone (the decode-width tiles) the same way."""
     blk, ow = block_for("c4")
     x = synth.make_input(16384, 2048)
-    # parity on a 1024-token slice (the oracle finishes in seconds)
-    check_block(blk, ow, x[:1024].contiguous(), staged=True)
-    # full size: routing bit-exact, tokens independent of their batch
-    out_full, r = run_gpu_block(blk, x)
-    oi, ow_ = O.router(bf16_np(x), bf16_np(blk.gate), 10)
-    np.testing.assert_array_equal(r.indices.cpu().numpy(), oi)
-    out_part, _ = run_gpu_block(blk, x[:1024].contiguous())
-    assert_close_bf16(bf16_np(out_full[:1024]), bf16_np(out_part), 1e-2, 1e-2, "batch independence")
-    assert torch.isfinite(out_full.float()).all()
+    check_full_batch_prefix(blk, ow, x, 1024, staged=True)
+    check_block(blk, ow, x[:1024].contiguous(), staged=False)
 
 
-def test_c5_large_block_decode_and_prefill_slice():
+def test_c5_large_block_decode_and_full_prefill():
+    """C5: the 256-token decode batch in full, and the 8192-token Zipf prefill
+    at full size (D=4096, I=1536, 128-token tiles) against the oracle on its
+    first 512 tokens."""
     blk, ow = block_for("c5")
     check_block(blk, ow, synth.make_input(256, 4096, stream_offset=1), staged=False)
     x = synth.make_input(8192, 4096)
-    check_block(blk, ow, x[:512].contiguous(), staged=False)
-    out_full, r = run_gpu_block(blk, x)
-    bias = blk.router_bias.cpu().numpy()
-    oi, _ = O.router(bf16_np(x), bf16_np(blk.gate), 8, bias)
-    np.testing.assert_array_equal(r.indices.cpu().numpy(), oi)
-    out_part, _ = run_gpu_block(blk, x[:512].contiguous())
-    assert_close_bf16(bf16_np(out_full[:512]), bf16_np(out_part), 1e-2, 1e-2, "batch independence")
+    check_full_batch_prefix(blk, ow, x, 512)
+
+
+@pytest.mark.parametrize("bits,D", [(8, 384), (4, 384), (8, 512)])
+def test_wide_tiles_against_oracle(bits, D):
+    """Batches with 256 rows per expert so that the widest token tiles run
+    (256-token down tiles when D is not a multiple of 256, 128-token gate/up
+    tiles otherwise), with a shared expert, in full against the oracle."""
+    cfg = MoeConfig(D, 16, 4, 256, 256, 64, bits, bits)
+    blk = synth.make_block(cfg, 21, False)
+    ow = block_to_oracle(blk)
+    check_block(blk, ow, synth.make_input(1024, D, stream_offset=21), staged=True)
 
 
 def test_edge_cases_empty_ragged_and_hot_expert():

@@ -285,3 +285,104 @@ def test_ep_loopback_gemma4_branch(T, world):
         torch.cuda.synchronize()
         assert_close_bf16(bf16_np(outs[r]), bf16_np(want), ATOL, RTOL, f"rank {r}")
         assert_mostly_tight(bf16_np(outs[r]), bf16_np(want), TIGHT_ATOL, TIGHT_RTOL, TIGHT_FRAC, f"rank {r} tight")
+
+
+class _OneRankComm:
+    """A peer-memory communicator of world 1 (no other process, no IPC): the
+    rank's own exchange buffer, created through the C ABI."""
+
+    def __init__(self, cap, hidden, k):
+        import ctypes as C
+
+        from mlxr_moe import _lib
+
+        self.comm, self.cap, self.epoch = C.c_void_p(), cap, 0
+        handle = (C.c_uint8 * 64)()
+        _lib.call("mlxr_cu_ep_comm_create", 1, 0, cap, hidden, k, C.byref(self.comm), handle)
+
+    def close(self):
+        from mlxr_moe import _lib
+
+        _lib.call("mlxr_cu_ep_comm_destroy", self.comm)
+
+
+def test_ep_p2p_one_rank_step_timeout_and_poisoned_flag():
+    """The peer-memory step on one GPU with a world-1 communicator: a normal
+    step matches the one-device block; an expert step whose epoch no dispatch
+    published lets its bounded wait run out and reports MLXR_CU_ERR_TIMEOUT;
+    a step whose expert side already failed publishes a poisoned flag, and the
+    combine that waits on it reports the failed peer. Every wait here either
+    finds its flag set or expires on its own limit."""
+    import ctypes as C
+
+    from mlxr_moe import _lib
+
+    full = block_for("c2")
+    cfg = full.cfg
+    blk = ExpertParallelMoeBlock.from_block(full, 0, 1)
+    comm = _OneRankComm(64, cfg.hidden_size, cfg.num_experts_per_tok)
+    try:
+        x = synth.make_input(40, cfg.hidden_size, stream_offset=77)
+        out = blk.forward_p2p(x, comm)
+        want = full.forward(x)
+        torch.cuda.synchronize()
+        blk.status()
+        assert_close_bf16(bf16_np(out), bf16_np(want), ATOL, RTOL, "one-rank p2p step")
+
+        ws = blk._ws
+        st = torch.cuda.current_stream().cuda_stream
+        K, T = cfg.num_experts_per_tok, x.shape[0]
+        n_loc = len(blk.experts_here)
+        pair_pos = torch.empty(T * K, dtype=torch.int32, device="cuda")
+
+        def experts(epoch):
+            _lib.call("mlxr_cu_moe_ep_experts_p2p", C.byref(blk._ccfg), C.byref(blk._cw_loc), n_loc, comm.comm,
+                      comm.cap * K, epoch, ws.data_ptr(), ws.numel(), st)
+
+        def dispatch(epoch):
+            _lib.call("mlxr_cu_moe_ep_dispatch_p2p", C.byref(blk._ccfg), C.byref(blk._cw_rep), comm.comm,
+                      blk.placement.data_ptr(), x.data_ptr(), T, pair_pos.data_ptr(), None, epoch,
+                      ws.data_ptr(), ws.numel(), st)
+
+        def combine(epoch):
+            _lib.call("mlxr_cu_moe_ep_combine_p2p", C.byref(blk._ccfg), C.byref(blk._cw_rep), comm.comm,
+                      x.data_ptr(), T, pair_pos.data_ptr(), None, out.data_ptr(), epoch, ws.data_ptr(),
+                      ws.numel(), st)
+
+        # 1. No dispatch published epoch 3: the expert step's wait expires.
+        dispatch(2)
+        experts(2)
+        combine(2)
+        blk.status()
+        experts(3)
+        with pytest.raises(_lib.MlxrError) as e:
+            blk.status()
+        assert e.value.status == _lib.ERR_TIMEOUT
+
+        # 2. Epoch 4: dispatch is fine, but the status word holds a failure
+        # when the expert step publishes, so its flag is poisoned; the combine
+        # (status cleared first) finds the poison and reports the failed peer.
+        dispatch(4)
+        ws[:4].view(torch.int32).fill_(2)
+        experts(4)
+        ws[:4].view(torch.int32).zero_()
+        combine(4)
+        with pytest.raises(_lib.MlxrError) as e:
+            blk.status()
+        assert e.value.status == _lib.ERR_TIMEOUT and "another rank" in e.value.what
+
+        # 3. Epochs outside [1, 2^31) are refused on the host.
+        with pytest.raises(_lib.MlxrError):
+            experts(0x80000001)
+        _lib.LIB.mlxr_cu_clear_error()
+
+        # 4. The next clean step works again.
+        dispatch(5)
+        experts(5)
+        combine(5)
+        torch.cuda.synchronize()
+        blk.status()
+        assert_close_bf16(bf16_np(out), bf16_np(want), ATOL, RTOL, "one-rank p2p step after the failures")
+    finally:
+        torch.cuda.synchronize()
+        comm.close()

@@ -12,7 +12,9 @@ import numpy as np
 import pytest
 import torch
 
+import oracle as O
 from conftest import ATOL, RTOL, assert_close_bf16, bf16_np
+from gpu_helpers import block_to_oracle
 
 pytestmark = pytest.mark.gpu
 
@@ -29,6 +31,7 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls():
     from mlxr_moe import _lib, synth
 
     blk = synth.make_block(synth.CONFIGS["c2"]["cfg"], seed=0)
+    cfg, W = block_to_oracle(blk)
     status = torch.full((1,), -1, dtype=torch.int32, device="cuda")
     for call, (T, offset) in enumerate(((64, 31), (8, 32))):  # two calls in a row, different inputs
         x = synth.make_input(T, 2048, stream_offset=offset)
@@ -39,6 +42,9 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls():
         torch.cuda.synchronize()
         assert int(status.item()) == 0, f"device status {int(status.item())} on call {call}"
         assert_close_bf16(bf16_np(got), bf16_np(want), ATOL, RTOL, f"noalloc call {call}")
+        # and directly against the CPU oracle on the same inputs
+        o_fu, _, _ = O.moe_block(cfg, W, bf16_np(x), "fused")
+        assert_close_bf16(bf16_np(got), o_fu, ATOL, RTOL, f"noalloc call {call} vs oracle")
 
 
 def test_noalloc_rejects_batches_beyond_its_scratch():
