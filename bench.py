@@ -2,24 +2,30 @@
 
 `python bench.py --gpus N --steps K --warmup W` prints ONE JSON line.
 
-Workload (the decode sweep): the Qwen 3.5/3.6 MoE
-block with hidden 2048, 128 experts, top-8, expert intermediate 768, 4-bit
-affine gs64 experts, bf16 router; one step = one block forward at each token
-batch T in {1, 8, 64} on fresh inputs (73 tokens per step per GPU). Each
-forward is a captured CUDA graph of the library's block call. L2 is flushed
-(a 512 MiB write) before every forward; only the forwards are timed, with
-CUDA events on the launching stream. N > 1: one process per GPU, each serving
-its own decode batches with the experts replicated (the decode sweep's units,
-token batches, are independent: no data-path collective), "scaling": "weak",
-value = all tokens / max-over-ranks time. At N > 1 the line also carries
-"expert_parallel": the largest configurations (C5 prefill 8192 tokens, C4
-16384 tokens, C5 decode 256) run expert-parallel over the N ranks with NCCL
-all-to-all dispatch and combine, strong scaling, beside the same batch on one
-GPU measured in the same run.
+Workload (C5, the largest configuration): the Qwen
+3.5/3.6 MoE block with hidden 4096, 128 experts, top-8, expert intermediate
+1536, 4-bit affine gs64 experts, bf16 router, Zipf(1.1)-skewed routing. One
+step = one block forward over an 8192-token prefill batch plus one over a
+256-token decode batch (8448 tokens), on fresh inputs (two input sets
+alternate). L2 is flushed (a 512 MiB write) before every forward; only the
+forwards are timed, with CUDA events on the launching stream.
+
+N = 1: each forward is a captured CUDA graph of the library's block call.
+N > 1: the same C5 step, expert-parallel over the N ranks (one process per
+GPU): every rank routes 8192/N prefill and 256/N decode tokens, experts are
+placed by measured load, and pairs and partial rows cross NVLink inside the
+library's kernels (peer memory, no collective library on the data path).
+Strong scaling: the total batch is fixed, value = 8448 tokens per step / the
+max-over-ranks step time.
+
+The other configurations (the C2 decode sweep with its HBM roofline, C1, C3,
+C4 and the Gemma 4 branch) are reported under "extra" at N = 1; at N > 1 the
+same C5 step over NCCL all-to-all and the C4 block run expert-parallel under
+"expert_parallel".
 
 `--impl reference` times the CPU restatement of the reference block (the
 reference's own MLX CPU path cannot be built here) on the host cores, on a
-bounded sample of the same workload.
+bounded sample of the same C5 step.
 """
 from __future__ import annotations
 
@@ -35,11 +41,16 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "mlx-rs_b200"))
 
-WORKLOAD = "c2"
-BATCHES = [1, 8, 64]
-METRIC = "MoE-block tokens/s (decode sweep T=1,8,64; D=2048 E=128 K=8 I=768 q4 gs64)"
+HEADLINE = "c5"
+PREFILL_T, DECODE_T = 8192, 256
+STEP_TOKENS = PREFILL_T + DECODE_T
+METRIC = ("MoE-block tokens/s (C5: D=4096 E=128 K=8 I=1536 q4 gs64, Zipf(1.1) routing; "
+          "one step = 8192-token prefill + 256-token decode forward)")
 UNIT = "tokens/s"
 L2_FLUSH_BYTES = 512 << 20
+DATA = ("synthetic (Philox seed 0): experts N(0,0.02) bf16 -> 4-bit affine gs64 (MLX affine_quantize), "
+        "router bf16 N(0,0.02) + fixed Zipf(1.1) logit bias, x N(0,1) bf16")
+C2_BATCHES = [1, 8, 64]
 
 
 def measured_peaks():
@@ -182,6 +193,337 @@ def distinct_experts(routing) -> int:
 
 
 # ---------------------------------------------------------------- GPU arm ----
+def ep_kernels_per_forward(cfg, T: int, world: int) -> int:
+    """Library kernels one expert-parallel peer-memory step launches on a rank
+    with T tokens (the launch choices of the three p2p entry points)."""
+    K = cfg.num_experts_per_tok
+    n = (2 if T > 256 else 1) if T else 0                      # router
+    n += 1                                                     # ep_pair_dest
+    n += 1 if T * K <= 2048 else 3                             # permute of the pairs by rank
+    n += 3                                                     # ep_counts, ep_pair_meta, ep_send
+    n += 2                                                     # wait, ep_slot_expert
+    n += 1 if world * T * K <= 2048 else 3                     # permute of the received slots
+    n += 1 + 2 + 1                                             # row gather, gate|up, down, reduce_send
+    n += 2                                                     # wait, combine
+    if cfg.shared_expert_intermediate_size:
+        n += 1 + 2 + (1 if (T < 256 or (cfg.shared_bits or cfg.bits) == 4) else 0)
+    return n
+
+
+class _Timer:
+    """CUDA events around each timed forward on the launching stream."""
+
+    def __init__(self, torch, st):
+        self.torch, self.st, self.pairs = torch, st, []
+
+    def begin(self):
+        a = self.torch.cuda.Event(enable_timing=True)
+        a.record(self.st)
+        return a
+
+    def end(self, a, key):
+        b = self.torch.cuda.Event(enable_timing=True)
+        b.record(self.st)
+        self.pairs.append((key, a, b))
+
+    def totals(self):
+        out = {}
+        for key, a, b in self.pairs:
+            out.setdefault(key, []).append(a.elapsed_time(b))
+        return out
+
+
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+
+    from mlxr_moe import synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(dev)
+    peaks = measured_peaks()
+    # Everything (weight synthesis, inputs, workspaces, forwards) runs on one
+    # stream, so the caching allocator never hands a buffer that pending work
+    # on another stream still touches to the block.
+    st = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(st)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    spec = synth.CONFIGS[HEADLINE]
+    cfg = spec["cfg"]
+    blk = synth.make_block(cfg, seed=0, zipf=spec["zipf"], device=dev)
+    torch.cuda.synchronize(dev)
+    if world == 1:
+        head = headline_one_gpu(args, torch, dev, st, flush, blk, peaks)
+    else:
+        head = headline_ep(args, torch, dist, dev, st, flush, blk, world, rank)
+
+    extra, ep_extra, cpu = {}, None, None
+    if world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(blk, head.pop("_inputs"), args)
+    head.pop("_inputs", None)
+    del blk
+    torch.cuda.empty_cache()
+    if world == 1 and not args.no_extra:
+        extra = bench_extra(args, dev, st, flush, peaks)
+    if world > 1 and not args.no_extra:
+        ep_extra = bench_ep_extra(args, dev, st, world, rank)
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": head["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": DATA,
+            "config": {"workload": "c5: one block forward over 8192 prefill tokens + one over 256 decode tokens "
+                                   "per step (Zipf(1.1) routing)",
+                       "hidden": cfg.hidden_size, "experts": cfg.num_experts, "top_k": cfg.num_experts_per_tok,
+                       "moe_intermediate": cfg.moe_intermediate_size, "bits": cfg.bits,
+                       "group_size": cfg.group_size, "prefill_tokens": PREFILL_T, "decode_tokens": DECODE_T,
+                       "l2": "flushed before every forward (512 MiB write); weights 1.36 GB > L2",
+                       "graphs": head["graphs"], "parallelism": head["parallelism"]},
+            "roofline": head.get("roofline"),
+            "cpu_baseline": cpu,
+            "e2e": head["e2e"],
+            "gpu_launches": head["gpu_launches"],
+            "clocks": head["clocks"],
+            "forwards": head["forwards"],
+            "extra": extra,
+            "expert_parallel": ep_extra,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def headline_one_gpu(args, torch, dev, st, flush, blk, peaks):
+    """The C5 step on one GPU: two captured graphs (prefill 8192, decode 256)."""
+    from mlxr_moe import synth
+    from mlxr_moe.moe import Routing
+    import ctypes as C
+
+    from mlxr_moe import _lib
+
+    cfg = blk.cfg
+    D, K, I = cfg.hidden_size, cfg.num_experts_per_tok, cfg.moe_intermediate_size
+    nsets = 2
+    G = {}
+    with torch.cuda.stream(st):
+        for name, T in (("prefill", PREFILL_T), ("decode", DECODE_T)):
+            xs = [synth.make_input(T, D, seed=0, stream_offset=(10 if name == "prefill" else 20) + i, device=dev)
+                  for i in range(nsets)]
+            x_static = torch.empty_like(xs[0])
+            out = torch.empty_like(xs[0])
+            ws = torch.empty(blk.workspace_bytes(T), dtype=torch.uint8, device=dev)
+            x_static.copy_(xs[0])
+            for _ in range(2):  # warm: sets kernel attributes outside capture
+                blk.forward(x_static, out=out, workspace=ws)
+            torch.cuda.synchronize(dev)
+            blk.status(ws)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=st):
+                blk.forward(x_static, out=out, workspace=ws)
+            r = Routing(T, K, cfg.num_experts, dev)
+            blk.forward(xs[0], routing=r, workspace=ws)
+            torch.cuda.synchronize(dev)
+            blk.status(ws)
+            G[name] = dict(T=T, x=xs, xs=x_static, out=out, ws=ws, g=g, U=distinct_experts(r),
+                           rows_max=int(r.counts.max().item()))
+
+    def run_steps(nsteps, timer=None):
+        with torch.cuda.stream(st):
+            for s in range(nsteps):
+                for name in ("prefill", "decode"):
+                    g = G[name]
+                    g["xs"].copy_(g["x"][s % nsets])
+                    flush.fill_(s & 0xFF)
+                    a = timer.begin() if timer else None
+                    g["g"].replay()
+                    if timer:
+                        timer.end(a, name)
+
+    run_steps(args.warmup)
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(smi_id(torch, dev))
+    clocks.start()
+    timer = _Timer(torch, st)
+    run_steps(args.steps, timer)
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    tt = timer.totals()
+    total_ms = sum(sum(v) for v in tt.values())
+    value = STEP_TOKENS * args.steps / (total_ms / 1e3)
+
+    # Live per-stage timing (stage events recorded between the kernels of a
+    # second captured graph of each forward).
+    stage = {n: stage_times(torch, C, _lib, blk, G[n]["x"], G[n]["xs"], G[n]["out"], G[n]["ws"], st, flush,
+                            max(5, args.steps // 2), dev) for n in G}
+
+    # e2e: the same step through the public API with pinned host buffers:
+    # x copied in and the output copied back inside the timed region.
+    host_in = {n: [G[n]["x"][i].cpu().pin_memory() for i in range(nsets)] for n in G}
+    host_out = {n: torch.empty_like(G[n]["out"], device="cpu").pin_memory() for n in G}
+    etimer = _Timer(torch, st)
+    with torch.cuda.stream(st):
+        for s in range(args.warmup + args.steps):
+            for n in ("prefill", "decode"):
+                g = G[n]
+                flush.fill_(s & 0xFF)
+                a = etimer.begin()
+                g["xs"].copy_(host_in[n][s % nsets], non_blocking=True)
+                g["g"].replay()
+                host_out[n].copy_(g["out"], non_blocking=True)
+                if s >= args.warmup:
+                    etimer.end(a, n)
+                else:
+                    etimer.end(a, "warm")
+    torch.cuda.synchronize(dev)
+    et = etimer.totals()
+    e2e_ms = sum(et["prefill"]) + sum(et["decode"])
+    e2e = {"value": STEP_TOKENS * args.steps / (e2e_ms / 1e3), "unit": UNIT,
+           "h2d_bytes_per_step": STEP_TOKENS * D * 2, "d2h_bytes_per_step": STEP_TOKENS * D * 2,
+           "note": "pinned host x -> device, graph replay of Qwen35MoeBlock.forward (mlxr_cu_moe_block_forward), "
+                   "out -> pinned host, per forward"}
+
+    # Roofline of the dominant kernel: the prefill forward's expert GEMMs
+    # (grouped_dequant_gemm_kernel, gate|up + SwiGLU then down: two launches),
+    # tensor-bound. Algorithmic FLOPs = 2 * 3 * I * D per routed row, rows =
+    # 8192 tokens x top-8 (no padding counted).
+    R = PREFILL_T * K
+    gemm_flops = 2 * 3 * I * D * R
+    gemm_ms = stage["prefill"]["gate_up_ms"] + stage["prefill"]["down_ms"]
+    achieved = gemm_flops / (gemm_ms / 1e3) / 1e12
+    tr = ncu_traffic("experts_c5_prefill")
+    roofline = dict(bound="tensor", achieved=achieved, peak=peaks["bf16_tflops"], unit="TFLOP/s",
+                    frac=achieved / peaks["bf16_tflops"], traffic=tr,
+                    kernel="grouped_dequant_gemm_kernel: the C5 prefill forward's expert GEMMs (gate|up + SwiGLU, "
+                           "then down), 8192 tokens x top-8 = 65536 routed rows",
+                    peak_source=peaks["source"] + " bf16_tflops (cuBLAS burst)",
+                    algorithmic_flops_per_forward=gemm_flops,
+                    gate_up_ms=stage["prefill"]["gate_up_ms"], down_ms=stage["prefill"]["down_ms"],
+                    traffic_note="ncu dram__bytes_read.sum + dram__bytes_write.sum of the two launches of one "
+                                 "prefill forward (profiles/*.md)",
+                    timing="stage events around the expert GEMM launches inside the captured forward")
+    # The decode forward's expert GEMM (one fused launch), HBM-bound.
+    dec_bytes = int(G["decode"]["U"] * synth.expert_bytes(cfg) + DECODE_T * K * (D + I) * 2 * 2)
+    dec_ms = stage["decode"]["gate_up_ms"] + stage["decode"]["down_ms"]
+    roofline["decode_gemm"] = dict(bound="hbm", achieved=dec_bytes / (dec_ms / 1e3) / 1e9, peak=peaks["hbm_gbs"],
+                                   unit="GB/s", frac=dec_bytes / (dec_ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+                                   algorithmic_bytes=dec_bytes, ms=dec_ms)
+    forwards = {}
+    for n in ("prefill", "decode"):
+        T = G[n]["T"]
+        ms = statistics.median(tt[n])
+        fl = synth.algorithmic_flops(cfg, T)
+        by = synth.algorithmic_bytes(cfg, T, G[n]["U"])
+        forwards[n] = dict(tokens=T, ms=ms, tokens_per_s=T / (ms / 1e3), tflops=fl / (ms / 1e3) / 1e12,
+                           tensor_frac=fl / (ms / 1e3) / 1e12 / peaks["bf16_tflops"],
+                           gbs=by / (ms / 1e3) / 1e9, hbm_frac=by / (ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+                           distinct_experts=G[n]["U"], busiest_expert_rows=G[n]["rows_max"],
+                           stages_ms={k: round(v, 5) for k, v in stage[n].items()})
+    inputs = {"prefill": G["prefill"]["x"][0], "decode": G["decode"]["x"][0]}
+    launches = (kernels_per_forward(cfg, PREFILL_T) + kernels_per_forward(cfg, DECODE_T)) * args.steps
+    return dict(value=value, ms_per_step=total_ms / args.steps, e2e=e2e, roofline=roofline, clocks=clk,
+                forwards=forwards, gpu_launches=launches, graphs="each forward replayed from a captured CUDA graph",
+                parallelism="single GPU", _inputs=inputs)
+
+
+def headline_ep(args, torch, dist, dev, st, flush, blk_full, world, rank):
+    """The C5 step expert-parallel over `world` ranks, exchange over peer memory."""
+    from mlxr_moe import synth
+    from mlxr_moe.ep import ExpertParallelMoeBlock, PeerComm, balanced_placement
+
+    cfg = blk_full.cfg
+    D, K = cfg.hidden_size, cfg.num_experts_per_tok
+    Tp, Td = PREFILL_T // world, DECODE_T // world
+    nsets = 2
+    xs = {"prefill": [synth.make_input(PREFILL_T, D, stream_offset=10 + i, device=dev)[rank * Tp:(rank + 1) * Tp]
+                      .contiguous() for i in range(nsets)],
+          "decode": [synth.make_input(DECODE_T, D, stream_offset=20 + i, device=dev)[rank * Td:(rank + 1) * Td]
+                     .contiguous() for i in range(nsets)]}
+    # Placement from measured expert loads on a calibration batch (summed over ranks).
+    calib = synth.make_input(Tp, D, stream_offset=900 + rank, device=dev)
+    idx, _ = blk_full.router(calib)
+    loads = torch.bincount(idx.reshape(-1).long(), minlength=cfg.num_experts).to(torch.float64)
+    dist.all_reduce(loads)
+    place = balanced_placement(loads.cpu().tolist(), world)
+    blk = ExpertParallelMoeBlock.from_block(blk_full, rank, world, place)
+    comm = PeerComm(rank, world, cap=Tp, hidden=D, k=K)
+    exp_rows = {"prefill": max(1, PREFILL_T * K // world), "decode": max(1, DECODE_T * K // world)}
+    outs = {n: torch.empty_like(xs[n][0]) for n in xs}
+
+    def step(s, timer=None, host=None):
+        with torch.cuda.stream(st):
+            for n in ("prefill", "decode"):
+                flush.fill_(s & 0xFF)
+                a = timer.begin() if timer else None
+                if host is not None:
+                    xs[n][s % nsets].copy_(host[0][n][s % nsets], non_blocking=True)
+                blk.forward_p2p(xs[n][s % nsets], comm, expected_rows=exp_rows[n], out=outs[n])
+                if host is not None:
+                    host[1][n].copy_(outs[n], non_blocking=True)
+                if timer:
+                    timer.end(a, n)
+
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize(dev)
+    blk.status()
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(smi_id(torch, dev))
+    clocks.start()
+    timer = _Timer(torch, st)
+    for s in range(args.steps):
+        step(s, timer)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    blk.status()
+    tt = timer.totals()
+    per = torch.tensor([sum(tt["prefill"]), sum(tt["decode"])], dtype=torch.float64, device=dev)
+    tot = per.sum().reshape(1).clone()
+    dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+    dist.all_reduce(per, op=dist.ReduceOp.MAX)
+    total_ms = float(tot.item())
+    value = STEP_TOKENS * args.steps / (total_ms / 1e3)
+    # e2e with pinned host buffers (this rank's share of the batch)
+    host_in = {n: [xs[n][i].cpu().pin_memory() for i in range(nsets)] for n in xs}
+    host_out = {n: torch.empty_like(outs[n], device="cpu").pin_memory() for n in xs}
+    etimer = _Timer(torch, st)
+    for s in range(args.warmup + args.steps):
+        step(s, etimer if s >= args.warmup else None, (host_in, host_out))
+    torch.cuda.synchronize(dev)
+    blk.status()
+    et = etimer.totals()
+    e = torch.tensor([sum(et["prefill"]) + sum(et["decode"])], dtype=torch.float64, device=dev)
+    dist.all_reduce(e, op=dist.ReduceOp.MAX)
+    e2e = {"value": STEP_TOKENS * args.steps / (float(e.item()) / 1e3), "unit": UNIT,
+           "h2d_bytes_per_step": STEP_TOKENS * D * 2, "d2h_bytes_per_step": STEP_TOKENS * D * 2,
+           "note": "every rank: its pinned host x share -> device, ExpertParallelMoeBlock.forward_p2p "
+                   "(mlxr_cu_moe_ep_*_p2p), out -> pinned host; max over ranks; bytes summed over ranks"}
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    comm.close()
+    launches = (ep_kernels_per_forward(cfg, Tp, world) + ep_kernels_per_forward(cfg, Td, world)) * args.steps
+    forwards = {"prefill": dict(tokens=PREFILL_T, tokens_per_rank=Tp, ms=float(per[0].item()) / args.steps),
+                "decode": dict(tokens=DECODE_T, tokens_per_rank=Td, ms=float(per[1].item()) / args.steps)}
+    return dict(value=value, ms_per_step=total_ms / args.steps, e2e=e2e, roofline=None, clocks=clk,
+                forwards=forwards, gpu_launches=launches,
+                graphs="not captured: host issues the three peer-memory steps per forward",
+                parallelism=f"ep{world}: experts spread over {world} ranks by measured load; tokens split "
+                            f"evenly; dispatch/combine over NVLink peer memory inside the kernels")
+
+
 def stage_times(torch, C, _lib, blk, x_in, x_static, out, ws, st, flush, reps, dev):
     """Median per-stage times (ms) of one block forward: a graph of the
     forward captured with the library's stage events recorded between its
@@ -213,219 +555,6 @@ def stage_times(torch, C, _lib, blk, x_in, x_static, out, ws, st, flush, reps, d
                 combine_ms=med[5])
 
 
-def run_gpu(args):
-    import torch
-    import torch.distributed as dist
-
-    from mlxr_moe import synth
-    from mlxr_moe.moe import Routing
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        torch.cuda.set_device(local)
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
-    dev = torch.device("cuda", local if world > 1 else 0)
-    torch.cuda.set_device(dev)
-    peaks = measured_peaks()
-    spec = synth.CONFIGS[WORKLOAD]
-    cfg = spec["cfg"]
-    # Everything (weight synthesis, inputs, workspaces, forwards) runs on one
-    # stream, so the caching allocator never hands a buffer that pending work
-    # on another stream still touches to the block.
-    st = torch.cuda.Stream(dev)
-    torch.cuda.set_stream(st)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    blk = synth.make_block(cfg, seed=0, zipf=spec["zipf"], device=dev)
-    D = cfg.hidden_size
-    torch.cuda.synchronize(dev)
-    nsets = 4  # distinct input batches cycled through the steps
-
-    # Per batch size: static input/output/workspace buffers and one graph.
-    graphs = {}
-    with torch.cuda.stream(st):
-        for T in BATCHES:
-            xs = [synth.make_input(T, D, seed=0, stream_offset=1000 * rank + 10 * T + i, device=dev)
-                  for i in range(nsets)]
-            x_static = torch.empty_like(xs[0])
-            out = torch.empty_like(xs[0])
-            ws = torch.empty(blk.workspace_bytes(T), dtype=torch.uint8, device=dev)
-            x_static.copy_(xs[0])
-            for _ in range(2):  # warm: sets kernel attributes outside capture
-                blk.forward(x_static, out=out, workspace=ws)
-            torch.cuda.synchronize(dev)
-            blk.status(ws)
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=st):
-                blk.forward(x_static, out=out, workspace=ws)
-            r = Routing(T, cfg.num_experts_per_tok, cfg.num_experts, dev)
-            blk.forward(xs[0], routing=r, workspace=ws)
-            torch.cuda.synchronize(dev)
-            graphs[T] = dict(x=xs, xs=x_static, out=out, ws=ws, g=g, U=distinct_experts(r))
-
-    # Stage events for the live per-kernel timing (dominant kernel: gate/up GEMM).
-    import ctypes as C
-
-    from mlxr_moe import _lib
-
-    def run_steps(nsteps, timed, stage_capture=False):
-        ev = []
-        with torch.cuda.stream(st):
-            for s in range(nsteps):
-                for T in BATCHES:
-                    G = graphs[T]
-                    G["xs"].copy_(G["x"][s % nsets])
-                    flush.fill_(s & 0xFF)
-                    if timed:
-                        a = torch.cuda.Event(enable_timing=True)
-                        b = torch.cuda.Event(enable_timing=True)
-                        a.record(st)
-                    G["g"].replay()
-                    if timed:
-                        b.record(st)
-                        ev.append((T, a, b))
-        return ev
-
-    run_steps(args.warmup, timed=False)
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    clocks = ClockSampler(smi_id(torch, dev))
-    clocks.start()
-    evs = run_steps(args.steps, timed=True)
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    clk = clocks.stop()
-    per_T = {T: [] for T in BATCHES}
-    for T, a, b in evs:
-        per_T[T].append(a.elapsed_time(b))
-    total_ms = sum(sum(v) for v in per_T.values())
-    if world > 1:
-        t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
-    tokens_per_step = sum(BATCHES)
-    value = world * tokens_per_step * args.steps / (total_ms / 1e3)
-
-    # Live stage timing: a second graph per batch size with the library's
-    # stage events recorded between its kernels (event-record nodes).
-    stage = {T: stage_times(torch, C, _lib, blk, graphs[T]["x"], graphs[T]["xs"], graphs[T]["out"], graphs[T]["ws"],
-                            st, flush, max(5, args.steps), dev) for T in BATCHES}
-
-    # e2e: the same sweep through the public API with pinned host buffers.
-    e2e_ms = 0.0
-    h2d = d2h = 0
-    host_in = {T: [graphs[T]["x"][i].cpu().pin_memory() for i in range(nsets)] for T in BATCHES}
-    host_out = {T: torch.empty_like(graphs[T]["out"], device="cpu").pin_memory() for T in BATCHES}
-    e2e_evs = []
-    with torch.cuda.stream(st):
-        for s in range(args.warmup + args.steps):
-            for T in BATCHES:
-                G = graphs[T]
-                flush.fill_(s & 0xFF)
-                a = torch.cuda.Event(enable_timing=True)
-                b = torch.cuda.Event(enable_timing=True)
-                a.record(st)
-                G["xs"].copy_(host_in[T][s % nsets], non_blocking=True)
-                G["g"].replay()
-                host_out[T].copy_(G["out"], non_blocking=True)
-                b.record(st)
-                if s >= args.warmup:
-                    e2e_evs.append((a, b))
-    torch.cuda.synchronize(dev)
-    e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_evs)
-    for T in BATCHES:
-        h2d += T * D * 2
-        d2h += T * D * 2
-    if world > 1:
-        t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_value = world * tokens_per_step * args.steps / (e2e_ms / 1e3)
-
-    # Roofline of the dominant kernel and of the whole block. The dominant
-    # kernel is the expert GEMM: at decode widths gate|up (+SwiGLU) and the
-    # down projection run as ONE fused launch, so its algorithmic bytes are
-    # the routed experts' packed weights (all three matrices) plus the
-    # activation rows it reads and writes (x in, h out and back in, y out).
-    K_, I_ = cfg.num_experts_per_tok, cfg.moe_intermediate_size
-    ex_bytes_unit = synth.expert_bytes(cfg)
-
-    def expert_gemm_bytes(T, U):
-        return int(U * ex_bytes_unit + T * K_ * (D + I_) * 2 * 2)
-
-    sweep = []
-    ex_bytes_total = ex_ms_total = 0.0
-    for T in BATCHES:
-        G = graphs[T]
-        ms = statistics.median(per_T[T])
-        U = G["U"]
-        blk_bytes = synth.algorithmic_bytes(cfg, T, U)
-        ex_bytes_total += expert_gemm_bytes(T, U)
-        ex_ms_total += stage[T]["gate_up_ms"] + stage[T]["down_ms"]
-        sweep.append(dict(tokens=T, distinct_experts=U, ms=ms, tokens_per_s=T / (ms / 1e3),
-                          block_gbs=blk_bytes / (ms / 1e3) / 1e9,
-                          block_hbm_frac=blk_bytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"],
-                          stages_ms={k: round(v, 5) for k, v in stage[T].items()}))
-    achieved = ex_bytes_total / (ex_ms_total / 1e3) / 1e9
-    roofline = dict(bound="hbm",
-                    kernel="grouped_dequant_gemm: expert GEMMs (gate|up + SwiGLU, down; one fused launch at "
-                           "T=8 and T=64, split-K launches at T=1)",
-                    achieved=achieved, peak=peaks["hbm_gbs"], unit="GB/s", frac=achieved / peaks["hbm_gbs"],
-                    peak_source=peaks["source"] + " hbm_gbs (burst copy)",
-                    traffic=ncu_traffic("experts_c2_T64"),
-                    traffic_note="ncu DRAM bytes of the fused launch at T=64 (profiles/*.md)",
-                    algorithmic_bytes_per_launch={str(T): expert_gemm_bytes(T, graphs[T]["U"]) for T in BATCHES},
-                    timing="stage events around the expert GEMM launch(es) inside the captured forward")
-
-    extra = {}
-    if rank == 0 and not args.no_extra and world == 1:
-        extra = bench_extra(args, dev, st, flush, peaks)
-    ep = None
-    if world > 1 and not args.no_extra:
-        ep = bench_ep(args, dev, st, world, rank)
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_baseline(blk, graphs, args)
-
-    if world > 1:
-        dist.barrier()
-    del graphs
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (Philox seed 0): experts N(0,0.02) bf16 -> 4-bit affine gs64, router bf16, x N(0,1)",
-            "config": {"workload": "c2 decode sweep: one block forward at T=1, 8, 64 per step",
-                       "hidden": D, "experts": cfg.num_experts, "top_k": cfg.num_experts_per_tok,
-                       "moe_intermediate": cfg.moe_intermediate_size, "bits": cfg.bits, "group_size": cfg.group_size,
-                       "batches": BATCHES, "l2": "flushed before every forward (512 MiB write)",
-                       "graphs": "each forward replayed from a captured CUDA graph",
-                       "parallelism": f"dp{world}: token batches per rank, experts replicated" if world > 1
-                       else "single GPU"},
-            "roofline": roofline,
-            "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "note": "pinned host x -> device, graph replay, out -> pinned host, per forward"},
-            "gpu_launches": sum(kernels_per_forward(cfg, T) for T in BATCHES) * args.steps,
-            "clocks": clk,
-            "sweep": sweep,
-            "extra": extra,
-            "expert_parallel": ep,
-        }
-        print(json.dumps(line))
-    if world > 1:
-        dist.destroy_process_group()
-
-
 # The Gemma 4 MoE branch (model_kind 1) on a synthetic block of the C2
 # sizes (no Gemma 4 checkpoint or BASELINE configuration exists here):
 # hidden 2048, 128 experts, top-8, expert intermediate 768, 4-bit gs64.
@@ -455,10 +584,23 @@ def bench_extra(args, dev, st, flush, peaks):
     def gemma4():
         return synth.make_gemma4_branch(GEMMA4_CFG, 0, dev), False
 
-    for name, T, make in (("c1", 32, lambda: baseline("c1")), ("c3", 4096, lambda: baseline("c3")),
-                          ("c5_decode", 256, lambda: baseline("c5")), ("c5_prefill", 8192, lambda: baseline("c5")),
-                          ("c4", 16384, lambda: baseline("c4")), ("gemma4_decode", 64, gemma4),
-                          ("gemma4_prefill", 4096, gemma4)):
+    cache = {}
+
+    def once(key, fn):
+        if key not in cache:
+            cache.clear()
+            torch.cuda.empty_cache()
+            cache[key] = fn()
+        return cache[key]
+
+    for name, T, make in (("c2_T1", 1, lambda: once("c2", lambda: baseline("c2"))),
+                          ("c2_T8", 8, lambda: once("c2", lambda: baseline("c2"))),
+                          ("c2_T64", 64, lambda: once("c2", lambda: baseline("c2"))),
+                          ("c1", 32, lambda: once("c1", lambda: baseline("c1"))),
+                          ("c3", 4096, lambda: once("c3", lambda: baseline("c3"))),
+                          ("c4", 16384, lambda: once("c4", lambda: baseline("c4"))),
+                          ("gemma4_decode", 64, lambda: once("g4", gemma4)),
+                          ("gemma4_prefill", 4096, lambda: once("g4", gemma4))):
         blk, zipf = make()
         cfg = blk.cfg
         x = synth.make_input(T, cfg.hidden_size, stream_offset=7, device=dev)
@@ -497,10 +639,26 @@ def bench_extra(args, dev, st, flush, peaks):
                          frac=(tfl / peaks["bf16_tflops"]) if prefill else (gbs / peaks["hbm_gbs"]),
                          distinct_experts=U, zipf=zipf,
                          stages_ms={k: round(v, 5) for k, v in stg.items()})
+        if name.startswith("c2_"):
+            # expert GEMM bytes: the routed experts' packed weights (all three
+            # matrices) plus the x, h and y rows the launches read and write
+            K_, I_, D_ = cfg.num_experts_per_tok, cfg.moe_intermediate_size, cfg.hidden_size
+            res[name]["expert_gemm_bytes"] = int(U * synth.expert_bytes(cfg) + T * K_ * (D_ + I_) * 2 * 2)
+            res[name]["expert_gemm_ms"] = stg["gate_up_ms"] + stg["down_ms"]
         if name == "gemma4_decode" and not args.no_cpu:
             res[name]["cpu_baseline"] = gemma4_cpu_baseline(blk, x)
-        del g, blk, ws, out, x
-        torch.cuda.empty_cache()
+        del g, ws, out, x, blk
+    cache.clear()
+    torch.cuda.empty_cache()
+    # The decode sweep's expert GEMMs as one HBM roofline (T = 1, 8, 64).
+    by = sum(res[f"c2_T{T}"]["expert_gemm_bytes"] for T in C2_BATCHES)
+    ms = sum(res[f"c2_T{T}"]["expert_gemm_ms"] for T in C2_BATCHES)
+    blk_ms = sum(res[f"c2_T{T}"]["ms"] for T in C2_BATCHES)
+    res["c2_sweep"] = dict(tokens_per_s=sum(C2_BATCHES) / (blk_ms / 1e3), block_ms=blk_ms,
+                           expert_gemm_gbs=by / (ms / 1e3) / 1e9, expert_gemm_frac=by / (ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+                           expert_gemm_ms=ms, traffic_T64=ncu_traffic("experts_c2_T64"),
+                           note="expert GEMM launches (fused gate|up + down at T=8, 64; split-K at T=1), "
+                                "stage-event timed, L2 flushed; peak = measured hbm_gbs")
     return res
 
 
@@ -532,14 +690,10 @@ def gemma4_cpu_baseline(branch, x):
             "sample": f"2 forwards of {xs.shape[0]} tokens, median; oracle fused-fp32, OpenMP {O.max_threads()} threads"}
 
 
-def bench_ep(args, dev, st, world, rank):
-    """Expert parallelism across the `world` ranks: the largest BASELINE
-    configurations with their token batch split evenly over the ranks (strong
-    scaling: fixed total tokens). Experts are placed by loads measured on a
-    calibration batch. The step exchanges pairs and partial rows inside the
-    kernels over peer memory (the product path); the same step over NCCL
-    all-to-all is timed beside it. Times are max over ranks; the whole batch on
-    rank 0 alone (full block, one GPU) gives the one-GPU time in the same run."""
+def bench_ep_extra(args, dev, st, world, rank):
+    """Expert parallelism beside the headline: the C5 step with the exchange
+    over NCCL all-to-all (counts, pair rows, slot rows, partial rows), and the
+    C4 block (16384 tokens) over peer memory; strong scaling, max over ranks."""
     import torch
     import torch.distributed as dist
 
@@ -548,92 +702,69 @@ def bench_ep(args, dev, st, world, rank):
 
     ex = TorchDistExchange()
     res = {}
-    for name, T_total in (("c5_prefill", 8192), ("c4", 16384), ("c5_decode", 256)):
-        spec = synth.CONFIGS[name.split("_")[0]]
+    for name, key, T_total, via in (("c5_prefill_nccl", "c5", PREFILL_T, "nccl"), ("c4", "c4", 16384, "p2p")):
+        spec = synth.CONFIGS[key]
         cfg = spec["cfg"]
         D, K = cfg.hidden_size, cfg.num_experts_per_tok
         T = T_total // world
         full = synth.make_block(cfg, 0, spec["zipf"], dev)
         xs = [synth.make_input(T, D, stream_offset=500 + 16 * rank + i, device=dev) for i in range(2)]
-        # Placement from measured expert loads: every rank routes a calibration
-        # batch (its own tokens), the counts are summed over ranks, and the
-        # experts are spread greedily so each rank gets about the same rows.
         calib = synth.make_input(T, D, stream_offset=900 + rank, device=dev)
         idx, _ = full.router(calib)
         loads = torch.bincount(idx.reshape(-1).long(), minlength=cfg.num_experts).to(torch.float64)
         dist.all_reduce(loads)
         place = balanced_placement(loads.cpu().tolist(), world)
         blk = ExpertParallelMoeBlock.from_block(full, rank, world, place)
-        bounds = dict(max_recv_pairs=world * T, max_recv_rows=world * T * K)
         n_steps = max(5, args.steps // 2)
-        comm = PeerComm(rank, world, cap=T, hidden=D, k=K)
-        exp_rows = max(1, T_total * K // world)
+        comm = PeerComm(rank, world, cap=T, hidden=D, k=K) if via == "p2p" else None
+        bounds = dict(max_recv_pairs=world * T, max_recv_rows=world * T * K)
 
-        def timed(fn):
-            with torch.cuda.stream(st):
-                for i in range(3):
-                    fn(xs[i % 2])
-                torch.cuda.synchronize(dev)
-                blk.status()
-                dist.barrier()
-                times = []
-                for i in range(n_steps):
-                    a = torch.cuda.Event(enable_timing=True)
-                    b = torch.cuda.Event(enable_timing=True)
-                    a.record(st)
-                    fn(xs[i % 2])
-                    b.record(st)
-                    b.synchronize()
-                    times.append(a.elapsed_time(b))
+        def fn(xx):
+            if via == "p2p":
+                return blk.forward_p2p(xx, comm, expected_rows=max(1, T_total * K // world))
+            return blk.forward(xx, ex, **bounds)
+
+        with torch.cuda.stream(st):
+            for i in range(3):
+                fn(xs[i % 2])
             torch.cuda.synchronize(dev)
             blk.status()
-            t = torch.tensor([statistics.median(times)], dtype=torch.float64, device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            return float(t.item())
-
-        # Peer-memory exchange (the product path), then the NCCL exchange for reference.
-        ms = timed(lambda xx: blk.forward_p2p(xx, comm, expected_rows=exp_rows))
-        ms_nccl = timed(lambda xx: blk.forward(xx, ex, **bounds))
+            dist.barrier()
+            times = []
+            for i in range(n_steps):
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record(st)
+                fn(xs[i % 2])
+                b.record(st)
+                b.synchronize()
+                times.append(a.elapsed_time(b))
         torch.cuda.synchronize(dev)
+        blk.status()
+        t = torch.tensor([statistics.median(times)], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
         dist.barrier()
-        comm.close()
-        one = None
-        if rank == 0:  # the whole batch on this GPU alone, for the speed-up
-            x1 = synth.make_input(T_total, D, stream_offset=600, device=dev)
-            out1 = torch.empty_like(x1)
-            ws1 = torch.empty(full.workspace_bytes(T_total), dtype=torch.uint8, device=dev)
-            with torch.cuda.stream(st):
-                t1 = []
-                for i in range(3 + n_steps):
-                    a = torch.cuda.Event(enable_timing=True)
-                    b = torch.cuda.Event(enable_timing=True)
-                    a.record(st)
-                    full.forward(x1, out=out1, workspace=ws1)
-                    b.record(st)
-                    b.synchronize()
-                    if i >= 3:
-                        t1.append(a.elapsed_time(b))
-            one = statistics.median(t1)
-            del x1, out1, ws1
-        dist.barrier()
+        if comm is not None:
+            comm.close()
         fl = synth.algorithmic_flops(cfg, T_total)
         res[name] = dict(tokens=T_total, tokens_per_rank=T, ms=ms, tokens_per_s=T_total / (ms / 1e3),
-                         tflops_total=fl / (ms / 1e3) / 1e12, one_gpu_ms=one,
-                         speedup_vs_one_gpu=(one / ms) if one else None, zipf=spec["zipf"],
-                         exchange="peer memory: dispatch/combine kernels store into the other ranks' CUDA-IPC "
-                                  "buffers over NVLink, flag waits on the GPU, no host synchronisation",
-                         nccl_ms=ms_nccl, nccl_speedup_vs_one_gpu=(one / ms_nccl) if one else None,
-                         placement="balanced: experts spread greedily by loads measured on a calibration batch",
-                         nccl_exchange="NCCL all_to_all_single: counts, pair rows, slot rows, partial rows")
+                         tflops_total=fl / (ms / 1e3) / 1e12, exchange=via, zipf=spec["zipf"])
         del blk, full, xs
         torch.cuda.empty_cache()
     return res
 
 
 # ---------------------------------------------------------- CPU baseline ----
-def cpu_baseline(blk, graphs, args):
+def _c5_sample_sizes():
+    """The bounded CPU sample of one C5 step: 1/32 of each batch (256 prefill
+    and 8 decode tokens), so prefill and decode keep the step's proportions."""
+    return PREFILL_T // 32, DECODE_T // 32
+
+
+def cpu_baseline(blk, inputs, args):
     """The oracle (CPU restatement of the reference block, fused-fp32 mode,
-    OpenMP on every host core) on a bounded sample: the same sweep batches."""
+    OpenMP on every host core) on a bounded sample of the C5 step."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import oracle as O
@@ -643,59 +774,83 @@ def cpu_baseline(blk, graphs, args):
 
     cfg, W = block_to_oracle(blk)
     cores = O.max_threads()
+    sp, sd = _c5_sample_sizes()
+    xp = bf16_np(inputs["prefill"][:sp])
+    xd = bf16_np(inputs["decode"][:sd])
     times = []
-    reps = 5
-    for rep in range(reps):
+    for rep in range(3):
         t0 = time.perf_counter()
-        for T in BATCHES:
-            O.moe_block(cfg, W, bf16_np(graphs[T]["x"][rep % 4]), "fused")
+        O.moe_block(cfg, W, xp, "fused")
+        O.moe_block(cfg, W, xd, "fused")
         times.append(time.perf_counter() - t0)
     sec = statistics.median(times)
-    return {"value": sum(BATCHES) / sec, "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"{reps} sweeps (T=1,8,64) of the block, median; oracle fused-fp32 mode, OpenMP {cores} threads"}
+    return {"value": (sp + sd) / sec, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"3 runs of {sp} prefill + {sd} decode tokens of the C5 step (1/32 of each batch), median; "
+                      f"oracle fused-fp32 mode, OpenMP {cores} threads"}
 
 
-def run_reference(args):
-    """--impl reference: the CPU port of the reference block (MLX's own CPU
-    path cannot be built here) timed on all host cores; rank 0 only."""
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+def _oracle_c5_block():
+    """The C5 block's weights generated on the host by the oracle (same
+    Philox streams and quantiser as the GPU arm's synth.make_block)."""
     import numpy as np
 
     import oracle as O
 
-    cfgd = dict(hidden=2048, num_experts=128, top_k=8, moe_intermediate=768, group_size=64, bits=4)
-    W = {"router": O.normal_bf16(0, 0, (128, 2048), 0.02)}
-    W["gate"] = O.quantize(O.normal_bf16(0, 1, (128, 768, 2048), 0.02), 64, 4)
-    W["up"] = O.quantize(O.normal_bf16(0, 2, (128, 768, 2048), 0.02), 64, 4)
-    W["down"] = O.quantize(O.normal_bf16(0, 3, (128, 2048, 768), 0.02), 64, 4)
-    xs = {T: O.normal_bf16(0, 8 + 10 * T, (T, 2048), 1.0) for T in BATCHES}
+    D, E, K, I = 4096, 128, 8, 1536
+    W = {"router": O.normal_bf16(0, 0, (E, D), 0.02)}
+    for name, stream, shape in (("gate", 1, (E, I, D)), ("up", 2, (E, I, D)), ("down", 3, (E, D, I))):
+        W[name] = O.quantize(O.normal_bf16(0, stream, shape, 0.02), 64, 4)
+    keys = O.bf16_to_f32(O.normal_bf16(0, 9, (E,), 1.0))
+    order = np.argsort(keys, kind="stable")
+    ranks = np.empty(E, np.int64)
+    ranks[order] = np.arange(1, E + 1)
+    beta, s = 0.62, 1.1
+    W["router_bias"] = (-(beta * 0.02 * np.sqrt(D) * s) * np.log(ranks.astype(np.float64))).astype(np.float32)
+    cfg = dict(hidden=D, num_experts=E, top_k=K, moe_intermediate=I, group_size=64, bits=4)
+    return cfg, W
+
+
+def run_reference(args):
+    """--impl reference: the CPU port of the reference block (MLX's own CPU
+    path cannot be built here) timed on all host cores; rank 0 only. Each step
+    is the bounded sample of the C5 step (1/32 of the prefill and decode
+    batches, fresh tokens per step)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    cfg, W = _oracle_c5_block()
+    sp, sd = _c5_sample_sizes()
+    nsets = 2
+    xp = [O.normal_bf16(0, 8 + 16 * (10 + i), (PREFILL_T, 4096), 1.0)[:sp] for i in range(nsets)]
+    xd = [O.normal_bf16(0, 8 + 16 * (20 + i), (DECODE_T, 4096), 1.0)[:sd] for i in range(nsets)]
     cores = O.max_threads()
-    for _ in range(args.warmup):
-        for T in BATCHES:
-            O.moe_block(cfgd, W, xs[T], "fused")
+    for s in range(args.warmup):
+        O.moe_block(cfg, W, xp[s % nsets], "fused")
+        O.moe_block(cfg, W, xd[s % nsets], "fused")
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        for T in BATCHES:
-            O.moe_block(cfgd, W, xs[T], "fused")
+    for s in range(args.steps):
+        O.moe_block(cfg, W, xp[s % nsets], "fused")
+        O.moe_block(cfg, W, xd[s % nsets], "fused")
     sec = time.perf_counter() - t0
-    value = sum(BATCHES) * args.steps / sec
+    value = (sp + sd) * args.steps / sec
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": 1e3 * sec / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (Philox seed 0), same configuration as the GPU arm",
-        "config": {"workload": "c2 decode sweep: one block forward at T=1, 8, 64 per step",
-                   "hidden": 2048, "experts": 128, "top_k": 8, "moe_intermediate": 768, "bits": 4, "group_size": 64,
-                   "batches": BATCHES, "host": f"CPU, {cores} threads (rank 0 only; the GPUs are unused)"},
+        "warmup": args.warmup, "ms_per_step": 1e3 * sec / args.steps, "higher_is_better": True,
+        "scaling": "strong" if args.gpus > 1 else "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": DATA,
+        "config": {"workload": "c5: one block forward over 8192 prefill tokens + one over 256 decode tokens "
+                               "per step (Zipf(1.1) routing)",
+                   "hidden": 4096, "experts": 128, "top_k": 8, "moe_intermediate": 1536, "bits": 4, "group_size": 64,
+                   "prefill_tokens": PREFILL_T, "decode_tokens": DECODE_T,
+                   "host": f"CPU, {cores} threads (rank 0 only; the GPUs are unused)"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"{args.steps} full sweeps on the oracle (CPU restatement; MLX unbuildable here)"},
+                         "sample": f"each step {sp} prefill + {sd} decode tokens (1/32 of each batch of the C5 step) "
+                                   f"through the oracle (CPU restatement; MLX unbuildable here), fused-fp32"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
-    _ = np
 
 
 def run_case(args):
@@ -727,7 +882,7 @@ def main():
     ap.add_argument("--no-extra", action="store_true", help="skip the other BASELINE configurations")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--case", default=None,
-                    help="profiling driver: CONFIG:TOKENS (e.g. c2:64, gemma4:64); runs only block forwards, prints nothing timed")
+                    help="profiling driver: CONFIG:TOKENS (e.g. c5:8192, gemma4:64); runs only block forwards, prints nothing timed")
     ap.add_argument("--iters", type=int, default=3, help="forwards for --case")
     args = ap.parse_args()
     if args.case:
