@@ -81,6 +81,34 @@ static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
     ta2 = ta0;
     tb2 = tb;
   }
+  // Scale/bias maps for the staging ring: [rows, K/64] bf16 viewed as 2-D,
+  // a {8 groups x 128 rows} box. TMA needs 16-byte aligned bases and row
+  // pitches (a multiple of 8 groups); shapes that miss either keep the
+  // per-thread loads (the flag stays 0 and the maps are not used).
+  CUtensorMap ts0 = ta0, tz0 = ta0, ts1 = ta0, tz1 = ta0, ts2 = ta0, tz2 = ta0;
+  auto sb_maps = [&](const uint16_t* sc, const uint16_t* bi, int64_t rows, int k_dim, CUtensorMap* ms,
+                     CUtensorMap* mz) -> int {
+    const int groups = k_dim / 64;
+    if (SPLITK || groups % C::SB_K != 0 || !sc || !bi || (reinterpret_cast<uintptr_t>(sc) & 15) ||
+        (reinterpret_cast<uintptr_t>(bi) & 15))
+      return 0;
+    if (make_map_2d(ms, sc, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (uint64_t)groups, (uint64_t)rows, C::SB_K, C::BM,
+                    CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        make_map_2d(mz, bi, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (uint64_t)groups, (uint64_t)rows, C::SB_K, C::BM,
+                    CU_TENSOR_MAP_SWIZZLE_NONE)) {
+      mlxr_cu_clear_error();  // not an error: the kernel falls back to per-thread loads
+      return 0;
+    }
+    return 1;
+  };
+  int sb1 = sb_maps(p.s[0], p.b[0], p.w_rows, p.k_dim, &ts0, &tz0);
+  if (sb1 && NMAT == 2)
+    sb1 = sb_maps(p.s[1], p.b[1], p.w_rows1 > 0 ? p.w_rows1 : p.w_rows, p.k_dim, &ts1, &tz1);
+  else if (sb1) {
+    ts1 = ts0;
+    tz1 = tz0;
+  }
+  const int sb2 = FUSED ? sb_maps(p.s2, p.b2, p.w2_rows, p.k_dim2, &ts2, &tz2) : 0;
   auto kern = grouped_dequant_gemm_kernel<NMAT, BN, BITS, SPLITK, FUSED, GLU>;
   static std::atomic<uint64_t> attr_done{0};  // per instantiation and device
   if (int rc = ensure_smem_attr(kern, C::SMEM_BYTES, attr_done)) return rc;
@@ -101,6 +129,8 @@ static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
   a.pair = p.pair;
   a.w_rows1 = p.w_expert_rows > 0 ? p.w_expert_rows : p.n_out;
   a.status = p.status;
+  a.sb1 = sb1;
+  a.sb2 = sb2;
   a.splits = p.splits > 1 ? p.splits : 1;
   a.max_split_rows = p.max_split_rows;
   a.partial = p.partial;
@@ -123,7 +153,7 @@ static int launch_one(const GroupedGemmProblem& p, cudaStream_t st) {
     return set_error(MLXR_CU_ERR_INVALID_ARGUMENT, "grouped gemm: K=%d over %d splits leaves a work item one k-step",
                      p.k_dim, a.splits);
   const int grid = p.grid > 0 ? p.grid : num_sms_current();
-  launch_pdl(kern, grid, C::NUM_THREADS, C::SMEM_BYTES, st, ta0, ta1, tb, ta2, tb2, a);
+  launch_pdl(kern, grid, C::NUM_THREADS, C::SMEM_BYTES, st, ta0, ta1, tb, ta2, tb2, ts0, tz0, ts1, tz1, ts2, tz2, a);
   MLXR_LAUNCH_CHECK("grouped_dequant_gemm_kernel");
   return MLXR_CU_OK;
 }

@@ -68,11 +68,18 @@ struct GG {
   static constexpr int A_COLS = NMAT * 32;                // one A stage: NMAT x (128 x 64 bf16)
   static constexpr int AB = (2 * ACC_COLS + 2 * A_COLS <= 512) ? 2 : 1;
   static constexpr int OS_FIT = (512 - AB * ACC_COLS) / A_COLS;
+  // Scales and biases staged in shared memory by TMA: one block holds SB_K
+  // k-steps (groups) of the 128 rows' scales and biases of every matrix of
+  // the item (a {SB_K x 128} bf16 box each, rows 16 bytes apart).
+  static constexpr int SB_K = 8;
+  static constexpr int SB_BOX = BM * SB_K * 2;
+  static constexpr int SB_STAGE = NMAT * 2 * SB_BOX;
+  static constexpr int SBS = 3;
   // Stage ring depth. A stage is one k-step: a dequantised A tile in TMEM
   // and the activation tile in shared memory, released together by one
   // MMA commit per issuer. Bounded by tensor memory and by shared memory
   // (keeping room for at least four raw stages).
-  static constexpr int SMEM_RINGS = 200 * 1024;
+  static constexpr int SMEM_RINGS = 200 * 1024 - SBS * SB_STAGE;
   static constexpr int OS_SMEM = (SMEM_RINGS - 4 * RAW_STAGE) / B_STAGE;
   static constexpr int OS_T = OS_FIT > 6 ? 6 : OS_FIT;
   static constexpr int OS = OS_T < OS_SMEM ? OS_T : OS_SMEM;
@@ -106,8 +113,9 @@ struct GG {
   static constexpr int WBYTES = NCH * BITS;          // packed bytes per thread per k-step
   static constexpr int OFF_B = 0;
   static constexpr int OFF_RAW = OFF_B + OS * B_STAGE;
-  static constexpr int OFF_BAR = OFF_RAW + RS * RAW_STAGE;
-  static constexpr int NUM_BARS = 2 * RS + 3 * OS + 2 * AB + 1;
+  static constexpr int OFF_SB = OFF_RAW + RS * RAW_STAGE;
+  static constexpr int OFF_BAR = OFF_SB + SBS * SB_STAGE;
+  static constexpr int NUM_BARS = 2 * RS + 3 * OS + 2 * AB + 1 + 2 * SBS;
   static constexpr int SCHED_Q = 16;  // work-queue entries published ahead (shared-memory ring)
   // At least 120 KB so that two CTAs never share an SM: each CTA holds its
   // tensor memory for its whole (persistent) lifetime.
@@ -134,6 +142,10 @@ struct GemmArgs {
   int32_t w_rows1;            // weight rows per expert of the first phase: Nout, or 2*Nout
                               // for a packed gate|up [E, 2*Nout, K] (up = rows Nout..)
   int* status;
+  // Scales and biases come through the TMA staging ring (their tensor maps
+  // are valid: 16-byte aligned rows of a multiple of 8 groups) for the items
+  // of phase 1 / phase 2; otherwise every dequant thread loads its own.
+  int sb1, sb2;
   // Split-K (splits > 1): every (tile, row slice) is split into `splits`
   // k-ranges; each writes its fp32 accumulators to `partial`, and the last
   // split to finish (per TMEM lane quarter, counted in `counters`, zero on
@@ -248,7 +260,10 @@ template <int NMAT, int BN, int BITS, bool SPLITK, bool FUSED, bool GLU>
 __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
     grouped_dequant_gemm_kernel(const __grid_constant__ CUtensorMap tm_a0, const __grid_constant__ CUtensorMap tm_a1,
                                 const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_a2,
-                                const __grid_constant__ CUtensorMap tm_b2, const GemmArgs args) {
+                                const __grid_constant__ CUtensorMap tm_b2, const __grid_constant__ CUtensorMap tm_s0,
+                                const __grid_constant__ CUtensorMap tm_z0, const __grid_constant__ CUtensorMap tm_s1,
+                                const __grid_constant__ CUtensorMap tm_z1, const __grid_constant__ CUtensorMap tm_s2,
+                                const __grid_constant__ CUtensorMap tm_z2, const GemmArgs args) {
   static_assert(!(SPLITK && FUSED), "split-K and the fused launch are separate variants");
   static_assert(!FUSED || NMAT == 2, "the fused launch pairs gate|up with row pairs of down");
   using C = GG<NMAT, BN, BITS>;
@@ -256,6 +271,7 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sB = smem + C::OFF_B;
   uint8_t* sRaw = smem + C::OFF_RAW;
+  uint8_t* sSB = smem + C::OFF_SB;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* raw_full = bars;
   uint64_t* raw_empty = raw_full + C::RS;
@@ -265,7 +281,9 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
   uint64_t* acc_full = b_full + C::OS;
   uint64_t* acc_empty = acc_full + C::AB;
   uint64_t* fin_bar = acc_empty + C::AB;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin_bar + 1);
+  uint64_t* sb_full = fin_bar + 1;          // scale/bias block landed (TMA)
+  uint64_t* sb_empty = sb_full + C::SBS;    // block read by every dequant warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sb_empty + C::SBS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // Work-queue ring: entry n of this CTA's item sequence in s_ring[n % Q];
   // s_pub = entries published, s_cons = entries the epilogue has finished.
@@ -291,6 +309,10 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       mbar_init(&acc_empty[i], 4);
     }
     mbar_init(fin_bar, C::ISSUERS);
+    for (int i = 0; i < C::SBS; ++i) {
+      mbar_init(&sb_full[i], 1);
+      mbar_init(&sb_empty[i], C::DQ_WARPS);
+    }
     *abort_flag = 0;
     *s_pub = 1;  // entry 0 is blockIdx.x, known to every role
     *s_cons = 0;
@@ -307,6 +329,18 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
     if (FUSED) {
       prefetch_tmap(&tm_a2);
       prefetch_tmap(&tm_b2);
+    }
+    if (!SPLITK && args.sb1) {
+      prefetch_tmap(&tm_s0);
+      prefetch_tmap(&tm_z0);
+      if (NMAT == 2) {
+        prefetch_tmap(&tm_s1);
+        prefetch_tmap(&tm_z1);
+      }
+    }
+    if (FUSED && args.sb2) {
+      prefetch_tmap(&tm_s2);
+      prefetch_tmap(&tm_z2);
     }
   }
   tc_fence_before();
@@ -369,6 +403,14 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
     return d;
   };
 
+  // Items whose scales and biases come through the staging ring: whole-K
+  // items (no split) with a multiple of SB_K k-steps and valid maps. The
+  // producer and the dequant warps evaluate the same predicate per item.
+  auto item_sb = [&](const Item& d) -> bool {
+    if (SPLITK) return false;
+    return ((FUSED && d.ph2) ? args.sb2 : args.sb1) != 0 && d.ksteps % C::SB_K == 0 && d.k_lo == 0;
+  };
+
   // Entry n of this CTA's work sequence (-1: no more). Entry 0 is item
   // blockIdx.x. Decode-width launches (their items are uneven: 32-k-step
   // gate|up items and 12-k-step down items, and a static round-robin left
@@ -404,6 +446,7 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
     // ---------------------------------------------- raw weight producer --
     if (lane == 0) {
       uint32_t it = 0;
+      uint32_t sbi = 0;  // scale/bias blocks issued
       for (int n = 0; !*abort_flag; ++n) {
         int item;
         if (n == 0 || !dynamic) {
@@ -438,7 +481,27 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
         const int a_row = t.expert * d.wstride + d.m * d.mrows;
         const CUtensorMap* ma = (FUSED && d.ph2) ? &tm_a2 : &tm_a0;
         const CUtensorMap* mb = (FUSED && d.ph2) ? &tm_a2 : &tm_a1;
+        const bool use_sb = item_sb(d);
+        const CUtensorMap* ms0 = (FUSED && d.ph2) ? &tm_s2 : &tm_s0;
+        const CUtensorMap* mz0 = (FUSED && d.ph2) ? &tm_z2 : &tm_z0;
+        const CUtensorMap* ms1 = (FUSED && d.ph2) ? &tm_s2 : &tm_s1;
+        const CUtensorMap* mz1 = (FUSED && d.ph2) ? &tm_z2 : &tm_z1;
+        const int row1 = a_row + (d.pair ? C::BM : 0);
         for (int ks = d.k_lo; ks < d.k_hi; ++ks, ++it) {
+          if (use_sb && ks % C::SB_K == 0) {
+            // The next SB_K groups of every matrix's scales and biases.
+            const int q = sbi % C::SBS;
+            if (!mbar_wait(&sb_empty[q], ((sbi / C::SBS) & 1) ^ 1, abort_flag, args.status)) break;
+            mbar_arrive_expect_tx(&sb_full[q], C::SB_STAGE);
+            uint8_t* dst = sSB + q * C::SB_STAGE;
+            tma_load_2d(dst, ms0, &sb_full[q], ks, a_row);
+            tma_load_2d(dst + C::SB_BOX, mz0, &sb_full[q], ks, a_row);
+            if (NMAT == 2) {
+              tma_load_2d(dst + 2 * C::SB_BOX, ms1, &sb_full[q], ks, row1);
+              tma_load_2d(dst + 3 * C::SB_BOX, mz1, &sb_full[q], ks, row1);
+            }
+            ++sbi;
+          }
           const int s = it % C::RS;
           if (!mbar_wait(&raw_empty[s], ((it / C::RS) & 1) ^ 1, abort_flag, args.status)) break;
           mbar_arrive_expect_tx(&raw_full[s], C::RAW_STAGE);
@@ -449,6 +512,7 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
         }
       }
       drain_ring<C::RS>(raw_full, it, abort_flag, args.status);
+      drain_ring<C::SBS>(sb_full, sbi, abort_flag, args.status);
     }
   } else if (warp == C::W_B) {
     // ------------------------------------------- activation producer ----
@@ -593,6 +657,7 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
     int rs = 0, os = 0;          // ring slots of global k-step `it`, advanced incrementally
     uint32_t rph = 0, oph = 0;   // their phases
     uint32_t it = 0;
+    uint32_t sbi = 0;            // scale/bias blocks finished by this warp
     bool ok = true;
     auto advance = [&](int n) {
       rs += n;
@@ -626,10 +691,25 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       int ks = k_lo + first;
       advance(ks < k_hi ? first : k_hi - k_lo);
       if (ks >= k_hi) continue;
-      uint32_t s_nx = __ldg(sp + ks), b_nx = __ldg(bp + ks);  // one k-step ahead
+      // Staged items: SB_K is a multiple of NGRP and items start at k-step 0,
+      // so every group takes SB_K / NGRP k-steps of each block, the first at
+      // position grp.
+      const bool use_sb = item_sb(d);
+      uint32_t s_nx = 0, b_nx = 0;
+      if (!use_sb) {  // one k-step ahead
+        s_nx = __ldg(sp + ks);
+        b_nx = __ldg(bp + ks);
+      }
       for (; ks < k_hi; ks += NGRP) {
-        const uint32_t s16 = s_nx, b16 = b_nx;
-        if (ks + NGRP < k_hi) {
+        uint32_t s16 = s_nx, b16 = b_nx;
+        const int kb = ks % C::SB_K;
+        const int sq = sbi % C::SBS;
+        if (use_sb) {
+          if (kb < NGRP && !mbar_wait(&sb_full[sq], (sbi / C::SBS) & 1, abort_flag, args.status)) {
+            ok = false;
+            break;
+          }
+        } else if (ks + NGRP < k_hi) {
           s_nx = __ldg(sp + ks + NGRP);
           b_nx = __ldg(bp + ks + NGRP);
         }
@@ -649,6 +729,11 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
             wv[4 * i + 3] = v.w;
           }
         }
+        if (use_sb) {
+          const uint16_t* sbm = reinterpret_cast<const uint16_t*>(sSB + sq * C::SB_STAGE + mat * 2 * C::SB_BOX);
+          s16 = sbm[row * C::SB_K + kb];
+          b16 = sbm[C::BM * C::SB_K + row * C::SB_K + kb];
+        }
         uint32_t av[32];  // this thread's A row for the k-step, bf16 pairs
         if (BITS == 4) {
           const uint32_t s2w = s16 | (s16 << 16), b2w = b16 | (b16 << 16);
@@ -667,11 +752,17 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
             av[4 * c + 3] = o.w;
           }
         }
-        // The codes are in registers: release the raw slot (TMA refills it
-        // through the async proxy, so order this warp's generic reads first).
+        // The codes (and scale and bias) are in registers: release the raw
+        // slot, and the scale/bias block after this group's last k-step in it
+        // (TMA refills them through the async proxy, so order this warp's
+        // generic reads first).
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&raw_empty[rs]);
+        if (use_sb && kb + NGRP >= C::SB_K) {
+          if (lane == 0) mbar_arrive(&sb_empty[sq]);
+          ++sbi;
+        }
         // Only the TMEM store needs the stage: wait for its release here, after
         // the arithmetic, so the dequantisation overlaps the MMA round trip.
         if (!mbar_wait(&op_empty[os], oph ^ 1, abort_flag, args.status)) {
