@@ -33,7 +33,8 @@
 //               (warp 22 also allocates TMEM)
 // TMEM columns: [0, AB*NMAT*BN*KP) accumulators (double-buffered when they fit,
 // so the epilogue of item i overlaps the main loop of item i+1), then OS
-// stages of NMAT x 32 columns (128 rows x 64 bf16) of dequantised A.
+// stages of NMAT x 32 columns (128 rows x 64 bf16) of dequantised A. The
+// activation tiles have their own, deeper ring of OSB shared-memory stages.
 #pragma once
 
 #include "common.cuh"
@@ -75,21 +76,26 @@ struct GG {
   static constexpr int SB_BOX = BM * SB_K * 2;
   static constexpr int SB_STAGE = NMAT * 2 * SB_BOX;
   static constexpr int SBS = 3;
-  // Stage ring depth. A stage is one k-step: a dequantised A tile in TMEM
-  // and the activation tile in shared memory, released together by one
-  // MMA commit per issuer. Bounded by tensor memory and by shared memory
-  // (keeping room for at least four raw stages).
-  static constexpr int SMEM_RINGS = 200 * 1024 - SBS * SB_STAGE;
-  static constexpr int OS_SMEM = (SMEM_RINGS - 4 * RAW_STAGE) / B_STAGE;
+  // Two rings per k-step, each released by the MMA commits of that k-step:
+  // the dequantised A tile in TMEM (OS stages, bounded by tensor memory)
+  // and the activation (B) tile in shared memory (OSB stages). The B ring
+  // is deeper than the A ring: the activation tile's TMA load is the
+  // longest round trip of a k-step (about 1.8 us on the 128-token prefill
+  // tiles, issued only once its slot is free), so with the two rings tied
+  // together at four stages a k-step took (TMA latency + MMA) / 4.
+  static constexpr int SMEM_RINGS = 220 * 1024 - SBS * SB_STAGE;  // B + packed-weight rings
   static constexpr int OS_T = OS_FIT > 6 ? 6 : OS_FIT;
-  static constexpr int OS = OS_T < OS_SMEM ? OS_T : OS_SMEM;
+  static constexpr int OS = OS_T;
+  static constexpr int OSB_ROOM = (SMEM_RINGS - 4 * RAW_STAGE) / B_STAGE;
+  static constexpr int OSB = OSB_ROOM > 8 ? 8 : OSB_ROOM;
   // Packed-weight ring: up to 96 KB (16 stages) in what shared memory leaves.
-  static constexpr int RS_ROOM = (SMEM_RINGS - OS * B_STAGE) / RAW_STAGE;
+  static constexpr int RS_ROOM = (SMEM_RINGS - OSB * B_STAGE) / RAW_STAGE;
   static constexpr int RS_WANT = (96 * 1024) / RAW_STAGE;
   static constexpr int RS_A = RS_WANT > 16 ? 16 : RS_WANT;
   static constexpr int RS = RS_A < RS_ROOM ? RS_A : RS_ROOM;
   static_assert(RS >= 4, "shared memory too small for the packed-weight ring");
   static_assert(OS >= 2, "tensor memory too small for two A stages");
+  static_assert(OSB >= 2, "shared memory too small for two activation stages");
   static constexpr int A_BASE = AB * ACC_COLS;
   static constexpr int TMEM_NEED = A_BASE + OS * A_COLS;
   static constexpr int TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128
@@ -112,10 +118,10 @@ struct GG {
   static constexpr int NCH = 8;                      // 8-weight chunks per row per k-step
   static constexpr int WBYTES = NCH * BITS;          // packed bytes per thread per k-step
   static constexpr int OFF_B = 0;
-  static constexpr int OFF_RAW = OFF_B + OS * B_STAGE;
+  static constexpr int OFF_RAW = OFF_B + OSB * B_STAGE;
   static constexpr int OFF_SB = OFF_RAW + RS * RAW_STAGE;
   static constexpr int OFF_BAR = OFF_SB + SBS * SB_STAGE;
-  static constexpr int NUM_BARS = 2 * RS + 3 * OS + 2 * AB + 1 + 2 * SBS;
+  static constexpr int NUM_BARS = 2 * RS + 2 * OS + 2 * OSB + 2 * AB + 1 + 2 * SBS;
   static constexpr int SCHED_Q = 16;  // work-queue entries published ahead (shared-memory ring)
   // At least 120 KB so that two CTAs never share an SM: each CTA holds its
   // tensor memory for its whole (persistent) lifetime.
@@ -276,9 +282,10 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
   uint64_t* raw_full = bars;
   uint64_t* raw_empty = raw_full + C::RS;
   uint64_t* op_full = raw_empty + C::RS;   // dequantised A stage written to TMEM (dequant warps)
-  uint64_t* op_empty = op_full + C::OS;     // stage (A and activation tile) consumed (MMA commit)
+  uint64_t* op_empty = op_full + C::OS;     // A stage consumed (MMA commit)
   uint64_t* b_full = op_empty + C::OS;      // activation tile landed (TMA)
-  uint64_t* acc_full = b_full + C::OS;
+  uint64_t* b_empty = b_full + C::OSB;      // activation tile consumed (MMA commit)
+  uint64_t* acc_full = b_empty + C::OSB;
   uint64_t* acc_empty = acc_full + C::AB;
   uint64_t* fin_bar = acc_empty + C::AB;
   uint64_t* sb_full = fin_bar + 1;          // scale/bias block landed (TMA)
@@ -303,7 +310,10 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       mbar_init(&op_full[i], C::GRP_WARPS);
       mbar_init(&op_empty[i], C::STAGE_COMMITS);
     }
-    for (int i = 0; i < C::OS; ++i) mbar_init(&b_full[i], 1);
+    for (int i = 0; i < C::OSB; ++i) {
+      mbar_init(&b_full[i], 1);
+      mbar_init(&b_empty[i], C::STAGE_COMMITS);
+    }
     for (int i = 0; i < C::AB; ++i) {
       mbar_init(&acc_full[i], C::ISSUERS);
       mbar_init(&acc_empty[i], 4);
@@ -537,16 +547,16 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
           }
         }
         for (int ks = d.k_lo; ks < d.k_hi; ++ks, ++it) {
-          if (!mbar_wait(&op_empty[s], ph ^ 1, abort_flag, args.status)) break;
+          if (!mbar_wait(&b_empty[s], ph ^ 1, abort_flag, args.status)) break;
           mbar_arrive_expect_tx(&b_full[s], C::B_STAGE);
           tma_load_2d(sB + s * C::B_STAGE, mbt, &b_full[s], ks * C::BK, t.row_start);
-          if (++s == C::OS) {
+          if (++s == C::OSB) {
             s = 0;
             ph ^= 1;
           }
         }
       }
-      drain_ring<C::OS>(b_full, it, abort_flag, args.status);
+      drain_ring<C::OSB>(b_full, it, abort_flag, args.status);
     }
   } else if (warp >= C::W_MMA) {
     // ---------------------------------------------------- MMA issuers ----
@@ -560,8 +570,8 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       const uint64_t bdesc0 = umma_desc_sw128(smem_u32(sB));
       const uint32_t a0 = tmem_base + (uint32_t)C::A_BASE;
       uint32_t li = 0, git = 0;
-      int s = 0;
-      uint32_t ph = 0;
+      int s = 0, sb = 0;         // A (TMEM) and activation (shared memory) stages
+      uint32_t ph = 0, bph = 0;
       bool ok = true;
       for (int n = 0; ok; ++n) {
         const int item = sched_item(n);
@@ -577,23 +587,28 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
         uint32_t acc = 0;
         for (int ks = di.k_lo; ks < di.k_hi; ++ks, ++git) {
           if ((git & 1u) == (uint32_t)mi) {
-            if (!mbar_wait(&b_full[s], ph, abort_flag, args.status) ||
+            if (!mbar_wait(&b_full[sb], bph, abort_flag, args.status) ||
                 !mbar_wait(&op_full[s], ph, abort_flag, args.status)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint64_t bd = bdesc0 + (uint64_t)(s * (C::B_STAGE >> 4));
+            const uint64_t bd = bdesc0 + (uint64_t)(sb * (C::B_STAGE >> 4));
             const uint32_t as = a0 + (uint32_t)(s * C::A_COLS);
 #pragma unroll
             for (int m = 0; m < NMAT; ++m)
               umma_bf16_ts_k64(d0 + (uint32_t)(m * 2 * BN), as + (uint32_t)(m * 32), bd, C::IDESC, acc);
             acc = 1;
             umma_commit(&op_empty[s]);
+            umma_commit(&b_empty[sb]);
           }
           if (++s == C::OS) {
             s = 0;
             ph ^= 1;
+          }
+          if (++sb == C::OSB) {
+            sb = 0;
+            bph ^= 1;
           }
         }
         // (with no k-step of its parity in the item the commit arrives at once
@@ -606,8 +621,8 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
       const uint64_t bdesc0 = umma_desc_sw128(smem_u32(sB));
       const uint32_t a0 = tmem_base + (uint32_t)(C::A_BASE + mi * 32);
       uint32_t li = 0;
-      int s = 0;
-      uint32_t ph = 0;
+      int s = 0, sb = 0;         // A (TMEM) and activation (shared memory) stages
+      uint32_t ph = 0, bph = 0;
       bool ok = true;
       for (int n = 0; ok; ++n) {
         const int item = sched_item(n);
@@ -622,18 +637,23 @@ __global__ void __launch_bounds__(GG<NMAT, BN, BITS>::NUM_THREADS, 1)
         const uint32_t d = tmem_base + (uint32_t)(ab * C::ACC_COLS + mi * BN);
         const int k_lo = di.k_lo, k_hi = di.k_hi;
         for (int ks = k_lo; ks < k_hi; ++ks) {
-          if (!mbar_wait(&b_full[s], ph, abort_flag, args.status) ||
+          if (!mbar_wait(&b_full[sb], bph, abort_flag, args.status) ||
               !mbar_wait(&op_full[s], ph, abort_flag, args.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          umma_bf16_ts_k64(d, a0 + (uint32_t)(s * C::A_COLS), bdesc0 + (uint64_t)(s * (C::B_STAGE >> 4)), C::IDESC,
+          umma_bf16_ts_k64(d, a0 + (uint32_t)(s * C::A_COLS), bdesc0 + (uint64_t)(sb * (C::B_STAGE >> 4)), C::IDESC,
                            ks != k_lo ? 1u : 0u);
           umma_commit(&op_empty[s]);
+          umma_commit(&b_empty[sb]);
           if (++s == C::OS) {
             s = 0;
             ph ^= 1;
+          }
+          if (++sb == C::OSB) {
+            sb = 0;
+            bph ^= 1;
           }
         }
         if (ok) umma_commit(&acc_full[ab]);
