@@ -853,12 +853,73 @@ def run_reference(args):
     }))
 
 
+def _case_ep1(cfg_name: str, T: int, iters: int):
+    """Expert-parallel peer-memory steps with a world-1 communicator (the
+    rank's own exchange buffer, no other process): every ep_* kernel runs on
+    this GPU, for ncu captures."""
+    import ctypes as C
+
+    import torch
+
+    from mlxr_moe import _lib, synth
+    from mlxr_moe.ep import ExpertParallelMoeBlock
+
+    spec = synth.CONFIGS[cfg_name]
+    full = synth.make_block(spec["cfg"], 0, spec["zipf"])
+    cfg = full.cfg
+    blk = ExpertParallelMoeBlock.from_block(full, 0, 1)
+
+    class _Comm:
+        pass
+
+    comm = _Comm()
+    comm.comm, comm.cap, comm.epoch = C.c_void_p(), T, 0
+    handle = (C.c_uint8 * 64)()
+    _lib.call("mlxr_cu_ep_comm_create", 1, 0, T, cfg.hidden_size, cfg.num_experts_per_tok, C.byref(comm.comm), handle)
+    x = synth.make_input(T, cfg.hidden_size)
+    for _ in range(iters):
+        blk.forward_p2p(x, comm)
+    torch.cuda.synchronize()
+    blk.status()
+    _lib.call("mlxr_cu_ep_comm_destroy", comm.comm)
+
+
+def _case_ops(iters: int):
+    """The op family (quantize, dequantize, quantized_matmul, gather_qmm,
+    gather_mm) at C2 expert shapes, for ncu captures."""
+    import torch
+
+    from mlxr_moe import ops, synth
+
+    w = synth.ops.synth_normal_bf16(0, 1, (16, 768, 2048), 0.02)
+    x = synth.make_input(64, 2048)
+    idx = torch.arange(64, dtype=torch.int32, device="cuda") % 16
+    for _ in range(iters):
+        wq, s, b = ops.quantize(w, 64, 4)
+        wd = ops.dequantize(wq[0], s[0], b[0], 64, 4)
+        ops.quantized_matmul(x, wq[0], s[0], b[0], True, 64, 4)
+        ops.gather_qmm(x.reshape(64, 1, 2048), wq, s, b, None, idx, True, 64, 4)
+        ops.gather_mm(x.reshape(64, 1, 2048), wd.t().contiguous().reshape(1, 2048, 768), None, None)
+    torch.cuda.synchronize()
+
+
 def run_case(args):
-    """Block forwards of one configuration, for ncu captures (not a bench number)."""
+    """Block forwards of one configuration, for ncu captures (not a bench
+    number). CONFIG:TOKENS for a block forward; ep1:CONFIG:TOKENS for the
+    expert-parallel peer-memory step of one rank; ops for the op family."""
     import torch
 
     from mlxr_moe import synth
 
+    if args.case == "ops":
+        _case_ops(args.iters)
+        print(f"case ops: {args.iters} rounds ok")
+        return
+    if args.case.startswith("ep1:"):
+        _, cname, T = args.case.split(":")
+        _case_ep1(cname, int(T), args.iters)
+        print(f"case {args.case}: {args.iters} steps ok")
+        return
     name, T = args.case.split(":")
     if name == "gemma4":
         blk = synth.make_gemma4_branch(_gemma4_cfg(), 0)
