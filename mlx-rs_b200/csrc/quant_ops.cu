@@ -87,19 +87,54 @@ __device__ inline uint32_t get_code(const uint32_t* row, int64_t k, int bits) {
 //   then exactly representable); q0 == 0: bias = 0;
 //   q = clamp(rint((w - bias) / scale), 0, n_bins) from the fp32 pair; the
 //   pair is rounded to the weight dtype only when stored.
+// The group's elements are read 16 bytes at a time (vec != 0: w is 16-byte
+// aligned; groups of 32, 64 or 128 elements are then 16-byte aligned too).
+template <int DT>
+struct QVec {
+  static constexpr int N = DT == MLXR_CU_FLOAT32 ? 4 : 8;  // elements per 16-byte load
+  static __device__ void load(const void* w, int64_t i, float (&v)[8]) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(w) + i * (16 / N)));
+    const uint32_t a[4] = {u.x, u.y, u.z, u.w};
+    if constexpr (DT == MLXR_CU_FLOAT32) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = __uint_as_float(a[j]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[2 * j] = IO<DT>::load(&a[j], 0);
+        v[2 * j + 1] = IO<DT>::load(&a[j], 1);
+      }
+    }
+  }
+};
+
 template <int DT>
 __global__ void quantize_kernel(const void* __restrict__ w, int64_t rows, int64_t cols, int gs, int bits,
-                                uint32_t* __restrict__ wq, void* __restrict__ scales, void* __restrict__ biases) {
+                                uint32_t* __restrict__ wq, void* __restrict__ scales, void* __restrict__ biases,
+                                int vec) {
   const int64_t ngroups = cols / gs;
   const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (gid >= rows * ngroups) return;
   const int64_t r = gid / ngroups, g = gid % ngroups;
   const int64_t base = r * cols + g * gs;
+  constexpr int NV = QVec<DT>::N;
   float mn = INFINITY, mx = -INFINITY;
-  for (int i = 0; i < gs; ++i) {
-    const float v = IO<DT>::load(w, base + i);
-    mn = fminf(mn, v);
-    mx = fmaxf(mx, v);
+  if (vec) {
+    for (int i = 0; i < gs; i += NV) {
+      float v[8];
+      QVec<DT>::load(w, base + i, v);
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        mn = fminf(mn, v[j]);
+        mx = fmaxf(mx, v[j]);
+      }
+    }
+  } else {
+    for (int i = 0; i < gs; ++i) {
+      const float v = IO<DT>::load(w, base + i);
+      mn = fminf(mn, v);
+      mx = fmaxf(mx, v);
+    }
   }
   const float nbins = (float)((1 << bits) - 1);
   const bool min_edge = fabsf(mn) > fabsf(mx);
@@ -114,14 +149,32 @@ __global__ void quantize_kernel(const void* __restrict__ w, int64_t rows, int64_
   }
   const int per = 32 / bits;
   uint32_t* qrow = wq + r * (cols / per) + g * gs / per;
-  for (int wi = 0; wi < gs / per; ++wi) {
+  auto code = [&](float v) {
+    return (uint32_t)fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(v, bi), sc)), 0.0f), nbins);
+  };
+  if (vec) {
+    // word wi holds elements [wi*per, wi*per + per); per (4, 8 or 16) and NV
+    // (4 or 8) divide the group, so each load feeds whole or partial words.
     uint32_t word = 0;
-    for (int j = 0; j < per; ++j) {
-      const float v = IO<DT>::load(w, base + wi * per + j);
-      const float q = fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(v, bi), sc)), 0.0f), nbins);
-      word |= ((uint32_t)q) << (j * bits);
+    for (int i = 0; i < gs; i += NV) {
+      float v[8];
+      QVec<DT>::load(w, base + i, v);
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        const int e = i + j;
+        word |= code(v[j]) << ((e % per) * bits);
+        if (e % per == per - 1) {
+          qrow[e / per] = word;
+          word = 0;
+        }
+      }
     }
-    qrow[wi] = word;
+  } else {
+    for (int wi = 0; wi < gs / per; ++wi) {
+      uint32_t word = 0;
+      for (int j = 0; j < per; ++j) word |= code(IO<DT>::load(w, base + wi * per + j)) << (j * bits);
+      qrow[wi] = word;
+    }
   }
   IO<DT>::store(scales, gid, sc);
   IO<DT>::store(biases, gid, bi);
@@ -326,8 +379,9 @@ int mlxr_cu_quantize(const void* w, mlxr_cu_dtype dtype, int64_t rows, int64_t c
   if (rows == 0) return MLXR_CU_OK;
   const int64_t n = rows * (cols / group_size);
   cudaStream_t st = (cudaStream_t)stream;
+  const int vec = (reinterpret_cast<uintptr_t>(w) & 15) == 0;
   MLXR_DISPATCH_DTYPE(dtype, DT, quantize_kernel<DT><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
-                                     w, rows, cols, group_size, bits, wq, scales, biases));
+                                     w, rows, cols, group_size, bits, wq, scales, biases, vec));
   MLXR_LAUNCH_CHECK("quantize_kernel");
   return MLXR_CU_OK;
 }

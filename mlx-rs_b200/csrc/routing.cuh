@@ -909,10 +909,10 @@ __global__ void __launch_bounds__(256) permute_gather_kernel(const int32_t* __re
     }
     const uint4* src = reinterpret_cast<const uint4*>(x + src_row * D);
     uint4* dst = reinterpret_cast<uint4*>(x_sorted + pos * D);
-    for (int v = lane; v < dvec; v += 32) {
-      // coherent: through L2 only (the rows were stored by a peer GPU);
-      // otherwise the read-only path, which keeps rows gathered K times in L1.
-      uint4 a = coherent ? __ldcg(src + v) : __ldg(src + v);
+    // coherent: through L2 only (the rows were stored by a peer GPU);
+    // otherwise the read-only path, which keeps rows gathered K times in L1.
+    auto ld = [&](int v) { return coherent ? __ldcg(src + v) : __ldg(src + v); };
+    auto st = [&](int v, uint4 a) {
       if (kperm) {
         uint4 b;
         b.x = __byte_perm(a.x, a.z, 0x5410);
@@ -922,7 +922,18 @@ __global__ void __launch_bounds__(256) permute_gather_kernel(const int32_t* __re
         a = b;
       }
       dst[v] = a;
+    };
+    // Eight 16-byte loads of the row in flight per lane before any store
+    // (one load at a time left the copy latency-bound at half the HBM rate).
+    int v = lane;
+    for (; v + 7 * 32 < dvec; v += 8 * 32) {
+      uint4 a[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a[j] = ld(v + j * 32);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) st(v + j * 32, a[j]);
     }
+    for (; v < dvec; v += 32) st(v, ld(v));
   }
 }
 
