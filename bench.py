@@ -511,12 +511,29 @@ def headline_ep(args, torch, dist, dev, st, flush, blk_full, world, rank):
            "h2d_bytes_per_step": STEP_TOKENS * D * 2, "d2h_bytes_per_step": STEP_TOKENS * D * 2,
            "note": "every rank: its pinned host x share -> device, ExpertParallelMoeBlock.forward_p2p "
                    "(mlxr_cu_moe_ep_*_p2p), out -> pinned host; max over ranks; bytes summed over ranks"}
+    # Phase times of each forward (dispatch, experts, combine): events between
+    # the three peer-memory calls on a few extra steps, medians, max over ranks.
+    ph = {n: [] for n in xs}
+    with torch.cuda.stream(st):
+        for s in range(max(3, args.steps // 2)):
+            for n in ("prefill", "decode"):
+                flush.fill_(s & 0xFF)
+                evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+                blk.forward_p2p(xs[n][s % nsets], comm, expected_rows=exp_rows[n], out=outs[n], events=evs)
+                ph[n].append(evs)
+    torch.cuda.synchronize(dev)
+    blk.status()
+    phase = torch.tensor([[statistics.median(e[j].elapsed_time(e[j + 1]) for e in ph[n]) for j in range(3)]
+                          for n in ("prefill", "decode")], dtype=torch.float64, device=dev)
+    dist.all_reduce(phase, op=dist.ReduceOp.MAX)
     dist.barrier()
     torch.cuda.synchronize(dev)
     comm.close()
     launches = (ep_kernels_per_forward(cfg, Tp, world) + ep_kernels_per_forward(cfg, Td, world)) * args.steps
-    forwards = {"prefill": dict(tokens=PREFILL_T, tokens_per_rank=Tp, ms=float(per[0].item()) / args.steps),
-                "decode": dict(tokens=DECODE_T, tokens_per_rank=Td, ms=float(per[1].item()) / args.steps)}
+    forwards = {n: dict(tokens=T_, tokens_per_rank=Tr, ms=float(per[i].item()) / args.steps,
+                        phases_ms={k: round(float(phase[i, j].item()), 5)
+                                   for j, k in enumerate(("dispatch", "experts", "combine"))})
+                for i, (n, T_, Tr) in enumerate((("prefill", PREFILL_T, Tp), ("decode", DECODE_T, Td)))}
     return dict(value=value, ms_per_step=total_ms / args.steps, e2e=e2e, roofline=None, clocks=clk,
                 forwards=forwards, gpu_launches=launches,
                 graphs="not captured: host issues the three peer-memory steps per forward",

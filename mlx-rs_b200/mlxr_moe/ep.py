@@ -220,9 +220,11 @@ class ExpertParallelMoeBlock:
         return self.combine(x, back, plan, ws)
 
     def forward_p2p(self, x: torch.Tensor, comm: "PeerComm", expected_rows: int | None = None,
-                     out: torch.Tensor | None = None) -> torch.Tensor:
+                     out: torch.Tensor | None = None, events=None) -> torch.Tensor:
         """One step over peer memory; every rank calls it together (same order of
-        steps on every rank, each GPU one rank)."""
+        steps on every rank, each GPU one rank). events: optional four CUDA
+        events recorded on the stream before dispatch, after dispatch, after
+        the experts step and after combine (phase timing)."""
         x = x.reshape(-1, self.cfg.hidden_size).contiguous()
         T, K = x.shape[0], self.cfg.num_experts_per_tok
         if expected_rows is None:
@@ -241,14 +243,22 @@ class ExpertParallelMoeBlock:
         pair_pos = torch.empty(max(T * K, 1), dtype=torch.int32, device=x.device)
         sg = torch.empty(max(T, 1), dtype=torch.float32, device=x.device) if self.shared_expert is not None else None
         out = torch.empty_like(x) if out is None else out
+        if events is not None:
+            events[0].record()
         _lib.call("mlxr_cu_moe_ep_dispatch_p2p", C.byref(self._ccfg), C.byref(self._cw_rep), comm.comm,
                   self.placement.data_ptr(), x.data_ptr() if T else None, T, pair_pos.data_ptr(),
                   None if sg is None else sg.data_ptr(), ep, ws.data_ptr(), ws.numel(), st)
+        if events is not None:
+            events[1].record()
         _lib.call("mlxr_cu_moe_ep_experts_p2p", C.byref(self._ccfg), C.byref(self._cw_loc), len(self.experts_here),
                   comm.comm, expected_rows, ep, ws.data_ptr(), ws.numel(), st)
+        if events is not None:
+            events[2].record()
         _lib.call("mlxr_cu_moe_ep_combine_p2p", C.byref(self._ccfg), C.byref(self._cw_rep), comm.comm,
                   x.data_ptr() if T else None, T, pair_pos.data_ptr(), None if sg is None else sg.data_ptr(),
                   out.data_ptr() if T else None, ep, ws.data_ptr(), ws.numel(), st)
+        if events is not None:
+            events[3].record()
         return out
 
 
