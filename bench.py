@@ -80,11 +80,33 @@ def ncu_traffic(kernel_key: str):
     return None
 
 
+def _clock_sampler_proc(uuid, stop, out_q, period_s):
+    """Runs in its own process (spawned): polls the GPU's SM clock and clock
+    event reasons through NVML until `stop` is set. Being another process,
+    it takes no time from the benchmark's launching thread."""
+    samples, err, max_mhz = [], None, None
+    try:
+        import pynvml as N
+
+        N.nvmlInit()
+        h = N.nvmlDeviceGetHandleByUUID(uuid)
+        max_mhz = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+        names = {k: getattr(N, v, 0) for k, v in ClockSampler.REASONS}
+        while not stop.is_set():
+            mhz = N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)
+            rs = N.nvmlDeviceGetCurrentClocksEventReasons(h)
+            samples.append((mhz, [k for k, bit in names.items() if rs & bit]))
+            time.sleep(period_s)
+    except Exception as e:  # no NVML: report it instead of a clock
+        err = f"nvml unavailable: {e}"[:200]
+    out_q.put((samples, max_mhz, err))
+
+
 class ClockSampler:
     """SM clock and clock-event (throttle) reasons sampled through NVML every
-    5 ms while the timed region runs (the nvidia-smi clocks query reads the
-    same counters, but its 200 ms period is longer than a timed region).
-    Read-only: no clock or power setting is touched."""
+    5 ms while the timed region runs, in a separate process (the nvidia-smi
+    clocks query reads the same counters, but its 200 ms period is longer
+    than a timed region). Read-only: no clock or power setting is touched."""
 
     REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
                ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
@@ -94,52 +116,33 @@ class ClockSampler:
 
     def __init__(self, uuid: str):
         self.uuid = uuid
-        self.samples = []
+        self.p = None
         self.err = None
-        self._stop = threading.Event()
-        self.t = None
 
     def start(self):
-        try:
-            import pynvml as N
+        import multiprocessing as mp
 
-            N.nvmlInit()
-            self.N = N
-            self.h = N.nvmlDeviceGetHandleByUUID(self.uuid)
-            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM)
-        except Exception as e:  # no NVML: report it instead of a clock
-            self.err = f"nvml unavailable: {e}"[:200]
-            return
-        self.t = threading.Thread(target=self._run, daemon=True)
-        self.t.start()
-
-    def _run(self):
-        N = self.N
-        while not self._stop.is_set():
-            try:
-                mhz = N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM)
-                rs = N.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                self.samples.append((mhz, rs))
-            except Exception as e:
-                self.err = str(e)[:200]
-                return
-            time.sleep(0.005)
+        ctx = mp.get_context("spawn")
+        self.stop_ev, self.q = ctx.Event(), ctx.Queue()
+        self.p = ctx.Process(target=_clock_sampler_proc, args=(self.uuid, self.stop_ev, self.q, 0.005), daemon=True)
+        self.p.start()
+        time.sleep(2.0)  # let the sampler start polling before the timed region
 
     def stop(self):
-        if self.t is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "error": self.err}
-        self._stop.set()
-        self.t.join(timeout=2)
-        sm = [m for m, _ in self.samples]
-        reasons = set()
-        for _, rs in self.samples:
-            for name, const in self.REASONS:
-                if rs & getattr(self.N, const, 0):
-                    reasons.add(name)
-        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
-               "reasons": sorted(reasons), "samples": len(sm), "source": "nvml 5 ms"}
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "error": "not started"}
+        self.stop_ev.set()
+        try:
+            samples, max_mhz, err = self.q.get(timeout=30)
+        except Exception as e:
+            samples, max_mhz, err = [], None, f"sampler: {e}"[:200]
+        self.p.join(timeout=5)
+        sm = [m for m, _ in samples]
+        reasons = sorted({r for _, rs in samples for r in rs})
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max_mhz, "reasons": reasons,
+               "samples": len(sm), "source": "nvml 5 ms, separate process"}
         if not sm:
-            out["error"] = self.err or "no samples"
+            out["error"] = err or "no samples"
         return out
 
 
@@ -491,6 +494,9 @@ def headline_ep(args, torch, dist, dev, st, flush, blk_full, world, rank):
     blk.status()
     tt = timer.totals()
     per = torch.tensor([sum(tt["prefill"]), sum(tt["decode"])], dtype=torch.float64, device=dev)
+    med = torch.tensor([statistics.median(tt["prefill"]), statistics.median(tt["decode"]),
+                        max(tt["prefill"]), max(tt["decode"])], dtype=torch.float64, device=dev)
+    dist.all_reduce(med, op=dist.ReduceOp.MAX)
     tot = per.sum().reshape(1).clone()
     dist.all_reduce(tot, op=dist.ReduceOp.MAX)
     dist.all_reduce(per, op=dist.ReduceOp.MAX)
@@ -531,6 +537,7 @@ def headline_ep(args, torch, dist, dev, st, flush, blk_full, world, rank):
     comm.close()
     launches = (ep_kernels_per_forward(cfg, Tp, world) + ep_kernels_per_forward(cfg, Td, world)) * args.steps
     forwards = {n: dict(tokens=T_, tokens_per_rank=Tr, ms=float(per[i].item()) / args.steps,
+                        ms_median=float(med[i].item()), ms_max=float(med[2 + i].item()),
                         phases_ms={k: round(float(phase[i, j].item()), 5)
                                    for j, k in enumerate(("dispatch", "experts", "combine"))})
                 for i, (n, T_, Tr) in enumerate((("prefill", PREFILL_T, Tp), ("decode", DECODE_T, Td)))}
