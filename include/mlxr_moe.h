@@ -114,6 +114,38 @@ MLXR_CU_API int mlxr_cu_gather_qmm(const void* x, mlxr_cu_dtype x_dtype, int64_t
                        const uint32_t* lhs_indices, const uint32_t* rhs_indices, int64_t num_indices, int transpose,
                        int group_size, int bits, const char* mode, int sorted_indices, void* out, void* stream);
 
+/* gather_qmm with a caller-provided workspace (the same call as
+ * mlxr_cu_gather_qmm, quantization.rs:171-221, as QuantizedSwitchLinear::apply
+ * issues it, crates/mlxr-lm/src/nn/switch.rs:148-167). For bf16 x, transpose,
+ * group_size 64, bits 4 or 8, K and N multiples of 128 and at most 1024
+ * weight batches, the rows f = p * M + m are sorted by rhs[p] on the device
+ * (counting sort, any index order), gathered (x[lhs[p]][m]) and multiplied on
+ * the tensor cores by the block's grouped dequantising GEMM (tcgen05, fp32
+ * accumulation, weights dequantised to bf16), then written back in index
+ * order; every other shape runs mlxr_cu_gather_qmm unchanged (no workspace
+ * used). Out-of-range indices are reported through mlxr_cu_op_status. The
+ * workspace must be 256-byte aligned and at least
+ * mlxr_cu_gather_qmm_workspace_size bytes (0 when the shape takes the
+ * general kernel). */
+MLXR_CU_API int mlxr_cu_gather_qmm_workspace_size(mlxr_cu_dtype x_dtype, int64_t x_batch, int64_t M, int64_t K,
+                                                  int64_t w_batch, int64_t N, int64_t num_indices, int transpose,
+                                                  int group_size, int bits, size_t* bytes);
+MLXR_CU_API int mlxr_cu_gather_qmm_ws(const void* x, mlxr_cu_dtype x_dtype, int64_t x_batch, int64_t M, int64_t K,
+                                      const uint32_t* w, const void* scales, const void* biases, int64_t w_batch,
+                                      int64_t N, const uint32_t* lhs_indices, const uint32_t* rhs_indices,
+                                      int64_t num_indices, int transpose, int group_size, int bits, const char* mode,
+                                      int sorted_indices, void* out, void* workspace, size_t workspace_bytes,
+                                      void* stream);
+
+/* quantized_matmul with a caller-provided workspace (QuantizedLinear::forward,
+ * crates/mlxr/src/layers/quantized.rs:356-371): the one-matrix case of
+ * mlxr_cu_gather_qmm_ws (x_batch 1, w_batch 1, one index, M rows); workspace
+ * size from mlxr_cu_gather_qmm_workspace_size(x_dtype, 1, M, K, 1, N, 1, ...). */
+MLXR_CU_API int mlxr_cu_quantized_matmul_ws(const void* x, mlxr_cu_dtype x_dtype, int64_t M, int64_t K,
+                                            const uint32_t* w, const void* scales, const void* biases, int64_t N,
+                                            int transpose, int group_size, int bits, const char* mode, void* out,
+                                            void* workspace, size_t workspace_bytes, void* stream);
+
 /* gather_mm (crates/mlxr/src/ops/arithmetic.rs:1577-1609 -> mlx_gather_mm):
  * out[p] = a[lhs[p]] @ b[rhs[p]], a [a_batch, M, K], b [b_batch, K, N], all in
  * dtype, fp32 accumulation. */

@@ -54,6 +54,20 @@ extern "C" {
                               lhs: *const u32, rhs: *const u32, num_indices: i64, transpose: c_int,
                               group_size: c_int, bits: c_int, mode: *const c_char, sorted_indices: c_int,
                               out: *mut c_void, stream: *mut c_void) -> c_int;
+    pub fn mlxr_cu_gather_qmm_workspace_size(x_dtype: c_int, x_batch: i64, m: i64, k: i64, w_batch: i64, n: i64,
+                                             num_indices: i64, transpose: c_int, group_size: c_int, bits: c_int,
+                                             bytes: *mut usize) -> c_int;
+    pub fn mlxr_cu_gather_qmm_ws(x: *const c_void, x_dtype: c_int, x_batch: i64, m: i64, k: i64, w: *const u32,
+                                 scales: *const c_void, biases: *const c_void, w_batch: i64, n: i64,
+                                 lhs: *const u32, rhs: *const u32, num_indices: i64, transpose: c_int,
+                                 group_size: c_int, bits: c_int, mode: *const c_char, sorted_indices: c_int,
+                                 out: *mut c_void, workspace: *mut c_void, workspace_bytes: usize,
+                                 stream: *mut c_void) -> c_int;
+    pub fn mlxr_cu_quantized_matmul_ws(x: *const c_void, x_dtype: c_int, m: i64, k: i64, w: *const u32,
+                                       scales: *const c_void, biases: *const c_void, n: i64, transpose: c_int,
+                                       group_size: c_int, bits: c_int, mode: *const c_char, out: *mut c_void,
+                                       workspace: *mut c_void, workspace_bytes: usize,
+                                       stream: *mut c_void) -> c_int;
     pub fn mlxr_cu_gather_mm(a: *const c_void, b: *const c_void, dtype: c_int, a_batch: i64, m: i64, k: i64,
                              b_batch: i64, n: i64, lhs: *const u32, rhs: *const u32, num_indices: i64,
                              sorted_indices: c_int, out: *mut c_void, stream: *mut c_void) -> c_int;

@@ -593,6 +593,145 @@ static Layout ep_experts_layout(const mlxr_cu_moe_config* lc, int64_t num_pairs,
   return make_layout(lc, num_pairs, num_rows);
 }
 
+// -------------------------------------------- gather_qmm on tensor cores --
+// gather_qmm (crates/mlxr/src/ops/quantization.rs:171-221) as QuantizedSwitchLinear::apply
+// (crates/mlxr-lm/src/nn/switch.rs:148-167) issues it: bf16 rows, weights [E, N, K] 4- or
+// 8-bit with group 64, transpose. The rows f = p * M + m of the output are
+// treated as single-expert "tokens" (top-1, expert rhs[p]) and run through the
+// block's machinery: the counting sort by expert builds the expert-sorted
+// order and tile list, the rows are gathered (x[lhs[p]][m]), one grouped
+// dequantising GEMM (tcgen05, plain epilogue) computes the expert-sorted
+// outputs, and a final copy puts them back in index order.
+
+// flat[f] = rhs[f / M] (or f / M without rhs); an index outside [0, E) is
+// reported and replaced by expert 0 so the pass stays in bounds.
+__global__ void gqmm_flat_experts_kernel(const uint32_t* __restrict__ rhs, int64_t R, int64_t M, int E,
+                                         int32_t* __restrict__ flat, int* status) {
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; f < R; f += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t p = f / M;
+    const int64_t e = rhs ? (int64_t)rhs[p] : p;
+    if (e < 0 || e >= E) {
+      atomicCAS(status, 0, (int)kDevBadIndex);
+      flat[f] = 0;
+    } else {
+      flat[f] = (int32_t)e;
+    }
+  }
+}
+
+// xs[pos] = x[lhs[p]][m] for f = sorted[pos] = p * M + m (lhs absent: p),
+// one warp per row with eight 16-byte loads in flight per lane; kperm stores
+// each 8-element chunk in the 4-bit dequantiser's K order {0,4,1,5,2,6,3,7}.
+__global__ void __launch_bounds__(256) gqmm_gather_kernel(const int32_t* __restrict__ sorted, int64_t R,
+                                                         const uint32_t* __restrict__ lhs, int64_t M,
+                                                         int64_t x_batch, const uint16_t* __restrict__ x, int D,
+                                                         int kperm, uint16_t* __restrict__ xs, int* status) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int dvec = D / 8;
+  for (int64_t pos = (int64_t)blockIdx.x * 8 + warp; pos < R; pos += (int64_t)gridDim.x * 8) {
+    const int64_t f = sorted[pos];
+    if (f < 0 || f >= R) {
+      if (lane == 0) atomicCAS(status, 0, (int)kDevBadIndex);
+      continue;
+    }
+    const int64_t p = f / M, m = f - p * M;
+    const int64_t src = lhs ? (int64_t)lhs[p] : p;
+    if (src < 0 || src >= x_batch) {
+      if (lane == 0) atomicCAS(status, 0, (int)kDevBadIndex);
+      continue;
+    }
+    const uint4* in = reinterpret_cast<const uint4*>(x + (src * M + m) * D);
+    uint4* outp = reinterpret_cast<uint4*>(xs + pos * D);
+    auto st = [&](int v, uint4 a) {
+      if (kperm) {
+        uint4 b;
+        b.x = __byte_perm(a.x, a.z, 0x5410);
+        b.y = __byte_perm(a.x, a.z, 0x7632);
+        b.z = __byte_perm(a.y, a.w, 0x5410);
+        b.w = __byte_perm(a.y, a.w, 0x7632);
+        a = b;
+      }
+      outp[v] = a;
+    };
+    int v = lane;
+    for (; v + 7 * 32 < dvec; v += 8 * 32) {
+      uint4 a[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a[j] = __ldg(in + v + j * 32);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) st(v + j * 32, a[j]);
+    }
+    for (; v < dvec; v += 32) st(v, __ldg(in + v));
+  }
+}
+
+// out[f] = y[inv[f]] (N columns, 16-byte copies); the pass's device status
+// is forwarded to the op family's status word at the end.
+__global__ void __launch_bounds__(256) gqmm_unpermute_kernel(const uint16_t* __restrict__ y,
+                                                            const int32_t* __restrict__ inv, int64_t R, int N,
+                                                            uint16_t* __restrict__ out, const int* status,
+                                                            int* op_status) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nvec = N / 8;
+  for (int64_t f = (int64_t)blockIdx.x * 8 + warp; f < R; f += (int64_t)gridDim.x * 8) {
+    const int64_t r = inv[f];
+    if (r < 0 || r >= R) {
+      if (lane == 0) atomicCAS(op_status, 0, (int)kDevBadIndex);
+      continue;
+    }
+    const uint4* in = reinterpret_cast<const uint4*>(y + r * N);
+    uint4* o = reinterpret_cast<uint4*>(out + f * N);
+    for (int v = lane; v < nvec; v += 32) o[v] = __ldg(in + v);
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    const int s = *reinterpret_cast<const volatile int*>(status);
+    if (s != 0) atomicCAS(op_status, 0, s);
+  }
+}
+
+// The tensor-core path applies to bf16 rows, transposed weights, group 64,
+// 4 or 8 bits, K and N multiples of 128, at most PERM_MAX_E experts.
+static bool gqmm_fast_ok(mlxr_cu_dtype x_dtype, int64_t K, int64_t N, int64_t w_batch, int transpose, int gs,
+                         int bits, int64_t R) {
+  return x_dtype == MLXR_CU_BFLOAT16 && transpose && gs == 64 && (bits == 4 || bits == 8) && K % 128 == 0 &&
+         N % 128 == 0 && K <= (int64_t)1 << 20 && N <= (int64_t)1 << 20 && w_batch >= 1 && w_batch <= PERM_MAX_E &&
+         R > 0 && R < (int64_t)1 << 30;
+}
+
+static mlxr_cu_moe_config gqmm_cfg(int64_t K, int64_t N, int64_t w_batch, int bits) {
+  mlxr_cu_moe_config c{};
+  c.hidden_size = (int32_t)K;
+  c.num_experts = (int32_t)w_batch;
+  c.num_experts_per_tok = 1;
+  c.moe_intermediate_size = (int32_t)N;
+  c.group_size = 64;
+  c.bits = bits;
+  c.shared_bits = bits;
+  c.norm_topk_prob = 1;
+  return c;
+}
+
+// The pass's workspace: the block layout for R one-expert rows (its status
+// slot, routing arrays, tile list, x_sorted [R, K] and the expert-sorted
+// outputs in its h buffer [R, N]) plus the flat expert array.
+struct GqmmLayout {
+  Layout L;
+  size_t flat = 0, total = 0;
+};
+static GqmmLayout gqmm_layout(const mlxr_cu_moe_config* c, int64_t R) {
+  GqmmLayout g;
+  g.L = make_layout(c, R);
+  g.flat = align256(g.L.total);
+  g.total = align256(g.flat + (size_t)R * 4);
+  return g;
+}
+
 }  // namespace mlxr
 
 using namespace mlxr;
@@ -1330,6 +1469,109 @@ int mlxr_cu_moe_ep_combine_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_
              (int64_t)c->world * c->cap, ysh, shared_gate, static_cast<uint16_t*>(out), at<int>(ws, L.status));
   MLXR_LAUNCH_CHECK("ep_combine_kernel(p2p)");
   return MLXR_CU_OK;
+}
+
+int mlxr_cu_gather_qmm_workspace_size(mlxr_cu_dtype x_dtype, int64_t x_batch, int64_t M, int64_t K, int64_t w_batch,
+                                      int64_t N, int64_t num_indices, int transpose, int group_size, int bits,
+                                      size_t* bytes) {
+  MLXR_CHECK_ARG(bytes != nullptr, "gather_qmm_workspace_size: bytes is NULL");
+  MLXR_CHECK_ARG(M >= 0 && K > 0 && N > 0 && x_batch > 0 && w_batch > 0 && num_indices >= 0,
+                 "gather_qmm_workspace_size: bad shape");
+  group_size = group_size == 0 ? 64 : group_size;
+  bits = bits == 0 ? 4 : bits;
+  const int64_t R = num_indices * M;
+  *bytes = 0;
+  if (!gqmm_fast_ok(x_dtype, K, N, w_batch, transpose, group_size, bits, R)) return MLXR_CU_OK;
+  const mlxr_cu_moe_config c = gqmm_cfg(K, N, w_batch, bits);
+  *bytes = gqmm_layout(&c, R).total;
+  return MLXR_CU_OK;
+}
+
+int mlxr_cu_gather_qmm_ws(const void* x, mlxr_cu_dtype x_dtype, int64_t x_batch, int64_t M, int64_t K,
+                          const uint32_t* w, const void* scales, const void* biases, int64_t w_batch, int64_t N,
+                          const uint32_t* lhs_indices, const uint32_t* rhs_indices, int64_t num_indices,
+                          int transpose, int group_size, int bits, const char* mode, int sorted_indices, void* out,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  const int gs = group_size == 0 ? 64 : group_size;
+  const int b = bits == 0 ? 4 : bits;
+  const int64_t R = num_indices * M;
+  const bool fast = (mode == nullptr || std::strcmp(mode, "affine") == 0) &&
+                    gqmm_fast_ok(x_dtype, K, N, w_batch, transpose, gs, b, R) && x && w && scales && biases && out;
+  if (!fast)  // every other shape: the general CUDA-core kernel (no workspace)
+    return mlxr_cu_gather_qmm(x, x_dtype, x_batch, M, K, w, scales, biases, w_batch, N, lhs_indices, rhs_indices,
+                              num_indices, transpose, group_size, bits, mode, sorted_indices, out, stream);
+  MLXR_CHECK_ARG(lhs_indices || num_indices <= x_batch, "gather_qmm: num_indices exceeds x batch without lhs_indices");
+  MLXR_CHECK_ARG(rhs_indices || num_indices <= w_batch, "gather_qmm: num_indices exceeds w batch without rhs_indices");
+  MLXR_CHECK_ARG(aligned16(x) && aligned16(out) && aligned16(w), "gather_qmm_ws: x, out and w must be 16-byte aligned");
+  MLXR_CHECK_ARG((reinterpret_cast<uintptr_t>(scales) & 3) == 0 && (reinterpret_cast<uintptr_t>(biases) & 3) == 0,
+                 "gather_qmm_ws: scales/biases must be 4-byte aligned");
+  const mlxr_cu_moe_config c = gqmm_cfg(K, N, w_batch, b);
+  const GqmmLayout G = gqmm_layout(&c, R);
+  const Layout& L = G.L;
+  if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) != 0 || workspace_bytes < G.total)
+    return set_error(MLXR_CU_ERR_WORKSPACE,
+                     "gather_qmm_ws: workspace NULL, not 256-byte aligned or smaller than %zu bytes", G.total);
+  int* op_status = op_status_word();
+  if (!op_status) return MLXR_CU_ERR_CUDA;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* ws = workspace;
+  int* status = at<int>(ws, L.status);
+  MLXR_CUDA_TRY(cudaMemsetAsync(status, 0, kStatusSlotBytes, st));
+  int32_t* flat = at<int32_t>(ws, G.flat);
+  const int fgrid = (int)std::min<int64_t>((R + 255) / 256, 4 * 148);
+  launch_pdl(gqmm_flat_experts_kernel, fgrid, 256, 0, st, rhs_indices, R, M, (int)w_batch, flat, status);
+  MLXR_LAUNCH_CHECK("gqmm_flat_experts_kernel");
+  // Counting sort by expert (no row gather: the rows come through lhs below).
+  if (int rc = run_permute(L, flat, nullptr, ws, at<int32_t>(ws, L.counts), at<int32_t>(ws, L.offsets),
+                           at<int32_t>(ws, L.sorted), at<int32_t>(ws, L.inv), nullptr, 0, st))
+    return rc;
+  const int ggrid = (int)std::min<int64_t>((R + 7) / 8, 4 * 148);
+  launch_pdl(gqmm_gather_kernel, ggrid, 256, 0, st, at<int32_t>(ws, L.sorted), R, lhs_indices, M, x_batch,
+             static_cast<const uint16_t*>(x), (int)K, b == 4 ? 1 : 0, at<uint16_t>(ws, L.xs), status);
+  MLXR_LAUNCH_CHECK("gqmm_gather_kernel");
+  GroupedGemmProblem p{};
+  // Two 128-row blocks of the weight per work item (two accumulators, two
+  // MMA issuers, plain stores) when N allows it, as the block's down
+  // projection runs.
+  p.pair = (N % 256 == 0) ? 1 : 0;
+  p.nmat = p.pair ? 2 : 1;
+  p.bn = L.bn1;
+  p.bits = b;
+  p.w[0] = p.w[1] = w;
+  p.s[0] = p.s[1] = static_cast<const uint16_t*>(scales);
+  p.b[0] = p.b[1] = static_cast<const uint16_t*>(biases);
+  p.w_rows = w_batch * N;
+  p.n_out = (int)N;
+  p.k_dim = (int)K;
+  p.num_experts = (int)w_batch;
+  p.act = at<uint16_t>(ws, L.xs);
+  p.act_rows = L.rows_pad;
+  p.tiles = at<GemmTile>(ws, L.t1);
+  p.num_tiles = at<int32_t>(ws, L.n1);
+  p.max_tiles = L.max_t1;
+  p.out = at<uint16_t>(ws, L.h);
+  p.out_rows = L.rows;
+  p.perm_out = 0;
+  p.status = status;
+  p.splits = L.s1;
+  p.max_split_rows = L.split_rows;
+  p.partial = L.split_rows ? at<float>(ws, L.part) : nullptr;
+  p.counters = L.split_rows ? at<int32_t>(ws, L.cnt) : nullptr;
+  p.sched = status + kSchedExperts1;
+  if (int rc = launch_grouped_gemm(p, st)) return rc;
+  launch_pdl(gqmm_unpermute_kernel, ggrid, 256, 0, st, at<uint16_t>(ws, L.h), at<int32_t>(ws, L.inv), R, (int)N,
+             static_cast<uint16_t*>(out), status, op_status);
+  MLXR_LAUNCH_CHECK("gqmm_unpermute_kernel");
+  return MLXR_CU_OK;
+}
+
+int mlxr_cu_quantized_matmul_ws(const void* x, mlxr_cu_dtype x_dtype, int64_t M, int64_t K, const uint32_t* w,
+                                const void* scales, const void* biases, int64_t N, int transpose, int group_size,
+                                int bits, const char* mode, void* out, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+  // One weight matrix, M rows: the gather with one index and rows M.
+  return mlxr_cu_gather_qmm_ws(x, x_dtype, 1, M, K, w, scales, biases, 1, N, nullptr, nullptr, 1, transpose,
+                               group_size, bits, mode, 0, out, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

@@ -35,6 +35,9 @@ EXPORTS = (
     "mlxr_cu_dequantize",
     "mlxr_cu_quantized_matmul",
     "mlxr_cu_gather_qmm",
+    "mlxr_cu_gather_qmm_workspace_size",
+    "mlxr_cu_gather_qmm_ws",
+    "mlxr_cu_quantized_matmul_ws",
     "mlxr_cu_gather_mm",
     "mlxr_cu_moe_workspace_size",
     "mlxr_cu_moe_block_forward",
@@ -143,6 +146,12 @@ def _load():
     lib.mlxr_cu_quantized_matmul.argtypes = [P, I32, I64, I64, P, P, P, I64, I32, I32, I32, C.c_char_p, P, P]
     lib.mlxr_cu_gather_qmm.argtypes = [P, I32, I64, I64, I64, P, P, P, I64, I64, P, P, I64, I32, I32, I32,
                                        C.c_char_p, I32, P, P]
+    lib.mlxr_cu_gather_qmm_workspace_size.argtypes = [I32, I64, I64, I64, I64, I64, I64, I32, I32, I32,
+                                                      C.POINTER(C.c_size_t)]
+    lib.mlxr_cu_gather_qmm_ws.argtypes = [P, I32, I64, I64, I64, P, P, P, I64, I64, P, P, I64, I32, I32, I32,
+                                          C.c_char_p, I32, P, P, C.c_size_t, P]
+    lib.mlxr_cu_quantized_matmul_ws.argtypes = [P, I32, I64, I64, P, P, P, I64, I32, I32, I32, C.c_char_p, P, P,
+                                                C.c_size_t, P]
     lib.mlxr_cu_gather_mm.argtypes = [P, P, I32, I64, I64, I64, I64, I64, P, P, I64, I32, P, P]
     lib.mlxr_cu_moe_workspace_size.argtypes = [C.POINTER(MoeConfig), I64, C.POINTER(C.c_size_t)]
     lib.mlxr_cu_moe_block_forward.argtypes = [C.POINTER(MoeConfig), C.POINTER(MoeWeights), P, I64, P,

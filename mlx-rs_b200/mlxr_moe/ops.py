@@ -11,6 +11,7 @@ CUDA library through its C ABI on the current stream.
 """
 from __future__ import annotations
 
+import ctypes as C
 import math
 
 import torch
@@ -93,10 +94,22 @@ def quantized_matmul(x, w, scales, biases=None, transpose: bool = False, group_s
     M = x.numel() // K
     N = w.shape[0] if transpose else w.shape[1] * 32 // b
     out = torch.empty(x.shape[:-1] + (N,), dtype=x.dtype, device=x.device)
-    _lib.call("mlxr_cu_quantized_matmul", _ptr(x), _dt(x), M, K, _ptr(w.contiguous()), _ptr(scales.contiguous()),
+    ws = _workspace(x, 1, M, K, 1, N, 1, transpose, gs, b)
+    _lib.call("mlxr_cu_quantized_matmul_ws", _ptr(x), _dt(x), M, K, _ptr(w.contiguous()), _ptr(scales.contiguous()),
               _ptr(None if biases is None else biases.contiguous()), N, int(transpose), gs, b, _mode(mode),
-              _ptr(out), _stream(x))
+              _ptr(out), _ptr(ws), 0 if ws is None else ws.numel(), _stream(x))
     return out
+
+
+def _workspace(x, x_batch, M, K, w_batch, N, num_indices, transpose, gs, b):
+    """Device workspace of the tensor-core gather_qmm path (None when the
+    shape takes the general kernel)."""
+    n = C.c_size_t(0)
+    _lib.call("mlxr_cu_gather_qmm_workspace_size", _dt(x), x_batch, M, K, w_batch, N, num_indices, int(transpose),
+              gs, b, C.byref(n))
+    if n.value == 0:
+        return None
+    return torch.empty(int(n.value), dtype=torch.uint8, device=x.device)
 
 
 def _broadcast_indices(lhs, rhs, bx, bw, device):
@@ -116,6 +129,28 @@ def gather_qmm(x, w, scales, biases=None, lhs_indices=None, rhs_indices=None, tr
                group_size: int | None = None, bits: int | None = None, sorted_indices: bool = False,
                mode: str = "affine"):
     """out[idx] = x[lhs[idx]] @ dequant(w[rhs[idx]])^T; shape broadcast(lhs, rhs) + [M, N]."""
+    gs = group_size or DEFAULT_GROUP_SIZE
+    b = bits or DEFAULT_BITS
+    _cuda(x, w, scales, biases, lhs_indices, rhs_indices)
+    x = x.contiguous()
+    M, K = x.shape[-2], x.shape[-1]
+    N = w.shape[-2] if transpose else w.shape[-1] * 32 // b
+    lf, rf, shape, nx, nw = _broadcast_indices(lhs_indices, rhs_indices, x.shape[:-2], w.shape[:-2], x.device)
+    out = torch.empty(shape + (M, N), dtype=x.dtype, device=x.device)
+    ws = _workspace(x, nx, M, K, nw, N, lf.numel(), transpose, gs, b)
+    _lib.call("mlxr_cu_gather_qmm_ws", _ptr(x), _dt(x), nx, M, K, _ptr(w.contiguous()), _ptr(scales.contiguous()),
+              _ptr(None if biases is None else biases.contiguous()), nw, N, _ptr(lf), _ptr(rf), lf.numel(),
+              int(transpose), gs, b, _mode(mode), int(sorted_indices), _ptr(out), _ptr(ws),
+              0 if ws is None else ws.numel(), _stream(x))
+    return out
+
+
+def gather_qmm_general(x, w, scales, biases=None, lhs_indices=None, rhs_indices=None, transpose: bool = True,
+                       group_size: int | None = None, bits: int | None = None, sorted_indices: bool = False,
+                       mode: str = "affine"):
+    """gather_qmm through the general CUDA-core kernel for every shape
+    (mlxr_cu_gather_qmm, no workspace); the reference point of the tensor-core
+    path's tests."""
     gs = group_size or DEFAULT_GROUP_SIZE
     b = bits or DEFAULT_BITS
     _cuda(x, w, scales, biases, lhs_indices, rhs_indices)

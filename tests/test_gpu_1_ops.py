@@ -190,3 +190,95 @@ def test_out_of_range_index_reports_status():
         ops.op_status()
     assert ei.value.status == _lib.ERR_DEVICE_INDEX
     ops.op_status()  # cleared by the read
+
+
+def _ws_bytes(ops, x_batch, M, K, w_batch, N, P, bits):
+    import ctypes as C
+
+    from mlxr_moe import _lib
+
+    n = C.c_size_t(0)
+    _lib.call("mlxr_cu_gather_qmm_workspace_size", 0, x_batch, M, K, w_batch, N, P, 1, 64, bits, C.byref(n))
+    return n.value
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_gather_qmm_tensor_core_path_vs_oracle(bits):
+    """The tensor-core gather_qmm (counting sort by rhs, gather of x[lhs], the
+    grouped tcgen05 GEMM, write-back in index order) on unsorted rhs with lhs
+    indices and M > 1 rows per index, against the oracle (fp32 accumulation;
+    bf16 output and bf16-dequantised weights: |err| < 2e-2 + 1e-2 |ref|) and
+    against the general CUDA-core kernel."""
+    from mlxr_moe import ops
+
+    xb, M, K, E, N, P = 6, 3, 512, 12, 384, 40
+    assert _ws_bytes(ops, xb, M, K, E, N, P, bits) > 0
+    x = ops.synth_normal_bf16(0, 100 + bits, (xb, M, K), 1.0)
+    w = ops.synth_normal_bf16(0, 110 + bits, (E, N, K), 0.05)
+    wq, s, b = ops.quantize(w, 64, bits)
+    g = torch.Generator().manual_seed(bits)
+    lhs = torch.randint(0, xb, (P,), generator=g, dtype=torch.int32).cuda()
+    rhs = torch.randint(0, E, (P,), generator=g, dtype=torch.int32).cuda()
+    y = ops.gather_qmm(x, wq, s, b, lhs, rhs, True, 64, bits)
+    assert tuple(y.shape) == (P, M, N)
+    yo = O.gather_qmm(bf16_np(x), u32(wq), bf16_np(s), bf16_np(b), lhs.cpu().numpy(), rhs.cpu().numpy(), True, 64,
+                      bits)
+    np.testing.assert_allclose(y.float().cpu().numpy(), yo, atol=2e-2, rtol=1e-2)
+    yg = ops.gather_qmm_general(x, wq, s, b, lhs, rhs, True, 64, bits)
+    np.testing.assert_allclose(y.float().cpu().numpy(), yg.float().cpu().numpy(), atol=2e-2, rtol=1e-2)
+    ops.op_status()
+
+
+def test_gather_qmm_tensor_core_path_moe_sized():
+    """A switch-layer sized call (T=512 tokens, top-8 of 64 experts, D=1024,
+    N=768) through the tensor-core path against the oracle."""
+    from mlxr_moe import ops
+
+    T, Kt, E, D, N = 512, 8, 64, 1024, 768
+    x = ops.synth_normal_bf16(0, 120, (T, 1, 1, D), 1.0)
+    w = ops.synth_normal_bf16(0, 121, (E, N, D), 0.03)
+    wq, s, b = ops.quantize(w, 64, 4)
+    g = torch.Generator().manual_seed(7)
+    idx = torch.stack([torch.randperm(E, generator=g)[:Kt] for _ in range(T)]).to(torch.int32).cuda()
+    y = ops.gather_qmm(x, wq, s, b, None, idx, True, 64, 4)
+    assert tuple(y.shape) == (T, Kt, 1, N)
+    yo = O.gather_qmm(bf16_np(x).reshape(T, 1, D), u32(wq), bf16_np(s), bf16_np(b),
+                      np.repeat(np.arange(T), Kt).astype(np.int32), idx.reshape(-1).cpu().numpy(), True, 64, 4)
+    np.testing.assert_allclose(y.float().reshape(T * Kt, N).cpu().numpy(), yo.reshape(T * Kt, N), atol=2e-2,
+                               rtol=1e-2)
+    ops.op_status()
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_quantized_matmul_tensor_core_path(bits):
+    """QuantizedLinear::forward shape (transpose, bf16) on the tensor-core
+    path: M = 300 rows (two partial 128-row tiles) against the oracle."""
+    from mlxr_moe import ops
+
+    M, K, N = 300, 768, 512
+    assert _ws_bytes(ops, 1, M, K, 1, N, 1, bits) > 0
+    x = ops.synth_normal_bf16(0, 130 + bits, (M, K), 1.0)
+    w = ops.synth_normal_bf16(0, 140 + bits, (N, K), 0.04)
+    wq, s, b = ops.quantize(w, 64, bits)
+    y = ops.quantized_matmul(x, wq, s, b, True, 64, bits)
+    yo = O.quantized_matmul(bf16_np(x), u32(wq), bf16_np(s), bf16_np(b), True, 64, bits)
+    np.testing.assert_allclose(y.float().cpu().numpy(), yo, atol=2e-2, rtol=1e-2)
+    ops.op_status()
+
+
+def test_gather_qmm_tensor_core_path_bad_index_status():
+    """An out-of-range rhs index on the tensor-core path: the row is skipped
+    and the op status word reports it."""
+    from mlxr_moe import MlxrError, _lib, ops
+
+    ops.op_status()
+    x = ops.synth_normal_bf16(0, 150, (4, 1, 256), 1.0)
+    w = ops.synth_normal_bf16(0, 151, (3, 128, 256), 0.02)
+    wq, s, b = ops.quantize(w, 64, 4)
+    assert _ws_bytes(ops, 4, 1, 256, 3, 128, 4, 4) > 0
+    bad = torch.tensor([0, 7, 1, 2], dtype=torch.int32, device="cuda")
+    ops.gather_qmm(x, wq, s, b, None, bad, True, 64, 4)
+    with pytest.raises(MlxrError) as ei:
+        ops.op_status()
+    assert ei.value.status == _lib.ERR_DEVICE_INDEX
+    ops.op_status()
