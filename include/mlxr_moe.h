@@ -290,8 +290,10 @@ MLXR_CU_API int mlxr_cu_moe_status(const void* workspace, void* stream);
  * workspace instead. */
 MLXR_CU_API int mlxr_cu_op_status(void* stream);
 
-/* Router alone (moe.rs:123-138): logits = x @ gate^T (+bias) rounded to
- * bf16, softmax (fp32 inside, bf16 probabilities), top-k by (prob desc,
+/* Router alone (moe.rs:123-138): logits = bf16(fp32(x . gate[e]) + bias[e])
+ * where x . gate[e] is the exact dot product of the bf16 rows rounded once
+ * to fp32 (the same value whatever the summation order; T > 256 runs it on
+ * the int8 tensor cores), softmax (fp32 inside, bf16 probabilities), top-k by (prob desc,
  * expert asc), renormalised bf16 weights. logits / probs [T, E] bf16 may be
  * NULL. Bit-exact with the routing contract the oracle states.
  * model_kind 1 (Gemma 4, text.rs:622-664): x is the layer's h; logits are

@@ -19,7 +19,7 @@ LIB = os.path.join(HERE, "libmlxr_moe.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
-SOURCES = ["quant_ops.cu", "grouped_gemm.cu", "moe_block.cu"]
+SOURCES = ["quant_ops.cu", "grouped_gemm.cu", "router_tc.cu", "moe_block.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",

@@ -183,6 +183,19 @@ __device__ inline bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* a
   }
 }
 
+// After a producer stops (normally or on abort), wait (bounded) until every
+// TMA load it issued into a ring of STAGES slots has landed, so no copy is
+// still writing shared memory when the CTA exits. `issued` = loads issued.
+template <int STAGES>
+__device__ inline void drain_ring(uint64_t* full, uint32_t issued, volatile int* abort_flag, int* status) {
+  for (uint32_t s = 0; s < (uint32_t)STAGES && s < issued; ++s) {
+    const uint32_t last = issued - 1 - ((issued - 1 - s) % STAGES);
+    int dummy_abort = 0;
+    (void)abort_flag;
+    mbar_wait(&full[s], (last / STAGES) & 1, &dummy_abort, status);
+  }
+}
+
 // -------------------------------------------------------------- TMA -----
 __device__ inline void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t c0, int32_t c1) {
   asm volatile(

@@ -1,0 +1,205 @@
+// Exact dot products of bf16 vectors rounded once to fp32: the router
+// logit's sum (logit = bf16(fp32(sum x_i * w_i) + bias)). The product of two
+// bf16 values is exact, so the sum has one defined value whatever the
+// summation order; every router kernel produces its correctly rounded fp32
+// value (round to nearest, ties to even; an exact zero is +0).
+//
+//  * rn32_limbs: round a multi-limb integer times a power of two to fp32.
+//  * dot_rn32_warp: the exact sum by one warp with fixed-point limb
+//    accumulators (the fallback when a faster path cannot decide the result).
+//  * logit_from_f64: the bf16 logit when the sum is only known to lie in an
+//    interval; it is decided when both ends give the same bf16 value,
+//    since fp32 rounding, the fp32 bias add and bf16 rounding are all
+//    monotone non-decreasing.
+//  * rn32_i128: the rounding of an exact integer sum (the tensor-core path).
+#pragma once
+
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace mlxr {
+
+// Round (-1)^neg * mag * 2^lsb to fp32, nearest-even. mag: n little-endian
+// 64-bit limbs. Exact zero -> +0; a nonzero value that rounds to zero keeps
+// its sign; overflow -> +-inf; subnormal results are rounded once at 2^-149.
+__device__ inline float rn32_limbs(const uint64_t* mag, int n, int neg, int lsb) {
+  int top = n - 1;
+  while (top >= 0 && mag[top] == 0) --top;
+  if (top < 0) return 0.0f;
+  const int hb = top * 64 + 63 - __clzll((long long)mag[top]);
+  const uint32_t sign = neg ? 0x80000000u : 0u;
+  const int e = hb + lsb;
+  if (e > 127) return __uint_as_float(sign | 0x7f800000u);
+  int q = e - 23 < -149 ? -149 : e - 23;
+  const int sh = q - lsb;  // bits of mag below the result's last place
+  auto bits_at = [&](int pos) -> uint64_t {  // 64 bits of mag starting at bit pos (pos >= 0)
+    const int li = pos >> 6, off = pos & 63;
+    uint64_t v = li < n ? mag[li] >> off : 0u;
+    if (off && li + 1 < n) v |= mag[li + 1] << (64 - off);
+    return v;
+  };
+  uint64_t mant;
+  if (sh <= 0) {
+    mant = mag[0] << (-sh);  // the value is below 2^24 units of 2^q: one limb, exact
+  } else {
+    mant = bits_at(sh) & ((1ull << 25) - 1);
+    const uint64_t rb = (bits_at(sh - 1)) & 1u;
+    bool sticky = false;
+    const int below = sh - 1;  // bits [0, below) are the sticky bits
+    for (int li = 0; li < n && li * 64 < below && !sticky; ++li) {
+      const int nb = below - li * 64;
+      const uint64_t m = nb >= 64 ? ~0ull : ((1ull << nb) - 1);
+      sticky = (mag[li] & m) != 0;
+    }
+    if (rb && (sticky || (mant & 1u))) ++mant;
+  }
+  if (mant == (1ull << 24)) {
+    mant >>= 1;
+    ++q;
+  }
+  if (mant >= (1ull << 23)) {
+    if (q + 23 > 127) return __uint_as_float(sign | 0x7f800000u);
+    return __uint_as_float(sign | ((uint32_t)(q + 150) << 23) | ((uint32_t)mant & 0x7fffffu));
+  }
+  return __uint_as_float(sign | (uint32_t)mant);
+}
+
+// bf16 logit of a sum s (fp32 already): bf16(s + bias).
+__device__ __forceinline__ uint16_t logit_bits(float s, float bias) { return f32_to_bf16_bits(__fadd_rn(s, bias)); }
+
+// The exact sum of x[i] * w[i] over i < D by the whole warp (every lane
+// calls it with the same arguments; every lane gets the result). Lane j
+// takes elements j, j+32, ...: each product m * 2^p (|m| < 2^16,
+// p >= -266) is added into the lane's positive or negative 576-bit
+// accumulator (last bit 2^-266); the accumulators are summed across the
+// warp with carries, and the difference is rounded once. Infinite or NaN
+// operands give NaN (a NaN product, or infinite products of both signs) or
+// +-inf, as the real sum would.
+static __device__ __noinline__ float dot_rn32_warp(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, int D,
+                                           int lane) {
+  constexpr int NL = 9;
+  uint64_t pos[NL], neg[NL];
+#pragma unroll
+  for (int k = 0; k < NL; ++k) pos[k] = neg[k] = 0u;
+  uint32_t cls = 0;  // bit 0: NaN product, bit 1: +inf product, bit 2: -inf product
+  for (int i = lane; i < D; i += 32) {
+    const uint32_t a = x[i], b = w[i];
+    const bool fa = ((a >> 7) & 0xffu) == 0xffu, fb = ((b >> 7) & 0xffu) == 0xffu;
+    if (fa || fb) {
+      const bool na = fa && (a & 0x7fu), nb = fb && (b & 0x7fu);
+      const bool za = (a & 0x7fffu) == 0, zb = (b & 0x7fffu) == 0;
+      if (na || nb || (fa && zb) || (fb && za)) cls |= 1u;
+      else cls |= (((a ^ b) & 0x8000u) == 0) ? 2u : 4u;
+      continue;
+    }
+    const int bea = (a >> 7) & 0xff, beb = (b >> 7) & 0xff;
+    const uint32_t ma = bea ? ((a & 0x7fu) | 0x80u) : (a & 0x7fu);
+    const uint32_t mb = beb ? ((b & 0x7fu) | 0x80u) : (b & 0x7fu);
+    const uint64_t m = (uint64_t)(ma * mb);
+    if (m == 0) continue;
+    const int at = ((bea ? bea : 1) - 134) + ((beb ? beb : 1) - 134) + 266;
+    uint64_t* acc = ((a ^ b) & 0x8000u) ? neg : pos;
+    const int li = at >> 6, off = at & 63;
+    const uint64_t lo = m << off, hi = off ? (m >> (64 - off)) : 0u;
+    uint64_t t = acc[li] + lo;
+    uint32_t c = t < lo;
+    acc[li] = t;
+    if (li + 1 < NL) {
+      const uint64_t t1 = acc[li + 1] + hi;
+      const uint32_t c1 = t1 < hi;
+      acc[li + 1] = t1 + c;
+      c = c1 | (acc[li + 1] < t1);
+      for (int k = li + 2; k < NL && c; ++k) {
+        acc[k] += 1u;
+        c = acc[k] == 0u;
+      }
+    }
+  }
+  cls = __reduce_or_sync(0xffffffffu, cls);
+  if (cls & 1u || (cls & 6u) == 6u) return __uint_as_float(0x7fc00000u);
+  if (cls & 2u) return __uint_as_float(0x7f800000u);
+  if (cls & 4u) return __uint_as_float(0xff800000u);
+  // Sum the accumulators over the warp (xor butterfly; every lane ends with the total).
+#pragma unroll 1
+  for (int s = 16; s >= 1; s >>= 1) {
+    uint32_t cp = 0, cn = 0;
+#pragma unroll
+    for (int k = 0; k < NL; ++k) {
+      const uint64_t op = __shfl_xor_sync(0xffffffffu, pos[k], s);
+      const uint64_t on = __shfl_xor_sync(0xffffffffu, neg[k], s);
+      const uint64_t tp = pos[k] + op, tn = neg[k] + on;
+      const uint32_t c1p = tp < op, c1n = tn < on;
+      pos[k] = tp + cp;
+      neg[k] = tn + cn;
+      cp = c1p | (pos[k] < tp);
+      cn = c1n | (neg[k] < tn);
+    }
+  }
+  int cmp = 0;
+#pragma unroll
+  for (int k = NL - 1; k >= 0; --k)
+    if (cmp == 0) cmp = pos[k] > neg[k] ? 1 : (pos[k] < neg[k] ? -1 : 0);
+  uint64_t mag[NL];
+  uint32_t borrow = 0;
+#pragma unroll
+  for (int k = 0; k < NL; ++k) {
+    const uint64_t big = cmp >= 0 ? pos[k] : neg[k], small = cmp >= 0 ? neg[k] : pos[k];
+    const uint64_t t = big - small;
+    const uint32_t b1 = big < small;
+    mag[k] = t - borrow;
+    borrow = b1 | (t < (uint64_t)borrow);
+  }
+  return rn32_limbs(mag, NL, cmp < 0, -266);
+}
+
+// fp32 rounding of a signed 128-bit integer times 2^lsb, with a fast path
+// through the hardware int64 -> fp32 conversion (correctly rounded) and an
+// exact exponent shift when the result is a normal number.
+__device__ __forceinline__ float rn32_i128(__int128 v, int lsb) {
+  const bool neg = v < 0;
+  const unsigned __int128 mag = neg ? (unsigned __int128)(-v) : (unsigned __int128)v;
+  if (mag == 0) return 0.0f;
+  if ((uint64_t)(mag >> 63) == 0) {
+    const float f = __ll2float_rn((long long)v);
+    const uint32_t fb = __float_as_uint(f);
+    const int ex = (int)((fb >> 23) & 0xffu) + lsb;
+    if (ex >= 2 && ex <= 254) return __uint_as_float((fb & 0x807fffffu) | ((uint32_t)ex << 23));
+  }
+  const uint64_t limbs[2] = {(uint64_t)mag, (uint64_t)(mag >> 64)};
+  return rn32_limbs(limbs, 2, neg, lsb);
+}
+
+// The bf16 logit of a sum known to lie within err of s (fp64): decided when
+// both ends of [s - err, s + err] give the same logit. Returns false when
+// the interval straddles a rounding boundary or s is not finite.
+__device__ __forceinline__ bool logit_from_f64(double s, double err, float bias, uint16_t* out) {
+  if (!isfinite(s) || !isfinite(err)) return false;
+  const uint16_t a = logit_bits(__double2float_rn(__dsub_rd(s, err)), bias);
+  const uint16_t b = logit_bits(__double2float_rn(__dadd_ru(s, err)), bias);
+  *out = a;
+  return a == b;
+}
+
+// bf16 (the low 16 bits of b) -> fp64, exact for every finite value: the
+// bf16 exponent and fraction bits placed at the bottom of the fp64 exponent
+// and the top of its fraction give the value times 2^-896 (a subnormal fp64
+// for bf16 subnormals), and the power-of-two scale restores it exactly. inf
+// and NaN come out finite (>= 2^128 in magnitude); callers detect them from
+// the largest |bits| of the row (>= 0x7f80).
+__device__ __forceinline__ double bf16_to_f64(uint32_t b) {
+  const uint32_t hi = ((b & 0x7fffu) << 13) | ((b & 0x8000u) << 16);
+  return __hiloint2double((int)hi, 0) * 0x1.0p+896;
+}
+
+// Error bound of an fp64 sum of D exact products that each went through at
+// most `depth` roundings: |s - S| <= gamma_depth * sum|x_i w_i| with
+// gamma_depth = depth 2^-53 / (1 - depth 2^-53), and sum|x_i w_i| <=
+// D max|x| max|w|. mx, mw: the largest |bf16 bits| of each row (finite).
+// The factor (depth + 8) 2^-52 covers gamma and the roundings of this bound.
+__device__ __forceinline__ double f64_sum_err(int depth, int D, uint32_t mx, uint32_t mw) {
+  const double f = (double)(depth + 8) * 0x1.0p-52 * (double)D;
+  return __dmul_ru(__dmul_ru(f, bf16_to_f64(mx)), bf16_to_f64(mw));
+}
+
+}  // namespace mlxr

@@ -1,6 +1,7 @@
 // Launch interface of the grouped dequantising GEMM (grouped_gemm.cu).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -56,6 +57,10 @@ struct GroupedGemmProblem {
 };
 
 int launch_grouped_gemm(const GroupedGemmProblem& p, cudaStream_t st);
+// 2-D row-major TMA tensor map (grouped_gemm.cu): `inner` elements of
+// elem_bytes per row, `rows` rows, box box_inner x box_rows.
+int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                uint64_t rows, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz);
 int num_sms_current();
 
 }  // namespace mlxr

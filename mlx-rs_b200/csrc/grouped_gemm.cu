@@ -23,7 +23,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 }
 
 // 2-D row-major tensor map: inner extent `inner` elements, `rows` rows.
-static int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
                        uint64_t rows, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz) {
   auto enc = get_encode_fn();
   if (!enc) return set_error(MLXR_CU_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");

@@ -228,19 +228,6 @@ __device__ inline uint4 dequant_words8(uint32_t w0, uint32_t w1, float s, float 
   return o;
 }
 
-// After a producer stops (normally or on abort), wait (bounded) until every
-// TMA load it issued into a ring of STAGES slots has landed, so no copy is
-// still writing shared memory when the CTA exits. `issued` = loads issued.
-template <int STAGES>
-__device__ inline void drain_ring(uint64_t* full, uint32_t issued, volatile int* abort_flag, int* status) {
-  for (uint32_t s = 0; s < (uint32_t)STAGES && s < issued; ++s) {
-    const uint32_t last = issued - 1 - ((issued - 1 - s) % STAGES);
-    int dummy_abort = 0;
-    (void)abort_flag;
-    mbar_wait(&full[s], (last / STAGES) & 1, &dummy_abort, status);
-  }
-}
-
 // Bounded wait until *p >= target (a counter other CTAs of this grid raise).
 __device__ inline bool wait_counter_geq(const int32_t* p, int target, volatile int* abort_flag, int* status) {
   const unsigned long long t0 = global_ns();

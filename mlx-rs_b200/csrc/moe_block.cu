@@ -20,6 +20,7 @@
 
 #include "common.cuh"
 #include "gemm_launch.h"
+#include "router_tc.h"
 #include "routing.cuh"
 
 namespace mlxr {
@@ -55,7 +56,7 @@ static inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 constexpr size_t kStatusSlotBytes = 256;
 constexpr int kSchedExperts1 = 32, kSchedExperts2 = 34, kSchedShared1 = 36, kSchedShared2 = 38;
 constexpr int kSplitRouterMaxT = 64;   // batches up to this size use router_split_kernel
-constexpr int kTileRouterMinT = 256;   // batches above this size use router_logits_tile_kernel
+constexpr int kTileRouterMinT = 256;   // batches above this size use the tensor-core router (router_tc.cu)
 
 struct Layout {
   // R: flat (token, k) rows; rows: expert rows the buffers hold (R, or fewer
@@ -70,7 +71,7 @@ struct Layout {
   int max_t1 = 0, max_t2 = 0, max_tsh = 0;
   size_t status = 0, logits = 0, idx = 0, w = 0, sig = 0, bcounts = 0, bbase = 0, counts = 0, offsets = 0,
          sorted = 0, inv = 0, t1 = 0, n1 = 0, t2 = 0, n2 = 0, tsh = 0, nsh = 0, xs = 0, h = 0, y = 0, xpad = 0,
-         hsh = 0, ysh = 0, part = 0, cnt = 0, ready = 0, gxr = 0, gxe = 0, total = 0;
+         hsh = 0, ysh = 0, part = 0, cnt = 0, ready = 0, gxr = 0, gxe = 0, rtc = 0, total = 0;
 };
 
 // Token-tile width from the mean number of rows per expert.
@@ -216,6 +217,12 @@ static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T, int64_t rows_c
     L.gxr = take((size_t)T * L.D * 2);
     L.gxe = take((size_t)T * L.D * 2);
   }
+  // The tensor-core router's digit planes: in the x_sorted buffer when they
+  // fit (the permute fills it only after the router has finished), else apart.
+  if (T > kTileRouterMinT && router_tc_supported(L.D)) {
+    const size_t need = router_tc_layout(T, L.E, L.D).total;
+    L.rtc = need <= (size_t)L.rows_pad * L.D * 2 ? L.xs : take(need);
+  }
   if (L.split_rows > 0) {
     const int smax = L.s1 > L.s2 ? L.s1 : L.s2;
     const int bmax = L.bn1 > L.bn2 ? L.bn1 : L.bn2;
@@ -305,24 +312,20 @@ static int run_router(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
                                                                         probs, sg, sig, counter, es);
     MLXR_LAUNCH_CHECK("router_split_kernel");
     return MLXR_CU_OK;
-  } else if (L.T > kTileRouterMinT) {
+  } else if (L.T > kTileRouterMinT && router_tc_supported(L.D)) {
+    // Large batches: the logits on the int8 tensor cores (router_tc.cu), then
+    // one warp per token routes them.
     uint16_t* lg = logits ? logits : at<uint16_t>(ws, L.logits);
-    static std::atomic<uint64_t> attr_done{0};  // 48 KB of dynamic shared memory
-    if (int rc = ensure_smem_attr(router_logits_tile_kernel, RT_TILE_SMEM, attr_done)) return rc;
-    const dim3 grid((unsigned)((L.E + RT_TE - 1) / RT_TE), (unsigned)((L.T + RT_TT - 1) / RT_TT));
-    launch_pdl(router_logits_tile_kernel, grid, RT_TILE_THREADS, RT_TILE_SMEM, st, xp, L.T, L.D, wg, L.E, rbias, lg);
-    MLXR_LAUNCH_CHECK("router_logits_tile_kernel");
+    RouterTcProblem rp{xp, L.T, wg, L.E, L.D, rbias, lg, at<void>(ws, L.rtc), at<int>(ws, L.status)};
+    if (int rc = launch_router_tc(rp, st)) return rc;
     launch_pdl(route_rows_kernel, (unsigned)((L.T + RT_ROUTE_WARPS - 1) / RT_ROUTE_WARPS), RT_ROUTE_WARPS * 32, RT_ROUTE_WARPS * L.E * sizeof(float), st, lg, xp, L.T, L.D, L.E, L.K, c->norm_topk_prob,
                                                                     at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w),
                                                                     probs, sg, sig, es);
     MLXR_LAUNCH_CHECK("route_rows_kernel");
     return MLXR_CU_OK;
-  } else if (L.T <= 256) {
-    launch_pdl(router_fused_kernel<1>, (unsigned)L.T, RT_THREADS, L.E * sizeof(float), st, 
-        xp, L.T, L.D, wg, L.E, rbias, L.K, c->norm_topk_prob, at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w),
-        logits, probs, sg, sig, es);
   } else {
-    launch_pdl(router_fused_kernel<4>, (unsigned)((L.T + 3) / 4), RT_THREADS, 4 * L.E * sizeof(float), st, 
+    // 64 < T <= 256 (and larger batches with D beyond the tensor-core path): one token per CTA.
+    launch_pdl(router_fused_kernel<1>, (unsigned)L.T, RT_THREADS, L.E * sizeof(float), st,
         xp, L.T, L.D, wg, L.E, rbias, L.K, c->norm_topk_prob, at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w),
         logits, probs, sg, sig, es);
   }

@@ -1,0 +1,34 @@
+// Launch interface of the tensor-core router logits (router_tc.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace mlxr {
+
+// Workspace of one launch: digit planes of the tokens and of the router
+// rows (4 int8 planes each, rows padded to the tile, D padded to 128) and
+// the per-row exponent / truncation count.
+struct RouterTcLayout {
+  int64_t Dp = 0, rows_pad_x = 0, rows_pad_w = 0;
+  size_t xdig = 0, wdig = 0, xinfo = 0, winfo = 0, total = 0;
+};
+RouterTcLayout router_tc_layout(int64_t T, int E, int D);
+bool router_tc_supported(int D);
+
+// logits lg [T, E] bf16 = bf16(fp32(exact x[t] . wg[e]) + bias[e]) (bias may be NULL).
+struct RouterTcProblem {
+  const uint16_t* x;   // [T, D] bf16, 16-byte aligned
+  int64_t T;
+  const uint16_t* wg;  // [E, D] bf16, 16-byte aligned
+  int E;
+  int D;
+  const float* bias;
+  uint16_t* lg;
+  void* workspace;     // router_tc_layout(T, E, D).total bytes, 256-byte aligned
+  int* status;         // device status word (timeouts)
+};
+int launch_router_tc(const RouterTcProblem& p, cudaStream_t st);
+
+}  // namespace mlxr

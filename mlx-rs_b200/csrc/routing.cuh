@@ -25,6 +25,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "exact_dot.cuh"
 #include "grouped_gemm.cuh"
 
 namespace mlxr {
@@ -227,11 +228,19 @@ __global__ void __launch_bounds__(RT_THREADS) router_fused_kernel(
     const uint4* wr[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) wr[j] = reinterpret_cast<const uint4*>(wg + (int64_t)(e0 + j < E ? e0 + j : E - 1) * D);
-    float acc[TPB][8];
+    // fp64 sums of the exact products (and of the squares, for the error
+    // bound); the logit is decided from the interval or, failing that, by
+    // the exact warp sum.
+    double acc[TPB][8];
+    uint32_t mx[TPB], mw[8];  // largest |bf16 bits| of each row (error bound, inf/NaN detection)
 #pragma unroll
-    for (int i = 0; i < TPB; ++i)
+    for (int i = 0; i < TPB; ++i) {
+      mx[i] = 0u;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+      for (int j = 0; j < 8; ++j) acc[i][j] = 0.0;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) mw[j] = 0u;
 #pragma unroll 2
     for (int c = lane; c < nchunks; c += 32) {
       uint4 xv[TPB], wv[8];
@@ -241,40 +250,54 @@ __global__ void __launch_bounds__(RT_THREADS) router_fused_kernel(
       for (int j = 0; j < 8; ++j) wv[j] = __ldg(wr[j] + c);
 #pragma unroll
       for (int el = 0; el < 8; ++el) {
-        float xf[TPB], wf[8];
+        double xf[TPB], wf[8];
 #pragma unroll
         for (int i = 0; i < TPB; ++i) {
           const uint32_t wd = el < 2 ? xv[i].x : el < 4 ? xv[i].y : el < 6 ? xv[i].z : xv[i].w;
-          xf[i] = (el & 1) ? bf_hi(wd) : bf_lo(wd);
+          const uint32_t b = (el & 1) ? (wd >> 16) : (wd & 0xffffu);
+          xf[i] = bf16_to_f64(b);
+          mx[i] = max(mx[i], b & 0x7fffu);
         }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const uint32_t wd = el < 2 ? wv[j].x : el < 4 ? wv[j].y : el < 6 ? wv[j].z : wv[j].w;
-          wf[j] = (el & 1) ? bf_hi(wd) : bf_lo(wd);
+          const uint32_t b = (el & 1) ? (wd >> 16) : (wd & 0xffffu);
+          wf[j] = bf16_to_f64(b);
+          mw[j] = max(mw[j], b & 0x7fffu);
         }
 #pragma unroll
         for (int i = 0; i < TPB; ++i)
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(xf[i], wf[j], acc[i][j]);
+          for (int j = 0; j < 8; ++j) acc[i][j] = __fma_rn(xf[i], wf[j], acc[i][j]);
       }
     }
-    float mine = 0.0f;
+#pragma unroll
+    for (int i = 0; i < TPB; ++i) mx[i] = __reduce_max_sync(0xffffffffu, mx[i]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) mw[j] = __reduce_max_sync(0xffffffffu, mw[j]);
+    const int depth = 8 * ((nchunks + 31) / 32) + 5;
+    uint16_t mine = 0;
 #pragma unroll
     for (int i = 0; i < TPB; ++i)
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        float v = acc[i][j];
+        double v = acc[i][j];
 #pragma unroll
-        for (int s = 16; s >= 1; s >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, s));
-        if (lane == i * 8 + j) mine = v;
+        for (int s = 16; s >= 1; s >>= 1) v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, s));
+        const int e = e0 + j < E ? e0 + j : E - 1;
+        const float b = bias ? bias[e] : 0.0f;
+        uint16_t lb;
+        if (mx[i] >= 0x7f80u || mw[j] >= 0x7f80u || !logit_from_f64(v, f64_sum_err(depth, D, mx[i], mw[j]), b, &lb)) {
+          const int64_t t = t0 + i < T ? t0 + i : T - 1;
+          lb = logit_bits(dot_rn32_warp(x + t * D, wg + (int64_t)e * D, D, lane), b);
+        }
+        if (lane == i * 8 + j) mine = lb;
       }
     if (lane < TPB * 8) {
       const int i = lane >> 3, e = e0 + (lane & 7);
       if (e < E) {
-        const float b = bias ? bias[e] : 0.0f;
-        const uint16_t lb = f32_to_bf16_bits(__fadd_rn(mine, b));
-        s_lg[i * E + e] = bf16_bits_to_f32(lb);
-        if (logits_out && t0 + i < T) logits_out[(t0 + i) * E + e] = lb;
+        s_lg[i * E + e] = bf16_bits_to_f32(mine);
+        if (logits_out && t0 + i < T) logits_out[(t0 + i) * E + e] = mine;
       }
     }
   }
@@ -320,11 +343,16 @@ __global__ void __launch_bounds__(RS_WARPS * 32) router_split_kernel(
 #pragma unroll
     for (int j = 0; j < EPW; ++j)
       wr[j] = reinterpret_cast<const uint4*>(wg + (int64_t)(e0 + j < E ? e0 + j : E - 1) * D);
-    float acc[TPB][EPW];
+    double acc[TPB][EPW];
+    uint32_t mx[TPB], mw[EPW];  // largest |bf16 bits| of each row (error bound, inf/NaN detection)
 #pragma unroll
-    for (int i = 0; i < TPB; ++i)
+    for (int i = 0; i < TPB; ++i) {
+      mx[i] = 0u;
 #pragma unroll
-      for (int j = 0; j < EPW; ++j) acc[i][j] = 0.0f;
+      for (int j = 0; j < EPW; ++j) acc[i][j] = 0.0;
+    }
+#pragma unroll
+    for (int j = 0; j < EPW; ++j) mw[j] = 0u;
     for (int cb = 0; cb < nchunks; cb += 32 * UNR) {
       uint4 xv[UNR][TPB], wv[UNR][EPW];
 #pragma unroll
@@ -342,40 +370,53 @@ __global__ void __launch_bounds__(RS_WARPS * 32) router_split_kernel(
         if (cb + 32 * u + lane >= nchunks) break;
 #pragma unroll
         for (int el = 0; el < 8; ++el) {
-          float xf[TPB], wf[EPW];
+          double xf[TPB], wf[EPW];
 #pragma unroll
           for (int i = 0; i < TPB; ++i) {
             const uint32_t wd = el < 2 ? xv[u][i].x : el < 4 ? xv[u][i].y : el < 6 ? xv[u][i].z : xv[u][i].w;
-            xf[i] = (el & 1) ? bf_hi(wd) : bf_lo(wd);
+            const uint32_t b = (el & 1) ? (wd >> 16) : (wd & 0xffffu);
+            xf[i] = bf16_to_f64(b);
+            mx[i] = max(mx[i], b & 0x7fffu);
           }
 #pragma unroll
           for (int j = 0; j < EPW; ++j) {
             const uint32_t wd = el < 2 ? wv[u][j].x : el < 4 ? wv[u][j].y : el < 6 ? wv[u][j].z : wv[u][j].w;
-            wf[j] = (el & 1) ? bf_hi(wd) : bf_lo(wd);
+            const uint32_t b = (el & 1) ? (wd >> 16) : (wd & 0xffffu);
+            wf[j] = bf16_to_f64(b);
+            mw[j] = max(mw[j], b & 0x7fffu);
           }
 #pragma unroll
           for (int i = 0; i < TPB; ++i)
 #pragma unroll
-            for (int j = 0; j < EPW; ++j) acc[i][j] = __fmaf_rn(xf[i], wf[j], acc[i][j]);
+            for (int j = 0; j < EPW; ++j) acc[i][j] = __fma_rn(xf[i], wf[j], acc[i][j]);
         }
       }
     }
-    float mine = 0.0f;
+#pragma unroll
+    for (int i = 0; i < TPB; ++i) mx[i] = __reduce_max_sync(0xffffffffu, mx[i]);
+#pragma unroll
+    for (int j = 0; j < EPW; ++j) mw[j] = __reduce_max_sync(0xffffffffu, mw[j]);
+    const int depth = 8 * ((nchunks + 31) / 32) + 5;
+    uint16_t mine = 0;
 #pragma unroll
     for (int i = 0; i < TPB; ++i)
 #pragma unroll
       for (int j = 0; j < EPW; ++j) {
-        float v = acc[i][j];
+        double v = acc[i][j];
 #pragma unroll
-        for (int s = 16; s >= 1; s >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, s));
-        if (lane == i * EPW + j) mine = v;
+        for (int s = 16; s >= 1; s >>= 1) v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, s));
+        const int e = e0 + j < E ? e0 + j : E - 1;
+        const float b = bias ? bias[e] : 0.0f;
+        uint16_t lb;
+        if (mx[i] >= 0x7f80u || mw[j] >= 0x7f80u || !logit_from_f64(v, f64_sum_err(depth, D, mx[i], mw[j]), b, &lb)) {
+          const int64_t t = t0 + i < T ? t0 + i : T - 1;
+          lb = logit_bits(dot_rn32_warp(x + t * D, wg + (int64_t)e * D, D, lane), b);
+        }
+        if (lane == i * EPW + j) mine = lb;
       }
     if (lane < TPB * EPW) {
       const int i = lane / EPW, e = e0 + lane % EPW;
-      if (e < E && t0 + i < T) {
-        const float b = bias ? bias[e] : 0.0f;
-        lg[(t0 + i) * E + e] = f32_to_bf16_bits(__fadd_rn(mine, b));
-      }
+      if (e < E && t0 + i < T) lg[(t0 + i) * E + e] = mine;
     }
   }
   // Publish this CTA's logits; the last CTA of the token block routes it.
@@ -393,147 +434,6 @@ __global__ void __launch_bounds__(RS_WARPS * 32) router_split_kernel(
     const int64_t t = t0 + i;
     route_token_warp(s_lg + i * E, t, E, K, renorm, lane, idx_out, w_out, probs_out, expert_scale);
     if (sig_out) shared_gate_warp(x + t * D, D, sg, lane, sig_out + t);
-  }
-}
-
-// Large batches: logits in CTA tiles of 32 tokens x 16 experts. Each
-// 32-chunk block of D (256 elements) of the tile's x rows and router rows is
-// copied to shared memory as bf16 by 8-byte cp.async into two planes, the low
-// and the high half of every 16-byte chunk ([plane][row][chunk][8 B]), double
-// buffered one block ahead. Warp w owns tokens 8*(w%4) .. +7 and experts
-// 8*(w/4) .. +7; lane j keeps the contract's chain over chunks j, j+32, ... of
-// D for each of its 64 (token, expert) pairs, two experts at a time with the
-// packed fp32x2 FMA (two IEEE round-to-nearest FMAs). Per half chunk a lane
-// loads the four elements of its 8 tokens and 8 experts (8-byte loads; a warp
-// reads 256 contiguous bytes, conflict-free) and widens them to fp32 in
-// registers (exact), so each logit is the same fp32 value as in
-// router_fused_kernel. (A layout that staged fp32 copies in shared memory
-// read twice the bytes per FMA and was bound by shared-memory bandwidth.)
-constexpr int RT_TT = 32, RT_TE = 16, RT_TILE_THREADS = 256;
-constexpr int RT_PLANE = (RT_TT + RT_TE) * 32 * 8;  // one half-chunk plane of a block: 12 KB
-constexpr int RT_BF_STAGE = 2 * RT_PLANE;           // one block: 24 KB
-constexpr int RT_TILE_SMEM = 2 * RT_BF_STAGE;       // double buffered: 48 KB
-
-__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src, bool valid) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(valid ? 8 : 0) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-
-__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-  return r;
-}
-__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
-}
-// d = a * b + d elementwise on two packed fp32 values (two IEEE fmaf).
-__device__ __forceinline__ void ffma2(uint64_t& d, uint64_t a, uint64_t b) {
-  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b));
-}
-// Element el (0..3) of a half chunk held as two bf16x2 words, as fp32.
-__device__ __forceinline__ float bf_el(const uint2& v, int el) {
-  const uint32_t w = el < 2 ? v.x : v.y;
-  return (el & 1) ? bf_hi(w) : bf_lo(w);
-}
-
-__global__ void __launch_bounds__(RT_TILE_THREADS, 2) router_logits_tile_kernel(const uint16_t* __restrict__ x, int64_t T,
-                                                                              int D, const uint16_t* __restrict__ wg,
-                                                                              int E, const float* __restrict__ bias,
-                                                                              uint16_t* __restrict__ lg) {
-  extern __shared__ __align__(16) uint8_t rt_smem[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e0 = blockIdx.x * RT_TE;
-  const int64_t t0 = (int64_t)blockIdx.y * RT_TT;
-  const int nchunks = D / 8;
-  const int nblocks = (nchunks + 31) / 32;
-  const uint32_t sbase = smem_u32(rt_smem);
-  auto stage_in = [&](int m) {
-    const uint32_t buf = sbase + (uint32_t)((m & 1) * RT_BF_STAGE);
-    for (int q = threadIdx.x; q < (RT_TT + RT_TE) * 32; q += RT_TILE_THREADS) {
-      const int r = q >> 5, cj = q & 31;
-      const int c = m * 32 + cj;
-      const uint16_t* src;
-      bool ok;
-      if (r < RT_TT) {
-        const int64_t t = t0 + r;
-        ok = t < T && c < nchunks;
-        src = x + (ok ? t : 0) * (int64_t)D + (ok ? c : 0) * 8;
-      } else {
-        const int e = e0 + (r - RT_TT);
-        ok = e < E && c < nchunks;
-        src = wg + (ok ? e : 0) * (int64_t)D + (ok ? c : 0) * 8;
-      }
-      cp_async8(buf + (uint32_t)(q * 8), src, ok);                 // plane 0: elements 0..3 of the chunk
-      cp_async8(buf + (uint32_t)(RT_PLANE + q * 8), src + 4, ok);  // plane 1: elements 4..7
-    }
-    cp_async_commit();
-  };
-  const int tg = warp & 3, eg = warp >> 2;
-  uint64_t acc[8][4];  // [token][expert pair]
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0ull;
-  stage_in(0);
-  for (int m = 0; m < nblocks; ++m) {
-    cp_async_wait_all();
-    __syncthreads();  // block m has landed for every thread, and block m-1's buffer is no longer read
-    if (m + 1 < nblocks) stage_in(m + 1);
-    if (m * 32 + lane < nchunks) {
-      const uint8_t* buf = rt_smem + (m & 1) * RT_BF_STAGE;
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {  // elements 4h .. 4h+3 of the chunk
-        const uint8_t* pl = buf + h * RT_PLANE;
-        uint2 xv[8], wv[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) xv[i] = *reinterpret_cast<const uint2*>(pl + ((tg * 8 + i) * 32 + lane) * 8);
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          wv[e] = *reinterpret_cast<const uint2*>(pl + ((RT_TT + eg * 8 + e) * 32 + lane) * 8);
-#pragma unroll
-        for (int el = 0; el < 4; ++el) {
-          uint64_t wp[4];
-#pragma unroll
-          for (int jp = 0; jp < 4; ++jp) wp[jp] = f2_pack(bf_el(wv[2 * jp], el), bf_el(wv[2 * jp + 1], el));
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float xe = bf_el(xv[i], el);
-            const uint64_t xx = f2_pack(xe, xe);
-#pragma unroll
-            for (int jp = 0; jp < 4; ++jp) ffma2(acc[i][jp], xx, wp[jp]);
-          }
-        }
-      }
-    }
-  }
-  float mine[2] = {0.0f, 0.0f};
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int jp = 0; jp < 4; ++jp) {
-      float va, vb;
-      f2_unpack(acc[i][jp], va, vb);
-#pragma unroll
-      for (int s = 16; s >= 1; s >>= 1) {
-        va = __fadd_rn(va, __shfl_xor_sync(0xffffffffu, va, s));
-        vb = __fadd_rn(vb, __shfl_xor_sync(0xffffffffu, vb, s));
-      }
-      const int ia = i * 8 + 2 * jp, ib = ia + 1;  // pair index = token * 8 + expert
-      if (lane == (ia & 31)) mine[ia >> 5] = va;
-      if (lane == (ib & 31)) mine[ib >> 5] = vb;
-    }
-#pragma unroll
-  for (int hh = 0; hh < 2; ++hh) {
-    const int idx = hh * 32 + lane;
-    const int i = idx >> 3, j = idx & 7;
-    const int64_t t = t0 + tg * 8 + i;
-    const int e = e0 + eg * 8 + j;
-    if (t < T && e < E) {
-      const float b = bias ? bias[e] : 0.0f;
-      lg[t * E + e] = f32_to_bf16_bits(__fadd_rn(mine[hh], b));
-    }
   }
 }
 

@@ -188,27 +188,120 @@ inline float exp_route(float x) {
   return a * 0x1.0p-64f;
 }
 
-// logit(t, e) = bf16_rne( sum + bias[e] ), where sum is the fp32 dot product
-// of x[t] and wg[e] in this fixed order: the D axis is cut into 16-byte
-// chunks of 8 elements; lane j (0..31) owns chunks j, j+32, j+64, ... and
-// folds each owned chunk's 8 elements in ascending order into one fmaf
-// chain; the 32 lane sums are then combined by an xor butterfly with
-// strides 16, 8, 4, 2, 1 (value at lane j becomes v[j] + v[j ^ s]).
+// Round (-1)^neg * mag * 2^lsb to fp32, to nearest with ties to even, where
+// mag is an n-limb little-endian unsigned integer. An exact zero gives +0; a
+// nonzero value that rounds to zero keeps its sign; above the fp32 range it
+// gives +-inf. Subnormal results are rounded once, at 2^-149.
+float rn32_limbs(const uint64_t* mag, int n, int neg, int lsb) {
+  int top = n - 1;
+  while (top >= 0 && mag[top] == 0) --top;
+  if (top < 0) return 0.0f;
+  const int hb = top * 64 + 63 - __builtin_clzll(mag[top]);  // highest set bit
+  const uint32_t sign = neg ? 0x80000000u : 0u;
+  const int e = hb + lsb;  // the value lies in [2^e, 2^(e+1))
+  if (e > 127) return u2f(sign | 0x7f800000u);
+  int q = std::max(e - 23, -149);  // exponent of the result's last place
+  const int sh = q - lsb;          // bits of mag below that place
+  auto bit = [&](int i) -> uint64_t { return (i >= 0 && i < 64 * n) ? (mag[i >> 6] >> (i & 63)) & 1u : 0u; };
+  uint64_t mant = 0;
+  for (int i = hb; i >= std::max(sh, 0); --i) mant = (mant << 1) | bit(i);
+  if (sh < 0) mant <<= -sh;
+  if (sh > 0) {
+    const uint64_t rb = bit(sh - 1);
+    bool sticky = false;
+    for (int i = sh - 2; i >= 0 && !sticky; --i) sticky = bit(i) != 0;
+    if (rb && (sticky || (mant & 1u))) ++mant;
+  }
+  if (mant == (1ull << 24)) {
+    mant >>= 1;
+    ++q;
+  }
+  if (mant >= (1ull << 23)) {
+    if (q + 23 > 127) return u2f(sign | 0x7f800000u);
+    return u2f(sign | ((uint32_t)(q + 150) << 23) | ((uint32_t)mant & 0x7fffffu));
+  }
+  return u2f(sign | (uint32_t)mant);  // subnormal (q == -149) or zero
+}
+
+// bf16 bits -> value = m * 2^p with m a signed integer, |m| < 2^8.
+inline void bf16_mp(uint16_t b, int* m, int* p) {
+  const int be = (b >> 7) & 0xff, f = b & 0x7f;
+  const int mag = be ? (f | 0x80) : f;
+  *p = (be ? be : 1) - 134;
+  *m = (b & 0x8000) ? -mag : mag;
+}
+
+// The exact dot product of two bf16 vectors rounded once to fp32. Each
+// product is an integer below 2^16 times 2^(px + pw) with px + pw >= -266, so
+// the positive and the negative products are summed exactly in two 576-bit
+// fixed-point accumulators whose last bit weighs 2^-266. With an infinite or
+// NaN operand the result is NaN when a product is NaN (NaN operand or
+// inf * 0) or when products of both signs are infinite, else +-inf: the value
+// of the real sum, independent of order.
+float dot_bf16_rn32(const uint16_t* x, const uint16_t* w, int D) {
+  constexpr int NL = 9;
+  uint64_t pos[NL] = {}, neg[NL] = {};
+  bool nan = false, pinf = false, ninf = false;
+  for (int i = 0; i < D; ++i) {
+    const uint16_t a = x[i], b = w[i];
+    const bool fa = ((a >> 7) & 0xff) == 0xff, fb = ((b >> 7) & 0xff) == 0xff;
+    if (fa || fb) {
+      const bool na = fa && (a & 0x7f), nb = fb && (b & 0x7f);
+      const bool za = (a & 0x7fff) == 0, zb = (b & 0x7fff) == 0;
+      if (na || nb || (fa && zb) || (fb && za)) nan = true;
+      else if (((a ^ b) & 0x8000) == 0) pinf = true;
+      else ninf = true;
+      continue;
+    }
+    int ma, pa, mb, pb;
+    bf16_mp(a, &ma, &pa);
+    bf16_mp(b, &mb, &pb);
+    const int64_t m = (int64_t)ma * mb;
+    if (m == 0) continue;
+    const int at = pa + pb + 266;
+    uint64_t* acc = m > 0 ? pos : neg;
+    const unsigned __int128 v = (unsigned __int128)(uint64_t)(m > 0 ? m : -m) << (at & 63);
+    int li = at >> 6;
+    uint64_t add[2] = {(uint64_t)v, (uint64_t)(v >> 64)};
+    unsigned carry = 0;
+    for (int k = li; k < NL; ++k) {
+      const uint64_t ad = (k - li < 2) ? add[k - li] : 0u;
+      const uint64_t t = acc[k] + ad;
+      const unsigned c1 = t < ad;
+      const uint64_t t2 = t + carry;
+      const unsigned c2 = t2 < t;
+      acc[k] = t2;
+      carry = c1 | c2;
+      if (k - li >= 1 && carry == 0) break;
+    }
+  }
+  if (nan || (pinf && ninf)) return u2f(0x7fc00000u);
+  if (pinf) return u2f(0x7f800000u);
+  if (ninf) return u2f(0xff800000u);
+  int cmp = 0;
+  for (int k = NL - 1; k >= 0 && cmp == 0; --k) cmp = pos[k] > neg[k] ? 1 : pos[k] < neg[k] ? -1 : 0;
+  const uint64_t* big = cmp >= 0 ? pos : neg;
+  const uint64_t* small = cmp >= 0 ? neg : pos;
+  uint64_t mag[NL];
+  unsigned borrow = 0;
+  for (int k = 0; k < NL; ++k) {
+    const uint64_t t = big[k] - small[k];
+    const unsigned b1 = big[k] < small[k];
+    mag[k] = t - borrow;
+    borrow = b1 | (t < (uint64_t)borrow);
+  }
+  return rn32_limbs(mag, NL, cmp < 0, -266);
+}
+
+// logit(t, e) = bf16_rne( fp32(sum) + bias[e] ): sum is the exact dot
+// product of x[t] and wg[e] (every product of two bf16 values is exact),
+// rounded once to fp32 (nearest, ties to even); the bias is added in fp32
+// and the result rounded to bf16. The reference computes the gate in bf16
+// with fp32 accumulation in an order it does not specify (MLX matmul,
+// moe.rs:123); rounding the exact sum makes the logit independent of
+// summation order, so tensor-core and CUDA-core kernels can all produce it.
 float route_logit(const uint16_t* xr, const uint16_t* wr, int D, float bias) {
-  float lane[32];
-  const int nchunks = D / 8;
-  for (int j = 0; j < 32; ++j) {
-    float acc = 0.0f;
-    for (int c = j; c < nchunks; c += 32)
-      for (int i = 0; i < 8; ++i) acc = std::fma(bf2f(xr[c * 8 + i]), bf2f(wr[c * 8 + i]), acc);
-    lane[j] = acc;
-  }
-  for (int s = 16; s >= 1; s >>= 1) {
-    float nv[32];
-    for (int j = 0; j < 32; ++j) nv[j] = lane[j] + lane[j ^ s];
-    std::memcpy(lane, nv, sizeof(lane));
-  }
-  return rbf(lane[0] + bias);
+  return rbf(dot_bf16_rn32(xr, wr, D) + bias);
 }
 
 // Softmax (fp32 inside, bf16 out: moe.rs:124, softmax_axis precise=true),
@@ -361,6 +454,11 @@ ORC_API void orc_f32_to_bf16(const float* in, int64_t n, uint16_t* out) {
 }
 ORC_API void orc_exp_route(const float* in, int64_t n, float* out) {
   for (int64_t i = 0; i < n; ++i) out[i] = exp_route(in[i]);
+}
+
+// Row-wise exact dot products: out[r] = dot_bf16_rn32(x[r], w[r], D).
+ORC_API void orc_dot_rn32(const uint16_t* x, const uint16_t* w, int64_t rows, int D, float* out) {
+  for (int64_t r = 0; r < rows; ++r) out[r] = dot_bf16_rn32(x + r * D, w + r * D, D);
 }
 
 // quantize: w [rows, cols] in dtype dt -> wq [rows, cols*bits/32],

@@ -109,6 +109,7 @@ def _declare(L):
     L.orc_normal_bf16.restype = None
     L.orc_f32_to_bf16.argtypes = [P, I64, P]
     L.orc_exp_route.argtypes = [P, I64, P]
+    L.orc_dot_rn32.argtypes = [P, P, I64, I32, P]
     L.orc_quantize.argtypes = [P, I32, I64, I64, I32, I32, P, P, P]
     L.orc_dequantize.argtypes = [P, P, P, I32, I64, I64, I32, I32, P, I32]
     L.orc_gather_qmm.argtypes = [P, I32, I64, I64, I64, P, P, P, I32, I64, I64, P, P, I64, I32, I32, I32, P]
@@ -167,6 +168,17 @@ def exp_route(x: np.ndarray) -> np.ndarray:
     x = np.ascontiguousarray(x, np.float32)
     out = np.empty_like(x)
     lib().orc_exp_route(_p(x), x.size, _p(out))
+    return out
+
+
+def dot_rn32(x: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """Row-wise exact dot products of bf16 bit arrays [rows, D], each rounded
+    once to fp32 (the router logit's sum)."""
+    x = np.ascontiguousarray(x, np.uint16)
+    w = np.ascontiguousarray(w, np.uint16)
+    assert x.shape == w.shape and x.ndim == 2
+    out = np.empty(x.shape[0], np.float32)
+    lib().orc_dot_rn32(_p(x), _p(w), x.shape[0], x.shape[1], _p(out))
     return out
 
 

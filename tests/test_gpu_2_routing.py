@@ -102,3 +102,40 @@ def test_permute_bad_index_reports_status():
     with pytest.raises(MlxrError) as ei:
         blk.status()
     assert ei.value.status == _lib.ERR_DEVICE_INDEX
+
+
+@pytest.mark.parametrize("T", [3, 100, 300, 1000])
+def test_router_undecided_and_non_finite_logits(T):
+    """Logits the fast paths cannot decide go through the exact sum: a token
+    whose sum with expert 5 is 1 + 2^-8 + 2^-24 + 2^-60 (the fp32 tie is broken
+    only by the 2^-60 term, below fp64's reach and below the tensor-core
+    path's digit range), and tokens holding inf or NaN. T = 3 and 100 run the
+    split and fused routers (fp64 sums), 300 and 1000 the int8 tensor-core
+    router; all must equal the oracle's logits (NaN compared as NaN) and,
+    for finite tokens, its routing."""
+    D, E, K = 2048, 128, 8
+    blk = _router_block(D, E, K)
+    g = blk.gate.clone()
+    g[5] = 0
+    g[5, :4] = torch.tensor([1.0, 1.0, 1.0, 2.0**-30], dtype=torch.bfloat16)
+    blk.gate.copy_(g)
+    x = synth.make_input(T, D, stream_offset=11).clone()
+    x[1] = 0
+    x[1, :4] = torch.tensor([1.0, 2.0**-8, 2.0**-24, 2.0**-30], dtype=torch.bfloat16)
+    x[2, 17] = float("inf")
+    if T > 100:
+        x[T - 1, 3] = float("nan")
+        x[T // 2, 0] = float("-inf")
+    idx, w, lg, pr = blk.router(x, want_logits=True)
+    torch.cuda.synchronize()
+    oi, ow, olg, opr = O.router(bf16_np(x), bf16_np(blk.gate), K, None, True, want_logits=True)
+    got, want = bf16_np(lg), olg
+    gnan = ((got & 0x7F80) == 0x7F80) & ((got & 0x7F) != 0)
+    wnan = ((want & 0x7F80) == 0x7F80) & ((want & 0x7F) != 0)
+    np.testing.assert_array_equal(gnan, wnan)
+    np.testing.assert_array_equal(np.where(gnan, 0, got), np.where(wnan, 0, want))
+    assert got[1, 5] == 0x3F81  # bf16(fp32(1 + 2^-8 + 2^-24 + 2^-60)) = 1 + 2^-7
+    xf = bf16_np(x)
+    finite = ((xf & 0x7F80) != 0x7F80).all(1)
+    np.testing.assert_array_equal(idx.cpu().numpy()[finite], oi[finite])
+    np.testing.assert_array_equal(bf16_np(w)[finite], ow[finite])

@@ -276,3 +276,120 @@ def test_block_empty_and_single_token():
     assert o.shape == (1, 256) and idx.shape == (1, 4)
     o0, idx0, _ = O.moe_block(cfg, W, x[:0], "fused")
     assert o0.shape == (0, 256) and idx0.shape == (0, 4)
+
+
+# ------------------------------------------- exact router dot product ----
+def _bf16_value(b):
+    """Exact value of bf16 bits as a Fraction (finite only)."""
+    from fractions import Fraction
+
+    be, f = (int(b) >> 7) & 0xFF, int(b) & 0x7F
+    m = (f | 0x80) if be else f
+    p = (be if be else 1) - 134
+    v = Fraction(m) * (Fraction(2) ** p)
+    return -v if int(b) & 0x8000 else v
+
+
+def _rn32(F):
+    """Fraction -> fp32 bits, round to nearest, ties to even (exact zero +0)."""
+    from fractions import Fraction
+
+    if F == 0:
+        return 0
+    sign = 0x80000000 if F < 0 else 0
+    a = abs(F)
+    e = a.numerator.bit_length() - a.denominator.bit_length()
+    if Fraction(2) ** e > a:
+        e -= 1
+    if e > 127:
+        return sign | 0x7F800000
+    q = max(e - 23, -149)
+    s = a / (Fraction(2) ** q)
+    mant = int(s)
+    rem = s - mant
+    if rem > Fraction(1, 2) or (rem == Fraction(1, 2) and mant & 1):
+        mant += 1
+    if mant == 1 << 24:
+        mant >>= 1
+        q += 1
+    if mant >= 1 << 23:
+        if q + 23 > 127:
+            return sign | 0x7F800000
+        return sign | ((q + 150) << 23) | (mant & 0x7FFFFF)
+    return sign | mant
+
+
+def _f32_bits(a):
+    return np.asarray(a, np.float32).view(np.uint32)
+
+
+def test_dot_rn32_matches_exact_rational_sum():
+    """The logit's sum: the exact dot product rounded once to fp32, checked
+    against rational arithmetic on vectors with wide exponent ranges,
+    subnormals, cancellation and ties."""
+    rng = np.random.default_rng(7)
+    rows, D = 48, 72
+    x = np.empty((rows, D), np.uint16)
+    w = np.empty((rows, D), np.uint16)
+    for r in range(rows):
+        # random sign, exponent field in a row-specific window, random mantissa
+        lo = int(rng.integers(0, 200))
+        hi = min(254, lo + int(rng.integers(1, 60)))
+        for arr in (x, w):
+            ex = rng.integers(lo, hi + 1, D)
+            arr[r] = (rng.integers(0, 2, D) << 15) | (ex << 7) | rng.integers(0, 128, D)
+    # exact cancellation: the second half negates the first
+    x[0, D // 2:] = x[0, :D // 2] ^ 0x8000
+    w[0, D // 2:] = w[0, :D // 2]
+    # a fp32 tie that only the tiny term breaks: 1 + 2^-8 + 2^-24 + 2^-60
+    x[1] = 0
+    w[1] = 0
+    x[1, :4] = [0x3F80, 0x3B80, 0x3380, 0x3080]  # 1, 2^-8, 2^-24, 2^-30
+    w[1, :4] = [0x3F80, 0x3F80, 0x3F80, 0x3080]  # 1, 1, 1, 2^-30
+    # the same without the tiny term: a tie, rounds to even
+    x[2] = x[1]
+    w[2] = w[1]
+    x[2, 3] = 0
+    # all zero, and products that cancel to exactly zero
+    x[3] = 0
+    x[4, :] = 0
+    x[4, :2] = [0x3F80, 0xBF80]
+    w[4, :] = 0
+    w[4, :2] = [0x4000, 0x4000]
+    got = _f32_bits(O.dot_rn32(x, w))
+    for r in range(rows):
+        F = sum(_bf16_value(a) * _bf16_value(b) for a, b in zip(x[r], w[r]))
+        assert got[r] == _rn32(F), (r, hex(got[r]), hex(_rn32(F)))
+    assert got[1] == 0x3F808001  # 1 + 2^-8 + 2^-23: the 2^-60 term decides the tie
+    assert got[2] == 0x3F808000
+    assert got[3] == 0 and got[4] == 0  # exact zeros are +0
+
+
+def test_dot_rn32_non_finite_operands():
+    one, inf, ninf, nan, zero = 0x3F80, 0x7F80, 0xFF80, 0x7FC0, 0x0000
+    cases = [
+        ([inf, one], [one, one], 0x7F800000),
+        ([inf, ninf], [one, ninf], 0x7F800000),   # +inf and (-inf * -inf) = +inf
+        ([inf, ninf], [one, one], None),          # +inf + -inf -> NaN
+        ([inf, one], [zero, one], None),          # inf * 0 -> NaN
+        ([nan, one], [one, one], None),
+        ([ninf, one], [one, one], 0xFF800000),
+    ]
+    for xs, ws, want in cases:
+        got = _f32_bits(O.dot_rn32(np.array([xs], np.uint16), np.array([ws], np.uint16)))[0]
+        if want is None:
+            assert (got & 0x7F800000) == 0x7F800000 and (got & 0x7FFFFF) != 0
+        else:
+            assert got == want
+
+
+def test_router_logits_are_rounded_exact_sums():
+    """route_logit = bf16(fp32(exact sum) + bias) on the router's own shapes."""
+    D, E, T = 512, 16, 8
+    x = O.normal_bf16(0, 140, (T, D), 1.0)
+    wg = O.normal_bf16(0, 141, (E, D), 0.02)
+    bias = np.linspace(-1.0, 1.0, E).astype(np.float32)
+    _, _, lg, _ = O.router(x, wg, 4, bias, True, want_logits=True)
+    s = O.dot_rn32(np.repeat(x, E, 0), np.tile(wg, (T, 1))).reshape(T, E)
+    want = O.f32_to_bf16((s + bias[None, :]).astype(np.float32))
+    np.testing.assert_array_equal(lg, want)
