@@ -153,21 +153,59 @@ static __device__ __noinline__ float dot_rn32_warp(const uint16_t* __restrict__ 
   return rn32_limbs(mag, NL, cmp < 0, -266);
 }
 
-// fp32 rounding of a signed 128-bit integer times 2^lsb, with a fast path
-// through the hardware int64 -> fp32 conversion (correctly rounded) and an
-// exact exponent shift when the result is a normal number.
+// fp32 rounding of a signed 128-bit integer times 2^lsb. Fast path: shift
+// the magnitude right by k so that it fits 63 bits, folding the shifted-out
+// bits into bit 0 (a sticky bit: with 39 or more bits below the fp32
+// rounding position this keeps "below / at / above half" intact), convert
+// with the hardware's correctly rounded int64 -> fp32, and scale by
+// 2^(k + lsb) through the exponent field when the result is a normal number
+// (exponent field 2..254, so the exact value was normal too).
 __device__ __forceinline__ float rn32_i128(__int128 v, int lsb) {
   const bool neg = v < 0;
   const unsigned __int128 mag = neg ? (unsigned __int128)(-v) : (unsigned __int128)v;
   if (mag == 0) return 0.0f;
-  if ((uint64_t)(mag >> 63) == 0) {
-    const float f = __ll2float_rn((long long)v);
-    const uint32_t fb = __float_as_uint(f);
-    const int ex = (int)((fb >> 23) & 0xffu) + lsb;
-    if (ex >= 2 && ex <= 254) return __uint_as_float((fb & 0x807fffffu) | ((uint32_t)ex << 23));
+  const uint64_t hi = (uint64_t)(mag >> 64), lo = (uint64_t)mag;
+  const int nbits = hi ? 128 - __clzll((long long)hi) : 64 - __clzll((long long)lo);
+  const int k = nbits > 63 ? nbits - 63 : 0;
+  uint64_t m;
+  if (k == 0) {
+    m = lo;
+  } else {
+    const unsigned __int128 sh = mag >> k;
+    const unsigned __int128 lost = mag & ((((unsigned __int128)1) << k) - 1);
+    m = (uint64_t)sh | (lost != 0 ? 1u : 0u);
   }
-  const uint64_t limbs[2] = {(uint64_t)mag, (uint64_t)(mag >> 64)};
+  const float f = __ll2float_rn((long long)m);
+  const uint32_t fb = __float_as_uint(f);
+  const int ex = (int)((fb >> 23) & 0xffu) + k + lsb;
+  if (ex >= 2 && ex <= 254) return __uint_as_float((neg ? 0x80000000u : 0u) | (fb & 0x007fffffu) | ((uint32_t)ex << 23));
+  const uint64_t limbs[2] = {lo, hi};
   return rn32_limbs(limbs, 2, neg, lsb);
+}
+
+// The bf16 logit from the tensor-core router's digit sums: A[g] (g < 7) =
+// sum of the plane products of weight 2^(8 (6 - g)), so the exact integer
+// dot product is V = sum_g A[g] 2^(8 (6 - g)) and the sum is V 2^(u_x + u_w)
+// when no element was truncated (xi, wi = {u, truncated count}); otherwise
+// the sum lies within (n_x + n_w) 2^(30 + u_x + u_w) of it. *decided is
+// false when that interval straddles a bf16 logit boundary or a row holds
+// inf or NaN (count -1): the caller then computes the exact sum.
+__device__ __forceinline__ uint16_t logit_from_digit_sums(const int32_t (&A)[7], int2 xi, int2 wi, float bias,
+                                                          bool* decided) {
+  *decided = false;
+  if (xi.y < 0 || wi.y < 0) return 0;
+  const int64_t hi = (int64_t)A[0] * (1ll << 24) + (int64_t)A[1] * (1ll << 16) + (int64_t)A[2] * (1ll << 8) + A[3];
+  const int64_t lo = (int64_t)A[4] * (1ll << 16) + (int64_t)A[5] * (1ll << 8) + A[6];
+  const __int128 V = ((__int128)hi << 24) + (__int128)lo;
+  const int lsb = xi.x + wi.x;
+  const uint16_t lb = logit_bits(rn32_i128(V, lsb), bias);
+  const int nt = xi.y + wi.y;
+  if (nt > 0) {
+    const __int128 B = (__int128)nt << 30;
+    if (logit_bits(rn32_i128(V - B, lsb), bias) != lb || logit_bits(rn32_i128(V + B, lsb), bias) != lb) return lb;
+  }
+  *decided = true;
+  return lb;
 }
 
 // The bf16 logit of a sum known to lie within err of s (fp64): decided when

@@ -16,6 +16,7 @@
 // All scratch lives in the caller's workspace; nothing is allocated here.
 #include <algorithm>
 #include <cstring>
+#include <type_traits>
 #include <mutex>
 
 #include "common.cuh"
@@ -56,7 +57,6 @@ static inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 constexpr size_t kStatusSlotBytes = 256;
 constexpr int kSchedExperts1 = 32, kSchedExperts2 = 34, kSchedShared1 = 36, kSchedShared2 = 38;
 constexpr int kSplitRouterMaxT = 64;   // batches up to this size use router_split_kernel
-constexpr int kTileRouterMinT = 256;   // batches above this size use the tensor-core router (router_tc.cu)
 
 struct Layout {
   // R: flat (token, k) rows; rows: expert rows the buffers hold (R, or fewer
@@ -219,7 +219,7 @@ static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T, int64_t rows_c
   }
   // The tensor-core router's digit planes: in the x_sorted buffer when they
   // fit (the permute fills it only after the router has finished), else apart.
-  if (T > kTileRouterMinT && router_tc_supported(L.D)) {
+  if (T > kSplitRouterMaxT && router_tc_supported(L.D)) {
     const size_t need = router_tc_layout(T, L.E, L.D).total;
     L.rtc = need <= (size_t)L.rows_pad * L.D * 2 ? L.xs : take(need);
   }
@@ -285,9 +285,42 @@ static int run_router(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
     rbias = nullptr;
     es = static_cast<const uint16_t*>(wt->expert_scale);
   }
-  // Small batches: logits spread over many CTAs, the last CTA of each token
-  // block routes it. Up to 256 tokens: one token per CTA (latency); beyond,
-  // four per CTA (fewer re-reads of the router weight).
+  if (L.T > kSplitRouterMaxT && router_tc_supported(L.D)) {
+    // The logits on the int8 tensor cores (router_tc.cu). Large batches:
+    // logits from the kernel's epilogue, then one warp per token routes
+    // them. Small batches (split-K form): one warp per token sums the k
+    // slices, forms its logits and routes them.
+    uint16_t* lg = logits ? logits : at<uint16_t>(ws, L.logits);
+    const RouterTcLayout R = router_tc_layout(L.T, L.E, L.D);
+    RouterTcProblem rp{xp, L.T, wg, L.E, L.D, rbias, lg, at<void>(ws, L.rtc), at<int>(ws, L.status)};
+    if (int rc = launch_router_tc(rp, st)) return rc;
+    const unsigned grid = (unsigned)((L.T + RT_ROUTE_WARPS - 1) / RT_ROUTE_WARPS);
+    const size_t smem = RT_ROUTE_WARPS * L.E * sizeof(float);
+    // lane arrays of the routing sized for E (registers, not local memory)
+    auto route = [&](auto mv) {
+      constexpr int MV = decltype(mv)::value;
+      if (R.split) {
+        uint8_t* rb = at<uint8_t>(ws, L.rtc);
+        launch_pdl(route_partials_kernel<MV>, grid, RT_ROUTE_WARPS * 32, smem, st,
+                   reinterpret_cast<const int32_t*>(rb + R.part), R.splits, reinterpret_cast<const int2*>(rb + R.xinfo),
+                   reinterpret_cast<const int2*>(rb + R.winfo), xp, wg, rbias, L.T, L.D, L.E, L.K, c->norm_topk_prob,
+                   at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w), logits, probs, sg, sig, es);
+      } else {
+        launch_pdl(route_rows_kernel<MV>, grid, RT_ROUTE_WARPS * 32, smem, st, lg, xp, L.T, L.D, L.E, L.K,
+                   c->norm_topk_prob, at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w), probs, sg, sig, es);
+      }
+    };
+    if (L.E <= 128) route(std::integral_constant<int, 4>{});
+    else if (L.E <= 256) route(std::integral_constant<int, 8>{});
+    else if (L.E <= 512) route(std::integral_constant<int, 16>{});
+    else route(std::integral_constant<int, 32>{});
+    MLXR_LAUNCH_CHECK(R.split ? "route_partials_kernel" : "route_rows_kernel");
+    return MLXR_CU_OK;
+  }
+  // Small batches (latency: the tensor-core form costs more launches) and D
+  // beyond the tensor-core path: fp64 sums on the CUDA cores. Up to 64
+  // tokens the logits are spread over many CTAs and the last CTA of each
+  // token block routes it; beyond, one token per CTA.
   if (L.T <= kSplitRouterMaxT) {
     // 2 experts per warp; 1, 2 or 4 tokens per block.
     const int tpb = L.T <= 4 ? 1 : L.T <= 16 ? 2 : 4;
@@ -312,19 +345,7 @@ static int run_router(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
                                                                         probs, sg, sig, counter, es);
     MLXR_LAUNCH_CHECK("router_split_kernel");
     return MLXR_CU_OK;
-  } else if (L.T > kTileRouterMinT && router_tc_supported(L.D)) {
-    // Large batches: the logits on the int8 tensor cores (router_tc.cu), then
-    // one warp per token routes them.
-    uint16_t* lg = logits ? logits : at<uint16_t>(ws, L.logits);
-    RouterTcProblem rp{xp, L.T, wg, L.E, L.D, rbias, lg, at<void>(ws, L.rtc), at<int>(ws, L.status)};
-    if (int rc = launch_router_tc(rp, st)) return rc;
-    launch_pdl(route_rows_kernel, (unsigned)((L.T + RT_ROUTE_WARPS - 1) / RT_ROUTE_WARPS), RT_ROUTE_WARPS * 32, RT_ROUTE_WARPS * L.E * sizeof(float), st, lg, xp, L.T, L.D, L.E, L.K, c->norm_topk_prob,
-                                                                    at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w),
-                                                                    probs, sg, sig, es);
-    MLXR_LAUNCH_CHECK("route_rows_kernel");
-    return MLXR_CU_OK;
   } else {
-    // 64 < T <= 256 (and larger batches with D beyond the tensor-core path): one token per CTA.
     launch_pdl(router_fused_kernel<1>, (unsigned)L.T, RT_THREADS, L.E * sizeof(float), st,
         xp, L.T, L.D, wg, L.E, rbias, L.K, c->norm_topk_prob, at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w),
         logits, probs, sg, sig, es);

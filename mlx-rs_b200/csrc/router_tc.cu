@@ -24,6 +24,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 
 #include "common.cuh"
@@ -34,17 +35,21 @@
 namespace mlxr {
 
 constexpr int RG_BM = 128;                       // experts per CTA (MMA M)
-constexpr int RG_BN = 64;                        // tokens per CTA (MMA N)
 constexpr int RG_BK = 64;                        // digits per k-block (one 64-byte swizzle row)
 constexpr int RG_STAGES = 4;
 constexpr int RG_A_PLANE = RG_BM * RG_BK;        // 8 KB
-constexpr int RG_B_PLANE = RG_BN * RG_BK;        // 4 KB
-constexpr int RG_STAGE = 4 * RG_A_PLANE + 4 * RG_B_PLANE;  // 48 KB
-constexpr int RG_OFF_BAR = RG_STAGES * RG_STAGE;
-constexpr int RG_SMEM = RG_OFF_BAR + 128 + 1024;  // + barriers, + alignment slack
 constexpr int RG_THREADS = 224;                   // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue, warp 6 waiter
-constexpr int RG_TMEM_COLS = 512;                 // 7 accumulators x 64 columns
 constexpr int RD_WARPS = 8;
+// Token-tile width BN (MMA N): 64 for large batches (7 accumulators x 64 =
+// 448 of the 512 tensor-memory columns), 16 for the split-K form.
+template <int BN>
+struct RgCfg {
+  static constexpr int B_PLANE = BN * RG_BK;
+  static constexpr int STAGE = 4 * RG_A_PLANE + 4 * B_PLANE;  // 48 KB (BN 64), 36 KB (BN 16)
+  static constexpr int OFF_BAR = RG_STAGES * STAGE;
+  static constexpr int SMEM = OFF_BAR + 128 + 1024;           // + barriers, + alignment slack
+  static constexpr int TMEM_COLS = BN == 64 ? 512 : 128;
+};
 
 // bf16 rows -> digit planes dig[4][rows_pad][Dp] and info[r] = {u, n}
 // (n = truncated elements, -1 when the row holds inf or NaN). Rows
@@ -70,14 +75,26 @@ __device__ __forceinline__ int bf16_to_fixed(uint32_t b, int u, int& lost) {
   return (b & 0x8000u) ? -X : X;
 }
 
-__global__ void __launch_bounds__(RD_WARPS * 32) router_digits_kernel(const uint16_t* __restrict__ src, int64_t rows,
-                                                                     int64_t rows_pad, int D, int Dp,
-                                                                     int8_t* __restrict__ dig, int2* __restrict__ info) {
+struct DigitRows {
+  const uint16_t* src;
+  int64_t rows, rows_pad;
+  int8_t* dig;
+  int2* info;
+};
+
+// One CTA per row of two row sets (the router rows, then the tokens).
+__global__ void __launch_bounds__(RD_WARPS * 32) router_digits_kernel(DigitRows ra, DigitRows rb, int D, int Dp) {
   pdl_wait();
   pdl_launch_dependents();
   __shared__ int s_top[RD_WARPS], s_nonfin[RD_WARPS], s_lost[RD_WARPS];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t r = blockIdx.x;
+  const bool first = (int64_t)blockIdx.x < ra.rows_pad;
+  const DigitRows& q = first ? ra : rb;
+  const int64_t r = first ? (int64_t)blockIdx.x : (int64_t)blockIdx.x - ra.rows_pad;
+  const uint16_t* src = q.src;
+  const int64_t rows = q.rows, rows_pad = q.rows_pad;
+  int8_t* dig = q.dig;
+  int2* info = q.info;
   const size_t plane = (size_t)rows_pad * Dp;
   int8_t* out = dig + (size_t)r * Dp;
   const int nch = D / 8, npch = Dp / 8;
@@ -152,12 +169,12 @@ __global__ void __launch_bounds__(RD_WARPS * 32) router_digits_kernel(const uint
   }
 }
 
-// Seven 8-column TMEM loads (columns c0 + 64 j .. +7, j < 7) in one wait.
-__device__ inline void tmem_ld7_x8_wait(uint32_t t, uint32_t (&r)[56]) {
+// Seven 8-column TMEM loads (columns c0 + stride j .. +7, j < 7) in one wait.
+__device__ inline void tmem_ld7_x8_wait(uint32_t t, uint32_t (&r)[56], uint32_t stride) {
   asm volatile(
       "{\n\t.reg .b32 t1, t2, t3, t4, t5, t6;\n\t"
-      "add.u32 t1, %56, 64;\n\tadd.u32 t2, %56, 128;\n\tadd.u32 t3, %56, 192;\n\t"
-      "add.u32 t4, %56, 256;\n\tadd.u32 t5, %56, 320;\n\tadd.u32 t6, %56, 384;\n\t"
+      "add.u32 t1, %56, %57;\n\tadd.u32 t2, t1, %57;\n\tadd.u32 t3, t2, %57;\n\t"
+      "add.u32 t4, t3, %57;\n\tadd.u32 t5, t4, %57;\n\tadd.u32 t6, t5, %57;\n\t"
       "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%56];\n\t"
       "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%8, %9, %10, %11, %12, %13, %14, %15}, [t1];\n\t"
       "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%16, %17, %18, %19, %20, %21, %22, %23}, [t2];\n\t"
@@ -173,7 +190,7 @@ __device__ inline void tmem_ld7_x8_wait(uint32_t t, uint32_t (&r)[56]) {
         "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
         "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
         "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55])
-      : "r"(t)
+      : "r"(t), "r"(stride)
       : "memory");
 }
 
@@ -221,18 +238,27 @@ struct RouterTcArgs {
   const int2* winfo;
   const float* bias;
   uint16_t* lg;
+  int32_t* part;  // split-K form: [splits][7][T][E] digit sums of each k-slice
   int64_t T;
-  int E, D, nk;
+  int E, D, nk, kps;  // k-blocks in all, per split
   int rows_pad_x, rows_pad_w;
   int* status;
 };
 
+// SPLIT: CTA (x, y, z) sums k-blocks [z kps, (z + 1) kps) and writes its 7
+// digit sums per (token, expert) to part (route_partials_kernel finishes);
+// otherwise the epilogue forms the logits.
+template <int BN, bool SPLIT>
 __global__ void __launch_bounds__(RG_THREADS, 1)
     router_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                      const RouterTcArgs a) {
+  using G = RgCfg<BN>;
+  constexpr int RG_BN = BN;
+  constexpr int RG_B_PLANE = G::B_PLANE;
+  constexpr int RG_STAGE = G::STAGE;
   extern __shared__ __align__(1024) uint8_t rg_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(rg_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + RG_OFF_BAR);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::OFF_BAR);
   uint64_t* full = bars;                  // [RG_STAGES] digit tiles landed (TMA)
   uint64_t* empty = full + RG_STAGES;     // [RG_STAGES] stage consumed (MMA commit)
   uint64_t* acc_full = empty + RG_STAGES; // all MMAs done
@@ -253,7 +279,7 @@ __global__ void __launch_bounds__(RG_THREADS, 1)
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, RG_TMEM_COLS);
+    tmem_alloc(tmem_slot, G::TMEM_COLS);
     tmem_relinquish();
   }
   if (warp == 0 && lane == 0) {
@@ -266,22 +292,24 @@ __global__ void __launch_bounds__(RG_THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
   pdl_wait();  // the digit planes and row info come from the previous kernels
   pdl_launch_dependents();
+  const int kb0 = SPLIT ? (int)blockIdx.z * a.kps : 0;
+  const int nkb = SPLIT ? min(a.kps, a.nk - kb0) : a.nk;  // k-blocks of this CTA (>= 1)
 
   if (warp == 0) {
     if (lane == 0) {
       uint32_t issued = 0;
-      for (int kb = 0; kb < a.nk; ++kb) {
-        const int s = kb % RG_STAGES;
-        const uint32_t ph = (uint32_t)(kb / RG_STAGES) & 1u;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % RG_STAGES;
+        const uint32_t ph = (uint32_t)(i / RG_STAGES) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, a.status)) break;
         uint8_t* st = smem + s * RG_STAGE;
+        const int kx = (kb0 + i) * RG_BK;
         mbar_arrive_expect_tx(&full[s], RG_STAGE);
 #pragma unroll
-        for (int l = 0; l < 4; ++l)
-          tma_load_2d(st + l * RG_A_PLANE, &tm_w, &full[s], kb * RG_BK, l * a.rows_pad_w + m0);
+        for (int l = 0; l < 4; ++l) tma_load_2d(st + l * RG_A_PLANE, &tm_w, &full[s], kx, l * a.rows_pad_w + m0);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          tma_load_2d(st + 4 * RG_A_PLANE + k * RG_B_PLANE, &tm_x, &full[s], kb * RG_BK, k * a.rows_pad_x + n0);
+          tma_load_2d(st + 4 * RG_A_PLANE + k * RG_B_PLANE, &tm_x, &full[s], kx, k * a.rows_pad_x + n0);
         ++issued;
       }
       drain_ring<RG_STAGES>(full, issued, abort_flag, a.status);
@@ -291,11 +319,11 @@ __global__ void __launch_bounds__(RG_THREADS, 1)
     // wait in a thread with MMAs in flight lasts until they complete) and
     // publishes the count of landed k-blocks in shared memory.
     if (lane == 0) {
-      for (int kb = 0; kb < a.nk; ++kb) {
-        const int s = kb % RG_STAGES;
-        const uint32_t ph = (uint32_t)(kb / RG_STAGES) & 1u;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % RG_STAGES;
+        const uint32_t ph = (uint32_t)(i / RG_STAGES) & 1u;
         if (!mbar_wait(&full[s], ph, abort_flag, a.status)) break;
-        asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(s_ready)), "r"((uint32_t)(kb + 1))
+        asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(s_ready)), "r"((uint32_t)(i + 1))
                      : "memory");
       }
     }
@@ -303,7 +331,7 @@ __global__ void __launch_bounds__(RG_THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_s8(RG_BM, RG_BN);
       bool ok = true;
-      for (int kb = 0; kb < a.nk && ok; ++kb) {
+      for (int kb = 0; kb < nkb && ok; ++kb) {
         const int s = kb % RG_STAGES;
         // bounded poll of the waiter's count (plain shared-memory loads)
         const unsigned long long t0 = global_ns();
@@ -360,37 +388,44 @@ __global__ void __launch_bounds__(RG_THREADS, 1)
 #pragma unroll 1
     for (int c8 = 0; c8 < RG_BN / 8 && ok; ++c8) {
       uint32_t r[56];
-      tmem_ld7_x8_wait(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(c8 * 8), r);
-#pragma unroll 1
-      for (int j = 0; j < 8; ++j) {
+      tmem_ld7_x8_wait(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(c8 * 8), r, RG_BN);
+      uint32_t und = 0;  // bit j: this lane's logit of token j left undecided
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {  // unrolled: r stays in registers
         const int64_t t = n0 + c8 * 8 + j;
         const bool valid = e_ok && t < a.T;
-        const int2 xi = a.xinfo[t < a.T ? t : a.T - 1];
-        const int64_t hi = (int64_t)(int32_t)r[0 * 8 + j] * (1ll << 24) + (int64_t)(int32_t)r[1 * 8 + j] * (1ll << 16) +
-                           (int64_t)(int32_t)r[2 * 8 + j] * (1ll << 8) + (int64_t)(int32_t)r[3 * 8 + j];
-        const int64_t lo = (int64_t)(int32_t)r[4 * 8 + j] * (1ll << 16) + (int64_t)(int32_t)r[5 * 8 + j] * (1ll << 8) +
-                           (int64_t)(int32_t)r[6 * 8 + j];
-        const __int128 V = ((__int128)hi << 24) + (__int128)lo;
-        bool decided = !(xi.y < 0 || wi.y < 0);
-        uint16_t lb = 0;
-        if (decided) {
-          const int lsb = xi.x + wi.x;
-          lb = logit_bits(rn32_i128(V, lsb), b);
-          const int nt = xi.y + wi.y;
-          if (nt > 0) {
-            const __int128 B = (__int128)nt << 30;
-            decided = logit_bits(rn32_i128(V - B, lsb), b) == lb && logit_bits(rn32_i128(V + B, lsb), b) == lb;
+        int32_t A[7];
+#pragma unroll
+        for (int g = 0; g < 7; ++g) A[g] = (int32_t)r[g * 8 + j];
+        if constexpr (SPLIT) {
+          if (valid) {
+            int32_t* pp = a.part + (((int64_t)blockIdx.z * 7) * a.T + t) * a.E + e;
+#pragma unroll
+            for (int g = 0; g < 7; ++g) pp[(int64_t)g * a.T * a.E] = A[g];
           }
+        } else {
+          const int2 xi = a.xinfo[t < a.T ? t : a.T - 1];
+          bool decided;
+          const uint16_t lb = logit_from_digit_sums(A, xi, wi, b, &decided);
+          if (valid && decided) a.lg[t * a.E + e] = lb;
+          und |= (uint32_t)(valid && !decided) << j;
         }
-        uint32_t need = __ballot_sync(0xffffffffu, valid && !decided);
+      }
+      // Rare: logits the interval test left open, as exact sums by the whole warp.
+      uint32_t pend = __reduce_or_sync(0xffffffffu, und);
+#pragma unroll 1
+      while (pend) {
+        const int j = __ffs(pend) - 1;
+        pend &= pend - 1;
+        const int64_t t = n0 + c8 * 8 + j;
+        uint32_t need = __ballot_sync(0xffffffffu, (und >> j) & 1u);
         while (need) {
           const int src = __ffs(need) - 1;
           need &= need - 1;
           const int es = __shfl_sync(0xffffffffu, ec, src);
           const float v = dot_rn32_warp(a.x + t * (int64_t)a.D, a.wg + (int64_t)es * a.D, a.D, lane);
-          if (lane == src) lb = logit_bits(v, b);
+          if (lane == src) a.lg[t * a.E + e] = logit_bits(v, b);
         }
-        if (valid) a.lg[t * a.E + e] = lb;
       }
     }
   }
@@ -399,15 +434,27 @@ __global__ void __launch_bounds__(RG_THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, RG_TMEM_COLS);
+    tmem_dealloc(tmem_base, G::TMEM_COLS);
   }
 }
 
 RouterTcLayout router_tc_layout(int64_t T, int E, int D) {
   RouterTcLayout L;
+  L.split = T <= kRouterTcSplitMaxT;
+  L.bn = L.split ? 16 : 64;
   L.Dp = (D + 127) / 128 * 128;
-  L.rows_pad_x = (T + RG_BN - 1) / RG_BN * RG_BN;
+  L.rows_pad_x = (T + L.bn - 1) / L.bn * L.bn;
   L.rows_pad_w = (E + RG_BM - 1) / RG_BM * RG_BM;
+  const int nk = (int)(L.Dp / RG_BK);
+  L.kps = nk;
+  L.splits = 1;
+  if (L.split) {
+    // About one CTA per SM, at most 16 k-slices (each token's finish reads them all).
+    const int64_t tiles = (L.rows_pad_x / L.bn) * (L.rows_pad_w / RG_BM);
+    int want = (int)std::max<int64_t>(1, std::min<int64_t>(16, num_sms_current() / std::max<int64_t>(tiles, 1)));
+    L.kps = (nk + want - 1) / want;
+    L.splits = (nk + L.kps - 1) / L.kps;
+  }
   size_t o = 0;
   auto take = [&](size_t bytes) {
     const size_t at = o;
@@ -418,11 +465,24 @@ RouterTcLayout router_tc_layout(int64_t T, int E, int D) {
   L.wdig = take((size_t)4 * L.rows_pad_w * L.Dp);
   L.xinfo = take((size_t)L.rows_pad_x * sizeof(int2));
   L.winfo = take((size_t)L.rows_pad_w * sizeof(int2));
+  if (L.split) L.part = take((size_t)L.splits * 7 * T * E * sizeof(int32_t));
   L.total = o;
   return L;
 }
 
 bool router_tc_supported(int D) { return D >= 8 && D % 8 == 0 && D < 32768; }
+
+template <int BN, bool SPLIT>
+static int launch_tc(const RouterTcLayout& L, const CUtensorMap& tw, const CUtensorMap& tx, const RouterTcArgs& a,
+                     cudaStream_t st) {
+  auto kern = router_tc_kernel<BN, SPLIT>;
+  static std::atomic<uint64_t> attr_done{0};
+  if (int rc = ensure_smem_attr(kern, RgCfg<BN>::SMEM, attr_done)) return rc;
+  const dim3 grid((unsigned)(L.rows_pad_x / BN), (unsigned)(L.rows_pad_w / RG_BM), (unsigned)L.splits);
+  launch_pdl(kern, grid, RG_THREADS, RgCfg<BN>::SMEM, st, tw, tx, a);
+  MLXR_LAUNCH_CHECK("router_tc_kernel");
+  return MLXR_CU_OK;
+}
 
 int launch_router_tc(const RouterTcProblem& p, cudaStream_t st) {
   if (!router_tc_supported(p.D))
@@ -434,20 +494,17 @@ int launch_router_tc(const RouterTcProblem& p, cudaStream_t st) {
   int8_t* wdig = reinterpret_cast<int8_t*>(ws + L.wdig);
   int2* xinfo = reinterpret_cast<int2*>(ws + L.xinfo);
   int2* winfo = reinterpret_cast<int2*>(ws + L.winfo);
-  static std::atomic<uint64_t> attr_done{0};
-  if (int rc = ensure_smem_attr(router_tc_kernel, RG_SMEM, attr_done)) return rc;
-  launch_pdl(router_digits_kernel, (unsigned)L.rows_pad_w, RD_WARPS * 32, 0, st, p.wg,
-             (int64_t)p.E, (int64_t)L.rows_pad_w, p.D, L.Dp, wdig, winfo);
-  MLXR_LAUNCH_CHECK("router_digits_kernel(weights)");
-  launch_pdl(router_digits_kernel, (unsigned)L.rows_pad_x, RD_WARPS * 32, 0, st, p.x,
-             p.T, (int64_t)L.rows_pad_x, p.D, L.Dp, xdig, xinfo);
-  MLXR_LAUNCH_CHECK("router_digits_kernel(tokens)");
+  const DigitRows rw{p.wg, (int64_t)p.E, L.rows_pad_w, wdig, winfo};
+  const DigitRows rx{p.x, p.T, L.rows_pad_x, xdig, xinfo};
+  launch_pdl(router_digits_kernel, (unsigned)(L.rows_pad_w + L.rows_pad_x), RD_WARPS * 32, 0, st, rw, rx, p.D,
+             (int)L.Dp);
+  MLXR_LAUNCH_CHECK("router_digits_kernel");
   CUtensorMap tw, tx;
   if (int rc = make_map_2d(&tw, wdig, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)L.Dp, (uint64_t)4 * L.rows_pad_w,
                            RG_BK, RG_BM, CU_TENSOR_MAP_SWIZZLE_64B))
     return rc;
   if (int rc = make_map_2d(&tx, xdig, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)L.Dp, (uint64_t)4 * L.rows_pad_x,
-                           RG_BK, RG_BN, CU_TENSOR_MAP_SWIZZLE_64B))
+                           RG_BK, (uint32_t)L.bn, CU_TENSOR_MAP_SWIZZLE_64B))
     return rc;
   RouterTcArgs a;
   a.x = p.x;
@@ -456,17 +513,16 @@ int launch_router_tc(const RouterTcProblem& p, cudaStream_t st) {
   a.winfo = winfo;
   a.bias = p.bias;
   a.lg = p.lg;
+  a.part = L.split ? reinterpret_cast<int32_t*>(ws + L.part) : nullptr;
   a.T = p.T;
   a.E = p.E;
   a.D = p.D;
-  a.nk = L.Dp / RG_BK;
+  a.nk = (int)(L.Dp / RG_BK);
+  a.kps = L.kps;
   a.rows_pad_x = (int)L.rows_pad_x;
   a.rows_pad_w = (int)L.rows_pad_w;
   a.status = p.status;
-  const dim3 grid((unsigned)(L.rows_pad_x / RG_BN), (unsigned)(L.rows_pad_w / RG_BM));
-  launch_pdl(router_tc_kernel, grid, RG_THREADS, RG_SMEM, st, tw, tx, a);
-  MLXR_LAUNCH_CHECK("router_tc_kernel");
-  return MLXR_CU_OK;
+  return L.split ? launch_tc<16, true>(L, tw, tx, a, st) : launch_tc<64, false>(L, tw, tx, a, st);
 }
 
 }  // namespace mlxr

@@ -10,14 +10,23 @@ namespace mlxr {
 // Workspace of one launch: digit planes of the tokens and of the router
 // rows (4 int8 planes each, rows padded to the tile, D padded to 128) and
 // the per-row exponent / truncation count.
+// Batches up to this size take the split-K form (16-token tiles, the k
+// range cut over CTAs, partial digit sums finished by route_partials_kernel).
+constexpr int64_t kRouterTcSplitMaxT = 256;
+
 struct RouterTcLayout {
+  bool split = false;
+  int bn = 64, splits = 1, kps = 0;
   int64_t Dp = 0, rows_pad_x = 0, rows_pad_w = 0;
-  size_t xdig = 0, wdig = 0, xinfo = 0, winfo = 0, total = 0;
+  size_t xdig = 0, wdig = 0, xinfo = 0, winfo = 0, part = 0, total = 0;
 };
 RouterTcLayout router_tc_layout(int64_t T, int E, int D);
 bool router_tc_supported(int D);
 
-// logits lg [T, E] bf16 = bf16(fp32(exact x[t] . wg[e]) + bias[e]) (bias may be NULL).
+// logits lg [T, E] bf16 = bf16(fp32(exact x[t] . wg[e]) + bias[e]) (bias may
+// be NULL). In the split-K form (T <= kRouterTcSplitMaxT) it writes the
+// partial digit sums instead (layout.part, [splits][7][T][E] int32) and
+// route_partials_kernel forms the logits.
 struct RouterTcProblem {
   const uint16_t* x;   // [T, D] bf16, 16-byte aligned
   int64_t T;

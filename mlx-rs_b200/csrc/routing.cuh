@@ -58,7 +58,7 @@ __device__ inline float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ inline float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
 // ------------------------------------------------------------ router ---
-constexpr int RT_MAXV = 32;  // E <= 1024
+constexpr int RT_MAX_EXPERTS = 1024;  // routing lane arrays cover up to 32 groups of 32
 constexpr int RT_MAXK = 32;
 
 struct SharedGateArgs {
@@ -78,9 +78,13 @@ __device__ inline uint32_t bf16_order_key(uint32_t b) { return (b & 0x8000u) ? (
 // gemma4/text/text.rs:647-651): top-K by (score desc, expert asc); softmax
 // over the K picked scores (max = the first pick, exp_route, the sum in pick
 // order, IEEE division, bf16); times per_expert_scale[e] (bf16).
+// MV: groups of 32 experts the lane arrays cover (MV * 32 >= E); sized per
+// batch so that they stay in registers.
+template <int MV>
 __device__ inline void route_token_warp_gemma4(const float* lrow, int64_t t, int E, int K, int lane,
                                                int32_t* __restrict__ idx_out, uint16_t* __restrict__ w_out,
                                                const uint16_t* __restrict__ expert_scale) {
+  constexpr int RT_MAXV = MV;
   uint32_t key[RT_MAXV];
 #pragma unroll
   for (int m = 0; m < RT_MAXV; ++m) {
@@ -117,11 +121,13 @@ __device__ inline void route_token_warp_gemma4(const float* lrow, int64_t t, int
 }
 
 // expert_scale != NULL: the Gemma 4 routing above instead of this one.
-__device__ inline void route_token_warp(const float* lrow, int64_t t, int E, int K, int renorm, int lane,
-                                        int32_t* __restrict__ idx_out, uint16_t* __restrict__ w_out,
-                                        uint16_t* __restrict__ probs_out, const uint16_t* __restrict__ expert_scale) {
+template <int MV>
+__device__ inline void route_token_warp_mv(const float* lrow, int64_t t, int E, int K, int renorm, int lane,
+                                           int32_t* __restrict__ idx_out, uint16_t* __restrict__ w_out,
+                                           uint16_t* __restrict__ probs_out, const uint16_t* __restrict__ expert_scale) {
+  constexpr int RT_MAXV = MV;
   if (expert_scale) {
-    route_token_warp_gemma4(lrow, t, E, K, lane, idx_out, w_out, expert_scale);
+    route_token_warp_gemma4<MV>(lrow, t, E, K, lane, idx_out, w_out, expert_scale);
     return;
   }
   float lv[RT_MAXV];
@@ -182,6 +188,16 @@ __device__ inline void route_token_warp(const float* lrow, int64_t t, int E, int
     idx_out[t * K + lane] = my_e;
     w_out[t * K + lane] = renorm ? f32_to_bf16_bits(__fdiv_rn(my_p, dbf)) : f32_to_bf16_bits(my_p);
   }
+}
+
+// Routes one token (every lane of the warp calls it), with lane arrays sized for E.
+__device__ inline void route_token_warp(const float* lrow, int64_t t, int E, int K, int renorm, int lane,
+                                        int32_t* __restrict__ idx_out, uint16_t* __restrict__ w_out,
+                                        uint16_t* __restrict__ probs_out, const uint16_t* __restrict__ expert_scale) {
+  if (E <= 128) route_token_warp_mv<4>(lrow, t, E, K, renorm, lane, idx_out, w_out, probs_out, expert_scale);
+  else if (E <= 256) route_token_warp_mv<8>(lrow, t, E, K, renorm, lane, idx_out, w_out, probs_out, expert_scale);
+  else if (E <= 512) route_token_warp_mv<16>(lrow, t, E, K, renorm, lane, idx_out, w_out, probs_out, expert_scale);
+  else route_token_warp_mv<32>(lrow, t, E, K, renorm, lane, idx_out, w_out, probs_out, expert_scale);
 }
 
 // sigmoid(x . dequant(g_s)) of one token by one warp (moe.rs:119-120).
@@ -492,6 +508,7 @@ __global__ void __launch_bounds__(G4_NORM_WARPS * 32) gemma4_norm_kernel(
 // Softmax / top-K / renormalisation (and the shared-expert gate) of one
 // token per warp from the bf16 logits lg [T, E].
 constexpr int RT_ROUTE_WARPS = 8;
+template <int MV>
 __global__ void __launch_bounds__(RT_ROUTE_WARPS * 32) route_rows_kernel(
     const uint16_t* __restrict__ lg, const uint16_t* __restrict__ x, int64_t T, int D, int E, int K, int renorm,
     int32_t* __restrict__ idx_out, uint16_t* __restrict__ w_out, uint16_t* __restrict__ probs_out, SharedGateArgs sg,
@@ -505,7 +522,60 @@ __global__ void __launch_bounds__(RT_ROUTE_WARPS * 32) route_rows_kernel(
   float* row = s_row + warp * E;
   for (int e = lane; e < E; e += 32) row[e] = bf16_bits_to_f32(lg[t * E + e]);
   __syncwarp();
-  route_token_warp(row, t, E, K, renorm, lane, idx_out, w_out, probs_out, expert_scale);
+  route_token_warp_mv<MV>(row, t, E, K, renorm, lane, idx_out, w_out, probs_out, expert_scale);
+  if (sig_out) shared_gate_warp(x + t * D, D, sg, lane, sig_out + t);
+}
+
+// The tensor-core router's split-K form (router_tc.cu, small batches):
+// part[s][g][t][e] (s < splits, g < 7) are the digit sums of k-slice s. One
+// token per warp: each lane adds its experts' slices (exact integer sums),
+// forms the logit as router_tc_kernel's epilogue does (the exact sum when
+// the interval test cannot decide it), then the token is routed as in
+// route_rows_kernel.
+template <int MV>
+__global__ void __launch_bounds__(RT_ROUTE_WARPS * 32) route_partials_kernel(
+    const int32_t* __restrict__ part, int splits, const int2* __restrict__ xinfo, const int2* __restrict__ winfo,
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ wg, const float* __restrict__ bias, int64_t T, int D,
+    int E, int K, int renorm, int32_t* __restrict__ idx_out, uint16_t* __restrict__ w_out,
+    uint16_t* __restrict__ logits_out, uint16_t* __restrict__ probs_out, SharedGateArgs sg, float* __restrict__ sig_out,
+    const uint16_t* __restrict__ expert_scale) {
+  pdl_wait();
+  pdl_launch_dependents();
+  extern __shared__ float s_row[];  // [RT_ROUTE_WARPS][E]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * RT_ROUTE_WARPS + warp;
+  if (t >= T) return;
+  float* row = s_row + warp * E;
+  const int2 xi = xinfo[t];
+  const int64_t gstride = T * (int64_t)E, sstride = 7 * gstride;
+  for (int e0 = 0; e0 < E; e0 += 32) {
+    const int e = e0 + lane;
+    const bool valid = e < E;
+    const int ec = valid ? e : E - 1;
+    const int32_t* pp = part + t * E + ec;
+    int32_t A[7] = {0, 0, 0, 0, 0, 0, 0};
+#pragma unroll 4
+    for (int sp = 0; sp < splits; ++sp)
+#pragma unroll
+      for (int g = 0; g < 7; ++g) A[g] += __ldg(pp + sp * sstride + g * gstride);
+    const float b = bias ? bias[ec] : 0.0f;
+    bool decided;
+    uint16_t lb = logit_from_digit_sums(A, xi, winfo[ec], b, &decided);
+    uint32_t need = __ballot_sync(0xffffffffu, valid && !decided);
+    while (need) {
+      const int src = __ffs(need) - 1;
+      need &= need - 1;
+      const int es = __shfl_sync(0xffffffffu, ec, src);
+      const float v = dot_rn32_warp(x + t * D, wg + (int64_t)es * D, D, lane);
+      if (lane == src) lb = logit_bits(v, b);
+    }
+    if (valid) {
+      row[e] = bf16_bits_to_f32(lb);
+      if (logits_out) logits_out[t * E + e] = lb;
+    }
+  }
+  __syncwarp();
+  route_token_warp_mv<MV>(row, t, E, K, renorm, lane, idx_out, w_out, probs_out, expert_scale);
   if (sig_out) shared_gate_warp(x + t * D, D, sg, lane, sig_out + t);
 }
 

@@ -104,16 +104,17 @@ def test_permute_bad_index_reports_status():
     assert ei.value.status == _lib.ERR_DEVICE_INDEX
 
 
-@pytest.mark.parametrize("T", [3, 100, 300, 1000])
-def test_router_undecided_and_non_finite_logits(T):
+@pytest.mark.parametrize("D,T", [(2048, 3), (2048, 100), (2048, 300), (2048, 1000), (32768, 3), (32768, 100)])
+def test_router_undecided_and_non_finite_logits(D, T):
     """Logits the fast paths cannot decide go through the exact sum: a token
     whose sum with expert 5 is 1 + 2^-8 + 2^-24 + 2^-60 (the fp32 tie is broken
     only by the 2^-60 term, below fp64's reach and below the tensor-core
-    path's digit range), and tokens holding inf or NaN. T = 3 and 100 run the
-    split and fused routers (fp64 sums), 300 and 1000 the int8 tensor-core
-    router; all must equal the oracle's logits (NaN compared as NaN) and,
-    for finite tokens, its routing."""
-    D, E, K = 2048, 128, 8
+    path's digit range), and tokens holding inf or NaN. D = 2048 runs the
+    int8 tensor-core router (split-K form for T <= 256, direct beyond);
+    D = 32768 is past its int32 accumulator bound and runs the fp64 split
+    (T = 3) and fused (T = 100) routers. All must equal the oracle's logits
+    (NaN compared as NaN) and, for finite tokens, its routing."""
+    E, K = 128, 8
     blk = _router_block(D, E, K)
     g = blk.gate.clone()
     g[5] = 0
