@@ -307,6 +307,77 @@ def run_gpu(args):
         dist.destroy_process_group()
 
 
+def e2e_pipelined(args, torch, dev, st, flush, blk, G, nsets):
+    """End-to-end rate of the C5 step through Qwen35MoeBlock.forward with
+    host buffers (see headline_one_gpu): H2D on one copy stream, the
+    forward's graph on `st`, D2H on another copy stream; buffer b of a
+    forward kind is refilled only after the graph that read it and the copy
+    that drained its output have finished."""
+    h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    host_in = {n: [G[n]["x"][i].cpu().pin_memory() for i in range(nsets)] for n in G}
+    host_out = {n: [torch.empty_like(G[n]["out"], device="cpu").pin_memory() for _ in range(nsets)] for n in G}
+    B = {}
+    for n in G:
+        g = G[n]
+        bufs = []
+        for b in range(nsets):
+            xb, ob = torch.empty_like(g["xs"]), torch.empty_like(g["out"])
+            xb.copy_(g["x"][b])
+            with torch.cuda.stream(st):
+                blk.forward(xb, out=ob, workspace=g["ws"])  # warm (same launch shapes as the capture)
+            torch.cuda.synchronize(dev)
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=st):
+                blk.forward(xb, out=ob, workspace=g["ws"])
+            ev = {k: torch.cuda.Event() for k in ("in_ready", "done", "out_read")}
+            bufs.append(dict(x=xb, out=ob, g=gr, ev=ev, used=False))
+        B[n] = bufs
+    torch.cuda.synchronize(dev)
+
+    def run(nsteps, s0):
+        for s in range(s0, s0 + nsteps):
+            for n in ("prefill", "decode"):
+                q = B[n][s % nsets]
+                ev = q["ev"]
+                with torch.cuda.stream(h2d):
+                    if q["used"]:
+                        h2d.wait_event(ev["done"])  # the graph that read this input has finished
+                    q["x"].copy_(host_in[n][s % nsets], non_blocking=True)
+                    ev["in_ready"].record(h2d)
+                with torch.cuda.stream(st):
+                    st.wait_event(ev["in_ready"])
+                    if q["used"]:
+                        st.wait_event(ev["out_read"])  # this output buffer has been read back
+                    flush.fill_(s & 0xFF)
+                    q["g"].replay()
+                    ev["done"].record(st)
+                with torch.cuda.stream(d2h):
+                    d2h.wait_event(ev["done"])
+                    host_out[n][s % nsets].copy_(q["out"], non_blocking=True)
+                    ev["out_read"].record(d2h)
+                q["used"] = True
+
+    run(args.warmup, 0)
+    torch.cuda.synchronize(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(h2d)
+    run(args.steps, args.warmup)
+    t1.record(d2h)
+    torch.cuda.synchronize(dev)
+    e2e_ms = t0.elapsed_time(t1)
+    ok = all(torch.equal(host_out[n][(args.warmup + args.steps - 1) % nsets], B[n][(args.warmup + args.steps - 1) % nsets]["out"].cpu())
+             for n in G)
+    blk.status(G["prefill"]["ws"])
+    del B
+    D = G["prefill"]["x"][0].shape[-1]
+    return {"value": STEP_TOKENS * args.steps / (e2e_ms / 1e3), "unit": UNIT,
+            "h2d_bytes_per_step": STEP_TOKENS * D * 2, "d2h_bytes_per_step": STEP_TOKENS * D * 2,
+            "ms_per_step": e2e_ms / args.steps, "outputs_read_back": bool(ok),
+            "note": "every forward: pinned host x -> device (copy stream), graph replay of Qwen35MoeBlock.forward "
+                    "(mlxr_cu_moe_block_forward), out -> pinned host (second copy stream); copies overlap the "
+                    "neighbouring forwards' compute; device time from the first H2D to the last D2H"}
+
+
 def headline_one_gpu(args, torch, dev, st, flush, blk, peaks):
     """The C5 step on one GPU: two captured graphs (prefill 8192, decode 256)."""
     from mlxr_moe import synth
@@ -370,32 +441,15 @@ def headline_one_gpu(args, torch, dev, st, flush, blk, peaks):
     stage = {n: stage_times(torch, C, _lib, blk, G[n]["x"], G[n]["xs"], G[n]["out"], G[n]["ws"], st, flush,
                             max(5, args.steps // 2), dev) for n in G}
 
-    # e2e: the same step through the public API with pinned host buffers:
-    # x copied in and the output copied back inside the timed region.
-    host_in = {n: [G[n]["x"][i].cpu().pin_memory() for i in range(nsets)] for n in G}
-    host_out = {n: torch.empty_like(G[n]["out"], device="cpu").pin_memory() for n in G}
-    etimer = _Timer(torch, st)
-    with torch.cuda.stream(st):
-        for s in range(args.warmup + args.steps):
-            for n in ("prefill", "decode"):
-                g = G[n]
-                flush.fill_(s & 0xFF)
-                a = etimer.begin()
-                g["xs"].copy_(host_in[n][s % nsets], non_blocking=True)
-                g["g"].replay()
-                host_out[n].copy_(g["out"], non_blocking=True)
-                if s >= args.warmup:
-                    etimer.end(a, n)
-                else:
-                    etimer.end(a, "warm")
-    torch.cuda.synchronize(dev)
-    et = etimer.totals()
-    e2e_ms = sum(et["prefill"]) + sum(et["decode"])
-    e2e = {"value": STEP_TOKENS * args.steps / (e2e_ms / 1e3), "unit": UNIT,
-           "h2d_bytes_per_step": STEP_TOKENS * D * 2, "d2h_bytes_per_step": STEP_TOKENS * D * 2,
-           "note": "pinned host x -> device, graph replay of Qwen35MoeBlock.forward (mlxr_cu_moe_block_forward), "
-                   "out -> pinned host, per forward"}
-
+    # e2e: the same step through the public API with pinned host buffers,
+    # as a serving loop runs it: every forward's input is copied in from
+    # pinned host memory and its output read back inside the timed region,
+    # on two copy streams that overlap the copies with the neighbouring
+    # forwards' compute (double-buffered device inputs and outputs, one
+    # captured graph per buffer). Timed from the first host-to-device copy to
+    # the last device-to-host copy (events on the device), L2 flushed before
+    # every forward as in the device-timed loop.
+    e2e = e2e_pipelined(args, torch, dev, st, flush, blk, G, nsets)
     # Roofline of the dominant kernel: the prefill forward's expert GEMMs
     # (grouped_dequant_gemm_kernel, gate|up + SwiGLU then down: two launches),
     # tensor-bound. Algorithmic FLOPs = 2 * 3 * I * D per routed row, rows =
@@ -502,21 +556,60 @@ def headline_ep(args, torch, dist, dev, st, flush, blk_full, world, rank):
     dist.all_reduce(per, op=dist.ReduceOp.MAX)
     total_ms = float(tot.item())
     value = STEP_TOKENS * args.steps / (total_ms / 1e3)
-    # e2e with pinned host buffers (this rank's share of the batch)
+    # e2e with pinned host buffers (this rank's share of the batch), as a
+    # serving loop runs it: every forward's input copied in and its output
+    # read back inside the timed region, on two copy streams that overlap the
+    # copies with the neighbouring forwards (double-buffered inputs and
+    # outputs); device time from the first H2D to the last D2H, max over ranks.
+    h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     host_in = {n: [xs[n][i].cpu().pin_memory() for i in range(nsets)] for n in xs}
-    host_out = {n: torch.empty_like(outs[n], device="cpu").pin_memory() for n in xs}
-    etimer = _Timer(torch, st)
-    for s in range(args.warmup + args.steps):
-        step(s, etimer if s >= args.warmup else None, (host_in, host_out))
+    host_out = {n: [torch.empty_like(outs[n], device="cpu").pin_memory() for _ in range(nsets)] for n in xs}
+    bufs = {n: [dict(x=torch.empty_like(xs[n][0]), out=torch.empty_like(outs[n]), used=False,
+                     ev={k: torch.cuda.Event() for k in ("in_ready", "done", "out_read")}) for _ in range(nsets)]
+            for n in xs}
+
+    def e2e_steps(s0, nsteps):
+        for s in range(s0, s0 + nsteps):
+            for n in ("prefill", "decode"):
+                q = bufs[n][s % nsets]
+                ev = q["ev"]
+                with torch.cuda.stream(h2d):
+                    if q["used"]:
+                        h2d.wait_event(ev["done"])
+                    q["x"].copy_(host_in[n][s % nsets], non_blocking=True)
+                    ev["in_ready"].record(h2d)
+                with torch.cuda.stream(st):
+                    st.wait_event(ev["in_ready"])
+                    if q["used"]:
+                        st.wait_event(ev["out_read"])
+                    flush.fill_(s & 0xFF)
+                    blk.forward_p2p(q["x"], comm, expected_rows=exp_rows[n], out=q["out"])
+                    ev["done"].record(st)
+                with torch.cuda.stream(d2h):
+                    d2h.wait_event(ev["done"])
+                    host_out[n][s % nsets].copy_(q["out"], non_blocking=True)
+                    ev["out_read"].record(d2h)
+                q["used"] = True
+
+    e2e_steps(0, args.warmup)
     torch.cuda.synchronize(dev)
     blk.status()
-    et = etimer.totals()
-    e = torch.tensor([sum(et["prefill"]) + sum(et["decode"])], dtype=torch.float64, device=dev)
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(h2d)
+    e2e_steps(args.warmup, args.steps)
+    t1.record(d2h)
+    torch.cuda.synchronize(dev)
+    blk.status()
+    e = torch.tensor([t0.elapsed_time(t1)], dtype=torch.float64, device=dev)
     dist.all_reduce(e, op=dist.ReduceOp.MAX)
     e2e = {"value": STEP_TOKENS * args.steps / (float(e.item()) / 1e3), "unit": UNIT,
            "h2d_bytes_per_step": STEP_TOKENS * D * 2, "d2h_bytes_per_step": STEP_TOKENS * D * 2,
-           "note": "every rank: its pinned host x share -> device, ExpertParallelMoeBlock.forward_p2p "
-                   "(mlxr_cu_moe_ep_*_p2p), out -> pinned host; max over ranks; bytes summed over ranks"}
+           "ms_per_step": float(e.item()) / args.steps,
+           "note": "every rank, every forward: its pinned host x share -> device (copy stream), "
+                   "ExpertParallelMoeBlock.forward_p2p (mlxr_cu_moe_ep_*_p2p), out -> pinned host (second copy "
+                   "stream); copies overlap the neighbouring forwards; max over ranks; bytes summed over ranks"}
     # Phase times of each forward (dispatch, experts, combine): events between
     # the three peer-memory calls on a few extra steps, medians, max over ranks.
     ph = {n: [] for n in xs}

@@ -440,18 +440,21 @@ __global__ void __launch_bounds__(RG_THREADS, 1)
 
 RouterTcLayout router_tc_layout(int64_t T, int E, int D) {
   RouterTcLayout L;
-  L.split = T <= kRouterTcSplitMaxT;
-  L.bn = L.split ? 16 : 64;
+  // 16-token tiles up to kRouterTcSplitMaxT tokens, else 64; the k range is
+  // cut over CTAs while the tiles alone fill less than about one wave.
+  L.bn = T <= kRouterTcSplitMaxT ? 16 : 64;
   L.Dp = (D + 127) / 128 * 128;
   L.rows_pad_x = (T + L.bn - 1) / L.bn * L.bn;
   L.rows_pad_w = (E + RG_BM - 1) / RG_BM * RG_BM;
   const int nk = (int)(L.Dp / RG_BK);
+  const int sms = num_sms_current();
+  const int64_t tiles = (L.rows_pad_x / L.bn) * (L.rows_pad_w / RG_BM);
+  L.split = L.bn == 16 || tiles * 5 < (int64_t)sms * 4;
   L.kps = nk;
   L.splits = 1;
   if (L.split) {
     // About one CTA per SM, at most 16 k-slices (each token's finish reads them all).
-    const int64_t tiles = (L.rows_pad_x / L.bn) * (L.rows_pad_w / RG_BM);
-    int want = (int)std::max<int64_t>(1, std::min<int64_t>(16, num_sms_current() / std::max<int64_t>(tiles, 1)));
+    int want = (int)std::max<int64_t>(1, std::min<int64_t>(16, sms / std::max<int64_t>(tiles, 1)));
     L.kps = (nk + want - 1) / want;
     L.splits = (nk + L.kps - 1) / L.kps;
   }
@@ -522,7 +525,8 @@ int launch_router_tc(const RouterTcProblem& p, cudaStream_t st) {
   a.rows_pad_x = (int)L.rows_pad_x;
   a.rows_pad_w = (int)L.rows_pad_w;
   a.status = p.status;
-  return L.split ? launch_tc<16, true>(L, tw, tx, a, st) : launch_tc<64, false>(L, tw, tx, a, st);
+  if (L.bn == 16) return launch_tc<16, true>(L, tw, tx, a, st);
+  return L.split ? launch_tc<64, true>(L, tw, tx, a, st) : launch_tc<64, false>(L, tw, tx, a, st);
 }
 
 }  // namespace mlxr

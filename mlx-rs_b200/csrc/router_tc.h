@@ -10,8 +10,10 @@ namespace mlxr {
 // Workspace of one launch: digit planes of the tokens and of the router
 // rows (4 int8 planes each, rows padded to the tile, D padded to 128) and
 // the per-row exponent / truncation count.
-// Batches up to this size take the split-K form (16-token tiles, the k
-// range cut over CTAs, partial digit sums finished by route_partials_kernel).
+// Batches up to this size use 16-token tiles (else 64). Whenever the tiles
+// alone would fill less than about one wave of CTAs the launch takes the
+// split-K form: the k range cut over CTAs, partial digit sums finished by
+// route_partials_kernel.
 constexpr int64_t kRouterTcSplitMaxT = 256;
 
 struct RouterTcLayout {
@@ -24,7 +26,7 @@ RouterTcLayout router_tc_layout(int64_t T, int E, int D);
 bool router_tc_supported(int D);
 
 // logits lg [T, E] bf16 = bf16(fp32(exact x[t] . wg[e]) + bias[e]) (bias may
-// be NULL). In the split-K form (T <= kRouterTcSplitMaxT) it writes the
+// be NULL). In the split-K form (router_tc_layout(...).split) it writes the
 // partial digit sums instead (layout.part, [splits][7][T][E] int32) and
 // route_partials_kernel forms the logits.
 struct RouterTcProblem {
