@@ -286,35 +286,34 @@ static int run_router(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
     es = static_cast<const uint16_t*>(wt->expert_scale);
   }
   if (L.T > kSplitRouterMaxT && router_tc_supported(L.D)) {
-    // The logits on the int8 tensor cores (router_tc.cu). Large batches:
-    // logits from the kernel's epilogue, then one warp per token routes
-    // them. Small batches (split-K form): one warp per token sums the k
-    // slices, forms its logits and routes them.
+    // The logits on the int8 tensor cores (router_tc.cu): from the kernel's
+    // epilogue, or (split-K form) from its partial digit sums; then one
+    // warp per token routes them.
     uint16_t* lg = logits ? logits : at<uint16_t>(ws, L.logits);
     const RouterTcLayout R = router_tc_layout(L.T, L.E, L.D);
     RouterTcProblem rp{xp, L.T, wg, L.E, L.D, rbias, lg, at<void>(ws, L.rtc), at<int>(ws, L.status)};
     if (int rc = launch_router_tc(rp, st)) return rc;
+    if (R.split) {
+      uint8_t* rb = at<uint8_t>(ws, L.rtc);
+      const int64_t n = L.T * (int64_t)L.E;
+      launch_pdl(logits_from_partials_kernel, (unsigned)((n + 255) / 256), 256, 0, st,
+                 reinterpret_cast<const int32_t*>(rb + R.part), R.splits, reinterpret_cast<const int2*>(rb + R.xinfo),
+                 reinterpret_cast<const int2*>(rb + R.winfo), xp, wg, rbias, L.T, L.D, L.E, lg);
+      MLXR_LAUNCH_CHECK("logits_from_partials_kernel");
+    }
     const unsigned grid = (unsigned)((L.T + RT_ROUTE_WARPS - 1) / RT_ROUTE_WARPS);
     const size_t smem = RT_ROUTE_WARPS * L.E * sizeof(float);
     // lane arrays of the routing sized for E (registers, not local memory)
     auto route = [&](auto mv) {
       constexpr int MV = decltype(mv)::value;
-      if (R.split) {
-        uint8_t* rb = at<uint8_t>(ws, L.rtc);
-        launch_pdl(route_partials_kernel<MV>, grid, RT_ROUTE_WARPS * 32, smem, st,
-                   reinterpret_cast<const int32_t*>(rb + R.part), R.splits, reinterpret_cast<const int2*>(rb + R.xinfo),
-                   reinterpret_cast<const int2*>(rb + R.winfo), xp, wg, rbias, L.T, L.D, L.E, L.K, c->norm_topk_prob,
-                   at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w), logits, probs, sg, sig, es);
-      } else {
-        launch_pdl(route_rows_kernel<MV>, grid, RT_ROUTE_WARPS * 32, smem, st, lg, xp, L.T, L.D, L.E, L.K,
-                   c->norm_topk_prob, at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w), probs, sg, sig, es);
-      }
+      launch_pdl(route_rows_kernel<MV>, grid, RT_ROUTE_WARPS * 32, smem, st, lg, xp, L.T, L.D, L.E, L.K,
+                 c->norm_topk_prob, at<int32_t>(ws, L.idx), at<uint16_t>(ws, L.w), probs, sg, sig, es);
     };
     if (L.E <= 128) route(std::integral_constant<int, 4>{});
     else if (L.E <= 256) route(std::integral_constant<int, 8>{});
     else if (L.E <= 512) route(std::integral_constant<int, 16>{});
     else route(std::integral_constant<int, 32>{});
-    MLXR_LAUNCH_CHECK(R.split ? "route_partials_kernel" : "route_rows_kernel");
+    MLXR_LAUNCH_CHECK("route_rows_kernel");
     return MLXR_CU_OK;
   }
   // Small batches (latency: the tensor-core form costs more launches) and D

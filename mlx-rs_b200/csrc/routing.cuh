@@ -526,57 +526,44 @@ __global__ void __launch_bounds__(RT_ROUTE_WARPS * 32) route_rows_kernel(
   if (sig_out) shared_gate_warp(x + t * D, D, sg, lane, sig_out + t);
 }
 
-// The tensor-core router's split-K form (router_tc.cu, small batches):
-// part[s][g][t][e] (s < splits, g < 7) are the digit sums of k-slice s. One
-// token per warp: each lane adds its experts' slices (exact integer sums),
-// forms the logit as router_tc_kernel's epilogue does (the exact sum when
-// the interval test cannot decide it), then the token is routed as in
-// route_rows_kernel.
-template <int MV>
-__global__ void __launch_bounds__(RT_ROUTE_WARPS * 32) route_partials_kernel(
+// The tensor-core router's split-K form (router_tc.cu): part[s][g][t][e]
+// (s < splits, g < 7) are the digit sums of k-slice s. One thread per
+// (token, expert), experts fastest: the slices are added (exact integer
+// sums) and the logit formed as router_tc_kernel's epilogue does; logits the
+// interval test leaves open are computed as exact sums by the whole warp
+// (each undecided lane's token and expert in turn). route_rows_kernel then
+// routes the tokens.
+__global__ void __launch_bounds__(256) logits_from_partials_kernel(
     const int32_t* __restrict__ part, int splits, const int2* __restrict__ xinfo, const int2* __restrict__ winfo,
     const uint16_t* __restrict__ x, const uint16_t* __restrict__ wg, const float* __restrict__ bias, int64_t T, int D,
-    int E, int K, int renorm, int32_t* __restrict__ idx_out, uint16_t* __restrict__ w_out,
-    uint16_t* __restrict__ logits_out, uint16_t* __restrict__ probs_out, SharedGateArgs sg, float* __restrict__ sig_out,
-    const uint16_t* __restrict__ expert_scale) {
+    int E, uint16_t* __restrict__ lg) {
   pdl_wait();
   pdl_launch_dependents();
-  extern __shared__ float s_row[];  // [RT_ROUTE_WARPS][E]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t t = (int64_t)blockIdx.x * RT_ROUTE_WARPS + warp;
-  if (t >= T) return;
-  float* row = s_row + warp * E;
-  const int2 xi = xinfo[t];
-  const int64_t gstride = T * (int64_t)E, sstride = 7 * gstride;
-  for (int e0 = 0; e0 < E; e0 += 32) {
-    const int e = e0 + lane;
-    const bool valid = e < E;
-    const int ec = valid ? e : E - 1;
-    const int32_t* pp = part + t * E + ec;
-    int32_t A[7] = {0, 0, 0, 0, 0, 0, 0};
-#pragma unroll 4
-    for (int sp = 0; sp < splits; ++sp)
+  const int lane = threadIdx.x & 31;
+  const int64_t n = T * (int64_t)E;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const bool valid = i < n;
+  const int64_t ic = valid ? i : n - 1;
+  const int64_t t = ic / E;
+  const int e = (int)(ic - t * E);
+  const int64_t gstride = n, sstride = 7 * n;
+  int32_t A[7] = {0, 0, 0, 0, 0, 0, 0};
+  for (int sp = 0; sp < splits; ++sp)
 #pragma unroll
-      for (int g = 0; g < 7; ++g) A[g] += __ldg(pp + sp * sstride + g * gstride);
-    const float b = bias ? bias[ec] : 0.0f;
-    bool decided;
-    uint16_t lb = logit_from_digit_sums(A, xi, winfo[ec], b, &decided);
-    uint32_t need = __ballot_sync(0xffffffffu, valid && !decided);
-    while (need) {
-      const int src = __ffs(need) - 1;
-      need &= need - 1;
-      const int es = __shfl_sync(0xffffffffu, ec, src);
-      const float v = dot_rn32_warp(x + t * D, wg + (int64_t)es * D, D, lane);
-      if (lane == src) lb = logit_bits(v, b);
-    }
-    if (valid) {
-      row[e] = bf16_bits_to_f32(lb);
-      if (logits_out) logits_out[t * E + e] = lb;
-    }
+    for (int g = 0; g < 7; ++g) A[g] += __ldg(part + sp * sstride + g * gstride + ic);
+  const float b = bias ? bias[e] : 0.0f;
+  bool decided;
+  uint16_t lb = logit_from_digit_sums(A, xinfo[t], winfo[e], b, &decided);
+  uint32_t need = __ballot_sync(0xffffffffu, valid && !decided);
+  while (need) {
+    const int src = __ffs(need) - 1;
+    need &= need - 1;
+    const int64_t ts = __shfl_sync(0xffffffffu, t, src);
+    const int es = __shfl_sync(0xffffffffu, e, src);
+    const float v = dot_rn32_warp(x + ts * D, wg + (int64_t)es * D, D, lane);
+    if (lane == src) lb = logit_bits(v, b);
   }
-  __syncwarp();
-  route_token_warp_mv<MV>(row, t, E, K, renorm, lane, idx_out, w_out, probs_out, expert_scale);
-  if (sig_out) shared_gate_warp(x + t * D, D, sg, lane, sig_out + t);
+  if (valid) lg[i] = lb;
 }
 
 // ------------------------------------------------------- permutation ----
