@@ -80,10 +80,11 @@ def ncu_traffic(kernel_key: str):
     return None
 
 
-def _clock_sampler_proc(uuid, stop, out_q, period_s):
+def _clock_sampler_proc(uuid, stop, ready, out_q, period_s):
     """Runs in its own process (spawned): polls the GPU's SM clock and clock
-    event reasons through NVML until `stop` is set. Being another process,
-    it takes no time from the benchmark's launching thread."""
+    event reasons through NVML until `stop` is set, after setting `ready`
+    once it polls. Being another process, it takes no time from the
+    benchmark's launching thread."""
     samples, err, max_mhz = [], None, None
     try:
         import pynvml as N
@@ -92,6 +93,7 @@ def _clock_sampler_proc(uuid, stop, out_q, period_s):
         h = N.nvmlDeviceGetHandleByUUID(uuid)
         max_mhz = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
         names = {k: getattr(N, v, 0) for k, v in ClockSampler.REASONS}
+        ready.set()
         while not stop.is_set():
             mhz = N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)
             rs = N.nvmlDeviceGetCurrentClocksEventReasons(h)
@@ -99,6 +101,7 @@ def _clock_sampler_proc(uuid, stop, out_q, period_s):
             time.sleep(period_s)
     except Exception as e:  # no NVML: report it instead of a clock
         err = f"nvml unavailable: {e}"[:200]
+    ready.set()
     out_q.put((samples, max_mhz, err))
 
 
@@ -123,10 +126,12 @@ class ClockSampler:
         import multiprocessing as mp
 
         ctx = mp.get_context("spawn")
-        self.stop_ev, self.q = ctx.Event(), ctx.Queue()
-        self.p = ctx.Process(target=_clock_sampler_proc, args=(self.uuid, self.stop_ev, self.q, 0.005), daemon=True)
+        self.stop_ev, self.ready, self.q = ctx.Event(), ctx.Event(), ctx.Queue()
+        self.p = ctx.Process(target=_clock_sampler_proc, args=(self.uuid, self.stop_ev, self.ready, self.q, 0.005),
+                             daemon=True)
         self.p.start()
-        time.sleep(2.0)  # let the sampler start polling before the timed region
+        self.ready.wait(timeout=60)  # the sampler polls before the timed region starts
+        time.sleep(0.2)
 
     def stop(self):
         if self.p is None:
@@ -534,17 +539,21 @@ def headline_ep(args, torch, dist, dev, st, flush, blk_full, world, rank):
         step(s)
     torch.cuda.synchronize(dev)
     blk.status()
+    # Only rank 0 samples its GPU's clocks (the line reports rank 0's): one
+    # sampling process instead of one per rank, whose NVML polling could
+    # delay the other ranks' launches.
+    clocks = ClockSampler(smi_id(torch, dev)) if rank == 0 else None
+    if clocks:
+        clocks.start()
     dist.barrier()
     torch.cuda.synchronize(dev)
-    clocks = ClockSampler(smi_id(torch, dev))
-    clocks.start()
     timer = _Timer(torch, st)
     for s in range(args.steps):
         step(s, timer)
     torch.cuda.synchronize(dev)
     dist.barrier()
     torch.cuda.synchronize(dev)
-    clk = clocks.stop()
+    clk = clocks.stop() if clocks else None
     blk.status()
     tt = timer.totals()
     per = torch.tensor([sum(tt["prefill"]), sum(tt["decode"])], dtype=torch.float64, device=dev)

@@ -220,8 +220,9 @@ static Layout make_layout(const mlxr_cu_moe_config* c, int64_t T, int64_t rows_c
   // The tensor-core router's digit planes: in the x_sorted buffer when they
   // fit (the permute fills it only after the router has finished), else apart.
   if (T > kSplitRouterMaxT && router_tc_supported(L.D)) {
-    const size_t need = router_tc_layout(T, L.E, L.D).total;
-    L.rtc = need <= (size_t)L.rows_pad * L.D * 2 ? L.xs : take(need);
+    const size_t xs_bytes = (size_t)L.rows_pad * L.D * 2;
+    const size_t need = router_tc_layout(T, L.E, L.D, xs_bytes).total;
+    L.rtc = need <= xs_bytes ? L.xs : take(need);
   }
   if (L.split_rows > 0) {
     const int smax = L.s1 > L.s2 ? L.s1 : L.s2;
@@ -290,8 +291,9 @@ static int run_router(const mlxr_cu_moe_config* c, const mlxr_cu_moe_weights* wt
     // epilogue, or (split-K form) from its partial digit sums; then one
     // warp per token routes them.
     uint16_t* lg = logits ? logits : at<uint16_t>(ws, L.logits);
-    const RouterTcLayout R = router_tc_layout(L.T, L.E, L.D);
-    RouterTcProblem rp{xp, L.T, wg, L.E, L.D, rbias, lg, at<void>(ws, L.rtc), at<int>(ws, L.status)};
+    const size_t budget = (size_t)L.rows_pad * L.D * 2;  // the same budget the workspace layout used
+    const RouterTcLayout R = router_tc_layout(L.T, L.E, L.D, budget);
+    RouterTcProblem rp{xp, L.T, wg, L.E, L.D, rbias, lg, at<void>(ws, L.rtc), at<int>(ws, L.status), budget};
     if (int rc = launch_router_tc(rp, st)) return rc;
     if (R.split) {
       uint8_t* rb = at<uint8_t>(ws, L.rtc);

@@ -106,20 +106,19 @@ __global__ void __launch_bounds__(RD_WARPS * 32) router_digits_kernel(DigitRows 
     return;
   }
   const uint4* row = reinterpret_cast<const uint4*>(src + r * (int64_t)D);
-  // pass 1: the largest exponent of a finite nonzero element; inf/NaN
-  uint32_t mb = 0, nonfin = 0;
+  // pass 1: the largest |bits| of the row, two halves per packed 16-bit max
+  // (|bits| >= 0x7f80 means inf or NaN: such a row is flagged as a whole,
+  // so those values may enter the max)
+  uint32_t m2 = 0;
   for (int c = threadIdx.x; c < nch; c += RD_WARPS * 32) {
     const uint4 v = __ldg(row + c);
-    const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      const uint32_t lo = wd[h] & 0x7fffu, hi = (wd[h] >> 16) & 0x7fffu;
-      nonfin |= (lo >= 0x7f80u) | (hi >= 0x7f80u);
-      mb = max(mb, max(lo < 0x7f80u ? lo : 0u, hi < 0x7f80u ? hi : 0u));
-    }
+    m2 = __vmaxu2(m2, v.x & 0x7fff7fffu);
+    m2 = __vmaxu2(m2, v.y & 0x7fff7fffu);
+    m2 = __vmaxu2(m2, v.z & 0x7fff7fffu);
+    m2 = __vmaxu2(m2, v.w & 0x7fff7fffu);
   }
-  mb = __reduce_max_sync(0xffffffffu, mb);
-  nonfin = __reduce_or_sync(0xffffffffu, nonfin);
+  uint32_t mb = __reduce_max_sync(0xffffffffu, max(m2 & 0xffffu, m2 >> 16));
+  uint32_t nonfin = mb >= 0x7f80u ? 1u : 0u;
   if (lane == 0) {
     s_top[warp] = (int)mb;
     s_nonfin[warp] = (int)nonfin;
@@ -438,7 +437,7 @@ __global__ void __launch_bounds__(RG_THREADS, 1)
   }
 }
 
-RouterTcLayout router_tc_layout(int64_t T, int E, int D) {
+RouterTcLayout router_tc_layout(int64_t T, int E, int D, size_t budget) {
   RouterTcLayout L;
   // 16-token tiles up to kRouterTcSplitMaxT tokens, else 64; the k range is
   // cut over CTAs while the tiles alone fill less than about one wave.
@@ -450,26 +449,26 @@ RouterTcLayout router_tc_layout(int64_t T, int E, int D) {
   const int sms = num_sms_current();
   const int64_t tiles = (L.rows_pad_x / L.bn) * (L.rows_pad_w / RG_BM);
   L.split = L.bn == 16 || tiles * 5 < (int64_t)sms * 4;
-  L.kps = nk;
-  L.splits = 1;
-  if (L.split) {
-    // About one CTA per SM, at most 16 k-slices (each token's finish reads them all).
-    int want = (int)std::max<int64_t>(1, std::min<int64_t>(16, sms / std::max<int64_t>(tiles, 1)));
+  // About one CTA per SM, at most 16 k-slices (each logit's finish reads
+  // them all), fewer when the partial sums would not fit `budget`.
+  int want = L.split ? (int)std::max<int64_t>(1, std::min<int64_t>(16, sms / std::max<int64_t>(tiles, 1))) : 1;
+  for (;; --want) {
     L.kps = (nk + want - 1) / want;
-    L.splits = (nk + L.kps - 1) / L.kps;
+    L.splits = L.split ? (nk + L.kps - 1) / L.kps : 1;
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+      const size_t at = o;
+      o = (o + bytes + 255) / 256 * 256;
+      return at;
+    };
+    L.xdig = take((size_t)4 * L.rows_pad_x * L.Dp);
+    L.wdig = take((size_t)4 * L.rows_pad_w * L.Dp);
+    L.xinfo = take((size_t)L.rows_pad_x * sizeof(int2));
+    L.winfo = take((size_t)L.rows_pad_w * sizeof(int2));
+    L.part = L.split ? take((size_t)L.splits * 7 * T * E * sizeof(int32_t)) : 0;
+    L.total = o;
+    if (L.total <= budget || want <= 1) break;
   }
-  size_t o = 0;
-  auto take = [&](size_t bytes) {
-    const size_t at = o;
-    o = (o + bytes + 255) / 256 * 256;
-    return at;
-  };
-  L.xdig = take((size_t)4 * L.rows_pad_x * L.Dp);
-  L.wdig = take((size_t)4 * L.rows_pad_w * L.Dp);
-  L.xinfo = take((size_t)L.rows_pad_x * sizeof(int2));
-  L.winfo = take((size_t)L.rows_pad_w * sizeof(int2));
-  if (L.split) L.part = take((size_t)L.splits * 7 * T * E * sizeof(int32_t));
-  L.total = o;
   return L;
 }
 
@@ -491,7 +490,7 @@ int launch_router_tc(const RouterTcProblem& p, cudaStream_t st) {
   if (!router_tc_supported(p.D))
     return set_error(MLXR_CU_ERR_INVALID_ARGUMENT, "router_tc: D=%d must be a multiple of 8 below 32768", p.D);
   if (p.T <= 0 || p.E <= 0) return MLXR_CU_OK;
-  const RouterTcLayout L = router_tc_layout(p.T, p.E, p.D);
+  const RouterTcLayout L = router_tc_layout(p.T, p.E, p.D, p.budget);
   uint8_t* ws = static_cast<uint8_t*>(p.workspace);
   int8_t* xdig = reinterpret_cast<int8_t*>(ws + L.xdig);
   int8_t* wdig = reinterpret_cast<int8_t*>(ws + L.wdig);

@@ -22,7 +22,10 @@ struct RouterTcLayout {
   int64_t Dp = 0, rows_pad_x = 0, rows_pad_w = 0;
   size_t xdig = 0, wdig = 0, xinfo = 0, winfo = 0, part = 0, total = 0;
 };
-RouterTcLayout router_tc_layout(int64_t T, int E, int D);
+// budget: bytes the caller would like the layout to stay within (the k
+// range is cut into fewer slices to get there; the total may still exceed
+// it at one slice).
+RouterTcLayout router_tc_layout(int64_t T, int E, int D, size_t budget = ~(size_t)0);
 bool router_tc_supported(int D);
 
 // logits lg [T, E] bf16 = bf16(fp32(exact x[t] . wg[e]) + bias[e]) (bias may
@@ -37,8 +40,9 @@ struct RouterTcProblem {
   int D;
   const float* bias;
   uint16_t* lg;
-  void* workspace;     // router_tc_layout(T, E, D).total bytes, 256-byte aligned
+  void* workspace;     // router_tc_layout(T, E, D, budget).total bytes, 256-byte aligned
   int* status;         // device status word (timeouts)
+  size_t budget;       // the layout's budget (the same value sizes the workspace)
 };
 int launch_router_tc(const RouterTcProblem& p, cudaStream_t st);
 
