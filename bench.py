@@ -160,6 +160,22 @@ def smi_id(torch, dev) -> str:
         return str(dev.index)
 
 
+def router_kernels(cfg, T: int, sms: int = 148) -> int:
+    """Router launches at T tokens (csrc/moe_block.cu run_router,
+    csrc/router_tc.cu router_tc_layout): the fp64 split router up to 64
+    tokens; beyond, digit planes + the int8 tensor-core kernel (+ the
+    partial-sum finish in its split-K form) + route rows."""
+    D, E = cfg.hidden_size, cfg.num_experts
+    if T == 0:
+        return 0
+    if T <= 64 or D >= 32768:
+        return 1
+    bn = 16 if T <= 256 else 64
+    tiles = -(-T // bn) * -(-E // 128)
+    split = bn == 16 or tiles * 5 < sms * 4
+    return 3 + (1 if split else 0)
+
+
 def kernels_per_forward(cfg, T: int, sms: int = 148) -> int:
     """Library kernels one block forward launches at T tokens (the launch
     choices of csrc/moe_block.cu: router variant, one-CTA or three-kernel
@@ -169,7 +185,7 @@ def kernels_per_forward(cfg, T: int, sms: int = 148) -> int:
     R = T * K
     if T == 0:
         return 0
-    n = 2 if T > 256 else 1                                    # router (tile + route rows above 256 tokens)
+    n = router_kernels(cfg, T, sms)                            # router
     small = R <= 2048
     n += 1 if small else 3                                     # permute
     n += 0 if (small and R <= 16) else 1                       # row gather (in the one-CTA permute up to 16 rows)
@@ -205,7 +221,8 @@ def ep_kernels_per_forward(cfg, T: int, world: int) -> int:
     """Library kernels one expert-parallel peer-memory step launches on a rank
     with T tokens (the launch choices of the three p2p entry points)."""
     K = cfg.num_experts_per_tok
-    n = (2 if T > 256 else 1) if T else 0                      # router
+    n = 1                                                      # ep_bump_epoch (device-resident epoch)
+    n += router_kernels(cfg, T)                                # router
     n += 1                                                     # ep_pair_dest
     n += 1 if T * K <= 2048 else 3                             # permute of the pairs by rank
     n += 3                                                     # ep_counts, ep_pair_meta, ep_send
@@ -520,18 +537,30 @@ def headline_ep(args, torch, dist, dev, st, flush, blk_full, world, rank):
     blk = ExpertParallelMoeBlock.from_block(blk_full, rank, world, place)
     comm = PeerComm(rank, world, cap=Tp, hidden=D, k=K)
     exp_rows = {"prefill": max(1, PREFILL_T * K // world), "decode": max(1, DECODE_T * K // world)}
-    outs = {n: torch.empty_like(xs[n][0]) for n in xs}
+    outs = {n: [torch.empty_like(xs[n][0]) for _ in range(nsets)] for n in xs}
+    # Every step uses the comm's device-resident epoch, so that each
+    # forward is one captured CUDA graph per (forward, buffer): the host
+    # issues one replay per forward, and every rank runs the same steps.
+    with torch.cuda.stream(st):
+        for n in ("prefill", "decode"):
+            for b in range(nsets):  # warm each buffer pair once (sets kernel attributes outside capture)
+                blk.forward_p2p(xs[n][b], comm, expected_rows=exp_rows[n], out=outs[n][b], device_epoch=True)
+    torch.cuda.synchronize(dev)
+    blk.status()
+    graphs = {}
+    for n in ("prefill", "decode"):
+        for b in range(nsets):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=st):
+                blk.forward_p2p(xs[n][b], comm, expected_rows=exp_rows[n], out=outs[n][b], device_epoch=True)
+            graphs[(n, b)] = gr
 
-    def step(s, timer=None, host=None):
+    def step(s, timer=None):
         with torch.cuda.stream(st):
             for n in ("prefill", "decode"):
                 flush.fill_(s & 0xFF)
                 a = timer.begin() if timer else None
-                if host is not None:
-                    xs[n][s % nsets].copy_(host[0][n][s % nsets], non_blocking=True)
-                blk.forward_p2p(xs[n][s % nsets], comm, expected_rows=exp_rows[n], out=outs[n])
-                if host is not None:
-                    host[1][n].copy_(outs[n], non_blocking=True)
+                graphs[(n, s % nsets)].replay()
                 if timer:
                     timer.end(a, n)
 
@@ -572,9 +601,9 @@ def headline_ep(args, torch, dist, dev, st, flush, blk_full, world, rank):
     # outputs); device time from the first H2D to the last D2H, max over ranks.
     h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     host_in = {n: [xs[n][i].cpu().pin_memory() for i in range(nsets)] for n in xs}
-    host_out = {n: [torch.empty_like(outs[n], device="cpu").pin_memory() for _ in range(nsets)] for n in xs}
-    bufs = {n: [dict(x=torch.empty_like(xs[n][0]), out=torch.empty_like(outs[n]), used=False,
-                     ev={k: torch.cuda.Event() for k in ("in_ready", "done", "out_read")}) for _ in range(nsets)]
+    host_out = {n: [torch.empty_like(outs[n][0], device="cpu").pin_memory() for _ in range(nsets)] for n in xs}
+    bufs = {n: [dict(x=xs[n][b], out=outs[n][b], g=graphs[(n, b)], used=False,
+                     ev={k: torch.cuda.Event() for k in ("in_ready", "done", "out_read")}) for b in range(nsets)]
             for n in xs}
 
     def e2e_steps(s0, nsteps):
@@ -592,7 +621,7 @@ def headline_ep(args, torch, dist, dev, st, flush, blk_full, world, rank):
                     if q["used"]:
                         st.wait_event(ev["out_read"])
                     flush.fill_(s & 0xFF)
-                    blk.forward_p2p(q["x"], comm, expected_rows=exp_rows[n], out=q["out"])
+                    q["g"].replay()
                     ev["done"].record(st)
                 with torch.cuda.stream(d2h):
                     d2h.wait_event(ev["done"])
@@ -627,7 +656,8 @@ def headline_ep(args, torch, dist, dev, st, flush, blk_full, world, rank):
             for n in ("prefill", "decode"):
                 flush.fill_(s & 0xFF)
                 evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-                blk.forward_p2p(xs[n][s % nsets], comm, expected_rows=exp_rows[n], out=outs[n], events=evs)
+                blk.forward_p2p(xs[n][s % nsets], comm, expected_rows=exp_rows[n], out=outs[n][s % nsets], events=evs,
+                                device_epoch=True)
                 ph[n].append(evs)
     torch.cuda.synchronize(dev)
     blk.status()
@@ -635,6 +665,8 @@ def headline_ep(args, torch, dist, dev, st, flush, blk_full, world, rank):
                           for n in ("prefill", "decode")], dtype=torch.float64, device=dev)
     dist.all_reduce(phase, op=dist.ReduceOp.MAX)
     dist.barrier()
+    torch.cuda.synchronize(dev)
+    del bufs, graphs
     torch.cuda.synchronize(dev)
     comm.close()
     launches = (ep_kernels_per_forward(cfg, Tp, world) + ep_kernels_per_forward(cfg, Td, world)) * args.steps
@@ -645,7 +677,7 @@ def headline_ep(args, torch, dist, dev, st, flush, blk_full, world, rank):
                 for i, (n, T_, Tr) in enumerate((("prefill", PREFILL_T, Tp), ("decode", DECODE_T, Td)))}
     return dict(value=value, ms_per_step=total_ms / args.steps, e2e=e2e, roofline=None, clocks=clk,
                 forwards=forwards, gpu_launches=launches,
-                graphs="not captured: host issues the three peer-memory steps per forward",
+                graphs="each forward one captured CUDA graph (device-resident step epoch)",
                 parallelism=f"ep{world}: experts spread over {world} ranks by measured load; tokens split "
                             f"evenly; dispatch/combine over NVLink peer memory inside the kernels")
 

@@ -418,7 +418,11 @@ MLXR_CU_API int mlxr_cu_moe_ep_combine(const mlxr_cu_moe_config* cfg, const mlxr
  * waits on it records the failure (mlxr_cu_moe_status then returns
  * MLXR_CU_ERR_TIMEOUT with a message naming a failed peer) instead of using
  * the rows. epoch must be in [1, 2^31) and grow by step; the top bit marks
- * the poison. Ranks must be on different GPUs. */
+ * the poison. epoch 0 (every step of the comm, on every rank) selects a
+ * device-resident step counter instead: dispatch_p2p advances it in the
+ * comm's buffer before any kernel of the step reads it, so a step captured
+ * in a CUDA graph replays with a new epoch each time. A comm uses one kind
+ * of epoch for its whole life. Ranks must be on different GPUs. */
 #define MLXR_CU_IPC_HANDLE_BYTES 64
 
 MLXR_CU_API int mlxr_cu_ep_comm_create(int world, int rank, int64_t cap, int hidden, int k, void** comm,

@@ -1362,7 +1362,7 @@ int mlxr_cu_moe_ep_dispatch_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe
                                 const int32_t* placement, const void* x, int64_t num_tokens, int32_t* pair_pos,
                                 float* shared_gate, uint32_t epoch, void* workspace, size_t workspace_bytes,
                                 void* stream) {
-  MLXR_CHECK_ARG(epoch >= 1 && epoch < EP_FLAG_POISON, "moe_ep: epoch=%u must be in [1, 2^31)", epoch);
+  MLXR_CHECK_ARG(epoch < EP_FLAG_POISON, "moe_ep: epoch=%u must be 0 (device counter) or in [1, 2^31)", epoch);
   if (int rc = validate(cfg, num_tokens)) return rc;
   if (int rc = ep_comm_check(comm, cfg)) return rc;
   EpComm* c = static_cast<EpComm*>(comm);
@@ -1377,6 +1377,10 @@ int mlxr_cu_moe_ep_dispatch_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe
   void* ws = workspace;
   const Layout L = make_layout(cfg, num_tokens);
   MLXR_CUDA_TRY(cudaMemsetAsync(at<int>(ws, L.status), 0, kStatusSlotBytes, st));
+  if (epoch == 0) {  // device-resident step counter: advance it before any kernel of the step reads it
+    launch_pdl(ep_bump_epoch_kernel, 1, 32, 0, st, c->local, c->bl, at<int>(ws, L.status));
+    MLXR_LAUNCH_CHECK("ep_bump_epoch_kernel");
+  }
   const int K = cfg->num_experts_per_tok;
   const int64_t R = L.R;
   int32_t* offsets = at<int32_t>(ws, L.offsets);
@@ -1427,7 +1431,7 @@ int mlxr_cu_moe_ep_dispatch_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe
 int mlxr_cu_moe_ep_experts_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* local_weights,
                                int num_local_experts, void* comm, int64_t expected_rows, uint32_t epoch,
                                void* workspace, size_t workspace_bytes, void* stream) {
-  MLXR_CHECK_ARG(epoch >= 1 && epoch < EP_FLAG_POISON, "moe_ep: epoch=%u must be in [1, 2^31)", epoch);
+  MLXR_CHECK_ARG(epoch < EP_FLAG_POISON, "moe_ep: epoch=%u must be 0 (device counter) or in [1, 2^31)", epoch);
   if (int rc = ep_comm_check(comm, cfg)) return rc;
   EpComm* c = static_cast<EpComm*>(comm);
   MLXR_CHECK_ARG(local_weights != nullptr && num_local_experts >= 1 && num_local_experts <= cfg->num_experts,
@@ -1443,7 +1447,7 @@ int mlxr_cu_moe_ep_experts_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_
   int* status = at<int>(ws, L.status);
   const uint8_t* b = c->local;
   launch_pdl(ep_wait_flags_kernel, 1, 64, 0, st, reinterpret_cast<const uint32_t*>(b + c->bl.flag_disp), c->world,
-             epoch, 5 * kWaitLimitNs, status);
+             epoch, reinterpret_cast<const uint32_t*>(b + c->bl.epoch), 5 * kWaitLimitNs, status);
   MLXR_LAUNCH_CHECK("ep_wait_flags_kernel(dispatch)");
   const int32_t* meta = reinterpret_cast<const int32_t*>(b + c->bl.recv_meta);
   const int32_t* counts = reinterpret_cast<const int32_t*>(b + c->bl.counts);
@@ -1466,7 +1470,7 @@ int mlxr_cu_moe_ep_experts_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_
 int mlxr_cu_moe_ep_combine_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_weights* weights, void* comm,
                                const void* x, int64_t num_tokens, const int32_t* pair_pos, const float* shared_gate,
                                void* out, uint32_t epoch, void* workspace, size_t workspace_bytes, void* stream) {
-  MLXR_CHECK_ARG(epoch >= 1 && epoch < EP_FLAG_POISON, "moe_ep: epoch=%u must be in [1, 2^31)", epoch);
+  MLXR_CHECK_ARG(epoch < EP_FLAG_POISON, "moe_ep: epoch=%u must be 0 (device counter) or in [1, 2^31)", epoch);
   if (int rc = validate(cfg, num_tokens)) return rc;
   if (int rc = ep_comm_check(comm, cfg)) return rc;
   EpComm* c = static_cast<EpComm*>(comm);
@@ -1485,7 +1489,8 @@ int mlxr_cu_moe_ep_combine_p2p(const mlxr_cu_moe_config* cfg, const mlxr_cu_moe_
     ysh = at<uint16_t>(ws, L.ysh);
   }
   launch_pdl(ep_wait_flags_kernel, 1, 64, 0, st, reinterpret_cast<const uint32_t*>(c->local + c->bl.flag_back),
-             c->world, epoch, 5 * kWaitLimitNs, at<int>(ws, L.status));
+             c->world, epoch, reinterpret_cast<const uint32_t*>(c->local + c->bl.epoch), 5 * kWaitLimitNs,
+             at<int>(ws, L.status));
   MLXR_LAUNCH_CHECK("ep_wait_flags_kernel(combine)");
   if (num_tokens == 0) return MLXR_CU_OK;
   MLXR_CHECK_ARG(pair_pos && out && aligned16(out), "moe_ep_combine_p2p: NULL or misaligned argument");

@@ -857,6 +857,10 @@ __global__ void __launch_bounds__(256) permute_gather_kernel(const int32_t* __re
     if (c > n_rows && blockIdx.x == 0 && threadIdx.x == 0) atomicCAS(status, 0, (int)kDevBadIndex);
     n = min(n_rows, c);
   }
+  // An output larger than half the L2 goes out with streaming (evict-first)
+  // stores: it cannot stay in L2 for the GEMM anyway, and normal stores
+  // would evict the x rows that the next K - 1 copies of each token read.
+  const bool stream_out = n_rows * (int64_t)D * 2 > (int64_t)(64ll << 20);
   for (int64_t pos = (int64_t)blockIdx.x * 8 + warp; pos < n; pos += (int64_t)gridDim.x * 8) {
     int64_t src_row = pos;
     if (sorted_rows) {
@@ -878,7 +882,8 @@ __global__ void __launch_bounds__(256) permute_gather_kernel(const int32_t* __re
         b.w = __byte_perm(a.y, a.w, 0x7632);
         a = b;
       }
-      dst[v] = a;
+      if (stream_out) __stcs(dst + v, a);
+      else dst[v] = a;
     };
     // Eight 16-byte loads of the row in flight per lane before any store
     // (one load at a time left the copy latency-bound at half the HBM rate).
@@ -1243,7 +1248,7 @@ __global__ void shared_tiles_kernel(GemmTile* __restrict__ tiles, int32_t* __res
 // me's buffer (back block r) and then a flag. Readers wait on the flags
 // (bounded) and read the data through L2.
 struct EpBufLayout {
-  int64_t recv_x, recv_meta, back, counts, rows, flag_disp, flag_back, done, total;
+  int64_t recv_x, recv_meta, back, counts, rows, flag_disp, flag_back, done, epoch, total;
 };
 
 __host__ __device__ inline EpBufLayout ep_buf_layout(int world, int64_t cap, int D, int K) {
@@ -1262,6 +1267,7 @@ __host__ __device__ inline EpBufLayout ep_buf_layout(int world, int64_t cap, int
   b.flag_disp = take((int64_t)world * 4);
   b.flag_back = take((int64_t)world * 4);
   b.done = take(16);
+  b.epoch = take(16);  // the device-resident step counter (steps called with epoch 0)
   b.total = o;
   return b;
 }
@@ -1304,6 +1310,7 @@ __global__ void __launch_bounds__(256) ep_send_kernel(EpPeers peers, EpBufLayout
                                                       int* __restrict__ done, int* status) {
   pdl_wait();
   pdl_launch_dependents();
+  if (epoch == 0) epoch = *reinterpret_cast<const volatile uint32_t*>(peers.base[me] + bl.epoch);
   __shared__ int s_off[EP_MAX_WORLD + 1];
   __shared__ int s_last;
   for (int i = threadIdx.x; i <= world; i += blockDim.x) s_off[i] = offsets[i];
@@ -1345,14 +1352,32 @@ __global__ void __launch_bounds__(256) ep_send_kernel(EpPeers peers, EpBufLayout
   if (threadIdx.x == 0) *done = 0;
 }
 
+// Steps called with epoch 0 use the device-resident counter in this rank's
+// exchange buffer: the dispatch advances it first (one thread), and every
+// kernel of the step reads it. Every rank advances its own counter once per
+// step, so the counters agree as the host epochs would, and a captured CUDA
+// graph of the step replays with a new epoch each time.
+__global__ void ep_bump_epoch_kernel(uint8_t* local, EpBufLayout bl, int* status) {
+  pdl_wait();
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    uint32_t* slot = reinterpret_cast<uint32_t*>(local + bl.epoch);
+    const uint32_t v = *slot + 1u;
+    if (v >= EP_FLAG_POISON) atomicCAS(status, 0, (int)kDevBadIndex);  // 2^31 steps: recreate the comm
+    else *slot = v;
+  }
+}
+
 // One CTA: wait until every rank has published `epoch` in flags[0..world)
 // (bounded; on expiry the status records a timeout and the data is not used).
 // A poisoned flag of this epoch ends the wait for that rank with
 // kDevPeerFailed in the status word.
 __global__ void ep_wait_flags_kernel(const uint32_t* __restrict__ flags, int world, uint32_t epoch,
-                                     unsigned long long limit_ns, int* status) {
+                                     const uint32_t* __restrict__ epoch_dev, unsigned long long limit_ns,
+                                     int* status) {
   pdl_wait();
   pdl_launch_dependents();
+  if (epoch == 0) epoch = *reinterpret_cast<const volatile uint32_t*>(epoch_dev);
   if (threadIdx.x < world) {
     const unsigned long long t0 = global_ns();
     for (uint32_t it = 0;; ++it) {
@@ -1413,6 +1438,7 @@ __global__ void __launch_bounds__(256) ep_reduce_send_kernel(EpPeers peers, EpBu
                                                              int* status) {
   pdl_wait();
   pdl_launch_dependents();
+  if (epoch == 0) epoch = *reinterpret_cast<const volatile uint32_t*>(peers.base[me] + bl.epoch);
   __shared__ int rws[RT_MAXK];
   __shared__ float wk[RT_MAXK];
   __shared__ int nk;

@@ -152,9 +152,17 @@ class ExpertParallelMoeBlock:
         return int(n.value)
 
     def workspace(self, T: int, max_recv_pairs: int, max_recv_rows: int, device) -> torch.Tensor:
+        """The step's workspace, grown when a step needs more. A buffer grown
+        between the steps of one forward (the received counts are known only
+        after the dispatch) starts as a copy of the old one (stream-ordered):
+        the experts and combine steps read the status word the dispatch
+        cleared."""
         need = self.workspace_bytes(T, max_recv_pairs, max_recv_rows)
         if self._ws is None or self._ws.numel() < need:
-            self._ws = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
+            new = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
+            if self._ws is not None:
+                new[: self._ws.numel()].copy_(self._ws)
+            self._ws = new
         return self._ws
 
     # -- the three device steps --------------------------------------------
@@ -220,11 +228,14 @@ class ExpertParallelMoeBlock:
         return self.combine(x, back, plan, ws)
 
     def forward_p2p(self, x: torch.Tensor, comm: "PeerComm", expected_rows: int | None = None,
-                     out: torch.Tensor | None = None, events=None) -> torch.Tensor:
+                     out: torch.Tensor | None = None, events=None, device_epoch: bool = False) -> torch.Tensor:
         """One step over peer memory; every rank calls it together (same order of
         steps on every rank, each GPU one rank). events: optional four CUDA
         events recorded on the stream before dispatch, after dispatch, after
-        the experts step and after combine (phase timing)."""
+        the experts step and after combine (phase timing). device_epoch: the
+        step's epoch comes from the comm's device-resident counter (advanced
+        by the dispatch), so the step can be captured in a CUDA graph and
+        replayed; a comm uses one kind of epoch for its whole life."""
         x = x.reshape(-1, self.cfg.hidden_size).contiguous()
         T, K = x.shape[0], self.cfg.num_experts_per_tok
         if expected_rows is None:
@@ -235,10 +246,18 @@ class ExpertParallelMoeBlock:
         if self._ws is None or self._ws.numel() < n.value:
             self._ws = torch.empty(max(int(n.value), 256), dtype=torch.uint8, device=x.device)
         ws = self._ws
-        comm.epoch += 1
-        if comm.epoch >= 1 << 31:  # the flag's top bit marks a failed step
-            raise _lib.MlxrError(_lib.ERR_INVALID_ARGUMENT, "peer communicator ran out of epochs; recreate it")
-        ep = comm.epoch
+        mode = "device" if device_epoch else "host"
+        if getattr(comm, "epoch_mode", None) not in (None, mode):
+            raise _lib.MlxrError(_lib.ERR_INVALID_ARGUMENT,
+                                 f"peer communicator uses {comm.epoch_mode} epochs; a comm keeps one kind")
+        comm.epoch_mode = mode
+        if device_epoch:
+            ep = 0
+        else:
+            comm.epoch += 1
+            if comm.epoch >= 1 << 31:  # the flag's top bit marks a failed step
+                raise _lib.MlxrError(_lib.ERR_INVALID_ARGUMENT, "peer communicator ran out of epochs; recreate it")
+            ep = comm.epoch
         st = torch.cuda.current_stream(x.device).cuda_stream
         pair_pos = torch.empty(max(T * K, 1), dtype=torch.int32, device=x.device)
         sg = torch.empty(max(T, 1), dtype=torch.float32, device=x.device) if self.shared_expert is not None else None

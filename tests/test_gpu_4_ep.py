@@ -232,7 +232,7 @@ def _p2p_worker(rank, world, port, result_path):
         for step, T in enumerate([48 + 16 * rank, 96 - 40 * rank, 0 if rank == 1 else 33]):
             x = (synth.make_input(T, cfg.hidden_size, stream_offset=100 + 4 * rank + step, device="cuda") if T
                  else torch.empty((0, cfg.hidden_size), dtype=torch.bfloat16, device="cuda"))
-            out = blk.forward_p2p(x, comm)
+            out = blk.forward_p2p(x, comm, device_epoch=zipf)  # c3: the device-resident epoch
             torch.cuda.synchronize()
             blk.status()
             if T:
@@ -257,7 +257,8 @@ def _p2p_worker(rank, world, port, result_path):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_ep_p2p_two_gpus(tmp_path):
     """Exchange inside the kernels over peer memory (CUDA IPC), two GPUs:
-    matches the one-device block, ragged and empty batches included."""
+    matches the one-device block, ragged and empty batches included; host
+    epochs for C4, the device-resident epoch for C3."""
     import torch.multiprocessing as mp
 
     res = tmp_path / "p2p.txt"
@@ -384,5 +385,48 @@ def test_ep_p2p_one_rank_step_timeout_and_poisoned_flag():
         blk.status()
         assert_close_bf16(bf16_np(out), bf16_np(want), ATOL, RTOL, "one-rank p2p step after the failures")
     finally:
+        torch.cuda.synchronize()
+        comm.close()
+
+
+def test_ep_p2p_one_rank_device_epoch_and_graph():
+    """Steps with the device-resident epoch (epoch 0): steps launched
+    directly, then the step captured in a CUDA graph and replayed on new
+    inputs (each replay advances the counter in the comm's buffer), all equal
+    to the one-device block; a comm that used device epochs refuses host
+    epochs."""
+    from mlxr_moe import _lib
+
+    full = block_for("c2")
+    cfg = full.cfg
+    blk = ExpertParallelMoeBlock.from_block(full, 0, 1)
+    comm = _OneRankComm(64, cfg.hidden_size, cfg.num_experts_per_tok)
+    g = None
+    try:
+        xs = [synth.make_input(40, cfg.hidden_size, stream_offset=90 + i) for i in range(4)]
+        for x in xs[:2]:
+            out = blk.forward_p2p(x, comm, device_epoch=True)
+            torch.cuda.synchronize()
+            blk.status()
+            assert_close_bf16(bf16_np(out), bf16_np(full.forward(x)), ATOL, RTOL, "device-epoch step")
+        st = torch.cuda.Stream()
+        xin, out = xs[0].clone(), torch.empty_like(xs[0])
+        with torch.cuda.stream(st):
+            blk.forward_p2p(xin, comm, out=out, device_epoch=True)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            blk.forward_p2p(xin, comm, out=out, device_epoch=True)
+        for x in xs[2:]:
+            with torch.cuda.stream(st):
+                xin.copy_(x)
+                g.replay()
+            torch.cuda.synchronize()
+            blk.status()
+            assert_close_bf16(bf16_np(out), bf16_np(full.forward(x)), ATOL, RTOL, "replayed device-epoch step")
+        with pytest.raises(_lib.MlxrError):
+            blk.forward_p2p(xs[0], comm)
+    finally:
+        del g
         torch.cuda.synchronize()
         comm.close()
