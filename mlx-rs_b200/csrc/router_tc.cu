@@ -245,7 +245,7 @@ struct RouterTcArgs {
 };
 
 // SPLIT: CTA (x, y, z) sums k-blocks [z kps, (z + 1) kps) and writes its 7
-// digit sums per (token, expert) to part (route_partials_kernel finishes);
+// digit sums per (token, expert) to part (logits_from_partials_kernel finishes);
 // otherwise the epilogue forms the logits.
 template <int BN, bool SPLIT>
 __global__ void __launch_bounds__(RG_THREADS, 1)

@@ -13,7 +13,7 @@ namespace mlxr {
 // Batches up to this size use 16-token tiles (else 64). Whenever the tiles
 // alone would fill less than about one wave of CTAs the launch takes the
 // split-K form: the k range cut over CTAs, partial digit sums finished by
-// route_partials_kernel.
+// logits_from_partials_kernel.
 constexpr int64_t kRouterTcSplitMaxT = 256;
 
 struct RouterTcLayout {
@@ -31,7 +31,7 @@ bool router_tc_supported(int D);
 // logits lg [T, E] bf16 = bf16(fp32(exact x[t] . wg[e]) + bias[e]) (bias may
 // be NULL). In the split-K form (router_tc_layout(...).split) it writes the
 // partial digit sums instead (layout.part, [splits][7][T][E] int32) and
-// route_partials_kernel forms the logits.
+// logits_from_partials_kernel forms the logits.
 struct RouterTcProblem {
   const uint16_t* x;   // [T, D] bf16, 16-byte aligned
   int64_t T;
