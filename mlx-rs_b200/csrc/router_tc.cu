@@ -135,15 +135,41 @@ __global__ void __launch_bounds__(RD_WARPS * 32) router_digits_kernel(DigitRows 
   const int be_max = (int)(mb >> 7);
   const int u = mb == 0 ? 0 : (be_max ? be_max : 1) - 127 - 29;
   int lost = 0;
+  // Fast form: X = trunc(x 2^-u) as one fp32 multiply (exact: x 2^-u is an
+  // integer of at most 30 bits, or 0, for every element that loses no bits)
+  // and a truncating conversion, when 2^-u is a normal fp32 (u >= -127).
+  // An element can lose bits only if its |bits| lie in (0, 128 (u + 134))
+  // (exponent field below u + 134, or subnormal); a chunk holding one takes
+  // the integer form, which also counts the truncated elements.
+  const bool fast = u >= -127;
+  const float scale = fast ? __uint_as_float((uint32_t)(127 - u) << 23) : 0.0f;
+  const int thr = u + 134;
+  const uint32_t lim = thr <= 0 ? 0u : (uint32_t)(thr * 128);  // <= 232 * 128 < 2^16
+  const uint32_t lim2 = (lim << 16) | lim;
   for (int c = threadIdx.x; c < npch; c += RD_WARPS * 32) {
     uint32_t o[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};  // digit words of the 8 elements
     if (c < nch && !nonfin) {
       const uint4 v = __ldg(row + c);
       const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+      uint32_t cand = fast ? 0u : 1u;
 #pragma unroll
-      for (int h = 0; h < 8; ++h) {
-        const uint32_t b = (wd[h >> 1] >> ((h & 1) * 16)) & 0xffffu;
-        o[h] = ((uint32_t)bf16_to_fixed(b, u, lost) + 0x808080u) ^ 0x808080u;
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t m = wd[q] & 0x7fff7fffu;
+        cand |= __vcmpltu2(m, lim2) & __vcmpne2(m, 0u);
+      }
+      if (cand == 0u) {
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+          const uint32_t fb = (h & 1) ? (wd[h >> 1] & 0xffff0000u) : (wd[h >> 1] << 16);
+          const int X = __float2int_rz(__uint_as_float(fb) * scale);
+          o[h] = ((uint32_t)X + 0x808080u) ^ 0x808080u;
+        }
+      } else {
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+          const uint32_t b = (wd[h >> 1] >> ((h & 1) * 16)) & 0xffffu;
+          o[h] = ((uint32_t)bf16_to_fixed(b, u, lost) + 0x808080u) ^ 0x808080u;
+        }
       }
     }
     // plane k takes byte 3 - k of each element's word
