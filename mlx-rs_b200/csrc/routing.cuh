@@ -6,10 +6,10 @@
 // equal probabilities undefined (crates/mlxr/src/ops/sort.rs:235-237); this
 // implementation fixes the routing contract so that CPU and GPU agree bit for
 // bit:
-//   * logit(t, e): fp32 fma chains, one per lane j of a warp, over the 16-byte
-//     chunks j, j+32, ... of the D axis (8 elements each, ascending), then an
-//     xor butterfly over the 32 lanes (strides 16, 8, 4, 2, 1); + bias[e];
-//     rounded to bf16.
+//   * logit(t, e) = bf16(fp32(S) + bias[e]), S the exact dot product of the
+//     bf16 rows x[t] and gate[e] rounded once to fp32 (exact_dot.cuh): the
+//     same value in whatever order a kernel sums, so the fp64 kernels below
+//     and the int8 tensor-core kernels (router_tc.cu) all produce it.
 //   * softmax: exact max, exp_route(l - max), lane sums over e = j, j+32, ...
 //     then the same butterfly, IEEE division, bf16 probabilities.
 //   * top-K by (probability desc, expert asc); denominator summed in rank
@@ -218,9 +218,11 @@ __device__ inline void shared_gate_warp(const uint16_t* __restrict__ xr, int D, 
 
 // The whole router for TPB tokens in one CTA of 16 warps. Warp w computes
 // the logits of expert groups w, w+16, ... (8 experts each) for the TPB
-// tokens into shared memory, in the contract's fixed FMA order: lane j folds
-// the 16-byte chunks j, j+32, ... of D (8 elements each, ascending), then an
-// xor butterfly; + bias; rounded to bf16. Warp t < TPB then routes token t.
+// tokens into shared memory: lane j sums the exact products of the 16-byte
+// chunks j, j+32, ... of D in fp64, an xor butterfly adds the lanes, and the
+// logit is taken from the error interval of that sum (or the exact warp sum
+// when the interval straddles a rounding boundary). Warp t < TPB then
+// routes token t.
 constexpr int RT_THREADS = 512;
 
 template <int TPB>
@@ -327,8 +329,8 @@ __global__ void __launch_bounds__(RT_THREADS) router_fused_kernel(
 
 // Small batches: the logits of TPB tokens are spread over many CTAs (warp w
 // of CTA (gx, gy) computes the EPW experts of group RS_WARPS*gx + w for
-// tokens gy*TPB ...), in the same per-logit FMA order as
-// router_fused_kernel, into the bf16 logits buffer lg [T, E]. Each lane
+// tokens gy*TPB ...), with router_fused_kernel's fp64 sums and interval
+// test, into the bf16 logits buffer lg [T, E]. Each lane
 // issues the loads of UNR chunk steps before using them, so a warp keeps
 // (TPB + EPW) * UNR 16-byte loads in flight: with few tokens the kernel is
 // bound by memory latency, not arithmetic. The CTA that finishes the last
