@@ -183,28 +183,41 @@ __device__ __forceinline__ float rn32_i128(__int128 v, int lsb) {
   return rn32_limbs(limbs, 2, neg, lsb);
 }
 
-// The bf16 logit from the tensor-core router's digit sums: A[g] (g < 7) =
-// sum of the plane products of weight 2^(8 (6 - g)), so the exact integer
-// dot product is V = sum_g A[g] 2^(8 (6 - g)) and the sum is V 2^(u_x + u_w)
-// when no element was truncated (xi, wi = {u, truncated count}); otherwise
-// the sum lies within (n_x + n_w) 2^(30 + u_x + u_w) of it. *decided is
-// false when that interval straddles a bf16 logit boundary or a row holds
-// inf or NaN (count -1): the caller then computes the exact sum.
-__device__ __forceinline__ uint16_t logit_from_digit_sums(const int32_t (&A)[7], int2 xi, int2 wi, float bias,
+// The tensor-core router's digit sums: the plane products of digits k
+// (token) and l (router row) are added per weight 2^(8 (6 - k - l)) into
+// NS sums A[g], g = k + l < NS. NS = 7 keeps all 16 products; NS = 5 (the
+// split-K form) drops the three with k + l = 5, 6, which add up to at most
+// D (2 * 2^14 * 2^8 + 2^14) units of the last digit pair (every balanced
+// digit is at most 128 in magnitude), and that bound joins the interval test.
+constexpr int kRouterSums = 5;  // the split-K form's sums per logit
+
+// Both ends of [V - B, V + B] give the logit lb (not inlined: it is called
+// from unrolled loops).
+static __device__ __noinline__ bool digit_interval_same(__int128 V, __int128 B, int lsb, float bias, uint32_t lb) {
+  return logit_bits(rn32_i128(V - B, lsb), bias) == lb && logit_bits(rn32_i128(V + B, lsb), bias) == lb;
+}
+
+// The bf16 logit from the digit sums: V = sum_g A[g] 2^(8 (6 - g)), and the
+// sum lies within B 2^(u_x + u_w) of V 2^(u_x + u_w), B = (n_x + n_w) 2^30
+// (a truncated element adds at most 2^30 units; xi, wi = {u, truncated
+// count}) plus D (2^23 + 2^14) when NS = 5. *decided is false when that
+// interval straddles a bf16 logit boundary or a row holds inf or NaN (count
+// -1): the caller then computes the exact sum.
+template <int NS>
+__device__ __forceinline__ uint16_t logit_from_digit_sums(const int32_t (&A)[NS], int2 xi, int2 wi, int D, float bias,
                                                           bool* decided) {
+  static_assert(NS == 5 || NS == 7, "5 or 7 digit sums");
   *decided = false;
   if (xi.y < 0 || wi.y < 0) return 0;
   const int64_t hi = (int64_t)A[0] * (1ll << 24) + (int64_t)A[1] * (1ll << 16) + (int64_t)A[2] * (1ll << 8) + A[3];
-  const int64_t lo = (int64_t)A[4] * (1ll << 16) + (int64_t)A[5] * (1ll << 8) + A[6];
+  int64_t lo = (int64_t)A[4] * (1ll << 16);
+  if constexpr (NS == 7) lo += (int64_t)A[5] * (1ll << 8) + A[6];
   const __int128 V = ((__int128)hi << 24) + (__int128)lo;
   const int lsb = xi.x + wi.x;
   const uint16_t lb = logit_bits(rn32_i128(V, lsb), bias);
-  const int nt = xi.y + wi.y;
-  if (nt > 0) {
-    const __int128 B = (__int128)nt << 30;
-    if (logit_bits(rn32_i128(V - B, lsb), bias) != lb || logit_bits(rn32_i128(V + B, lsb), bias) != lb) return lb;
-  }
-  *decided = true;
+  __int128 B = (__int128)(xi.y + wi.y) * (1ll << 30);
+  if constexpr (NS == 5) B += (__int128)D * ((1ll << 23) + (1ll << 14));
+  *decided = B == 0 || digit_interval_same(V, B, lsb, bias, lb);
   return lb;
 }
 

@@ -20,7 +20,10 @@
 //    (n_x + n_w) 2^(30 + u_x + u_w) of that (n = truncated elements of each
 //    row), and the logit is written when both ends of the interval give the
 //    same bf16 value; otherwise, and for rows holding inf or NaN, the warp
-//    computes the exact sum of the original rows (dot_rn32_warp).
+//    computes the exact sum of the original rows (dot_rn32_warp). The
+//    split-K form (small and mid batches) computes only the 13 products with
+//    k + l <= 4 into 5 sums and bounds the other three (exact_dot.cuh); its
+//    finish applies the wider interval test once per logit.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -41,7 +44,7 @@ constexpr int RG_A_PLANE = RG_BM * RG_BK;        // 8 KB
 constexpr int RG_THREADS = 224;                   // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue, warp 6 waiter
 constexpr int RD_WARPS = 8;
 // Token-tile width BN (MMA N): 64 for large batches (7 accumulators x 64 =
-// 448 of the 512 tensor-memory columns), 16 for the split-K form.
+// 448 of the 512 tensor-memory columns), 16 for the small-batch split-K form.
 template <int BN>
 struct RgCfg {
   static constexpr int B_PLANE = BN * RG_BK;
@@ -263,7 +266,7 @@ struct RouterTcArgs {
   const int2* winfo;
   const float* bias;
   uint16_t* lg;
-  int32_t* part;  // split-K form: [splits][7][T][E] digit sums of each k-slice
+  int32_t* part;  // split-K form: [splits][kRouterSums][T][E] digit sums of each k-slice
   int64_t T;
   int E, D, nk, kps;  // k-blocks in all, per split
   int rows_pad_x, rows_pad_w;
@@ -278,6 +281,9 @@ __global__ void __launch_bounds__(RG_THREADS, 1)
     router_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                      const RouterTcArgs a) {
   using G = RgCfg<BN>;
+  // digit sums per logit: all 16 products directly; 13 in the split-K form,
+  // whose finish (logits_from_partials_kernel) takes the wider interval test
+  constexpr int NSUMS = SPLIT ? kRouterSums : 7;
   constexpr int RG_BN = BN;
   constexpr int RG_B_PLANE = G::B_PLANE;
   constexpr int RG_STAGE = G::STAGE;
@@ -386,6 +392,7 @@ __global__ void __launch_bounds__(RG_THREADS, 1)
 #pragma unroll
           for (int l = 0; l < 4; ++l) {
             const int sg = k + l;
+            if (sg >= NSUMS) continue;  // split-K form: the three lowest-weight products are bounded, not computed
             const int first_k = sg > 3 ? sg - 3 : 0;
             const uint32_t accum = (kb > 0 || k != first_k) ? 1u : 0u;
             umma_i8_ss_k64(tmem_base + (uint32_t)(sg * RG_BN), umma_desc_sw64(st + l * RG_A_PLANE), bdesc, idesc,
@@ -419,19 +426,19 @@ __global__ void __launch_bounds__(RG_THREADS, 1)
       for (int j = 0; j < 8; ++j) {  // unrolled: r stays in registers
         const int64_t t = n0 + c8 * 8 + j;
         const bool valid = e_ok && t < a.T;
-        int32_t A[7];
+        int32_t A[NSUMS];
 #pragma unroll
-        for (int g = 0; g < 7; ++g) A[g] = (int32_t)r[g * 8 + j];
+        for (int g = 0; g < NSUMS; ++g) A[g] = (int32_t)r[g * 8 + j];
         if constexpr (SPLIT) {
           if (valid) {
-            int32_t* pp = a.part + (((int64_t)blockIdx.z * 7) * a.T + t) * a.E + e;
+            int32_t* pp = a.part + (((int64_t)blockIdx.z * kRouterSums) * a.T + t) * a.E + e;
 #pragma unroll
-            for (int g = 0; g < 7; ++g) pp[(int64_t)g * a.T * a.E] = A[g];
+            for (int g = 0; g < NSUMS; ++g) pp[(int64_t)g * a.T * a.E] = A[g];
           }
         } else {
           const int2 xi = a.xinfo[t < a.T ? t : a.T - 1];
           bool decided;
-          const uint16_t lb = logit_from_digit_sums(A, xi, wi, b, &decided);
+          const uint16_t lb = logit_from_digit_sums<NSUMS>(A, xi, wi, a.D, b, &decided);
           if (valid && decided) a.lg[t * a.E + e] = lb;
           und |= (uint32_t)(valid && !decided) << j;
         }
@@ -491,7 +498,7 @@ RouterTcLayout router_tc_layout(int64_t T, int E, int D, size_t budget) {
     L.wdig = take((size_t)4 * L.rows_pad_w * L.Dp);
     L.xinfo = take((size_t)L.rows_pad_x * sizeof(int2));
     L.winfo = take((size_t)L.rows_pad_w * sizeof(int2));
-    L.part = L.split ? take((size_t)L.splits * 7 * T * E * sizeof(int32_t)) : 0;
+    L.part = L.split ? take((size_t)L.splits * kRouterSums * T * E * sizeof(int32_t)) : 0;
     L.total = o;
     if (L.total <= budget || want <= 1) break;
   }

@@ -30,7 +30,7 @@ bool router_tc_supported(int D);
 
 // logits lg [T, E] bf16 = bf16(fp32(exact x[t] . wg[e]) + bias[e]) (bias may
 // be NULL). In the split-K form (router_tc_layout(...).split) it writes the
-// partial digit sums instead (layout.part, [splits][7][T][E] int32) and
+// partial digit sums instead (layout.part, [splits][5][T][E] int32) and
 // logits_from_partials_kernel forms the logits.
 struct RouterTcProblem {
   const uint16_t* x;   // [T, D] bf16, 16-byte aligned

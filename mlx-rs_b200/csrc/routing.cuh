@@ -529,7 +529,7 @@ __global__ void __launch_bounds__(RT_ROUTE_WARPS * 32) route_rows_kernel(
 }
 
 // The tensor-core router's split-K form (router_tc.cu): part[s][g][t][e]
-// (s < splits, g < 7) are the digit sums of k-slice s. One thread per
+// (s < splits, g < kRouterSums) are the digit sums of k-slice s. One thread per
 // (token, expert), experts fastest: the slices are added (exact integer
 // sums) and the logit formed as router_tc_kernel's epilogue does; logits the
 // interval test leaves open are computed as exact sums by the whole warp
@@ -548,14 +548,14 @@ __global__ void __launch_bounds__(256) logits_from_partials_kernel(
   const int64_t ic = valid ? i : n - 1;
   const int64_t t = ic / E;
   const int e = (int)(ic - t * E);
-  const int64_t gstride = n, sstride = 7 * n;
-  int32_t A[7] = {0, 0, 0, 0, 0, 0, 0};
+  const int64_t gstride = n, sstride = kRouterSums * n;
+  int32_t A[kRouterSums] = {0, 0, 0, 0, 0};
   for (int sp = 0; sp < splits; ++sp)
 #pragma unroll
-    for (int g = 0; g < 7; ++g) A[g] += __ldg(part + sp * sstride + g * gstride + ic);
+    for (int g = 0; g < kRouterSums; ++g) A[g] += __ldg(part + sp * sstride + g * gstride + ic);
   const float b = bias ? bias[e] : 0.0f;
   bool decided;
-  uint16_t lb = logit_from_digit_sums(A, xinfo[t], winfo[e], b, &decided);
+  uint16_t lb = logit_from_digit_sums<kRouterSums>(A, xinfo[t], winfo[e], D, b, &decided);
   uint32_t need = __ballot_sync(0xffffffffu, valid && !decided);
   while (need) {
     const int src = __ffs(need) - 1;
