@@ -253,4 +253,45 @@ __device__ __forceinline__ double f64_sum_err(int depth, int D, uint32_t mx, uin
   return __dmul_ru(__dmul_ru(f, bf16_to_f64(mx)), bf16_to_f64(mw));
 }
 
+// The bf16 logit of x . w + bias by the whole warp (every lane calls it with
+// the same arguments and gets the result), for logits an interval test left
+// open. First the fp64 sum of the exact products (one rounding per element,
+// lane j taking the 16-byte chunks j, j + 32, ..., then an xor butterfly:
+// depth 8 ceil(D / 256) + 5) with the bound of f64_sum_err; only when that
+// interval also straddles a rounding boundary, or a row holds inf or NaN,
+// the exact sum (dot_rn32_warp, whose limb accumulators cost ~30 us per
+// call at D = 4096 against ~1 us for this pass). D % 8 == 0, both rows
+// 16-byte aligned.
+static __device__ __noinline__ uint16_t logit_warp(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
+                                                   int D, float bias, int lane) {
+  const int nch = D / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x);
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  double acc = 0.0;
+  uint32_t mx = 0, mw = 0;
+  for (int c = lane; c < nch; c += 32) {
+    const uint4 xv = __ldg(xr + c), wv = __ldg(wr + c);
+    const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t a = h ? (xa[q] >> 16) : (xa[q] & 0xffffu);
+        const uint32_t b = h ? (wa[q] >> 16) : (wa[q] & 0xffffu);
+        mx = max(mx, a & 0x7fffu);
+        mw = max(mw, b & 0x7fffu);
+        acc = __fma_rn(bf16_to_f64(a), bf16_to_f64(b), acc);
+      }
+  }
+  mx = __reduce_max_sync(0xffffffffu, mx);
+  mw = __reduce_max_sync(0xffffffffu, mw);
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, s));
+  uint16_t lb;
+  if (mx < 0x7f80u && mw < 0x7f80u &&
+      logit_from_f64(acc, f64_sum_err(8 * ((nch + 31) / 32) + 5, D, mx, mw), bias, &lb))
+    return lb;
+  return logit_bits(dot_rn32_warp(x, w, D, lane), bias);
+}
+
 }  // namespace mlxr

@@ -20,7 +20,8 @@
 //    (n_x + n_w) 2^(30 + u_x + u_w) of that (n = truncated elements of each
 //    row), and the logit is written when both ends of the interval give the
 //    same bf16 value; otherwise, and for rows holding inf or NaN, the warp
-//    computes the exact sum of the original rows (dot_rn32_warp). The
+//    computes the logit from the original rows (logit_warp: an fp64 sum with
+//    its error bound, then the exact sum if that is still open). The
 //    split-K form (small and mid batches) computes only the 13 products with
 //    k + l <= 4 into 5 sums and bounds the other three (exact_dot.cuh); its
 //    finish applies the wider interval test once per logit.
@@ -443,7 +444,7 @@ __global__ void __launch_bounds__(RG_THREADS, 1)
           und |= (uint32_t)(valid && !decided) << j;
         }
       }
-      // Rare: logits the interval test left open, as exact sums by the whole warp.
+      // Rare: logits the interval test left open, by the whole warp (logit_warp).
       uint32_t pend = __reduce_or_sync(0xffffffffu, und);
 #pragma unroll 1
       while (pend) {
@@ -455,8 +456,9 @@ __global__ void __launch_bounds__(RG_THREADS, 1)
           const int src = __ffs(need) - 1;
           need &= need - 1;
           const int es = __shfl_sync(0xffffffffu, ec, src);
-          const float v = dot_rn32_warp(a.x + t * (int64_t)a.D, a.wg + (int64_t)es * a.D, a.D, lane);
-          if (lane == src) a.lg[t * a.E + e] = logit_bits(v, b);
+          const float bs = __shfl_sync(0xffffffffu, b, src);
+          const uint16_t r = logit_warp(a.x + t * (int64_t)a.D, a.wg + (int64_t)es * a.D, a.D, bs, lane);
+          if (lane == src) a.lg[t * a.E + e] = r;
         }
       }
     }

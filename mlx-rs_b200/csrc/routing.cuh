@@ -532,7 +532,7 @@ __global__ void __launch_bounds__(RT_ROUTE_WARPS * 32) route_rows_kernel(
 // (s < splits, g < kRouterSums) are the digit sums of k-slice s. One thread per
 // (token, expert), experts fastest: the slices are added (exact integer
 // sums) and the logit formed as router_tc_kernel's epilogue does; logits the
-// interval test leaves open are computed as exact sums by the whole warp
+// interval test leaves open are computed by the whole warp (logit_warp)
 // (each undecided lane's token and expert in turn). route_rows_kernel then
 // routes the tokens.
 __global__ void __launch_bounds__(256) logits_from_partials_kernel(
@@ -562,8 +562,9 @@ __global__ void __launch_bounds__(256) logits_from_partials_kernel(
     need &= need - 1;
     const int64_t ts = __shfl_sync(0xffffffffu, t, src);
     const int es = __shfl_sync(0xffffffffu, e, src);
-    const float v = dot_rn32_warp(x + ts * D, wg + (int64_t)es * D, D, lane);
-    if (lane == src) lb = logit_bits(v, b);
+    const float bs = __shfl_sync(0xffffffffu, b, src);
+    const uint16_t r = logit_warp(x + ts * D, wg + (int64_t)es * D, D, bs, lane);
+    if (lane == src) lb = r;
   }
   if (valid) lg[i] = lb;
 }

@@ -33,6 +33,7 @@ def _router_block(D, E, K, zipf=False, seed=0):
         (2048, 128, 8, 4096, True),   # C3 (Zipf-biased logits)
         (2048, 512, 10, 2048, False), # C4 router (subset of the 16384 tokens)
         (4096, 128, 8, 256, True),    # C5 decode batch
+        (4096, 128, 8, 256, False),   # C5 decode sizes without a bias (small logits reach the fallback)
         (2048, 128, 8, 5, False),     # split router, 2 tokens per block
         (2048, 128, 8, 20, True),     # split router, 4 tokens per block, ragged last block
         (2176, 72, 6, 300, False),    # tiled router: partial token tile, partial expert tile, partial D block
