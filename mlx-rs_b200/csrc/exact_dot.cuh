@@ -253,44 +253,103 @@ __device__ __forceinline__ double f64_sum_err(int depth, int D, uint32_t mx, uin
   return __dmul_ru(__dmul_ru(f, bf16_to_f64(mx)), bf16_to_f64(mw));
 }
 
+// Class of the product a * b of two bf16 values (bits): 0 when both are
+// finite, else bit 0 for NaN (a NaN operand, or inf times 0), bit 1 for
+// +inf, bit 2 for -inf. A sum holding any non-finite product is NaN when a
+// NaN product or infinite products of both signs occur, else the infinity
+// of their sign (class_sum).
+__device__ __forceinline__ uint32_t product_class(uint32_t a, uint32_t b) {
+  const bool fa = (a & 0x7f80u) == 0x7f80u, fb = (b & 0x7f80u) == 0x7f80u;
+  if (!(fa || fb)) return 0u;
+  const bool na = fa && (a & 0x7fu), nb = fb && (b & 0x7fu);
+  const bool za = (a & 0x7fffu) == 0, zb = (b & 0x7fffu) == 0;
+  if (na || nb || (fa && zb) || (fb && za)) return 1u;
+  return (((a ^ b) & 0x8000u) == 0) ? 2u : 4u;
+}
+
+__device__ __forceinline__ float class_sum(uint32_t cls) {
+  if (cls & 1u || (cls & 6u) == 6u) return __uint_as_float(0x7fc00000u);
+  return (cls & 2u) ? __uint_as_float(0x7f800000u) : __uint_as_float(0xff800000u);
+}
+
+// One pass of the whole warp over x . w (D % 8 == 0, both rows 16-byte
+// aligned): lane j takes the 16-byte chunks j, j + 32, ..., two in flight,
+// and returns (every lane) the fp64 sum of the exact products (one rounding
+// per element, then an xor butterfly: depth 8 ceil(D / 256) + 5), the
+// rows' largest |bf16 bits| and the OR of the product classes.
+__device__ __forceinline__ double dot_f64_warp(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, int D,
+                                               int lane, uint32_t* mx_out, uint32_t* mw_out, uint32_t* cls_out) {
+  const int nch = D / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x);
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  double acc = 0.0;
+  uint32_t mx = 0, mw = 0, cls = 0;
+  for (int c0 = lane; c0 < nch; c0 += 64) {
+    uint4 xv[2], wv[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int c = c0 + 32 * u;
+      xv[u] = c < nch ? __ldg(xr + c) : make_uint4(0u, 0u, 0u, 0u);
+      wv[u] = c < nch ? __ldg(wr + c) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const uint32_t xa[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w}, wa[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t a = h ? (xa[q] >> 16) : (xa[q] & 0xffffu);
+          const uint32_t b = h ? (wa[q] >> 16) : (wa[q] & 0xffffu);
+          mx = max(mx, a & 0x7fffu);
+          mw = max(mw, b & 0x7fffu);
+          cls |= product_class(a, b);
+          acc = __fma_rn(bf16_to_f64(a), bf16_to_f64(b), acc);  // zero padding adds exactly 0
+        }
+    }
+  }
+  *mx_out = __reduce_max_sync(0xffffffffu, mx);
+  *mw_out = __reduce_max_sync(0xffffffffu, mw);
+  *cls_out = __reduce_or_sync(0xffffffffu, cls);
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, s));
+  return acc;
+}
+
+// x . w by the whole warp when a row holds inf or NaN: every such element
+// makes its product inf or NaN, so the element classes alone decide the sum
+// (no limb sums). D % 8 == 0, both rows 16-byte aligned.
+static __device__ __noinline__ float dot_nonfinite_warp(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
+                                                        int D, int lane) {
+  uint32_t mx, mw, cls;
+  (void)dot_f64_warp(x, w, D, lane, &mx, &mw, &cls);
+  return class_sum(cls);
+}
+
+// The exact logit when the fp64 interval was not enough: the class pass for
+// rows holding inf or NaN (mx, mw: the rows' largest |bf16 bits|), else the
+// limb sum. Warp-uniform arguments; D % 8 == 0, rows 16-byte aligned.
+__device__ __forceinline__ uint16_t logit_exact_warp(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
+                                                     int D, float bias, uint32_t mx, uint32_t mw, int lane) {
+  const float v = (mx >= 0x7f80u || mw >= 0x7f80u) ? dot_nonfinite_warp(x, w, D, lane) : dot_rn32_warp(x, w, D, lane);
+  return logit_bits(v, bias);
+}
+
 // The bf16 logit of x . w + bias by the whole warp (every lane calls it with
 // the same arguments and gets the result), for logits an interval test left
-// open. First the fp64 sum of the exact products (one rounding per element,
-// lane j taking the 16-byte chunks j, j + 32, ..., then an xor butterfly:
-// depth 8 ceil(D / 256) + 5) with the bound of f64_sum_err; only when that
-// interval also straddles a rounding boundary, or a row holds inf or NaN,
+// open: one dot_f64_warp pass decides rows holding inf or NaN from the
+// product classes and the others from the fp64 interval (the bound of
+// f64_sum_err); only when that interval also straddles a rounding boundary
 // the exact sum (dot_rn32_warp, whose limb accumulators cost ~30 us per
 // call at D = 4096 against ~1 us for this pass). D % 8 == 0, both rows
 // 16-byte aligned.
 static __device__ __noinline__ uint16_t logit_warp(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
                                                    int D, float bias, int lane) {
-  const int nch = D / 8;
-  const uint4* xr = reinterpret_cast<const uint4*>(x);
-  const uint4* wr = reinterpret_cast<const uint4*>(w);
-  double acc = 0.0;
-  uint32_t mx = 0, mw = 0;
-  for (int c = lane; c < nch; c += 32) {
-    const uint4 xv = __ldg(xr + c), wv = __ldg(wr + c);
-    const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t a = h ? (xa[q] >> 16) : (xa[q] & 0xffffu);
-        const uint32_t b = h ? (wa[q] >> 16) : (wa[q] & 0xffffu);
-        mx = max(mx, a & 0x7fffu);
-        mw = max(mw, b & 0x7fffu);
-        acc = __fma_rn(bf16_to_f64(a), bf16_to_f64(b), acc);
-      }
-  }
-  mx = __reduce_max_sync(0xffffffffu, mx);
-  mw = __reduce_max_sync(0xffffffffu, mw);
-#pragma unroll
-  for (int s = 16; s >= 1; s >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, s));
+  uint32_t mx, mw, cls;
+  const double s = dot_f64_warp(x, w, D, lane, &mx, &mw, &cls);
+  if (cls) return logit_bits(class_sum(cls), bias);
   uint16_t lb;
-  if (mx < 0x7f80u && mw < 0x7f80u &&
-      logit_from_f64(acc, f64_sum_err(8 * ((nch + 31) / 32) + 5, D, mx, mw), bias, &lb))
-    return lb;
+  if (logit_from_f64(s, f64_sum_err(8 * ((D / 8 + 31) / 32) + 5, D, mx, mw), bias, &lb)) return lb;
   return logit_bits(dot_rn32_warp(x, w, D, lane), bias);
 }
 

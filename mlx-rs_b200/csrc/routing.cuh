@@ -307,7 +307,7 @@ __global__ void __launch_bounds__(RT_THREADS) router_fused_kernel(
         uint16_t lb;
         if (mx[i] >= 0x7f80u || mw[j] >= 0x7f80u || !logit_from_f64(v, f64_sum_err(depth, D, mx[i], mw[j]), b, &lb)) {
           const int64_t t = t0 + i < T ? t0 + i : T - 1;
-          lb = logit_bits(dot_rn32_warp(x + t * D, wg + (int64_t)e * D, D, lane), b);
+          lb = logit_exact_warp(x + t * D, wg + (int64_t)e * D, D, b, mx[i], mw[j], lane);
         }
         if (lane == i * 8 + j) mine = lb;
       }
@@ -428,7 +428,7 @@ __global__ void __launch_bounds__(RS_WARPS * 32) router_split_kernel(
         uint16_t lb;
         if (mx[i] >= 0x7f80u || mw[j] >= 0x7f80u || !logit_from_f64(v, f64_sum_err(depth, D, mx[i], mw[j]), b, &lb)) {
           const int64_t t = t0 + i < T ? t0 + i : T - 1;
-          lb = logit_bits(dot_rn32_warp(x + t * D, wg + (int64_t)e * D, D, lane), b);
+          lb = logit_exact_warp(x + t * D, wg + (int64_t)e * D, D, b, mx[i], mw[j], lane);
         }
         if (lane == i * EPW + j) mine = lb;
       }
