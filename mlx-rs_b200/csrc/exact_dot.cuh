@@ -183,6 +183,17 @@ __device__ __forceinline__ float rn32_i128(__int128 v, int lsb) {
   return rn32_limbs(limbs, 2, neg, lsb);
 }
 
+// The bf16 logit of a sum known to lie within err of s (fp64): decided when
+// both ends of [s - err, s + err] give the same logit. Returns false when
+// the interval straddles a rounding boundary or s is not finite.
+__device__ __forceinline__ bool logit_from_f64(double s, double err, float bias, uint16_t* out) {
+  if (!isfinite(s) || !isfinite(err)) return false;
+  const uint16_t a = logit_bits(__double2float_rn(__dsub_rd(s, err)), bias);
+  const uint16_t b = logit_bits(__double2float_rn(__dadd_ru(s, err)), bias);
+  *out = a;
+  return a == b;
+}
+
 // The tensor-core router's digit sums: the plane products of digits k
 // (token) and l (router row) are added per weight 2^(8 (6 - k - l)) into
 // NS sums A[g], g = k + l < NS. NS = 7 keeps all 16 products; NS = 5 (the
@@ -214,22 +225,27 @@ __device__ __forceinline__ uint16_t logit_from_digit_sums(const int32_t (&A)[NS]
   if constexpr (NS == 7) lo += (int64_t)A[5] * (1ll << 8) + A[6];
   const __int128 V = ((__int128)hi << 24) + (__int128)lo;
   const int lsb = xi.x + wi.x;
+  if constexpr (NS == 5) {
+    // First in fp64 (the three 128-bit roundings below cost more): |V| <
+    // 2^80, so (V >> 32) 2^32 is exact and adding the low 32 bits rounds
+    // once (relative error <= 2^-53); 2^lsb (lsb in [-310, 196]) scales
+    // exactly. The sum lies within B 2^lsb + 2^-52 |s| of s, both rounded up.
+    const double v = __dadd_rn(__ll2double_rn((long long)(V >> 32)) * 4294967296.0, (double)(uint32_t)V);
+    const double p2 = __hiloint2double((lsb + 1023) << 20, 0);
+    const double s = v * p2;
+    const long long Bd = (long long)(xi.y + wi.y) * (1ll << 30) + (long long)D * ((1ll << 23) + (1ll << 14));
+    const double err = __dadd_ru(__dmul_ru(__ll2double_ru(Bd), p2), __dmul_ru(fabs(s), 0x1p-52));
+    uint16_t lf;
+    if (logit_from_f64(s, err, bias, &lf)) {
+      *decided = true;
+      return lf;
+    }
+  }
   const uint16_t lb = logit_bits(rn32_i128(V, lsb), bias);
   __int128 B = (__int128)(xi.y + wi.y) * (1ll << 30);
   if constexpr (NS == 5) B += (__int128)D * ((1ll << 23) + (1ll << 14));
   *decided = B == 0 || digit_interval_same(V, B, lsb, bias, lb);
   return lb;
-}
-
-// The bf16 logit of a sum known to lie within err of s (fp64): decided when
-// both ends of [s - err, s + err] give the same logit. Returns false when
-// the interval straddles a rounding boundary or s is not finite.
-__device__ __forceinline__ bool logit_from_f64(double s, double err, float bias, uint16_t* out) {
-  if (!isfinite(s) || !isfinite(err)) return false;
-  const uint16_t a = logit_bits(__double2float_rn(__dsub_rd(s, err)), bias);
-  const uint16_t b = logit_bits(__double2float_rn(__dadd_ru(s, err)), bias);
-  *out = a;
-  return a == b;
 }
 
 // bf16 (the low 16 bits of b) -> fp64, exact for every finite value: the
